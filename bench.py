@@ -1,0 +1,404 @@
+#!/usr/bin/env python
+"""CP-ALS benchmark: seconds per ALS iteration on BASELINE config 4.
+
+Workload: order-3 synthetic tensor 12092 x 9184 x 28818 with 76.9M nonzeros,
+Zipf(1.1) indices per mode over a random permutation, lognormal values
+(cptc_gen_config(4)); CP rank R=32 (R=128 with --rank 128); one step = one
+CP-ALS iteration (3 mode updates + Gram fit).  The tensor views are streamed
+from HBM every MTTKRP (1.2 GB per mode, larger than the 126 MB L2), so no
+explicit L2 flush is needed between steps.
+
+  python bench.py [--gpus N --steps K --warmup W --rank R]
+  python bench.py --impl reference ...   # cpTC's own build (oracle/_ref)
+
+One JSON line on rank 0 (fields documented in DESIGN.md).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "CP-ALS sec/iter"
+UNIT = "s/iter"
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    p.add_argument("--config", type=int, default=4)
+    p.add_argument("--scale", type=float, default=1.0)
+    p.add_argument("--rank", type=int, default=32)
+    p.add_argument("--path", default="auto", choices=["auto", "tf32", "fp64"])
+    p.add_argument("--threshold", type=float, default=0.03)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def workload_name(a) -> str:
+    names = {1: "cfg1 128^3 200K uniform", 2: "cfg2 256^3 15.1M", 3: "cfg3 512^3 20M tiles+res",
+             4: "cfg4 12092x9184x28818 76.9M Zipf(1.1) lognormal", 5: "cfg5 183x24x1140x1717 3.3M"}
+    s = names.get(a.config, f"cfg{a.config}")
+    if a.scale != 1.0:
+        s += f" (nnz x{a.scale})"
+    return f"{s}, CP-ALS R={a.rank}"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self._nv, self._h = nv, h
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+            return self
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def _run(self):
+        nv, h = self._nv, self._h
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((sm, rs))
+            except Exception:
+                pass
+            time.sleep(0.05)
+
+    def stop(self) -> dict:
+        self._stop.set()
+        if self._t:
+            self._t.join()
+        if not self._nv or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        nv = self._nv
+        names = {
+            "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap,
+            "hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+            "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+            "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+            "hw_power_brake_slowdown": nv.nvmlClocksEventReasonHwPowerBrakeSlowdown,
+        }
+        seen = set()
+        for _, rs in self.samples:
+            for k, bit in names.items():
+                if rs & bit:
+                    seen.add(k)
+        return {"sm_mhz": float(np.median([s for s, _ in self.samples])),
+                "sm_max_mhz": float(self.max_mhz), "reasons": sorted(seen),
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# tensor generation (rank 0 generates, other ranks read the shared copy)
+# ---------------------------------------------------------------------------
+def get_tensor(a, rank: int, world: int, barrier):
+    import cptc_b200 as cp
+
+    if world == 1:
+        return cp.gen_config(a.config, a.scale)
+    path = Path(tempfile.gettempdir()) / f"cptc_bench_cfg{a.config}_{a.scale}.npz"
+    if rank == 0:
+        t = cp.gen_config(a.config, a.scale)
+        np.savez(path, dims=np.array(t.dims, dtype=np.uint64), vals=t.vals,
+                 **{f"i{m}": t.idx[m] for m in range(t.order)})
+        barrier()
+        return t
+    barrier()
+    z = np.load(path)
+    dims = tuple(int(x) for x in z["dims"])
+    return cp.CooTensor(dims, [z[f"i{m}"] for m in range(len(dims))], z["vals"])
+
+
+def algorithmic_bytes(nnz: int, order: int, R: int, rows: int) -> int:
+    """Bytes of one FP64 sparse MTTKRP per the survey's accounting: value,
+    N-1 indices and N-1 gathered factor rows per nonzero, output written
+    once."""
+    return nnz * (8 + 4 * (order - 1) + 8 * R * (order - 1)) + 8 * R * rows
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+def cpu_baseline(t, R: int) -> dict:
+    """The oracle (C++ COO MTTKRP, all host threads) on the same tensor: the
+    three MTTKRPs of one ALS iteration, which are >95% of its CPU time."""
+    from oracle import oracle as o
+
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    F = [rng.random((d, R)) for d in t.dims]
+    t0 = time.perf_counter()
+    for n in range(t.order):
+        o.mttkrp(t, F, n, threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": dt, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"one ALS iteration's {t.order} FP64 MTTKRPs on the full tensor "
+                      f"(oracle/cptc_oracle.cpp, OpenMP {threads} threads)"}
+
+
+# ---------------------------------------------------------------------------
+# engine arm
+# ---------------------------------------------------------------------------
+def run_engine(a):
+    import cptc_b200 as cp
+    from cptc_b200.engine import launch_count
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    t = get_tensor(a, rank, world, barrier)
+    eng = cp.Engine(local)
+    if world > 1:
+        uid = cp.comm_unique_id() if rank == 0 else None
+        obj = [uid]
+        dist.broadcast_object_list(obj, src=0)
+        eng.comm_init(obj[0], rank, world)
+
+    # ---- end to end through the C ABI: host COO in, factors out ----------
+    tb0 = time.perf_counter()
+    eng.load(t)
+    eng.build(a.rank, threshold=a.threshold, path=a.path)
+    eng.init_factors()
+    build_s = time.perf_counter() - tb0
+    st = eng.stats()
+
+    # warm-up iterations (also the e2e steps' starting point)
+    eng.als(a.warmup)
+
+    # ---- device-timed steps (inputs resident) ------------------------------
+    barrier()
+    clk = ClockSampler(local).start()
+    l0 = launch_count()
+    reps = eng.als(a.steps)
+    l1 = launch_count()
+    clocks = clk.stop()
+    dev_s = sum(r.ms for r in reps) / 1000.0
+    mode_ms = np.mean([r.mode_ms for r in reps], axis=0).tolist()
+    fits = [r.fit for r in reps]
+
+    # ---- e2e steps: factors from pinned host memory, ALS step, factors and
+    # fit back to host, all through the C ABI ---------------------------------
+    host_F = [eng.factor(m) for m in range(t.order)]
+    h2d = sum(f.nbytes for f in host_F)
+    barrier()
+    te0 = time.perf_counter()
+    for _ in range(a.steps):
+        for m in range(t.order):
+            eng.set_factor(m, host_F[m])
+        eng.als(1)
+        host_F = [eng.factor(m) for m in range(t.order)]
+        _ = eng.lam()
+    e2e_s = (time.perf_counter() - te0) / a.steps
+    d2h = sum(f.nbytes for f in host_F) + 8 * a.rank + 16
+
+    # ---- roofline of the dominant kernel -----------------------------------
+    prof = [eng.profile_mttkrp(n, reps=3) for n in range(t.order)]
+
+    if dist is not None:
+        import torch
+
+        v = torch.tensor([dev_s, e2e_s], dtype=torch.float64)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        dev_s, e2e_s = float(v[0]), float(v[1])
+
+    if rank != 0:
+        eng.close()
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    sp = [p["sparse_ms"] for p in prof]
+    tl = [p["tiles_ms"] for p in prof]
+    dominant = "k_mttkrp_view (FP64 sparse MTTKRP)"
+    nnz_view = st["sparse_nnz"]
+    algo = sum(algorithmic_bytes(nnz_view, t.order, a.rank, t.dims[n]) for n in range(t.order))
+    ktime = sum(sp) / 1000.0
+    peaks = measured_peaks()
+    achieved = algo / ktime / 1e9 if ktime > 0 else None
+    traffic = None
+    prof_file = ROOT / "profiles" / "traffic.json"
+    if prof_file.exists():
+        try:
+            traffic = json.loads(prof_file.read_text()).get(f"cfg{a.config}_R{a.rank}")
+        except Exception:
+            traffic = None
+
+    value = dev_s / a.steps
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": value * 1000.0,
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f64+tf32" if st["tf32_path"] else "f64",
+        "data": "synthetic (seeded generator, cptc_gen_config)",
+        "config": {
+            "workload": workload_name(a),
+            "rank": a.rank,
+            "nnz": t.nnz,
+            "dims": list(t.dims),
+            "path": "tf32 dense tiles + fp64 residual" if st["tf32_path"] else "fp64",
+            "dense_tiles": st["dense_tiles"],
+            "dense_nnz": st["dense_nnz"],
+            "avg_fill": st["avg_fill"],
+            "parallelism": f"row-slab x{world}" if world > 1 else "single GPU",
+            "l2": "views (1.2 GB/mode) stream from HBM each MTTKRP; no flush needed",
+            "build_s": build_s,
+            "mttkrp_ms_per_mode": mode_ms,
+            "final_fit": fits[-1],
+        },
+        "e2e": {"value": e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": int(l1 - l0),
+        "clocks": clocks,
+        "roofline": {
+            "bound": "hbm",
+            "kernel": dominant,
+            "achieved": achieved,
+            "peak": peaks["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": (achieved / peaks["hbm_gbs"]) if achieved else None,
+            "peak_src": peaks["src"],
+            "traffic": traffic,
+            "algorithmic_bytes_per_iter": algo,
+            "sparse_kernel_ms_per_mode": sp,
+            "tile_kernel_ms_per_mode": tl,
+        },
+    }
+    if not a.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(t, a.rank)
+    print(json.dumps(line), flush=True)
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# reference arm: cpTC's own sources rebuilt for sm_100a (oracle/_ref)
+# ---------------------------------------------------------------------------
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import cptc_b200 as cp
+
+    binary = ROOT / "oracle" / "_ref" / "cptc_opt"
+    t = cp.gen_config(a.config, a.scale)
+    if not binary.exists():
+        # Oracle port on the host cores instead.
+        from oracle import oracle as o
+
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        fits, _, _ = o.cp_als3(t, a.rank, 1, thr=a.threshold, path="fp64", threads=threads)
+        v = time.perf_counter() - t0
+        line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
+                "higher_is_better": False, "n_gpus": 0, "steps": 1, "warmup": 0,
+                "config": {"workload": workload_name(a)},
+                "cpu_baseline": {"kind": "port", "cores": threads, "value": v, "unit": UNIT,
+                                 "sample": "one full CP-ALS iteration incl. CADR and init"},
+                "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    with tempfile.TemporaryDirectory() as d:
+        tns = Path(d) / "bench.tns"
+        cp.write_tns(tns, t)
+        iters = a.warmup + a.steps
+        env = dict(os.environ)
+        r = subprocess.run([str(binary), str(tns), str(iters), str(a.rank), str(a.threshold)],
+                           capture_output=True, text=True, env=env, timeout=1800)
+        out = r.stdout
+    if r.returncode != 0:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          f"cpTC exited {r.returncode}: {r.stderr.strip()[-200:]}"}))
+        return
+    times, fits = [], []
+    for ln in out.splitlines():
+        if ln.startswith("[ALS] iter "):
+            parts = dict(kv.split("=") for kv in ln.split() if "=" in kv)
+            times.append(float(parts["time"]))
+            fits.append(float(parts["fit"]))
+    timed = times[a.warmup:]
+    v = float(np.mean(timed)) / 1000.0
+    selector = next((ln for ln in out.splitlines() if "avg_fill=" in ln), "")
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
+            "higher_is_better": False, "n_gpus": 1, "steps": len(timed), "warmup": a.warmup,
+            "ms_per_step": v * 1000.0, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f64+tf32", "data": "synthetic (same generator and seed)",
+            "config": {"workload": workload_name(a), "rank": a.rank, "nnz": t.nnz,
+                       "selector_line": selector[:300], "final_fit": fits[-1] if fits else None},
+            "cpu_baseline": {"kind": "reference", "cores": 0, "value": v, "unit": UNIT,
+                             "sample": "zhixianzhu/cpTC sources rebuilt for sm_100a "
+                                       "(oracle/build_ref.sh), per-iteration time it prints "
+                                       "([ALS] iter ... time=), after warm-up"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse_args()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_engine(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,566 @@
+// Small on-device kernels of the CP-ALS update: Gram, Hadamard, the R x R
+// inverse (truncated pseudo-inverse or ridge Cholesky), the solve applied to
+// all rows with its Gram fused in, column normalisation and the Gram fit.
+//
+// Reference counterparts: compute_gram_matrix (cuBLAS Dgemm, src/als.cu:
+// 115-134), g_gram_kernel (src/generic.cu:203-258), solve_als_system_svd
+// (cuSOLVER gesvdj + 2 Dgemm, src/solver.cu:900-1003), g_chol_solve_kernel
+// (src/generic.cu:746-819), update_mode normalisation (src/als.cu:480-517),
+// the N-order normalisation (src/generic.cu:2139-2159) and the Gram fit
+// (src/als.cu:659-715, src/generic.cu:2174-2214).
+//
+// Every reduction is two-stage with a fixed order (per-block partials, then
+// one block sums them in block order), so these kernels are deterministic.
+#include <cfloat>
+
+#include "kernels.hpp"
+
+namespace cptc {
+
+namespace {
+
+constexpr int kGramRows = 32;  // rows staged per block iteration
+
+__host__ __device__ inline int padded_rank(int R) {
+  return R <= 16 ? 16 : R <= 32 ? 32 : R <= 64 ? 64 : 128;
+}
+
+// acc[x][y] += sum_i tile[i][a0+x] * tile[i][b0+y] over nrows staged rows.
+template <int TM>
+__device__ __forceinline__ void gram_tile(const double* tile, int nrows, int Rp, int a0, int b0,
+                                          double (&acc)[TM][TM]) {
+  for (int i = 0; i < nrows; ++i) {
+    double av[TM], bv[TM];
+#pragma unroll
+    for (int x = 0; x < TM; ++x) av[x] = tile[i * Rp + a0 + x];
+#pragma unroll
+    for (int y = 0; y < TM; ++y) bv[y] = tile[i * Rp + b0 + y];
+#pragma unroll
+    for (int x = 0; x < TM; ++x)
+#pragma unroll
+      for (int y = 0; y < TM; ++y) acc[x][y] = fma(av[x], bv[y], acc[x][y]);
+  }
+}
+
+template <int TM>
+__device__ __forceinline__ void store_partial(double* part, int R, int a0, int b0,
+                                              const double (&acc)[TM][TM]) {
+#pragma unroll
+  for (int x = 0; x < TM; ++x)
+#pragma unroll
+    for (int y = 0; y < TM; ++y)
+      if (a0 + x < R && b0 + y < R) part[(a0 + x) * R + b0 + y] = acc[x][y];
+}
+
+template <int TM>
+__global__ void __launch_bounds__(256) k_gram_partial(const double* __restrict__ F, uint64_t rows,
+                                                      int R, double* __restrict__ part) {
+  constexpr int Rp = 16 * TM;
+  __shared__ double tile[kGramRows * Rp];
+  const int tid = threadIdx.x;
+  const int a0 = (tid / 16) * TM, b0 = (tid % 16) * TM;
+  double acc[TM][TM];
+#pragma unroll
+  for (int x = 0; x < TM; ++x)
+#pragma unroll
+    for (int y = 0; y < TM; ++y) acc[x][y] = 0.0;
+  for (uint64_t r0 = (uint64_t)blockIdx.x * kGramRows; r0 < rows;
+       r0 += (uint64_t)gridDim.x * kGramRows) {
+    const int nr = (int)((rows - r0 < (uint64_t)kGramRows) ? rows - r0 : kGramRows);
+    __syncthreads();
+    for (int k = tid; k < kGramRows * Rp; k += 256) {
+      const int i = k / Rp, c = k % Rp;
+      tile[k] = (i < nr && c < R) ? F[(r0 + i) * (uint64_t)R + c] : 0.0;
+    }
+    __syncthreads();
+    gram_tile<TM>(tile, nr, Rp, a0, b0, acc);
+  }
+  store_partial<TM>(part + (uint64_t)blockIdx.x * R * R, R, a0, b0, acc);
+}
+
+__global__ void k_partial_sum(const double* __restrict__ part, int nblk, int len,
+                              double* __restrict__ out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < len; i += gridDim.x * blockDim.x) {
+    double s = 0.0;
+    for (int b = 0; b < nblk; ++b) s += part[(uint64_t)b * len + i];
+    out[i] = s;
+  }
+}
+
+struct GPtrs {
+  const double* p[CPTC_MAX_ORDER];
+};
+
+__global__ void k_hadamard(GPtrs g, int ng, int R, double* __restrict__ out) {
+  const int RR = R * R;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < RR; i += gridDim.x * blockDim.x) {
+    double v = 1.0;
+    for (int k = 0; k < ng; ++k) v *= g.p[k][i];
+    out[i] = v;
+  }
+}
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Truncated pseudo-inverse of a symmetric positive semi-definite A (R <= 128)
+// by one-sided Jacobi (Hestenes 1958): W = A is rotated in column pairs
+// until its columns are mutually orthogonal, W = A V = U Sigma.  For PSD A,
+// U = V, so pinv(A) = sum_k s_k u_k u_k^T / sigma_k, s_k = sign(u_k^T A u_k)
+// (guards tiny negative eigenvalues from rounding).  sigma_k <= R*ulp(sigma
+// max) is dropped, the truncation rule of the reference (src/solver.cu:
+// 952-954).  Pairs follow a round-robin schedule: R/2 disjoint rotations per
+// step, one warp per pair, R-1 steps per sweep.  Only W lives in shared
+// memory (R*R doubles), so R = 128 fits one CTA.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) k_pinv_jacobi(const double* __restrict__ A, int R,
+                                                      double* __restrict__ Ainv,
+                                                      int* __restrict__ status) {
+  extern __shared__ double smem[];
+  double* W = smem;                        // column-major, W[c*R + r]
+  double* sig = smem + R * R;              // R
+  double* sgn = sig + R;                   // R
+  __shared__ int rotated;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  for (int k = tid; k < R * R; k += blockDim.x) {
+    const int r = k % R, c = k / R;
+    W[k] = A[r * R + c];
+  }
+  const int n = (R + 1) & ~1;  // players, with a dummy when R is odd
+  for (int sweep = 0; sweep < 40; ++sweep) {
+    if (tid == 0) rotated = 0;
+    __syncthreads();
+    for (int step = 0; step < n - 1; ++step) {
+      for (int k = warp; k < n / 2; k += nwarps) {
+        const int a = (k == 0) ? 0 : ((k - 1 + step) % (n - 1)) + 1;
+        const int bpos = n - 1 - k;
+        const int b = ((bpos - 1 + step) % (n - 1)) + 1;
+        int p = a < b ? a : b, q = a < b ? b : a;
+        if (q >= R) continue;
+        double al = 0.0, be = 0.0, ga = 0.0;
+        for (int i = lane; i < R; i += 32) {
+          const double wp = W[p * R + i], wq = W[q * R + i];
+          al = fma(wp, wp, al);
+          be = fma(wq, wq, be);
+          ga = fma(wp, wq, ga);
+        }
+        al = warp_sum(al);
+        be = warp_sum(be);
+        ga = warp_sum(ga);
+        if (fabs(ga) > 1e-15 * sqrt(al * be) && ga != 0.0) {
+          const double zeta = (be - al) / (2.0 * ga);
+          const double t = (zeta >= 0.0 ? 1.0 : -1.0) / (fabs(zeta) + sqrt(1.0 + zeta * zeta));
+          const double c = 1.0 / sqrt(1.0 + t * t), s = c * t;
+          for (int i = lane; i < R; i += 32) {
+            const double wp = W[p * R + i], wq = W[q * R + i];
+            W[p * R + i] = c * wp - s * wq;
+            W[q * R + i] = s * wp + c * wq;
+          }
+          if (lane == 0) rotated = 1;
+        }
+      }
+      __syncthreads();
+    }
+    if (!rotated) break;
+    __syncthreads();
+  }
+  // sigma_k = ||w_k||, sign from the Rayleigh quotient w_k^T A w_k.
+  for (int k = warp; k < R; k += nwarps) {
+    double s2 = 0.0, rq = 0.0;
+    for (int i = lane; i < R; i += 32) {
+      const double wi = W[k * R + i];
+      s2 = fma(wi, wi, s2);
+      double aw = 0.0;
+      for (int j = 0; j < R; ++j) aw = fma(A[i * R + j], W[k * R + j], aw);
+      rq = fma(wi, aw, rq);
+    }
+    s2 = warp_sum(s2);
+    rq = warp_sum(rq);
+    if (lane == 0) {
+      sig[k] = sqrt(s2);
+      sgn[k] = rq < 0.0 ? -1.0 : 1.0;
+    }
+  }
+  __syncthreads();
+  double smax = 0.0;
+  for (int k = 0; k < R; ++k) smax = fmax(smax, sig[k]);
+  const double tol = (double)R * (nextafter(smax, smax + 1.0) - smax);
+  for (int k = tid; k < R; k += blockDim.x) {
+    const double sk = sig[k];
+    // weight of u_k u_k^T = w_k w_k^T / sigma^2 in pinv: sign / sigma.
+    sgn[k] = (sk > tol && isfinite(sk)) ? sgn[k] / (sk * sk * sk) : 0.0;
+  }
+  __syncthreads();
+  for (int o = tid; o < R * R; o += blockDim.x) {
+    const int a = o / R, b = o % R;
+    double s = 0.0;
+    for (int k = 0; k < R; ++k) s = fma(W[k * R + a] * sgn[k], W[k * R + b], s);
+    Ainv[o] = s;
+    if (!isfinite(s)) atomicExch(status, 1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Inverse of A + eps*I by Cholesky, eps = 1e-12 * tr(A)/R + 1e-300 with the
+// reference's pivot rule (src/generic.cu:757-783): pivot s <= 0 -> sqrt(eps).
+// Right-looking factorisation in shared memory, then L^-1 column by column
+// and Ainv = L^-T L^-1.  Linv goes through `Ainv` as scratch row-major.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) k_chol_inverse(const double* __restrict__ A, int R,
+                                                       double* __restrict__ Ainv,
+                                                       double* __restrict__ Linv,
+                                                       int* __restrict__ status) {
+  extern __shared__ double L[];  // R*R row-major lower
+  __shared__ double eps_s;
+  const int tid = threadIdx.x;
+  for (int k = tid; k < R * R; k += blockDim.x) L[k] = A[k];
+  __syncthreads();
+  if (tid == 0) {
+    double tr = 0.0;
+    for (int i = 0; i < R; ++i) tr += L[i * R + i];
+    eps_s = 1e-12 * ((tr > 0.0) ? tr / (double)R : 1.0) + 1e-300;
+  }
+  __syncthreads();
+  const double eps = eps_s;
+  for (int i = tid; i < R; i += blockDim.x) L[i * R + i] += eps;
+  __syncthreads();
+  for (int j = 0; j < R; ++j) {
+    if (tid == 0) {
+      const double s = L[j * R + j];
+      L[j * R + j] = (s > 0.0) ? sqrt(s) : sqrt(eps);
+    }
+    __syncthreads();
+    const double d = L[j * R + j];
+    for (int i = j + 1 + tid; i < R; i += blockDim.x) L[i * R + j] /= d;
+    __syncthreads();
+    const int m = R - j - 1;
+    for (int k = tid; k < m * m; k += blockDim.x) {
+      const int i = j + 1 + k / m, c = j + 1 + k % m;
+      if (c <= i) L[i * R + c] -= L[i * R + j] * L[c * R + j];
+    }
+    __syncthreads();
+  }
+  // Linv (lower): column c by forward substitution, one thread per column.
+  for (int c = tid; c < R; c += blockDim.x) {
+    for (int i = 0; i < R; ++i) {
+      double s = (i == c) ? 1.0 : 0.0;
+      for (int k = c; k < i; ++k) s -= L[i * R + k] * Linv[k * R + c];
+      Linv[i * R + c] = (i < c) ? 0.0 : s / L[i * R + i];
+    }
+  }
+  __syncthreads();
+  for (int o = tid; o < R * R; o += blockDim.x) {
+    const int a = o / R, b = o % R;
+    const int k0 = a > b ? a : b;
+    double s = 0.0;
+    for (int k = k0; k < R; ++k) s = fma(Linv[k * R + a], Linv[k * R + b], s);
+    Ainv[o] = s;
+    if (!isfinite(s)) atomicExch(status, 1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// F[i, r] = sum_s FtV[i, s] * Ainv[s, r]  (Ainv symmetric), optionally divided
+// by lambda[r] (src/als.cu:496-500), with the Gram of the written rows
+// accumulated per block.  Rows are staged kGramRows at a time; Ainv lives in
+// shared memory.  Thread layout: 16 x 16 threads, each a TM x TM tile of the
+// 32-row x Rp output slab's Gram and of the product.
+// ---------------------------------------------------------------------------
+template <int TM>
+__global__ void __launch_bounds__(256) k_apply_solve(const double* __restrict__ FtV,
+                                                     const double* __restrict__ Ainv,
+                                                     const double* __restrict__ lambda,
+                                                     int divide_lambda, uint64_t rows, int R,
+                                                     double* __restrict__ F,
+                                                     double* __restrict__ part) {
+  constexpr int Rp = 16 * TM;
+  extern __shared__ double sm[];
+  double* sA = sm;                      // Rp * Rp
+  double* sX = sA + Rp * Rp;            // kGramRows * Rp  (FtV slab)
+  double* sY = sX + kGramRows * Rp;     // kGramRows * Rp  (result slab)
+  const int tid = threadIdx.x;
+  for (int k = tid; k < Rp * Rp; k += 256) {
+    const int a = k / Rp, b = k % Rp;
+    sA[k] = (a < R && b < R) ? Ainv[a * R + b] : 0.0;
+  }
+  const int a0 = (tid / 16) * TM, b0 = (tid % 16) * TM;
+  double acc[TM][TM];
+#pragma unroll
+  for (int x = 0; x < TM; ++x)
+#pragma unroll
+    for (int y = 0; y < TM; ++y) acc[x][y] = 0.0;
+  for (uint64_t r0 = (uint64_t)blockIdx.x * kGramRows; r0 < rows;
+       r0 += (uint64_t)gridDim.x * kGramRows) {
+    const int nr = (int)((rows - r0 < (uint64_t)kGramRows) ? rows - r0 : kGramRows);
+    __syncthreads();
+    for (int k = tid; k < kGramRows * Rp; k += 256) {
+      const int i = k / Rp, c = k % Rp;
+      sX[k] = (i < nr && c < R) ? FtV[(r0 + i) * (uint64_t)R + c] : 0.0;
+    }
+    __syncthreads();
+    // Product: thread handles rows i = tid / (Rp/ TM) ... flattened outputs.
+    for (int o = tid; o < kGramRows * Rp; o += 256) {
+      const int i = o / Rp, r = o % Rp;
+      double s = 0.0;
+      if (i < nr && r < R) {
+        for (int k = 0; k < R; ++k) s = fma(sX[i * Rp + k], sA[k * Rp + r], s);
+        if (divide_lambda) s /= lambda[r];
+        F[(r0 + i) * (uint64_t)R + r] = s;
+      }
+      sY[o] = s;
+    }
+    __syncthreads();
+    gram_tile<TM>(sY, nr, Rp, a0, b0, acc);
+  }
+  store_partial<TM>(part + (uint64_t)blockIdx.x * R * R, R, a0, b0, acc);
+}
+
+__global__ void k_norm_finalize(const double* __restrict__ part, int nblk, int R,
+                                int generic_norm, double* __restrict__ lambda,
+                                double* __restrict__ G, double* __restrict__ scale) {
+  extern __shared__ double sh[];  // R scales
+  const int RR = R * R;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    double s = 0.0;
+    for (int b = 0; b < nblk; ++b) s += part[(uint64_t)b * RR + r * R + r];
+    double nrm = sqrt(s);
+    double sc;
+    if (generic_norm) {
+      if (!isfinite(nrm) || nrm < 1e-14) nrm = 1.0;
+      lambda[r] = nrm;
+      sc = 1.0 / nrm;
+    } else {
+      if (nrm < 1e-14) {
+        lambda[r] = 0.0;
+        sc = 0.0;
+      } else {
+        lambda[r] = lambda[r] * nrm;
+        sc = 1.0 / nrm;
+      }
+    }
+    scale[r] = sc;
+    sh[r] = sc;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < RR; i += blockDim.x) {
+    double s = 0.0;
+    for (int b = 0; b < nblk; ++b) s += part[(uint64_t)b * RR + i];
+    G[i] = sh[i / R] * s * sh[i % R];
+  }
+}
+
+__global__ void k_scale_cols(double* __restrict__ F, uint64_t n, int R,
+                             const double* __restrict__ scale) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x)
+    F[i] *= scale[i % R];
+}
+
+__global__ void __launch_bounds__(256) k_col_dots(const double* __restrict__ F,
+                                                  const double* __restrict__ X, uint64_t rows,
+                                                  int R, double* __restrict__ part) {
+  __shared__ double sh[256];
+  // Thread t accumulates column (t % R) over rows t/R, t/R + 256/R, ...
+  const int tid = threadIdx.x;
+  const int per = 256 / R > 0 ? 256 / R : 1;
+  double s = 0.0;
+  if (R <= 256) {
+    const int c = tid % R, r0 = tid / R;
+    if (r0 < per)
+      for (uint64_t i = (uint64_t)blockIdx.x * per + r0; i < rows; i += (uint64_t)gridDim.x * per)
+        s = fma(F[i * R + c], X[i * R + c], s);
+  }
+  sh[tid] = s;
+  __syncthreads();
+  if (tid < R) {
+    double t = 0.0;
+    for (int k = 0; k < per; ++k) t += sh[k * R + tid];
+    part[(uint64_t)blockIdx.x * R + tid] = t;
+  }
+}
+
+__global__ void k_fit_final(const double* __restrict__ dot_part, int nblk,
+                            const double* __restrict__ lambda, GPtrs g, int ng, int R,
+                            double* __restrict__ out) {
+  __shared__ double sh[1024];
+  const int tid = threadIdx.x;
+  double ip = 0.0, m2 = 0.0;
+  for (int r = tid; r < R; r += blockDim.x) {
+    double d = 0.0;
+    for (int b = 0; b < nblk; ++b) d += dot_part[(uint64_t)b * R + r];
+    ip += lambda[r] * d;
+  }
+  for (int i = tid; i < R * R; i += blockDim.x) {
+    double v = lambda[i / R] * lambda[i % R];
+    for (int k = 0; k < ng; ++k) v *= g.p[k][i];
+    m2 += v;
+  }
+  sh[tid] = ip;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (tid < o) sh[tid] += sh[tid + o];
+    __syncthreads();
+  }
+  if (tid == 0) out[0] = sh[0];
+  __syncthreads();
+  sh[tid] = m2;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (tid < o) sh[tid] += sh[tid + o];
+    __syncthreads();
+  }
+  if (tid == 0) out[1] = sh[0];
+}
+
+__global__ void k_sumsq_partial(const double* __restrict__ v, uint64_t n, double* __restrict__ part) {
+  __shared__ double sh[256];
+  double s = 0.0;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x)
+    s = fma(v[i], v[i], s);
+  sh[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part[blockIdx.x] = sh[0];
+}
+
+__global__ void k_sum_serial(const double* __restrict__ part, int n, double* __restrict__ out) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    double s = 0.0;
+    for (int i = 0; i < n; ++i) s += part[i];
+    out[0] = s;
+  }
+}
+
+}  // namespace
+
+int launch_gram_partial(const double* F, uint64_t rows, int R, double* part, int max_blocks,
+                        cudaStream_t s) {
+  CPTC_REQUIRE(R >= 1 && R <= 128, CPTC_E_UNSUP, "rank must be in [1, 128]");
+  int nblk = (int)((rows + kGramRows - 1) / kGramRows);
+  if (nblk > max_blocks) nblk = max_blocks;
+  if (nblk < 1) nblk = 1;
+  switch (padded_rank(R)) {
+    case 16: k_gram_partial<1><<<nblk, 256, 0, s>>>(F, rows, R, part); break;
+    case 32: k_gram_partial<2><<<nblk, 256, 0, s>>>(F, rows, R, part); break;
+    case 64: k_gram_partial<4><<<nblk, 256, 0, s>>>(F, rows, R, part); break;
+    default: k_gram_partial<8><<<nblk, 256, 0, s>>>(F, rows, R, part); break;
+  }
+  CPTC_LAUNCH_CHECK();
+  return nblk;
+}
+
+void launch_partial_sum(const double* part, int nblk, int len, double* out, cudaStream_t s) {
+  k_partial_sum<<<grid_for((uint64_t)len, 256), 256, 0, s>>>(part, nblk, len, out);
+  CPTC_LAUNCH_CHECK();
+}
+
+void launch_gram_reduce(const double* part, int nblk, int R, double* G, cudaStream_t s) {
+  launch_partial_sum(part, nblk, R * R, G, s);
+}
+
+void launch_hadamard(const double* const* Gs, int ng, int R, double* FtF, cudaStream_t s) {
+  GPtrs g{};
+  for (int k = 0; k < ng; ++k) g.p[k] = Gs[k];
+  k_hadamard<<<grid_for((uint64_t)R * R, 256), 256, 0, s>>>(g, ng, R, FtF);
+  CPTC_LAUNCH_CHECK();
+}
+
+void launch_sym_inverse(const double* A, int R, int pinv, double* Ainv, int* status,
+                        cudaStream_t s) {
+  CPTC_REQUIRE(R >= 1 && R <= 128, CPTC_E_UNSUP, "rank must be in [1, 128]");
+  if (pinv) {
+    const int n = (R + 1) & ~1;
+    int threads = 32 * (n / 2);
+    if (threads > 1024) threads = 1024;
+    if (threads < 64) threads = 64;
+    const size_t smem = ((size_t)R * R + 2 * R) * sizeof(double);
+    CPTC_CUDA(cudaFuncSetAttribute(k_pinv_jacobi, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)smem));
+    k_pinv_jacobi<<<1, threads, smem, s>>>(A, R, Ainv, status);
+  } else {
+    const size_t smem = (size_t)R * R * sizeof(double);
+    CPTC_CUDA(cudaFuncSetAttribute(k_chol_inverse, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)smem));
+    // Linv scratch: the upper half of Ainv's storage is not enough, so the
+    // caller's Ainv buffer holds 2*R*R doubles.
+    k_chol_inverse<<<1, 512, smem, s>>>(A, R, Ainv, Ainv + (size_t)R * R, status);
+  }
+  CPTC_LAUNCH_CHECK();
+}
+
+int launch_apply_solve(const double* FtV, const double* Ainv, const double* lambda,
+                       int divide_lambda, uint64_t rows, int R, double* F, double* part,
+                       int max_blocks, cudaStream_t s) {
+  int nblk = (int)((rows + kGramRows - 1) / kGramRows);
+  if (nblk > max_blocks) nblk = max_blocks;
+  if (nblk < 1) nblk = 1;
+  const int Rp = padded_rank(R);
+  const size_t smem = ((size_t)Rp * Rp + 2 * (size_t)kGramRows * Rp) * sizeof(double);
+#define CPTC_APPLY(TM)                                                                       \
+  do {                                                                                       \
+    CPTC_CUDA(cudaFuncSetAttribute(k_apply_solve<TM>,                                        \
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+    k_apply_solve<TM><<<nblk, 256, smem, s>>>(FtV, Ainv, lambda, divide_lambda, rows, R, F,  \
+                                              part);                                         \
+  } while (0)
+  switch (Rp) {
+    case 16: CPTC_APPLY(1); break;
+    case 32: CPTC_APPLY(2); break;
+    case 64: CPTC_APPLY(4); break;
+    default: CPTC_APPLY(8); break;
+  }
+#undef CPTC_APPLY
+  CPTC_LAUNCH_CHECK();
+  return nblk;
+}
+
+void launch_norm_finalize(const double* part, int nblk, int R, int generic_norm,
+                          double* lambda, double* G, double* scale, cudaStream_t s) {
+  k_norm_finalize<<<1, 1024, R * sizeof(double), s>>>(part, nblk, R, generic_norm, lambda, G,
+                                                      scale);
+  CPTC_LAUNCH_CHECK();
+}
+
+void launch_scale_cols(double* F, uint64_t rows, int R, const double* scale, cudaStream_t s) {
+  const uint64_t n = rows * (uint64_t)R;
+  k_scale_cols<<<grid_for(n, 256, 148 * 32), 256, 0, s>>>(F, n, R, scale);
+  CPTC_LAUNCH_CHECK();
+}
+
+int launch_col_dots(const double* F, const double* FtV, uint64_t rows, int R, double* part,
+                    int max_blocks, cudaStream_t s) {
+  const int per = 256 / R > 0 ? 256 / R : 1;
+  int nblk = (int)((rows + per - 1) / per);
+  if (nblk > max_blocks) nblk = max_blocks;
+  if (nblk < 1) nblk = 1;
+  k_col_dots<<<nblk, 256, 0, s>>>(F, FtV, rows, R, part);
+  CPTC_LAUNCH_CHECK();
+  return nblk;
+}
+
+void launch_fit_final(const double* dot_part, int nblk, const double* lambda,
+                      const double* const* Gs, int ng, int R, double* out, cudaStream_t s) {
+  GPtrs g{};
+  for (int k = 0; k < ng; ++k) g.p[k] = Gs[k];
+  k_fit_final<<<1, 1024, 0, s>>>(dot_part, nblk, lambda, g, ng, R, out);
+  CPTC_LAUNCH_CHECK();
+}
+
+void launch_sumsq(const double* v, uint64_t n, double* part, int max_blocks, double* out,
+                  cudaStream_t s) {
+  int nblk = (int)grid_for(n, 256, (unsigned)max_blocks);
+  k_sumsq_partial<<<nblk, 256, 0, s>>>(v, n, part);
+  CPTC_LAUNCH_CHECK();
+  k_sum_serial<<<1, 32, 0, s>>>(part, nblk, out);
+  CPTC_LAUNCH_CHECK();
+}
+
+}  // namespace cptc

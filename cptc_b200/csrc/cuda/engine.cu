@@ -1,0 +1,653 @@
+// The CP-ALS engine: load, build (relabel, partition, views, path choice),
+// factor initialisation, MTTKRP and the ALS loop, plus the C ABI.
+//
+// Reference drivers: main (src/main.cu:22-680), execute_als_decomposition
+// (src/als.cu:362-821) and run_generic_cp (src/generic.cu:1639-2366).
+#include <omp.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <random>
+
+#include "../host/coo.hpp"
+#include "../host/reorder.hpp"
+#include "comm.hpp"
+#include "kernels.hpp"
+
+namespace cptc {
+
+unsigned long long g_launches = 0;
+
+namespace {
+
+__global__ void k_relabel(uint32_t* __restrict__ idx, uint64_t n, const uint32_t* __restrict__ map) {
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < n;
+       e += (uint64_t)gridDim.x * blockDim.x)
+    idx[e] = map[idx[e]];
+}
+
+// Rows of a relabelled matrix back to original order: out[a] = in[map[a]].
+void gather_rows_host(const std::vector<double>& in, const std::vector<uint32_t>& map, int R,
+                      double* out) {
+  const int64_t n = (int64_t)map.size();
+#pragma omp parallel for schedule(static)
+  for (int64_t a = 0; a < n; ++a)
+    std::memcpy(out + a * R, in.data() + (uint64_t)map[a] * R, R * sizeof(double));
+}
+
+}  // namespace
+
+Engine::Engine(int dev) : device(dev) {
+  int n = 0;
+  CPTC_CUDA(cudaGetDeviceCount(&n));
+  CPTC_REQUIRE(dev >= 0 && dev < n, CPTC_E_ARG, "no such CUDA device");
+  CPTC_CUDA(cudaSetDevice(dev));
+  CPTC_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  for (auto& e : ev) CPTC_CUDA(cudaEventCreate(&e));
+  CPTC_CUDA(cudaMallocHost((void**)&h_scal, 8 * sizeof(double)));
+}
+
+Engine::~Engine() {
+  cudaSetDevice(device);
+  if (stream) cudaStreamSynchronize(stream);
+  comm_destroy(*this);
+  for (auto& e : ev)
+    if (e) cudaEventDestroy(e);
+  if (h_scal) cudaFreeHost(h_scal);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+uint64_t Engine::device_bytes() const {
+  uint64_t b = vals.bytes();
+  for (int m = 0; m < N; ++m) b += idx[m].bytes() + F[m].bytes() + G[m].bytes();
+  for (const View& v : views)
+    b += v.gw.bytes() + v.oidx.bytes() + v.val.bytes() + v.rows.bytes() + v.task_row.bytes();
+  b += tiles.tile.bytes() + tiles.start.bytes() + tiles.lid.bytes() + tiles.val.bytes();
+  for (int m = 0; m < 3; ++m) b += tile_order[m].bytes();
+  b += FtV.bytes() + FtF.bytes() + Ainv.bytes() + gpart.bytes() + dots.bytes() + lambda.bytes();
+  return b;
+}
+
+void Engine::load(const cptc_coo* t) {
+  CPTC_REQUIRE(t && t->order >= 2 && t->order <= CPTC_MAX_ORDER, CPTC_E_ARG,
+               "tensor order must be in [2, 8]");
+  CPTC_REQUIRE(t->nnz < (1ull << 32), CPTC_E_UNSUP, "more than 2^32-1 nonzeros");
+  CPTC_CUDA(cudaSetDevice(device));
+  built = false;
+  have_factors = false;
+  views.clear();
+  N = t->order;
+  nnz = t->nnz;
+  for (int m = 0; m < N; ++m) {
+    CPTC_REQUIRE(t->dims[m] >= 1 && t->dims[m] <= 0xFFFFFFFFull, CPTC_E_ARG, "bad mode length");
+    dims[m] = t->dims[m];
+    CPTC_REQUIRE(t->idx[m] != nullptr || nnz == 0, CPTC_E_ARG, "null index array");
+  }
+  CPTC_REQUIRE(t->vals != nullptr || nnz == 0, CPTC_E_ARG, "null value array");
+  // Host-side bounds check: an index beyond its mode length would make
+  // every later kernel read out of bounds.
+  for (int m = 0; m < N; ++m) {
+    const uint32_t* ix = t->idx[m];
+    const uint64_t d = dims[m];
+    int bad = 0;
+#pragma omp parallel for reduction(| : bad) schedule(static)
+    for (int64_t e = 0; e < (int64_t)nnz; ++e) bad |= (ix[e] >= d);
+    CPTC_REQUIRE(!bad, CPTC_E_ARG, "index out of range for its mode length");
+  }
+  for (int m = 0; m < N; ++m) {
+    idx[m].alloc(nnz);
+    if (nnz) CPTC_CUDA(cudaMemcpyAsync(idx[m].p, t->idx[m], nnz * 4, cudaMemcpyHostToDevice, stream));
+  }
+  vals.alloc(nnz);
+  if (nnz) CPTC_CUDA(cudaMemcpyAsync(vals.p, t->vals, nnz * 8, cudaMemcpyHostToDevice, stream));
+  // Host copy of the coordinates for the relabelling (degree sort / HITS).
+  host_idx.assign(N, {});
+  for (int m = 0; m < N; ++m) host_idx[m].assign(t->idx[m], t->idx[m] + nnz);
+  CPTC_CUDA(cudaStreamSynchronize(stream));
+}
+
+void Engine::reorder() {
+  perm.assign(N, {});
+  int kind = opts.reorder;
+  if (!generic) {
+    // Order-3 hybrid pipeline: CADR unless explicitly disabled.
+    if (kind == CPTC_REORDER_DEFAULT) kind = CPTC_REORDER_CADR;
+    if (kind == CPTC_REORDER_CADR) {
+      for (int m = 0; m < N; ++m) cadr_perm_ref(dims[m], nnz, host_idx[m].data(), perm[m]);
+    } else if (kind != CPTC_REORDER_NONE) {
+      std::vector<const uint32_t*> ip(N);
+      for (int m = 0; m < N; ++m) ip[m] = host_idx[m].data();
+      reorder_generic(N, dims, nnz, ip.data(), kind, opts.reorder_rounds, opts.reorder_sample,
+                      perm, &reorder_note);
+      perm.resize(N);
+    }
+  } else {
+    if (kind == CPTC_REORDER_DEFAULT) kind = (N >= 4) ? CPTC_REORDER_HITS : CPTC_REORDER_CADR;
+    std::vector<const uint32_t*> ip(N);
+    for (int m = 0; m < N; ++m) ip[m] = host_idx[m].data();
+    reorder_generic(N, dims, nnz, ip.data(), kind, opts.reorder_rounds, opts.reorder_sample,
+                    perm, &reorder_note);
+    perm.resize(N);
+  }
+  for (int m = 0; m < N; ++m) {
+    if (perm[m].empty()) continue;
+    DArray<uint32_t> map(dims[m]);
+    CPTC_CUDA(cudaMemcpyAsync(map.p, perm[m].data(), dims[m] * 4, cudaMemcpyHostToDevice, stream));
+    k_relabel<<<grid_for(nnz, 256, 148 * 16), 256, 0, stream>>>(idx[m].p, nnz, map.p);
+    CPTC_LAUNCH_CHECK();
+    CPTC_CUDA(cudaStreamSynchronize(stream));
+  }
+}
+
+void Engine::alloc_workspace() {
+  uint64_t maxd = 0;
+  for (int m = 0; m < N; ++m) maxd = std::max<uint64_t>(maxd, dims[m]);
+  FtV.alloc(maxd * (uint64_t)R);
+  FtF.alloc((uint64_t)R * R);
+  Ainv.alloc(2 * (uint64_t)R * R);
+  gpart_blocks = 148;
+  gpart.alloc((uint64_t)gpart_blocks * R * R);
+  dots.alloc((uint64_t)gpart_blocks * R);
+  scal.alloc(8);
+  status.alloc(1);
+  lambda.alloc(R);
+  for (int m = 0; m < N; ++m) {
+    F[m].alloc(dims[m] * (uint64_t)R);
+    G[m].alloc((uint64_t)R * R);
+  }
+}
+
+void Engine::build(int R_, double threshold, const cptc_opts* o) {
+  CPTC_REQUIRE(N >= 2, CPTC_E_ARG, "load a tensor first");
+  CPTC_REQUIRE(R_ >= 1 && R_ <= 128, CPTC_E_UNSUP, "rank must be in [1, 128]");
+  CPTC_CUDA(cudaSetDevice(device));
+  const auto t0 = std::chrono::steady_clock::now();
+  if (o) opts = *o;
+  else cptc_opts_default(&opts);
+  R = R_;
+  generic = (N != 3) || opts.generic;
+  built = false;
+  have_factors = false;
+  views.clear();
+  tiles = TilePool{};
+  for (auto& t : tile_order) t.release();
+  tf32 = false;
+  avg_fill = 0.0;
+  cutoff = 0;
+
+  // Relabel from the original coordinates (the permutation depends on the
+  // path: CADR for order 3, HITS/CADR with tie-break for the N-order path).
+  for (int m = 0; m < N; ++m)
+    if (nnz)
+      CPTC_CUDA(cudaMemcpyAsync(idx[m].p, host_idx[m].data(), nnz * 4, cudaMemcpyHostToDevice,
+                                stream));
+  reorder();
+  {
+    DArray<double> part(148 * 16);
+    launch_sumsq(vals.p, nnz, part.p, 148 * 16, scal_tmp(), stream);
+    CPTC_CUDA(cudaMemcpyAsync(&x_norm_sq, scal_tmp(), sizeof(double), cudaMemcpyDeviceToHost,
+                              stream));
+    CPTC_CUDA(cudaStreamSynchronize(stream));
+  }
+
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  fill_min = opts.fill_min > 0.0 ? opts.fill_min
+                                 : std::max(0.08, 0.11 / std::sqrt((double)sms / 24.0));
+
+  DArray<uint32_t> sel;
+  uint64_t nsel = nnz;
+  bool use_sel = false;
+  if (!generic && opts.path != CPTC_PATH_FP64 && nnz > 0) {
+    partition_tiles3(*this, threshold, sel, nsel, tile_order);
+    avg_fill = tiles.ntiles ? (double)tiles.nnz / ((double)tiles.ntiles * 4096.0) : 0.0;
+    if (opts.path == CPTC_PATH_TF32) tf32 = true;
+    else tf32 = (avg_fill >= fill_min) && tiles.ntiles > 0 && (R % 8 == 0);
+    if (tf32) {
+      CPTC_REQUIRE(R % 8 == 0, CPTC_E_UNSUP,
+                   "the TF32 tile path needs the rank to be a multiple of 8");
+      use_sel = true;
+    } else {
+      tiles = TilePool{};
+      for (auto& t : tile_order) t.release();
+      sel.release();
+      nsel = nnz;
+    }
+  }
+  views.resize(N);
+  alloc_workspace();
+  comm_prepare(*this);
+  slab_tiles(*this);
+  for (int n = 0; n < N; ++n) {
+    if (nranks > 1) {
+      DArray<uint32_t> mine;
+      uint64_t nmine = 0;
+      slab_select(*this, n, use_sel ? sel.p : nullptr, use_sel ? nsel : nnz, mine, nmine);
+      build_view(*this, views[n], n, mine.p, nmine);
+    } else {
+      build_view(*this, views[n], n, use_sel ? sel.p : nullptr, use_sel ? nsel : nnz);
+    }
+  }
+  CPTC_CUDA(cudaStreamSynchronize(stream));
+  build_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  built = true;
+}
+
+double* Engine::scal_tmp() {
+  if (!scal.p) scal.alloc(8);
+  return scal.p;
+}
+
+void Engine::init_factors() {
+  CPTC_REQUIRE(built, CPTC_E_ARG, "call cptc_build first");
+  if (!generic) {
+    // src/common.cu:83-101: mt19937(42), U[0,1), modes in order, row-major,
+    // in the relabelled index space.
+    std::mt19937 gen(42);
+    std::uniform_real_distribution<double> dis(0.0, 1.0);
+    for (int m = 0; m < N; ++m) {
+      std::vector<double> h(dims[m] * (uint64_t)R);
+      for (auto& x : h) x = dis(gen);
+      CPTC_CUDA(cudaMemcpyAsync(F[m].p, h.data(), h.size() * 8, cudaMemcpyHostToDevice, stream));
+      CPTC_CUDA(cudaStreamSynchronize(stream));
+    }
+  } else {
+    // src/generic.cu:1754-1783: mt19937(seed) in original order, each row
+    // carried to its relabelled position.
+    std::mt19937 gen(opts.seed);
+    std::uniform_real_distribution<double> dis(0.0, 1.0);
+    for (int m = 0; m < N; ++m) {
+      std::vector<double> u(dims[m] * (uint64_t)R), h(u.size());
+      for (auto& x : u) x = dis(gen);
+      for (uint64_t a = 0; a < dims[m]; ++a) {
+        const uint64_t nw = perm[m].empty() ? a : perm[m][a];
+        std::memcpy(h.data() + nw * R, u.data() + a * R, R * sizeof(double));
+      }
+      CPTC_CUDA(cudaMemcpyAsync(F[m].p, h.data(), h.size() * 8, cudaMemcpyHostToDevice, stream));
+      CPTC_CUDA(cudaStreamSynchronize(stream));
+    }
+  }
+  std::vector<double> one(R, 1.0);
+  CPTC_CUDA(cudaMemcpyAsync(lambda.p, one.data(), R * 8, cudaMemcpyHostToDevice, stream));
+  CPTC_CUDA(cudaStreamSynchronize(stream));
+  have_factors = true;
+  grams_valid = false;
+}
+
+void Engine::set_factor(int m, const double* host) {
+  CPTC_REQUIRE(built && m >= 0 && m < N && host, CPTC_E_ARG, "bad mode or call order");
+  std::vector<double> h(dims[m] * (uint64_t)R);
+  for (uint64_t a = 0; a < dims[m]; ++a) {
+    const uint64_t nw = perm[m].empty() ? a : perm[m][a];
+    std::memcpy(h.data() + nw * R, host + a * R, R * sizeof(double));
+  }
+  CPTC_CUDA(cudaMemcpyAsync(F[m].p, h.data(), h.size() * 8, cudaMemcpyHostToDevice, stream));
+  CPTC_CUDA(cudaStreamSynchronize(stream));
+  if (!have_factors) {
+    std::vector<double> one(R, 1.0);
+    CPTC_CUDA(cudaMemcpyAsync(lambda.p, one.data(), R * 8, cudaMemcpyHostToDevice, stream));
+    CPTC_CUDA(cudaStreamSynchronize(stream));
+  }
+  have_factors = true;
+  grams_valid = false;
+}
+
+void Engine::get_factor(int m, double* host) {
+  CPTC_REQUIRE(built && have_factors && m >= 0 && m < N && host, CPTC_E_ARG,
+               "bad mode or call order");
+  std::vector<double> h(dims[m] * (uint64_t)R);
+  CPTC_CUDA(cudaMemcpyAsync(h.data(), F[m].p, h.size() * 8, cudaMemcpyDeviceToHost, stream));
+  CPTC_CUDA(cudaStreamSynchronize(stream));
+  if (perm[m].empty()) std::memcpy(host, h.data(), h.size() * 8);
+  else gather_rows_host(h, perm[m], R, host);
+}
+
+void Engine::fetch_rows(const double* dev, int m, double* host) {
+  std::vector<double> h(dims[m] * (uint64_t)R);
+  CPTC_CUDA(cudaMemcpyAsync(h.data(), dev, h.size() * 8, cudaMemcpyDeviceToHost, stream));
+  CPTC_CUDA(cudaStreamSynchronize(stream));
+  if (perm[m].empty()) std::memcpy(host, h.data(), h.size() * 8);
+  else gather_rows_host(h, perm[m], R, host);
+}
+
+// FtV = MTTKRP of `mode` (relabelled rows): zero, dense tiles, residual.
+void Engine::mttkrp(int mode) {
+  CPTC_CUDA(cudaMemsetAsync(FtV.p, 0, dims[mode] * (uint64_t)R * sizeof(double), stream));
+  mttkrp_tiles(mode);
+  mttkrp_sparse(mode);
+}
+
+void Engine::mttkrp_tiles(int mode) {
+  if (tf32 && tile_cnt[mode] > 0) {
+    // Order-3 roles (src/dense.cu:339-1075): mode 0 contracts j in TF32 and
+    // weights k-slabs; mode 1 contracts i, weights k; mode 2 contracts i,
+    // weights j.
+    TileArgs ta{};
+    ta.tile = tiles.tile.p;
+    ta.start = tiles.start.p;
+    ta.lid = tiles.lid.p;
+    ta.val = tiles.val.p;
+    ta.ntiles = tile_cnt[mode];
+    ta.R = R;
+    ta.tslot = mode;
+    ta.cslot = (mode == 0) ? 1 : 0;
+    ta.sslot = (mode == 2) ? 1 : 2;
+    for (int m = 0; m < 3; ++m) ta.dims[m] = dims[m];
+    ta.Fc = F[ta.cslot].p;
+    ta.Fs = F[ta.sslot].p;
+    ta.nouter = 0;
+    ta.store_dups = 1;
+    ta.out = FtV.p;
+    launch_mttkrp_tiles3(ta, tile_order[mode].p, stream);
+  }
+}
+
+void Engine::mttkrp_sparse(int mode) {
+  const View& v = views[mode];
+  MttkrpArgs a{};
+  a.gw = v.gw.p;
+  a.oidx = v.oidx.p;
+  a.val = v.val.p;
+  a.rows = v.rows.p;
+  a.task_row = v.task_row.p;
+  a.nnz = v.nnz;
+  a.ntasks = v.ntasks;
+  a.nout = v.nout;
+  a.R = R;
+  a.Fg = F[v.gmode].p;
+  for (int q = 0; q < v.nout; ++q) a.Fo[q] = F[v.omode[q]].p;
+  a.out = FtV.p;
+  launch_mttkrp_view(a, stream);
+}
+
+void Engine::gram_of(int m) {
+  const int nb = launch_gram_partial(F[m].p, dims[m], R, gpart.p, gpart_blocks, stream);
+  launch_gram_reduce(gpart.p, nb, R, G[m].p, stream);
+}
+
+// One mode update: Hadamard of the other Grams, MTTKRP, inverse, apply,
+// normalisation.  Order-3 semantics (src/als.cu:480-517): pseudo-inverse,
+// divide by lambda, norm < 1e-14 zeroes the column, lambda *= norm.
+// N-order semantics (src/generic.cu:2109-2170): ridge Cholesky (default),
+// lambda = norms with norm < 1e-14 -> 1.
+void Engine::update_mode(int n) {
+  const double* gs[CPTC_MAX_ORDER];
+  int ng = 0;
+  for (int m = 0; m < N; ++m)
+    if (m != n) gs[ng++] = G[m].p;
+  launch_hadamard(gs, ng, R, FtF.p, stream);
+  cudaEventRecord(ev[2 * n], stream);
+  mttkrp(n);
+  cudaEventRecord(ev[2 * n + 1], stream);
+  int pinv = generic ? 0 : 1;
+  if (opts.solver == CPTC_SOLVER_CHOL) pinv = 0;
+  if (opts.solver == CPTC_SOLVER_PINV) pinv = 1;
+  launch_sym_inverse(FtF.p, R, pinv, Ainv.p, status.p, stream);
+  comm_reduce_ftv(*this, n);
+  const uint64_t lo = row_lo(n), rows = row_hi(n) - lo;
+  const int nb = launch_apply_solve(FtV.p + lo * R, Ainv.p, lambda.p, generic ? 0 : 1, rows, R,
+                                    F[n].p + lo * R, gpart.p, gpart_blocks, stream);
+  comm_allreduce_gram(*this, nb);
+  launch_norm_finalize(gpart.p, comm_gram_blocks(*this, nb), R, generic ? 1 : 0, lambda.p,
+                       G[n].p, colscale(), stream);
+  launch_scale_cols(F[n].p + lo * R, rows, R, colscale(), stream);
+  comm_allgather_factor(*this, n);
+}
+
+double* Engine::colscale() {
+  if (!cscale.p) cscale.alloc(R);
+  return cscale.p;
+}
+
+void Engine::als(int iters, cptc_iter_cb cb, void* user) {
+  CPTC_REQUIRE(built && have_factors, CPTC_E_ARG, "call cptc_build and cptc_init_factors first");
+  CPTC_CUDA(cudaSetDevice(device));
+  if (!grams_valid) {
+    for (int m = 0; m < N; ++m) gram_of(m);
+    grams_valid = true;
+  }
+  CPTC_CUDA(cudaMemsetAsync(status.p, 0, sizeof(int), stream));
+  const double xn = std::sqrt(x_norm_sq);
+  for (int it = 0; it < iters; ++it) {
+    cudaEventRecord(ev[2 * CPTC_MAX_ORDER], stream);
+    for (int n = 0; n < N; ++n) update_mode(n);
+    // Gram fit from the last mode's MTTKRP and factor.
+    const int last = N - 1;
+    const uint64_t lo = row_lo(last), rows = row_hi(last) - lo;
+    const int nb = launch_col_dots(F[last].p + lo * R, FtV.p + lo * R, rows, R, dots.p,
+                                   gpart_blocks, stream);
+    comm_allreduce_dots(*this, nb);
+    const double* gs[CPTC_MAX_ORDER];
+    for (int m = 0; m < N; ++m) gs[m] = G[m].p;
+    launch_fit_final(dots.p, comm_dot_blocks(*this, nb), lambda.p, gs, N, R, scal.p, stream);
+    CPTC_CUDA(cudaMemcpyAsync(h_scal, scal.p, 2 * sizeof(double), cudaMemcpyDeviceToHost, stream));
+    int h_status = 0;
+    CPTC_CUDA(cudaMemcpyAsync(h_scal + 4, status.p, sizeof(int), cudaMemcpyDeviceToHost, stream));
+    cudaEventRecord(ev[2 * CPTC_MAX_ORDER + 1], stream);
+    CPTC_CUDA(cudaEventSynchronize(ev[2 * CPTC_MAX_ORDER + 1]));
+    std::memcpy(&h_status, h_scal + 4, sizeof(int));
+    CPTC_REQUIRE(h_status == 0, CPTC_E_NUMERIC, "non-finite values in the R x R solve");
+    const double iprod = h_scal[0], model2 = h_scal[1];
+    const double res2 = std::max(x_norm_sq - 2.0 * iprod + model2, 0.0);
+    const double fit = (xn > 0.0) ? 1.0 - std::sqrt(res2) / xn : 0.0;
+    float ms_it = 0.f;
+    cudaEventElapsedTime(&ms_it, ev[2 * CPTC_MAX_ORDER], ev[2 * CPTC_MAX_ORDER + 1]);
+    double mode_ms[CPTC_MAX_ORDER] = {0};
+    for (int n = 0; n < N; ++n) {
+      float t = 0.f;
+      cudaEventElapsedTime(&t, ev[2 * n], ev[2 * n + 1]);
+      mode_ms[n] = t;
+    }
+    last_iprod = iprod;
+    last_model2 = model2;
+    last_fit = fit;
+    if (cb) cb(it + 1, (double)ms_it, fit, mode_ms, N, user);
+  }
+}
+
+}  // namespace cptc
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+using cptc::CptcError;
+using cptc::Engine;
+
+struct cptc_ctx {
+  Engine* e = nullptr;
+  std::string err;
+};
+
+namespace {
+
+template <class F>
+int guarded(cptc_ctx* c, F&& f) {
+  if (!c || !c->e) return CPTC_E_ARG;
+  try {
+    f(*c->e);
+    c->err.clear();
+    return CPTC_OK;
+  } catch (const CptcError& x) {
+    c->err = x.what();
+    return x.code;
+  } catch (const std::bad_alloc&) {
+    c->err = "host allocation failed";
+    return CPTC_E_NOMEM;
+  } catch (const std::exception& x) {
+    c->err = x.what();
+    return CPTC_E_ARG;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int cptc_opts_default(cptc_opts* o) {
+  if (!o) return CPTC_E_ARG;
+  std::memset(o, 0, sizeof(*o));
+  o->path = CPTC_PATH_AUTO;
+  o->fill_min = 0.0;
+  o->generic = 0;
+  o->reorder = CPTC_REORDER_DEFAULT;
+  o->reorder_rounds = 3;
+  o->reorder_sample = 8000000ull;
+  o->solver = CPTC_SOLVER_DEFAULT;
+  o->seed = 42u;
+  o->dense_generic = 1;
+  o->dense_thr_generic = 0.03;
+  o->dense_inner[0] = 0;
+  o->dense_inner[1] = 1;
+  o->dense_inner[2] = 2;
+  o->verbose = 0;
+  return CPTC_OK;
+}
+
+int cptc_create(cptc_ctx** out, int device, int flags) {
+  (void)flags;
+  if (!out) return CPTC_E_ARG;
+  *out = nullptr;
+  cptc_ctx* c = new (std::nothrow) cptc_ctx;
+  if (!c) return CPTC_E_NOMEM;
+  try {
+    c->e = new Engine(device);
+  } catch (const CptcError& x) {
+    c->err = x.what();
+    const int code = x.code;
+    delete c;
+    return code;
+  }
+  *out = c;
+  return CPTC_OK;
+}
+
+int cptc_destroy(cptc_ctx* c) {
+  if (!c) return CPTC_E_ARG;
+  delete c->e;
+  delete c;
+  return CPTC_OK;
+}
+
+const char* cptc_last_error(const cptc_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+int cptc_load_coo(cptc_ctx* c, const cptc_coo* t) {
+  return guarded(c, [&](Engine& e) { e.load(t); });
+}
+
+int cptc_comm_init(cptc_ctx* c, const unsigned char id[128], int rank, int nranks) {
+  return guarded(c, [&](Engine& e) {
+    CPTC_REQUIRE(id != nullptr, CPTC_E_ARG, "null id");
+    cptc::comm_init(e, id, rank, nranks);
+  });
+}
+
+int cptc_build(cptc_ctx* c, int R, double threshold, const cptc_opts* o) {
+  return guarded(c, [&](Engine& e) { e.build(R, threshold, o); });
+}
+
+int cptc_init_factors(cptc_ctx* c) {
+  return guarded(c, [&](Engine& e) { e.init_factors(); });
+}
+
+int cptc_set_factors(cptc_ctx* c, int mode, const double* host) {
+  return guarded(c, [&](Engine& e) { e.set_factor(mode, host); });
+}
+
+int cptc_get_factors(cptc_ctx* c, int mode, double* host) {
+  return guarded(c, [&](Engine& e) { e.get_factor(mode, host); });
+}
+
+int cptc_get_lambda(cptc_ctx* c, double* host) {
+  return guarded(c, [&](Engine& e) {
+    CPTC_REQUIRE(e.built && e.have_factors && host, CPTC_E_ARG, "no factors yet");
+    CPTC_CUDA(cudaMemcpy(host, e.lambda.p, e.R * sizeof(double), cudaMemcpyDeviceToHost));
+  });
+}
+
+int cptc_mttkrp(cptc_ctx* c, int mode, double* host_out) {
+  return guarded(c, [&](Engine& e) {
+    CPTC_REQUIRE(e.built && e.have_factors && mode >= 0 && mode < e.N && host_out, CPTC_E_ARG,
+                 "bad mode or call order");
+    CPTC_CUDA(cudaSetDevice(e.device));
+    e.mttkrp(mode);
+    cptc::comm_reduce_ftv(e, mode);
+    e.fetch_rows(e.FtV.p, mode, host_out);
+  });
+}
+
+int cptc_mttkrp_timed(cptc_ctx* c, int mode, int reps, double* ms) {
+  return guarded(c, [&](Engine& e) {
+    CPTC_REQUIRE(e.built && e.have_factors && mode >= 0 && mode < e.N && reps > 0, CPTC_E_ARG,
+                 "bad mode or call order");
+    CPTC_CUDA(cudaSetDevice(e.device));
+    cudaEvent_t a = e.ev[0], b = e.ev[1];
+    CPTC_CUDA(cudaEventRecord(a, e.stream));
+    for (int r = 0; r < reps; ++r) e.mttkrp(mode);
+    CPTC_CUDA(cudaEventRecord(b, e.stream));
+    CPTC_CUDA(cudaEventSynchronize(b));
+    float t = 0.f;
+    CPTC_CUDA(cudaEventElapsedTime(&t, a, b));
+    if (ms) *ms = (double)t / reps;
+  });
+}
+
+int cptc_profile_mttkrp(cptc_ctx* c, int mode, int reps, double* ms3) {
+  return guarded(c, [&](Engine& e) {
+    CPTC_REQUIRE(e.built && e.have_factors && mode >= 0 && mode < e.N && reps > 0 && ms3,
+                 CPTC_E_ARG, "bad mode or call order");
+    CPTC_CUDA(cudaSetDevice(e.device));
+    cudaEvent_t* ev = e.ev;
+    CPTC_CUDA(cudaMemsetAsync(e.FtV.p, 0, e.dims[mode] * (uint64_t)e.R * sizeof(double),
+                              e.stream));
+    CPTC_CUDA(cudaEventRecord(ev[0], e.stream));
+    for (int r = 0; r < reps; ++r) e.mttkrp_tiles(mode);
+    CPTC_CUDA(cudaEventRecord(ev[1], e.stream));
+    for (int r = 0; r < reps; ++r) e.mttkrp_sparse(mode);
+    CPTC_CUDA(cudaEventRecord(ev[2], e.stream));
+    for (int r = 0; r < reps; ++r) e.mttkrp(mode);
+    CPTC_CUDA(cudaEventRecord(ev[3], e.stream));
+    CPTC_CUDA(cudaEventSynchronize(ev[3]));
+    float a = 0.f, b = 0.f, t = 0.f;
+    CPTC_CUDA(cudaEventElapsedTime(&a, ev[0], ev[1]));
+    CPTC_CUDA(cudaEventElapsedTime(&b, ev[1], ev[2]));
+    CPTC_CUDA(cudaEventElapsedTime(&t, ev[2], ev[3]));
+    ms3[0] = a / reps;
+    ms3[1] = b / reps;
+    ms3[2] = t / reps;
+  });
+}
+
+unsigned long long cptc_launch_count(void) { return cptc::g_launches; }
+
+int cptc_als(cptc_ctx* c, int iters, cptc_iter_cb cb, void* user) {
+  return guarded(c, [&](Engine& e) { e.als(iters, cb, user); });
+}
+
+int cptc_get_stats(cptc_ctx* c, cptc_stats* s) {
+  return guarded(c, [&](Engine& e) {
+    CPTC_REQUIRE(s != nullptr, CPTC_E_ARG, "null stats");
+    std::memset(s, 0, sizeof(*s));
+    s->order = e.N;
+    for (int m = 0; m < e.N; ++m) s->dims[m] = e.dims[m];
+    s->nnz = e.nnz;
+    s->rank = e.R;
+    s->tf32_path = e.tf32 ? 1 : 0;
+    s->dense_nnz = e.tf32 ? e.tiles.nnz : 0;
+    s->sparse_nnz = e.views.empty() ? e.nnz : e.views[0].nnz;
+    s->dense_tiles = e.tf32 ? e.tiles.ntiles : 0;
+    s->avg_fill = e.avg_fill;
+    s->fill_min = e.fill_min;
+    s->cutoff = e.cutoff;
+    s->x_norm_sq = e.x_norm_sq;
+    s->build_ms = e.build_ms;
+    s->device_bytes = e.device_bytes();
+    for (int m = 0; m < e.N && m < (int)e.views.size(); ++m)
+      s->fiber_mode[m] = e.views[m].nout > 0 ? e.views[m].omode[0] : -1;
+    s->nranks = e.nranks;
+    s->rank_id = e.rank;
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,145 @@
+// Engine state: the device-resident tensor, per-mode MTTKRP views, the dense
+// 16^3 tile pool, factors and the ALS workspace.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+#include "../../../include/cptc.h"
+#include "common.cuh"
+
+namespace cptc {
+
+// Element word of a view: bits 0..29 gathered-mode index, bit 30 starts a
+// fiber (a run of equal target and outer-mode indices), bit 31 starts a row.
+constexpr uint32_t kRowFlag = 0x80000000u;
+constexpr uint32_t kFibFlag = 0x40000000u;
+constexpr uint32_t kIdxMask = 0x3FFFFFFFu;
+constexpr uint64_t kMaxGatherDim = (1ull << 30);
+
+// Elements of one warp task in the sparse MTTKRP (multiple of 32).
+constexpr int kTask = 1024;
+
+// Sorted view of the nonzeros for one target mode, in the order
+// (target, outer modes..., gathered mode).  The rows of the outer modes are
+// reused along a fiber; the gathered mode's row is read per nonzero.
+struct View {
+  int target = -1;
+  int nout = 0;                  // number of outer (fiber) modes
+  int omode[CPTC_MAX_ORDER] = {0};  // outer modes then the gathered mode
+  int gmode = -1;
+  uint64_t nnz = 0;
+  uint64_t fibers = 0;
+  DArray<uint32_t> gw;           // element word (gathered index + flags)
+  DArray<uint32_t> oidx;         // nout * nnz outer indices (SoA)
+  DArray<double> val;
+  DArray<uint32_t> rows;         // non-empty target rows, in order
+  DArray<uint32_t> task_row;     // index into `rows` of each task's first row
+  uint64_t nrows = 0, ntasks = 0;
+};
+
+// Order-3 dense tiles: elements of tiles with at least `cutoff` nonzeros,
+// grouped by tile.  tile_info[t] = (b0, b1, b2) tile origins / 16.
+struct TilePool {
+  uint64_t ntiles = 0, nnz = 0;
+  DArray<int4> tile;        // x,y,z = tile block coords, w = element count
+  DArray<uint64_t> start;   // first element of each tile in the pool
+  DArray<uint16_t> lid;     // (li << 8) | (lj << 4) | lk
+  DArray<double> val;
+};
+
+// N-order dense units: a 16^3 tile over the inner modes with every outer
+// mode fixed (src/generic.cu:406-561).
+struct UnitPool {
+  uint64_t nunits = 0, nnz = 0;
+  int inner[3] = {0, 1, 2};
+  int nouter = 0;
+  int outer[CPTC_MAX_ORDER] = {0};
+  DArray<uint4> unit;        // x,y,z inner tile coords, w = count
+  DArray<uint64_t> start;
+  DArray<uint32_t> outer_idx;  // nouter * nunits
+  DArray<uint16_t> lid;
+  DArray<double> val;
+};
+
+struct Engine {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::string err;
+
+  // Tensor (device COO, relabelled in place by the build).
+  int N = 0;
+  uint64_t dims[CPTC_MAX_ORDER] = {0};
+  uint64_t nnz = 0;
+  DArray<uint32_t> idx[CPTC_MAX_ORDER];
+  DArray<double> vals;
+  double x_norm_sq = 0.0;
+
+  // Relabelling: perm[m][old] = new (host); identity when empty.
+  std::vector<std::vector<uint32_t>> perm;
+  std::vector<std::vector<uint32_t>> host_idx;  // original coordinates
+  std::string reorder_note;
+
+  // Build results.
+  bool built = false;
+  int R = 0;
+  cptc_opts opts{};
+  bool generic = false;  // N-order ALS semantics (Cholesky, lambda = norms)
+  bool tf32 = false;
+  std::vector<View> views;
+  TilePool tiles;
+  DArray<uint32_t> tile_order[3];
+  uint64_t tile_cnt[3] = {0, 0, 0};  // tiles of this rank per target mode
+  UnitPool units;
+  double avg_fill = 0.0, fill_min = 0.0;
+  int cutoff = 0;
+  double build_ms = 0.0;
+
+  // Factors (relabelled space) and ALS workspace.
+  bool have_factors = false;
+  bool grams_valid = false;
+  DArray<double> F[CPTC_MAX_ORDER];
+  DArray<double> G[CPTC_MAX_ORDER];
+  DArray<double> lambda;
+  DArray<double> FtV, FtF, Ainv, gpart, dots, scal, cscale;
+  DArray<int> status;
+  double* h_scal = nullptr;  // pinned, 8 doubles
+  int gpart_blocks = 0;
+  double last_iprod = 0.0, last_model2 = 0.0, last_fit = 0.0;
+
+  // Multi-GPU: mode-n rows [slab[n][r], slab[n][r+1]) belong to rank r.
+  void* nccl = nullptr;  // ncclComm_t
+  int nranks = 1, rank = 0;
+  std::vector<uint64_t> slab[CPTC_MAX_ORDER];
+  DArray<double> comm_buf;
+
+  cudaEvent_t ev[2 * CPTC_MAX_ORDER + 2] = {};
+
+  explicit Engine(int dev);
+  ~Engine();
+
+  void load(const cptc_coo* t);
+  void build(int R, double threshold, const cptc_opts* o);
+  void init_factors();
+  void set_factor(int m, const double* host);
+  void get_factor(int m, double* host);
+  void fetch_rows(const double* dev, int m, double* host);
+  void mttkrp(int mode);  // into FtV (relabelled rows), stream-ordered
+  void mttkrp_tiles(int mode);   // dense-tile TF32 part only (accumulates)
+  void mttkrp_sparse(int mode);  // FP64 view part only (accumulates)
+  void als(int iters, cptc_iter_cb cb, void* user);
+  uint64_t device_bytes() const;
+  uint64_t row_lo(int m) const { return slab[m].empty() ? 0 : slab[m][rank]; }
+  uint64_t row_hi(int m) const { return slab[m].empty() ? dims[m] : slab[m][rank + 1]; }
+  double* scal_tmp();
+  double* colscale();
+
+ private:
+  void reorder();
+  void alloc_workspace();
+  void update_mode(int n);
+  void gram_of(int m);
+};
+
+}  // namespace cptc

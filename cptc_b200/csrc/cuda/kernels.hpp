@@ -1,0 +1,99 @@
+// Launch interfaces of the engine's kernels.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "engine.hpp"
+
+namespace cptc {
+
+struct MttkrpArgs {
+  const uint32_t* gw;
+  const uint32_t* oidx;
+  const double* val;
+  const uint32_t* rows;
+  const uint32_t* task_row;
+  uint64_t nnz, ntasks;
+  int nout, R;
+  const double* Fg;
+  const double* Fo[CPTC_MAX_ORDER];
+  double* out;
+};
+
+void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s);
+
+// Dense 16^3 tiles on the tensor cores: TF32 slabs with FP64 weighting.
+// Slots 0,1,2 are the tile's three modes (order 3: modes 0,1,2; N-order
+// units: the inner modes).  For target slot t the contraction runs over
+// slot c in TF32 and each slab of slot s is weighted in FP64 by
+// Fs[s-row, r] * prod_q Fout_q[outer_q, r].
+struct TileArgs {
+  const int4* tile;         // x,y,z = block coords of slots 0,1,2, w = count
+  const uint64_t* start;
+  const uint16_t* lid;      // (l0 << 8) | (l1 << 4) | l2
+  const double* val;
+  uint64_t ntiles;
+  int R;
+  int tslot, cslot, sslot;
+  uint64_t dims[3];         // lengths of slots 0,1,2
+  const double* Fc;
+  const double* Fs;
+  int nouter;
+  const uint32_t* outer_idx;  // ntiles x nouter (tile-major), may be null
+  const double* Fout[CPTC_MAX_ORDER];
+  int store_dups;           // 1: last write wins (order-3), 0: duplicates sum
+  double* out;
+};
+// order: tile visiting order for this mode (sorted by target block).
+void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, cudaStream_t s);
+// Partition of Engine::tiles + residual selection (tiles.cu).
+void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64_t& nsel,
+                      DArray<uint32_t> tile_order[3]);
+// Views (views.cu).
+void build_view(Engine& E, View& v, int n, const uint32_t* d_sel, uint64_t nsel);
+
+// N-order dense units (units.cu): partition over the inner modes with the
+// outer modes fixed; fills E.units, returns residual selection.
+void partition_units(Engine& E, double threshold, DArray<uint32_t>& sel, uint64_t& nsel);
+
+// ---- ALS kernels (als_kernels.cu) ----
+// Per-block partial Grams of F (rows x R) into part[nblk][R][R]; returns nblk.
+int launch_gram_partial(const double* F, uint64_t rows, int R, double* part, int max_blocks,
+                        cudaStream_t s);
+// out[i] = sum_b part[b*len + i], i < len (fixed order).
+void launch_partial_sum(const double* part, int nblk, int len, double* out, cudaStream_t s);
+// G = sum of nblk partials (fixed order).
+void launch_gram_reduce(const double* part, int nblk, int R, double* G, cudaStream_t s);
+// FtF = prod_{m in list} G_m (elementwise).
+void launch_hadamard(const double* const* Gs, int ng, int R, double* FtF, cudaStream_t s);
+// Ainv = truncated pseudo-inverse (pinv=1, tol R*ulp(smax)) or ridge-
+// Cholesky inverse (pinv=0) of the SPD R x R matrix A; status[0] != 0 on
+// failure.
+void launch_sym_inverse(const double* A, int R, int pinv, double* Ainv, int* status,
+                        cudaStream_t s);
+// F[i,:] = (FtV[i,:] * Ainv) ./ (divide_lambda ? lambda : 1) for rows
+// [0, rows); partial Grams of the written rows into part; returns nblk.
+int launch_apply_solve(const double* FtV, const double* Ainv, const double* lambda,
+                       int divide_lambda, uint64_t rows, int R, double* F, double* part,
+                       int max_blocks, cudaStream_t s);
+// From the Gram partials of the solved factor: column norms, new lambda and
+// the Gram of the normalised factor; scale[r] = multiplier for column r.
+//   generic_norm = 0: order-3 rule (norm < 1e-14 -> column 0, lambda 0,
+//                     else lambda *= norm)
+//   generic_norm = 1: N-order rule (norm < 1e-14 or non-finite -> 1,
+//                     lambda = norm)
+void launch_norm_finalize(const double* part, int nblk, int R, int generic_norm,
+                          double* lambda, double* G, double* scale, cudaStream_t s);
+void launch_scale_cols(double* F, uint64_t rows, int R, const double* scale, cudaStream_t s);
+// dots[r] partials of sum_i F[i,r] * FtV[i,r]; returns nblk.
+int launch_col_dots(const double* F, const double* FtV, uint64_t rows, int R, double* part,
+                    int max_blocks, cudaStream_t s);
+// out[0] = iprod = sum_r lambda_r dot_r, out[1] = model^2.
+void launch_fit_final(const double* dot_part, int nblk, const double* lambda,
+                      const double* const* Gs, int ng, int R, double* out, cudaStream_t s);
+// out[0] = sum v^2 (two-stage, deterministic).
+void launch_sumsq(const double* v, uint64_t n, double* part, int max_blocks, double* out,
+                  cudaStream_t s);
+
+}  // namespace cptc

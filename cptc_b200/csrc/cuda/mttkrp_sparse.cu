@@ -1,0 +1,195 @@
+// FP64 sparse MTTKRP over a sorted view (the residual of the hybrid path, or
+// every nonzero on the FP64 path).
+//
+// Computes, for target mode n, FtV[t, r] += sum_e v_e * prod_{m != n} F_m[o_m(e), r]
+// (reference: mttkrp_rowsorted_coalesced_kernel, src/sparse.cu:614-711, and
+// g_mttkrp_seg_pack_kernel, src/generic.cu:271-343).
+//
+// B200 design:
+//  * nonzero-balanced tasks of kTask elements per lane group (a warp for
+//    R >= 32, R lanes for R < 32); row boundaries come from flags in the
+//    element word, so heavy (Zipf head) rows need no host-side segmenting;
+//  * lane = rank slice: 1, 2 or 4 consecutive ranks per lane, loaded as
+//    8- or 16-byte vectors, so one factor row is one coalesced request;
+//  * the view is sorted by (target, outer modes, gathered mode): along a
+//    fiber of equal outer indices the outer rows are loaded once and the
+//    fiber sum  sum_e v_e F_g[g_e]  is multiplied by them at the fiber end,
+//    so ~1/fiber-length of the second gather disappears;
+//  * element words/values are streamed with evict-first loads so the factor
+//    matrices stay resident in L1/L2; gathers of U elements are issued
+//    before any of them is consumed;
+//  * a row that starts and ends inside one task is written with a plain
+//    read-modify-write (it has no other writer in this launch); rows cut by
+//    a task boundary are combined with FP64 atomicAdd.
+#include "engine.hpp"
+#include "kernels.hpp"
+
+namespace cptc {
+
+namespace {
+
+template <int GW, int RPL, bool VEC>
+struct Lanes {
+  int r[RPL];
+  bool ok[RPL];
+  __device__ Lanes(int glane, int R) {
+#pragma unroll
+    for (int k = 0; k < RPL; ++k) {
+      r[k] = VEC ? glane * RPL + k : glane + k * GW;
+      ok[k] = r[k] < R;
+    }
+  }
+};
+
+template <int GW, int RPL, bool VEC>
+__device__ __forceinline__ void load_row(const double* __restrict__ F, uint64_t row, int R,
+                                         int glane, const Lanes<GW, RPL, VEC>& L, double (&x)[RPL]) {
+  const double* base = F + row * (uint64_t)R;
+  if constexpr (VEC && RPL == 1) {
+    x[0] = __ldg(base + glane);
+  } else if constexpr (VEC && RPL == 2) {
+    const double2 a = __ldg(reinterpret_cast<const double2*>(base) + glane);
+    x[0] = a.x;
+    x[1] = a.y;
+  } else if constexpr (VEC && RPL == 4) {
+    const double2 a = __ldg(reinterpret_cast<const double2*>(base) + 2 * glane);
+    const double2 b = __ldg(reinterpret_cast<const double2*>(base) + 2 * glane + 1);
+    x[0] = a.x;
+    x[1] = a.y;
+    x[2] = b.x;
+    x[3] = b.y;
+  } else {
+#pragma unroll
+    for (int k = 0; k < RPL; ++k) x[k] = L.ok[k] ? __ldg(base + L.r[k]) : 0.0;
+  }
+}
+
+template <int GW, int RPL, bool VEC, int U>
+__global__ void __launch_bounds__(256) k_mttkrp_view(MttkrpArgs a) {
+  constexpr int GPW = 32 / GW;
+  const int lane = threadIdx.x & 31;
+  const int glane = lane % GW;
+  const int gid = lane / GW;
+  const unsigned gmask = (GW == 32) ? 0xffffffffu : (((1u << GW) - 1u) << (gid * GW));
+  const uint64_t task =
+      ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + gid;
+  if (task >= a.ntasks) return;
+  const int R = a.R;
+  const Lanes<GW, RPL, VEC> L(glane, R);
+  const uint64_t p0 = task * (uint64_t)kTask;
+  const uint64_t p1 = (p0 + kTask < a.nnz) ? p0 + kTask : a.nnz;
+
+  uint32_t rowi = a.task_row[task];
+  uint32_t row = a.rows[rowi];
+  bool row_began_here = (a.gw[p0] & kRowFlag) != 0;
+  const bool last_row_ends_here = (p1 == a.nnz) || (a.gw[p1] & kRowFlag);
+
+  double accr[RPL], accf[RPL], ff[RPL];
+#pragma unroll
+  for (int k = 0; k < RPL; ++k) accr[k] = accf[k] = ff[k] = 0.0;
+
+  auto write_row = [&](bool owned) {
+    double* dst = a.out + (uint64_t)row * (uint64_t)R;
+#pragma unroll
+    for (int k = 0; k < RPL; ++k) {
+      if (!L.ok[k]) continue;
+      if (owned) dst[L.r[k]] += accr[k];
+      else atomicAdd(dst + L.r[k], accr[k]);
+      accr[k] = 0.0;
+    }
+  };
+
+  for (uint64_t b = p0; b < p1; b += GW) {
+    const uint64_t p = b + glane;
+    uint32_t w = 0, o0 = 0;
+    double v = 0.0;
+    if (p < p1) {
+      w = __ldcs(a.gw + p);
+      v = __ldcs(a.val + p);
+      if (a.nout > 0) o0 = __ldcs(a.oidx + p);
+    }
+    if (p == p0) w = (w & ~kRowFlag) | kFibFlag;  // row state is set; open a fiber
+    const int cnt = (p1 - b < (uint64_t)GW) ? (int)(p1 - b) : GW;
+#pragma unroll 1
+    for (int j0 = 0; j0 < cnt; j0 += U) {
+      uint32_t wj[U], oj[U];
+      double vj[U], g[U][RPL];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        wj[u] = __shfl_sync(gmask, w, j0 + u, GW);
+        oj[u] = __shfl_sync(gmask, o0, j0 + u, GW);
+        vj[u] = __shfl_sync(gmask, v, j0 + u, GW);
+        if (j0 + u < cnt) {
+          load_row<GW, RPL, VEC>(a.Fg, wj[u] & kIdxMask, R, glane, L, g[u]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < RPL; ++k) g[u][k] = 0.0;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (j0 + u >= cnt) break;
+        const uint32_t ww = wj[u];
+        if (ww & kFibFlag) {
+#pragma unroll
+          for (int k = 0; k < RPL; ++k) {
+            accr[k] = fma(accf[k], ff[k], accr[k]);
+            accf[k] = 0.0;
+          }
+          if (ww & kRowFlag) {
+            write_row(row_began_here);
+            row = a.rows[++rowi];
+            row_began_here = true;
+          }
+          if (a.nout == 0) {
+#pragma unroll
+            for (int k = 0; k < RPL; ++k) ff[k] = 1.0;
+          } else {
+            load_row<GW, RPL, VEC>(a.Fo[0], oj[u], R, glane, L, ff);
+            for (int q = 1; q < a.nout; ++q) {
+              const uint32_t oq = a.oidx[(uint64_t)q * a.nnz + b + j0 + u];
+              double t[RPL];
+              load_row<GW, RPL, VEC>(a.Fo[q], oq, R, glane, L, t);
+#pragma unroll
+              for (int k = 0; k < RPL; ++k) ff[k] *= t[k];
+            }
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < RPL; ++k) accf[k] = fma(vj[u], g[u][k], accf[k]);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < RPL; ++k) accr[k] = fma(accf[k], ff[k], accr[k]);
+  write_row(row_began_here && last_row_ends_here);
+}
+
+template <int GW, int RPL, bool VEC, int U>
+void launch(const MttkrpArgs& a, cudaStream_t s) {
+  constexpr int GPW = 32 / GW;
+  const uint64_t warps = (a.ntasks + GPW - 1) / GPW;
+  const unsigned blocks = (unsigned)((warps + 7) / 8);
+  k_mttkrp_view<GW, RPL, VEC, U><<<blocks, 256, 0, s>>>(a);
+  CPTC_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
+  if (a.nnz == 0 || a.ntasks == 0) return;
+  switch (a.R) {
+    case 8: launch<8, 1, true, 8>(a, s); return;
+    case 16: launch<16, 1, true, 8>(a, s); return;
+    case 32: launch<32, 1, true, 8>(a, s); return;
+    case 64: launch<32, 2, true, 8>(a, s); return;
+    case 128: launch<32, 4, true, 4>(a, s); return;
+    default: break;
+  }
+  if (a.R <= 32) launch<32, 1, false, 8>(a, s);
+  else if (a.R <= 64) launch<32, 2, false, 8>(a, s);
+  else if (a.R <= 128) launch<32, 4, false, 4>(a, s);
+  else throw CptcError(CPTC_E_UNSUP, "rank > 128 is not supported");
+}
+
+}  // namespace cptc

@@ -1,0 +1,472 @@
+// Order-3 hybrid partition into dense 16^3 tiles and an FP64 residual, and
+// the dense-tile MTTKRP on the tensor cores (TF32 slabs, FP64 weighting).
+//
+// Partition: reference partition_tensor_hybrid_gpu (src/partition.cu:
+// 581-1493).  Same tile ids, cutoff rule (count >= int(4096*thr), clamped to
+// [1, 4096]; thr <= 0 auto-balance of :1030-1098) and classification, but
+// the classification, offsets and scatter stay on the device (one readback
+// of four scalars) instead of the reference's host classify loop.
+//
+// Dense-tile MTTKRP: reference dense_tile_mttkrp_wmma (src/dense.cu:89-1076).
+// Per tile and slab s of the weighting mode, P = X_s (16 x 16) * F1_block
+// (16 x R) in TF32 with FP32 accumulation, then out += double(P) * F2[s, :]
+// in FP64 — the reference's numerics.  B200 mapping:
+//  * mma.sync m16n8k8 TF32: a tile slab is a single 16x16x(R) product, far
+//    below the 128-row M of tcgen05.mma, and the kernel is bound by loading
+//    the tile pool and building the tile in shared memory, not by the
+//    tensor pipe (see DESIGN.md for the ncu evidence);
+//  * the tile is scattered into shared memory in a per-mode (s, t, c) layout
+//    with a row stride of 20 floats, which makes every A-fragment load
+//    bank-conflict free; F1 (TF32) and F2 (FP64) rows of the tile sit in
+//    shared memory; B fragments stay in registers across the 16 slabs;
+//  * tiles are visited in target-block order, so a CTA accumulates
+//    consecutive tiles of the same 16 output rows in shared memory and
+//    issues the FP64 atomics once per row block instead of once per tile.
+#include <cfloat>
+
+#include <cub/cub.cuh>
+
+#include "kernels.hpp"
+
+namespace cptc {
+
+namespace {
+
+__global__ void k_tile_keys(const uint32_t* __restrict__ i0, const uint32_t* __restrict__ i1,
+                            const uint32_t* __restrict__ i2, uint64_t n, uint64_t nbj,
+                            uint64_t nbk, uint64_t* __restrict__ key, uint32_t* __restrict__ id) {
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < n;
+       e += (uint64_t)gridDim.x * blockDim.x) {
+    key[e] = ((uint64_t)(i0[e] >> 4) * nbj + (i1[e] >> 4)) * nbk + (i2[e] >> 4);
+    id[e] = (uint32_t)e;
+  }
+}
+
+__global__ void k_run_start_flags(const uint64_t* __restrict__ key, uint64_t n,
+                                  uint32_t* __restrict__ flag) {
+  for (uint64_t p = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; p < n;
+       p += (uint64_t)gridDim.x * blockDim.x)
+    flag[p] = (p == 0 || key[p] != key[p - 1]) ? 1u : 0u;
+}
+
+// Per element in sorted order: dense flag from its run's count.
+__global__ void k_elem_dense(const uint32_t* __restrict__ runid, const int* __restrict__ counts,
+                             uint64_t n, int cutoff, uint32_t* __restrict__ dflag) {
+  for (uint64_t p = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; p < n;
+       p += (uint64_t)gridDim.x * blockDim.x)
+    dflag[p] = counts[runid[p] - 1] >= cutoff ? 1u : 0u;
+}
+
+__global__ void k_scatter_split(const uint32_t* __restrict__ perm, const uint32_t* __restrict__ dflag,
+                                const uint64_t* __restrict__ dpos, uint64_t n,
+                                const uint32_t* __restrict__ i0, const uint32_t* __restrict__ i1,
+                                const uint32_t* __restrict__ i2, const double* __restrict__ vals,
+                                uint16_t* __restrict__ lid, double* __restrict__ pval,
+                                uint32_t* __restrict__ sel) {
+  for (uint64_t p = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; p < n;
+       p += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t e = perm[p];
+    if (dflag[p]) {
+      const uint64_t d = dpos[p];
+      lid[d] = (uint16_t)(((i0[e] & 15u) << 8) | ((i1[e] & 15u) << 4) | (i2[e] & 15u));
+      pval[d] = vals[e];
+    } else {
+      sel[p - dpos[p]] = e;
+    }
+  }
+}
+
+__global__ void k_tiles_from_runs(const uint32_t* __restrict__ runs_sel, uint64_t ntiles,
+                                  const uint64_t* __restrict__ ukeys, const int* __restrict__ counts,
+                                  uint64_t nbj, uint64_t nbk, int4* __restrict__ tile,
+                                  uint64_t* __restrict__ cnt64) {
+  for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < ntiles;
+       k += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t r = runs_sel[k];
+    const uint64_t key = ukeys[r];
+    const uint64_t bk = key % nbk, t = key / nbk, bj = t % nbj, bi = t / nbj;
+    tile[k] = make_int4((int)bi, (int)bj, (int)bk, counts[r]);
+    cnt64[k] = (uint64_t)counts[r];
+  }
+}
+
+__global__ void k_run_dense_flags(const int* __restrict__ counts, uint64_t nruns, int cutoff,
+                                  uint8_t* __restrict__ f) {
+  for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < nruns;
+       k += (uint64_t)gridDim.x * blockDim.x)
+    f[k] = counts[k] >= cutoff ? 1 : 0;
+}
+
+// First index whose inclusive prefix reaches target (prefix is monotone).
+__global__ void k_auto_cutoff(const unsigned long long* __restrict__ prefix,
+                              const int* __restrict__ sorted_desc, uint64_t n,
+                              unsigned long long target, int* __restrict__ out) {
+  if (threadIdx.x || blockIdx.x) return;
+  uint64_t lo = 0, hi = n;
+  while (lo < hi) {
+    const uint64_t mid = (lo + hi) >> 1;
+    if (prefix[mid] >= target) hi = mid;
+    else lo = mid + 1;
+  }
+  out[0] = (lo < n) ? sorted_desc[lo] : 1;
+}
+
+__global__ void k_tile_target_keys(const int4* __restrict__ tile, uint64_t n, int mode,
+                                   uint32_t* __restrict__ key, uint32_t* __restrict__ id) {
+  for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < n;
+       k += (uint64_t)gridDim.x * blockDim.x) {
+    const int4 t = tile[k];
+    key[k] = (uint32_t)(mode == 0 ? t.x : mode == 1 ? t.y : t.z);
+    id[k] = (uint32_t)k;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dense-tile TF32 MTTKRP.
+// ---------------------------------------------------------------------------
+constexpr int kSt = 20;               // t stride (floats) of the slab layout
+constexpr int kSs = 16 * kSt;         // s stride
+constexpr int kTileFloats = 16 * kSs; // 5120 floats = 20 KB
+
+__device__ __forceinline__ uint32_t tf32_bits(float x) {
+  return __float_as_uint(x) & 0xFFFFE000u;  // low 13 mantissa bits ignored
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Block of 4 warps, persistent over a contiguous range of the visiting
+// order.  Warp w owns n-tiles w, w+4, ... (R/8 n-tiles of 8 ranks); when
+// R < 32 the warps also split the 16 slabs and combine through shared
+// memory.  Per tile: zero + scatter the 16^3 tile in (s, t, c) layout, load
+// the c-slot rows (TF32) and the s-slot rows times the outer weights (FP64),
+// then 16 slabs x 2 k-steps of m16n8k8 with the FP64 epilogue in registers.
+template <int NTMAX>
+__global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __restrict__ order,
+                                               uint64_t per_block) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  const int R = a.R;
+  const int Rs = R + 8;                                         // fB row stride (floats)
+  float* X = reinterpret_cast<float*>(smraw);                  // kTileFloats
+  float* fB = X + kTileFloats;                                  // 16 * Rs
+  double* F2s = reinterpret_cast<double*>(fB + 16 * Rs);       // 16 * R
+  double* accS = F2s + 16 * R;                                  // 16 * R
+  double* wS = accS + 16 * R;                                   // R (outer weights)
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int ts = a.tslot, cs = a.cslot, ss = a.sslot;
+  const int NT = R / 8;
+  const int ntstep = NT >= 4 ? 4 : NT;
+  const int SG = 4 / ntstep;
+  const int my_sg = warp / ntstep;
+  const int nt0 = warp % ntstep;
+
+  const uint64_t k0 = (uint64_t)blockIdx.x * per_block;
+  uint64_t k1 = k0 + per_block;
+  if (k1 > a.ntiles) k1 = a.ntiles;
+  if (k0 >= k1) return;
+
+  for (int i = tid; i < 16 * R; i += 128) accS[i] = 0.0;
+  int cur_tb = -1;
+
+  auto flush = [&](int tb) {
+    for (int i = tid; i < 16 * R; i += 128) {
+      const int t = i / R, r = i % R;
+      const uint64_t row = (uint64_t)tb * 16 + t;
+      const double v = accS[i];
+      if (row < a.dims[ts] && v != 0.0) atomicAdd(a.out + row * (uint64_t)R + r, v);
+      accS[i] = 0.0;
+    }
+  };
+
+  for (uint64_t k = k0; k < k1; ++k) {
+    const uint32_t ti = order[k];
+    const int4 T = a.tile[ti];
+    const int blk[3] = {T.x, T.y, T.z};
+    const int tb = blk[ts], cb = blk[cs], sb = blk[ss];
+    __syncthreads();  // previous tile's shared-memory reads are done
+    if (tb != cur_tb) {
+      if (cur_tb >= 0) flush(cur_tb);
+      cur_tb = tb;
+    }
+    for (int i = tid; i < kTileFloats / 4; i += 128)
+      reinterpret_cast<float4*>(X)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (a.nouter > 0) {
+      for (int r = tid; r < R; r += 128) {
+        double w = 1.0;
+        for (int q = 0; q < a.nouter; ++q)
+          w *= a.Fout[q][(uint64_t)a.outer_idx[(uint64_t)ti * a.nouter + q] * R + r];
+        wS[r] = w;
+      }
+    }
+    __syncthreads();
+    for (int i = tid; i < 16 * R; i += 128) {
+      const int c = i / R, r = i % R;
+      const uint64_t cg = (uint64_t)cb * 16 + c, sg = (uint64_t)sb * 16 + c;
+      fB[c * Rs + r] = (cg < a.dims[cs]) ? (float)a.Fc[cg * R + r] : 0.0f;
+      double f2 = (sg < a.dims[ss]) ? a.Fs[sg * R + r] : 0.0;
+      if (a.nouter > 0) f2 *= wS[r];
+      F2s[c * R + r] = f2;
+    }
+    const uint64_t st = a.start[ti];
+    for (int j = tid; j < T.w; j += 128) {
+      const uint32_t l = a.lid[st + j];
+      const int loc[3] = {(int)(l >> 8), (int)((l >> 4) & 15), (int)(l & 15)};
+      double v = a.val[st + j];
+      v = v > FLT_MAX ? FLT_MAX : (v < -FLT_MAX ? -FLT_MAX : v);
+      float* dst = X + loc[ss] * kSs + loc[ts] * kSt + loc[cs];
+      if (a.store_dups) *dst = (float)v;
+      else atomicAdd(dst, (float)v);
+    }
+    __syncthreads();
+
+    uint32_t bf[NTMAX][2][2];
+    double acc[NTMAX][4];
+#pragma unroll
+    for (int q = 0; q < NTMAX; ++q) {
+      const int nt = nt0 + q * ntstep;
+#pragma unroll
+      for (int x = 0; x < 4; ++x) acc[q][x] = 0.0;
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        bf[q][ks][0] = bf[q][ks][1] = 0u;
+        if (nt < NT) {
+          bf[q][ks][0] = tf32_bits(fB[(ks * 8 + t4) * Rs + nt * 8 + g]);
+          bf[q][ks][1] = tf32_bits(fB[(ks * 8 + t4 + 4) * Rs + nt * 8 + g]);
+        }
+      }
+    }
+    for (int s = my_sg; s < 16; s += SG) {
+      uint32_t af[2][4];
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        const float* base = X + s * kSs + ks * 8;
+        af[ks][0] = tf32_bits(base[g * kSt + t4]);
+        af[ks][1] = tf32_bits(base[(g + 8) * kSt + t4]);
+        af[ks][2] = tf32_bits(base[g * kSt + t4 + 4]);
+        af[ks][3] = tf32_bits(base[(g + 8) * kSt + t4 + 4]);
+      }
+#pragma unroll
+      for (int q = 0; q < NTMAX; ++q) {
+        const int nt = nt0 + q * ntstep;
+        if (nt >= NT) break;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_tf32(d, af[0], bf[q][0][0], bf[q][0][1]);
+        mma_tf32(d, af[1], bf[q][1][0], bf[q][1][1]);
+        const int r = nt * 8 + 2 * t4;
+        const double w0 = F2s[s * R + r], w1 = F2s[s * R + r + 1];
+        acc[q][0] = fma((double)d[0], w0, acc[q][0]);
+        acc[q][1] = fma((double)d[1], w1, acc[q][1]);
+        acc[q][2] = fma((double)d[2], w0, acc[q][2]);
+        acc[q][3] = fma((double)d[3], w1, acc[q][3]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < NTMAX; ++q) {
+      const int nt = nt0 + q * ntstep;
+      if (nt >= NT) break;
+      const int r = nt * 8 + 2 * t4;
+      atomicAdd(&accS[g * R + r], acc[q][0]);
+      atomicAdd(&accS[g * R + r + 1], acc[q][1]);
+      atomicAdd(&accS[(g + 8) * R + r], acc[q][2]);
+      atomicAdd(&accS[(g + 8) * R + r + 1], acc[q][3]);
+    }
+  }
+  __syncthreads();
+  flush(cur_tb);
+}
+
+}  // namespace
+
+// Builds the dense tile pool (tiles with >= cutoff nonzeros) and the list of
+// residual elements.  Returns the residual selection in `sel` (device).
+void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64_t& nsel,
+                      DArray<uint32_t> tile_order[3]) {
+  cudaStream_t s = E.stream;
+  const uint64_t n = E.nnz;
+  const uint64_t nbj = (E.dims[1] + 15) / 16, nbk = (E.dims[2] + 15) / 16;
+  TilePool& P = E.tiles;
+  P = TilePool{};
+  const unsigned gb = grid_for(n, 256, 148 * 16);
+  DArray<uint64_t> key_a(n), key_b(n);
+  DArray<uint32_t> id_a(n), id_b(n);
+  k_tile_keys<<<gb, 256, 0, s>>>(E.idx[0].p, E.idx[1].p, E.idx[2].p, n, nbj, nbk, key_a.p, id_a.p);
+  CPTC_LAUNCH_CHECK();
+  const int kbits = bits_for(((E.dims[0] + 15) / 16) * nbj * nbk);
+  size_t tb = 0;
+  CPTC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tb, key_a.p, key_b.p, id_a.p, id_b.p,
+                                            (int64_t)n, 0, kbits, s));
+  DArray<unsigned char> temp(tb);
+  CPTC_CUDA(cub::DeviceRadixSort::SortPairs(temp.p, tb, key_a.p, key_b.p, id_a.p, id_b.p,
+                                            (int64_t)n, 0, kbits, s));
+  // Runs.
+  DArray<uint64_t> ukeys(n);
+  DArray<int> counts(n);
+  DArray<unsigned long long> nruns_d(1);
+  size_t rb = 0;
+  CPTC_CUDA(cub::DeviceRunLengthEncode::Encode(nullptr, rb, key_b.p, ukeys.p, counts.p,
+                                               nruns_d.p, (int64_t)n, s));
+  if (rb > temp.bytes()) temp.alloc(rb);
+  CPTC_CUDA(cub::DeviceRunLengthEncode::Encode(temp.p, rb, key_b.p, ukeys.p, counts.p,
+                                               nruns_d.p, (int64_t)n, s));
+  unsigned long long nruns = 0;
+  CPTC_CUDA(cudaMemcpyAsync(&nruns, nruns_d.p, sizeof(nruns), cudaMemcpyDeviceToHost, s));
+  CPTC_CUDA(cudaStreamSynchronize(s));
+
+  // Cutoff.
+  int cutoff;
+  if (threshold > 0.0) {
+    cutoff = (int)(4096.0 * threshold);
+    if (cutoff < 1) cutoff = 1;
+    if (cutoff > 4096) cutoff = 4096;
+  } else {
+    // Auto-balance of the reference: dense share rate_cuda/(rate_wmma +
+    // rate_cuda) with its RTX 4060 rates scaled by SMs/24.
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, E.device);
+    const double sm_scale = (double)sms / 24.0;
+    const double rw = 1.20 / sm_scale, rc = 0.688 / sm_scale;
+    const unsigned long long target = (unsigned long long)((double)n * (rc / (rw + rc)));
+    DArray<int> cdesc(nruns);
+    DArray<unsigned long long> pref(nruns);
+    size_t sb = 0;
+    CPTC_CUDA(cub::DeviceRadixSort::SortKeysDescending(nullptr, sb, counts.p, cdesc.p,
+                                                       (int64_t)nruns, 0, 13, s));
+    if (sb > temp.bytes()) temp.alloc(sb);
+    CPTC_CUDA(cub::DeviceRadixSort::SortKeysDescending(temp.p, sb, counts.p, cdesc.p,
+                                                       (int64_t)nruns, 0, 13, s));
+    size_t scb = 0;
+    auto conv = cub::TransformInputIterator<unsigned long long, cub::CastOp<unsigned long long>,
+                                            const int*>(cdesc.p, cub::CastOp<unsigned long long>());
+    CPTC_CUDA(cub::DeviceScan::InclusiveSum(nullptr, scb, conv, pref.p, (int64_t)nruns, s));
+    if (scb > temp.bytes()) temp.alloc(scb);
+    CPTC_CUDA(cub::DeviceScan::InclusiveSum(temp.p, scb, conv, pref.p, (int64_t)nruns, s));
+    DArray<int> cut_d(1);
+    k_auto_cutoff<<<1, 32, 0, s>>>(pref.p, cdesc.p, nruns, target, cut_d.p);
+    CPTC_LAUNCH_CHECK();
+    CPTC_CUDA(cudaMemcpyAsync(&cutoff, cut_d.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CPTC_CUDA(cudaStreamSynchronize(s));
+  }
+  E.cutoff = cutoff;
+
+  // Per-element run id (1-based) and dense flag; dense positions by scan.
+  DArray<uint32_t> flag(n), runid(n);
+  k_run_start_flags<<<gb, 256, 0, s>>>(key_b.p, n, flag.p);
+  CPTC_LAUNCH_CHECK();
+  size_t sc = 0;
+  CPTC_CUDA(cub::DeviceScan::InclusiveSum(nullptr, sc, flag.p, runid.p, (int64_t)n, s));
+  if (sc > temp.bytes()) temp.alloc(sc);
+  CPTC_CUDA(cub::DeviceScan::InclusiveSum(temp.p, sc, flag.p, runid.p, (int64_t)n, s));
+  k_elem_dense<<<gb, 256, 0, s>>>(runid.p, counts.p, n, cutoff, flag.p);
+  CPTC_LAUNCH_CHECK();
+  DArray<uint64_t> dpos(n + 1);
+  {
+    auto conv = cub::TransformInputIterator<uint64_t, cub::CastOp<uint64_t>, const uint32_t*>(
+        flag.p, cub::CastOp<uint64_t>());
+    size_t eb = 0;
+    CPTC_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, eb, conv, dpos.p, (int64_t)n, s));
+    if (eb > temp.bytes()) temp.alloc(eb);
+    CPTC_CUDA(cub::DeviceScan::ExclusiveSum(temp.p, eb, conv, dpos.p, (int64_t)n, s));
+  }
+  uint64_t dense_nnz = 0;
+  {
+    uint64_t last_pos = 0;
+    uint32_t last_flag = 0;
+    CPTC_CUDA(cudaMemcpyAsync(&last_pos, dpos.p + (n - 1), sizeof(uint64_t),
+                              cudaMemcpyDeviceToHost, s));
+    CPTC_CUDA(cudaMemcpyAsync(&last_flag, flag.p + (n - 1), sizeof(uint32_t),
+                              cudaMemcpyDeviceToHost, s));
+    CPTC_CUDA(cudaStreamSynchronize(s));
+    dense_nnz = last_pos + last_flag;
+  }
+  P.nnz = dense_nnz;
+  nsel = n - dense_nnz;
+  P.lid.alloc(dense_nnz);
+  P.val.alloc(dense_nnz);
+  sel.alloc(nsel);
+  k_scatter_split<<<gb, 256, 0, s>>>(id_b.p, flag.p, dpos.p, n, E.idx[0].p, E.idx[1].p,
+                                     E.idx[2].p, E.vals.p, P.lid.p, P.val.p, sel.p);
+  CPTC_LAUNCH_CHECK();
+
+  // Dense tiles, in tile-id order.
+  DArray<uint8_t> rflag(nruns);
+  k_run_dense_flags<<<grid_for(nruns, 256, 148 * 16), 256, 0, s>>>(counts.p, nruns, cutoff,
+                                                                   rflag.p);
+  CPTC_LAUNCH_CHECK();
+  DArray<uint32_t> rsel(nruns);
+  DArray<unsigned long long> nt_d(1);
+  cub::CountingInputIterator<uint32_t> cnt(0);
+  size_t fb = 0;
+  CPTC_CUDA(cub::DeviceSelect::Flagged(nullptr, fb, cnt, rflag.p, rsel.p, nt_d.p, (int64_t)nruns, s));
+  if (fb > temp.bytes()) temp.alloc(fb);
+  CPTC_CUDA(cub::DeviceSelect::Flagged(temp.p, fb, cnt, rflag.p, rsel.p, nt_d.p, (int64_t)nruns, s));
+  unsigned long long ntiles = 0;
+  CPTC_CUDA(cudaMemcpyAsync(&ntiles, nt_d.p, sizeof(ntiles), cudaMemcpyDeviceToHost, s));
+  CPTC_CUDA(cudaStreamSynchronize(s));
+  P.ntiles = ntiles;
+  P.tile.alloc(ntiles);
+  P.start.alloc(ntiles);
+  if (ntiles > 0) {
+    DArray<uint64_t> c64(ntiles);
+    k_tiles_from_runs<<<grid_for(ntiles, 256, 148 * 16), 256, 0, s>>>(rsel.p, ntiles, ukeys.p,
+                                                                      counts.p, nbj, nbk,
+                                                                      P.tile.p, c64.p);
+    CPTC_LAUNCH_CHECK();
+    size_t xb = 0;
+    CPTC_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, xb, c64.p, P.start.p, (int64_t)ntiles, s));
+    if (xb > temp.bytes()) temp.alloc(xb);
+    CPTC_CUDA(cub::DeviceScan::ExclusiveSum(temp.p, xb, c64.p, P.start.p, (int64_t)ntiles, s));
+    // Per-mode visiting order: by target block (stable).
+    for (int m = 0; m < 3; ++m) {
+      DArray<uint32_t> ka(ntiles), kb(ntiles), ia(ntiles);
+      tile_order[m].alloc(ntiles);
+      k_tile_target_keys<<<grid_for(ntiles, 256, 148 * 16), 256, 0, s>>>(P.tile.p, ntiles, m,
+                                                                          ka.p, ia.p);
+      CPTC_LAUNCH_CHECK();
+      size_t ob = 0;
+      CPTC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, ob, ka.p, kb.p, ia.p, tile_order[m].p,
+                                                (int64_t)ntiles, 0, 32, s));
+      if (ob > temp.bytes()) temp.alloc(ob);
+      CPTC_CUDA(cub::DeviceRadixSort::SortPairs(temp.p, ob, ka.p, kb.p, ia.p, tile_order[m].p,
+                                                (int64_t)ntiles, 0, 32, s));
+    }
+  }
+  CPTC_CUDA(cudaStreamSynchronize(s));
+}
+
+void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, cudaStream_t s) {
+  if (a.ntiles == 0) return;
+  CPTC_REQUIRE(a.R % 8 == 0 && a.R <= 128, CPTC_E_UNSUP,
+               "the TF32 tile path needs R a multiple of 8, <= 128");
+  const int R = a.R;
+  const size_t smem = (size_t)kTileFloats * 4 + (size_t)16 * (R + 8) * 4 +
+                      (size_t)(2 * 16 * R + R) * 8;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  uint64_t blocks = (uint64_t)sms * 4;
+  if (blocks > a.ntiles) blocks = a.ntiles;
+  const uint64_t per = (a.ntiles + blocks - 1) / blocks;
+  blocks = (a.ntiles + per - 1) / per;
+  const int NT = R / 8;
+#define CPTC_TILES(NTM)                                                                      \
+  do {                                                                                       \
+    CPTC_CUDA(cudaFuncSetAttribute(k_tiles<NTM>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                   (int)smem));                                              \
+    k_tiles<NTM><<<(unsigned)blocks, 128, smem, s>>>(a, order, per);                         \
+  } while (0)
+  if (NT <= 4) CPTC_TILES(1);
+  else if (NT <= 8) CPTC_TILES(2);
+  else if (NT <= 12) CPTC_TILES(3);
+  else CPTC_TILES(4);
+#undef CPTC_TILES
+  CPTC_LAUNCH_CHECK();
+}
+
+}  // namespace cptc

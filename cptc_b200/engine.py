@@ -1,0 +1,203 @@
+"""Python face of the CP-ALS engine (a thin ctypes layer over include/cptc.h).
+
+Mirrors the reference's operator interface for the MTTKRP hot path:
+
+  reference (zhixianzhu/cpTC)                      here
+  ----------------------------------------------   ---------------------------
+  load_tns_file / load_tns_generic                 read_tns() / Engine.load()
+  compute/apply_cadr_reordering,                   Engine.build()
+    partition_tensor_hybrid, build_mttkrp_views,
+    fill-rate selector (src/main.cu:316-426)
+  init_factors_random (src/common.cu:66-126)       Engine.init_factors()
+  run_mttkrp_mode: compute_dense_mttkrp_async +    Engine.mttkrp(mode)
+    compute_sparse_mttkrp_async (src/als.cu:535)
+  execute_als_decomposition / run_generic_cp       Engine.als(iters)
+  unpermute_factor_matrices                        Engine.factors()
+
+Errors raise CptcError with the library's message; nothing falls back to
+the CPU.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _native as N
+from .tensor import CooTensor
+
+PATHS = {"auto": 0, "tf32": 1, "fp64": 2}
+REORDERS = {"default": -1, "none": 0, "cadr": 1, "hits": 2, "auto": 3}
+SOLVERS = {"default": 0, "chol": 1, "cholesky": 1, "pinv": 2, "svd": 2}
+
+
+class CptcError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+@dataclass
+class IterReport:
+    iter: int
+    ms: float
+    fit: float
+    mode_ms: list
+
+
+def default_opts() -> N.Opts:
+    o = N.Opts()
+    N.engine_lib().cptc_opts_default(C.byref(o))
+    return o
+
+
+def launch_count() -> int:
+    """Kernels launched by libcptc.so since it was loaded."""
+    return int(N.engine_lib().cptc_launch_count())
+
+
+def comm_unique_id() -> bytes:
+    buf = (C.c_ubyte * 128)()
+    rc = N.engine_lib().cptc_comm_unique_id(buf)
+    if rc != 0:
+        raise CptcError(rc, "ncclGetUniqueId failed")
+    return bytes(buf)
+
+
+class Engine:
+    """One CP-ALS context on one GPU."""
+
+    def __init__(self, device: int = 0):
+        self._lib = N.engine_lib()
+        h = C.c_void_p()
+        rc = self._lib.cptc_create(C.byref(h), int(device), 0)
+        if rc != 0:
+            raise CptcError(rc, f"cptc_create(device={device}) failed")
+        self._h = h
+        self._tensor = None
+        self.R = 0
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.cptc_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def _check(self, rc: int, what: str) -> None:
+        if rc != 0:
+            msg = self._lib.cptc_last_error(self._h)
+            raise CptcError(rc, f"{what}: {msg.decode() if msg else ''}")
+
+    # -- multi-GPU -------------------------------------------------------
+    def comm_init(self, uid: bytes, rank: int, nranks: int) -> None:
+        buf = (C.c_ubyte * 128).from_buffer_copy(uid)
+        self._check(self._lib.cptc_comm_init(self._h, buf, int(rank), int(nranks)), "comm_init")
+
+    # -- tensor and build --------------------------------------------------
+    def load(self, t: CooTensor) -> None:
+        self._tensor = t
+        s = t.as_struct()
+        self._check(self._lib.cptc_load_coo(self._h, C.byref(s)), "load")
+
+    def build(self, R: int, threshold: float = 0.03, path: str = "auto", generic: bool = False,
+              reorder: str = "default", reorder_rounds: int = 3,
+              reorder_sample: int = 8_000_000, solver: str = "default", seed: int = 42,
+              dense_generic: bool = True, dense_thr_generic: float = 0.03,
+              fill_min: float = 0.0) -> None:
+        o = default_opts()
+        o.path = PATHS[path]
+        o.fill_min = float(fill_min)
+        o.generic = int(bool(generic))
+        o.reorder = REORDERS[reorder]
+        o.reorder_rounds = int(reorder_rounds)
+        o.reorder_sample = int(reorder_sample)
+        o.solver = SOLVERS[solver]
+        o.seed = int(seed)
+        o.dense_generic = int(bool(dense_generic))
+        o.dense_thr_generic = float(dense_thr_generic)
+        self._check(self._lib.cptc_build(self._h, int(R), float(threshold), C.byref(o)), "build")
+        self.R = int(R)
+
+    def init_factors(self) -> None:
+        self._check(self._lib.cptc_init_factors(self._h), "init_factors")
+
+    def stats(self) -> dict:
+        s = N.Stats()
+        self._check(self._lib.cptc_get_stats(self._h, C.byref(s)), "stats")
+        out = {k: getattr(s, k) for k, _ in N.Stats._fields_}
+        out["dims"] = tuple(int(s.dims[m]) for m in range(s.order))
+        out["fiber_mode"] = tuple(int(s.fiber_mode[m]) for m in range(s.order))
+        return out
+
+    # -- factors ---------------------------------------------------------
+    def _dims(self):
+        return self._tensor.dims
+
+    def set_factor(self, mode: int, F: np.ndarray) -> None:
+        F = np.ascontiguousarray(F, dtype=np.float64)
+        assert F.shape == (self._dims()[mode], self.R)
+        self._check(self._lib.cptc_set_factors(self._h, int(mode),
+                                               F.ctypes.data_as(C.POINTER(C.c_double))),
+                    "set_factors")
+
+    def factor(self, mode: int) -> np.ndarray:
+        out = np.empty((self._dims()[mode], self.R), dtype=np.float64)
+        self._check(self._lib.cptc_get_factors(self._h, int(mode),
+                                               out.ctypes.data_as(C.POINTER(C.c_double))),
+                    "get_factors")
+        return out
+
+    def factors(self) -> list:
+        return [self.factor(m) for m in range(len(self._dims()))]
+
+    def lam(self) -> np.ndarray:
+        out = np.empty(self.R, dtype=np.float64)
+        self._check(self._lib.cptc_get_lambda(self._h, out.ctypes.data_as(C.POINTER(C.c_double))),
+                    "get_lambda")
+        return out
+
+    # -- hot path --------------------------------------------------------
+    def mttkrp(self, mode: int) -> np.ndarray:
+        out = np.empty((self._dims()[mode], self.R), dtype=np.float64)
+        self._check(self._lib.cptc_mttkrp(self._h, int(mode),
+                                          out.ctypes.data_as(C.POINTER(C.c_double))), "mttkrp")
+        return out
+
+    def mttkrp_timed(self, mode: int, reps: int = 1) -> float:
+        ms = C.c_double(0.0)
+        self._check(self._lib.cptc_mttkrp_timed(self._h, int(mode), int(reps), C.byref(ms)),
+                    "mttkrp_timed")
+        return ms.value
+
+    def profile_mttkrp(self, mode: int, reps: int = 3) -> dict:
+        """Device ms of the dense-tile kernel, the FP64 view kernel and the
+        whole MTTKRP of `mode` (mean of `reps` launches each)."""
+        ms = (C.c_double * 3)()
+        self._check(self._lib.cptc_profile_mttkrp(self._h, int(mode), int(reps), ms),
+                    "profile_mttkrp")
+        return {"tiles_ms": ms[0], "sparse_ms": ms[1], "total_ms": ms[2]}
+
+    def als(self, iters: int, callback=None) -> list:
+        reports = []
+
+        def _cb(it, ms, fit, mode_ms, nm, user):
+            r = IterReport(it, ms, fit, [mode_ms[i] for i in range(nm)])
+            reports.append(r)
+            if callback is not None:
+                callback(r)
+
+        cb = N.ITER_CB(_cb)
+        self._check(self._lib.cptc_als(self._h, int(iters), cb, None), "als")
+        return reports

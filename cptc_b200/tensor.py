@@ -1,0 +1,98 @@
+"""Host sparse tensors: the synthetic benchmark workloads and FROSTT .tns I/O."""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _native as N
+
+
+@dataclass
+class CooTensor:
+    """Sparse tensor in coordinate form; idx[m] are 0-based uint32 indices."""
+
+    dims: tuple
+    idx: list
+    vals: np.ndarray
+    _keep: list = field(default_factory=list, repr=False)
+
+    @property
+    def order(self) -> int:
+        return len(self.dims)
+
+    @property
+    def nnz(self) -> int:
+        return int(self.vals.shape[0])
+
+    def as_struct(self) -> N.Coo:
+        """A cptc_coo view of the arrays (valid while self lives)."""
+        s = N.Coo()
+        s.order = self.order
+        for m, d in enumerate(self.dims):
+            s.dims[m] = int(d)
+        s.nnz = self.nnz
+        self.idx = [np.ascontiguousarray(a, dtype=np.uint32) for a in self.idx]
+        self.vals = np.ascontiguousarray(self.vals, dtype=np.float64)
+        for m in range(self.order):
+            s.idx[m] = self.idx[m].ctypes.data_as(C.POINTER(C.c_uint32))
+        s.vals = self.vals.ctypes.data_as(C.POINTER(C.c_double))
+        return s
+
+    def norm_sq(self) -> float:
+        return float(np.dot(self.vals, self.vals))
+
+
+def _take(s: N.Coo) -> CooTensor:
+    """Copies a library-owned cptc_coo into numpy and frees it."""
+    lib = N.host_lib()
+    n = int(s.nnz)
+    dims = tuple(int(s.dims[m]) for m in range(s.order))
+    idx = [np.ctypeslib.as_array(s.idx[m], (max(n, 1),))[:n].copy() for m in range(s.order)]
+    vals = np.ctypeslib.as_array(s.vals, (max(n, 1),))[:n].copy()
+    lib.cptc_coo_free(C.byref(s))
+    return CooTensor(dims, idx, vals)
+
+
+def gen_config(cfg: int, scale: float = 1.0, seed: int = 0) -> CooTensor:
+    """Benchmark workload `cfg` (1..5) with round(nnz*scale) nonzeros."""
+    lib = N.host_lib()
+    s = N.Coo()
+    rc = lib.cptc_gen_config(int(cfg), float(scale), int(seed), C.byref(s))
+    if rc != 0:
+        raise RuntimeError(f"cptc_gen_config: {lib.cptc_host_last_error().decode()}")
+    return _take(s)
+
+
+def gen_uniform(dims, nnz: int, seed: int = 0, values: str = "uniform") -> CooTensor:
+    """Distinct uniform coordinates; values uniform (0,1], lognormal, normal
+    or poisson (3)+1."""
+    kinds = {"uniform": 0, "lognormal": 1, "normal": 2, "poisson": 3}
+    lib = N.host_lib()
+    d = (C.c_uint64 * len(dims))(*[int(x) for x in dims])
+    s = N.Coo()
+    rc = lib.cptc_gen_uniform(len(dims), d, int(nnz), int(seed), kinds[values], C.byref(s))
+    if rc != 0:
+        raise RuntimeError(f"cptc_gen_uniform: {lib.cptc_host_last_error().decode()}")
+    return _take(s)
+
+
+def read_tns(path: str, order: int = 0) -> CooTensor:
+    lib = N.host_lib()
+    s = N.Coo()
+    rc = lib.cptc_tns_read(str(path).encode(), int(order), C.byref(s))
+    if rc != 0:
+        raise RuntimeError(f"cptc_tns_read({path}) failed with {rc}")
+    return _take(s)
+
+
+def write_tns(path: str, t: CooTensor) -> None:
+    lib = N.host_lib()
+    s = t.as_struct()
+    if lib.cptc_tns_write(str(path).encode(), C.byref(s)) != 0:
+        raise RuntimeError(f"cptc_tns_write({path}) failed")
+
+
+def probe_order(path: str) -> int:
+    return int(N.host_lib().cptc_tns_probe_order(str(path).encode()))

@@ -1,0 +1,161 @@
+/*
+ * cptc.h — C ABI of the cptc-b200 CP-ALS engine (sm_100a).
+ *
+ * The reference (zhixianzhu/cpTC) has no library interface: its operator
+ * boundary is a set of C++ functions over its HybridCOOTensor, called only by
+ * its own main().  Each entry point below names the reference function whose
+ * role it takes over (paths inside the reference project):
+ *
+ *   cptc_load_coo     <- load_tns_file / COO upload (src/tensor.cu:39-271)
+ *   cptc_build        <- compute/apply_cadr_reordering (src/cadr.cu:23-81),
+ *                        partition_tensor_hybrid (include/partition.hpp:335),
+ *                        build_mttkrp_views (include/partition.hpp:369),
+ *                        build_dense_mttkrp_views (:375), the fill-rate
+ *                        selector (src/main.cu:336-426); for the N-order path
+ *                        apply_reordering / build_dense_nd / ModeView build
+ *                        (src/generic.cu:1180-1376, 578-725, 1842-1958)
+ *   cptc_init_factors <- init_factors_random (src/common.cu:66-126) and the
+ *                        generic init (src/generic.cu:1754-1788)
+ *   cptc_mttkrp       <- run_mttkrp_mode (src/als.cu:535-604):
+ *                        zero FtV, compute_dense_mttkrp_async
+ *                        (include/dense.hpp:7) + compute_sparse_mttkrp_async
+ *                        (include/sparse.hpp:77)
+ *   cptc_als          <- execute_als_decomposition (include/als.hpp:7) and
+ *                        run_generic_cp (include/generic.hpp:42)
+ *   cptc_get_factors  <- unpermute_factor_matrices (include/cadr.hpp:21-32)
+ *
+ * Conventions: status 0 = OK, negative = error (message from
+ * cptc_last_error); the library never exits the process.  Host arrays are
+ * copied; factors are row-major FP64 I_n x R in the caller's original index
+ * space.  One context per host thread; a context is not thread-safe.
+ */
+#ifndef CPTC_H
+#define CPTC_H
+
+#include <stdint.h>
+
+#include "cptc_host.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct cptc_ctx cptc_ctx;
+
+enum {
+  CPTC_OK = 0,
+  CPTC_E_ARG = -1,      /* invalid argument or call order */
+  CPTC_E_CUDA = -2,     /* CUDA runtime / kernel launch failure */
+  CPTC_E_NOMEM = -3,    /* device or host allocation failed */
+  CPTC_E_UNSUP = -4,    /* configuration not supported */
+  CPTC_E_COMM = -5,     /* NCCL failure or timeout */
+  CPTC_E_NUMERIC = -6   /* solve failed (non-finite) */
+};
+
+/* Path selection (ALS_FORCE_WMMA / ALS_FORCE_CUDA of src/main.cu:395-402). */
+enum { CPTC_PATH_AUTO = 0, CPTC_PATH_TF32 = 1, CPTC_PATH_FP64 = 2 };
+/* Index relabelling before the build (src/generic.cu:1162-1169). */
+enum { CPTC_REORDER_NONE = 0, CPTC_REORDER_CADR = 1, CPTC_REORDER_HITS = 2,
+       CPTC_REORDER_AUTO = 3, CPTC_REORDER_DEFAULT = -1 };
+/* R x R solve (GEN_SOLVER of src/generic.cu:2114-2136). */
+enum { CPTC_SOLVER_DEFAULT = 0, CPTC_SOLVER_CHOL = 1, CPTC_SOLVER_PINV = 2 };
+
+typedef struct cptc_opts {
+  int path;                 /* CPTC_PATH_*                                   */
+  double fill_min;          /* <= 0: B200 default; else ALS_FILL_MIN         */
+  int generic;              /* 1: order-3 through the N-order path
+                               (ALS_GENERIC_FORCE)                           */
+  int reorder;              /* CPTC_REORDER_* (GEN_REORDER)                  */
+  int reorder_rounds;       /* HITS rounds (GEN_REORDER_T, 3)                */
+  uint64_t reorder_sample;  /* HITS sample budget (GEN_REORDER_SAMPLE, 8e6)  */
+  int solver;               /* CPTC_SOLVER_*                                 */
+  uint32_t seed;            /* N-order init seed (GEN_SEED, 42)              */
+  int dense_generic;        /* 0 disables N-order dense units (GEN_DENSE=0)  */
+  double dense_thr_generic; /* GEN_DENSE_THRESHOLD (0.03)                    */
+  int dense_inner[3];       /* GEN_DENSE_INNER (0,1,2)                       */
+  int verbose;              /* print the reference's progress lines          */
+} cptc_opts;
+
+/* Per-iteration report: iteration number (1-based), device time of the
+ * iteration in ms, Gram fit, and MTTKRP device ms per mode. */
+typedef void (*cptc_iter_cb)(int iter, double ms, double fit,
+                             const double* mttkrp_ms, int nmodes, void* user);
+
+typedef struct cptc_stats {
+  int order;
+  uint64_t dims[CPTC_MAX_ORDER];
+  uint64_t nnz;
+  int rank;
+  int tf32_path;            /* 1 if the dense-tile TF32 path is active       */
+  uint64_t dense_nnz;       /* nonzeros in dense tiles / units               */
+  uint64_t sparse_nnz;      /* nonzeros in the FP64 residual                 */
+  uint64_t dense_tiles;
+  double avg_fill;          /* dense_nnz / (tiles * 4096)                    */
+  double fill_min;          /* threshold used by the selector                */
+  int cutoff;               /* nonzeros per 16^3 tile to be dense            */
+  double x_norm_sq;         /* ||X||_F^2                                     */
+  double build_ms;          /* reorder + partition + views                   */
+  uint64_t device_bytes;    /* device memory held by the context             */
+  int fiber_mode[CPTC_MAX_ORDER]; /* per target mode: mode whose rows are
+                                     reused along a sorted run               */
+  int nranks, rank_id;
+} cptc_stats;
+
+int cptc_opts_default(cptc_opts* o);
+
+/* Creates a context on CUDA device `device` (flags reserved, pass 0). */
+int cptc_create(cptc_ctx** out, int device, int flags);
+int cptc_destroy(cptc_ctx* ctx);
+const char* cptc_last_error(const cptc_ctx* ctx);
+
+/* Multi-GPU (one process per GPU): rank 0 calls cptc_comm_unique_id and
+ * shares the 128 bytes; every rank then calls cptc_comm_init before
+ * cptc_build.  Mode-n rows are split into nranks contiguous slabs of equal
+ * nonzero count; each mode update ends with an all-reduce of the R x R Gram
+ * partials and an all-gather of the updated factor slab. */
+int cptc_comm_unique_id(unsigned char out_id[128]);
+int cptc_comm_init(cptc_ctx* ctx, const unsigned char id[128], int rank, int nranks);
+
+/* Copies a host COO tensor (order 2..8) to the device. */
+int cptc_load_coo(cptc_ctx* ctx, const cptc_coo* t);
+
+/* Reorders, partitions, builds per-mode views and selects the path for rank
+ * R.  threshold: dense 16^3 tile cutoff fraction (<= 0: auto balance). */
+int cptc_build(cptc_ctx* ctx, int R, double threshold, const cptc_opts* opts);
+
+/* The reference's initial factors (order-3: mt19937(42) in relabelled
+ * space; N-order: mt19937(seed) carried through the relabelling), lambda=1. */
+int cptc_init_factors(cptc_ctx* ctx);
+
+/* Factors in the caller's original index space, row-major I_n x R. */
+int cptc_set_factors(cptc_ctx* ctx, int mode, const double* host);
+int cptc_get_factors(cptc_ctx* ctx, int mode, double* host);
+int cptc_get_lambda(cptc_ctx* ctx, double* host_R);
+
+/* One MTTKRP of `mode` on the current factors (the path selected by
+ * cptc_build), result in original index space (I_mode x R, host). */
+int cptc_mttkrp(cptc_ctx* ctx, int mode, double* host_out);
+
+/* Device-resident MTTKRP into the context's FtV buffer; *ms = device time of
+ * `reps` back-to-back launches divided by reps (CUDA events on the
+ * context's stream). */
+int cptc_mttkrp_timed(cptc_ctx* ctx, int mode, int reps, double* ms);
+
+/* Device times (ms, mean of `reps` back-to-back launches on the context's
+ * stream) of one mode's MTTKRP parts: ms3[0] dense-tile TF32 kernel,
+ * ms3[1] FP64 view kernel, ms3[2] the whole MTTKRP (zero + both). */
+int cptc_profile_mttkrp(cptc_ctx* ctx, int mode, int reps, double ms3[3]);
+
+/* Number of kernels this library has launched since it was loaded. */
+unsigned long long cptc_launch_count(void);
+
+/* Runs `iters` CP-ALS iterations; cb (nullable) is called after each. */
+int cptc_als(cptc_ctx* ctx, int iters, cptc_iter_cb cb, void* user);
+
+int cptc_get_stats(cptc_ctx* ctx, cptc_stats* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CPTC_H */

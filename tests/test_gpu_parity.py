@@ -1,0 +1,186 @@
+"""CUDA engine (through the C ABI) against the CPU oracle on identical inputs.
+
+Tolerances are the reference's own bounds: FP64 paths 1e-12 relative
+(atomic reordering only), the TF32 dense-tile path 2e-3 relative per entry,
+and final fit 1e-4 absolute.  Norm-wise relative error is used for the FP64
+MTTKRP: || got - ref || / || ref ||.
+"""
+import numpy as np
+import pytest
+
+import cptc_b200 as cp
+
+pytestmark = pytest.mark.gpu
+
+FP64_TOL = 1e-12
+
+
+def rel(a, b):
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
+
+
+def rand_factors(dims, R, seed=7, signed=False):
+    rng = np.random.default_rng(seed)
+    return [(rng.standard_normal((d, R)) if signed else rng.random((d, R))) for d in dims]
+
+
+def engine_for(t, R, **kw):
+    e = cp.Engine(0)
+    e.load(t)
+    e.build(R, **kw)
+    return e
+
+
+CASES = [
+    # dims, nnz, R, values
+    ((128, 128, 128), 200000, 16, "uniform"),
+    ((128, 128, 128), 200000, 8, "normal"),
+    ((37, 45, 29), 5000, 17, "normal"),
+    ((37, 45, 29), 5000, 32, "lognormal"),
+    ((3000, 20, 50), 60000, 64, "uniform"),  # mode-1 rows of ~3000 nnz span tasks
+    ((500, 400, 300), 30000, 128, "normal"),
+    ((200, 1, 300), 4000, 24, "uniform"),    # a mode of length 1
+]
+
+
+@pytest.mark.parametrize("dims,nnz,R,values", CASES)
+def test_mttkrp_fp64_order3(gpu, oracle, dims, nnz, R, values):
+    t = cp.gen_uniform(dims, nnz, seed=21, values=values)
+    e = engine_for(t, R, path="fp64")
+    F = rand_factors(t.dims, R, signed=(values == "normal"))
+    for m in range(3):
+        e.set_factor(m, F[m])
+    for n in range(3):
+        got = e.mttkrp(n)
+        ref = oracle.mttkrp(t, F, n, threads=8)
+        assert rel(got, ref) < FP64_TOL, (n, rel(got, ref))
+
+
+def test_mttkrp_empty_rows_and_heavy_row(gpu, oracle):
+    # Indices only in the lower half of each mode, plus one row holding
+    # ~40% of the nonzeros: empty rows must come out exactly zero and the
+    # heavy row is split over many tasks (atomic combination).
+    rng = np.random.default_rng(3)
+    n = 50000
+    i = rng.integers(0, 60, n)
+    i[: n * 2 // 5] = 7
+    j = rng.integers(0, 50, n)
+    k = rng.integers(0, 40, n)
+    key = np.unique((i * 1000 + j) * 1000 + k)
+    t = cp.CooTensor((120, 100, 80), [(key // 1000000).astype(np.uint32),
+                                       (key // 1000 % 1000).astype(np.uint32),
+                                       (key % 1000).astype(np.uint32)],
+                     rng.standard_normal(len(key)))
+    R = 32
+    e = engine_for(t, R, path="fp64")
+    F = rand_factors(t.dims, R, signed=True)
+    for m in range(3):
+        e.set_factor(m, F[m])
+    for mode in range(3):
+        got = e.mttkrp(mode)
+        ref = oracle.mttkrp(t, F, mode, threads=8)
+        assert rel(got, ref) < FP64_TOL
+        empty = np.setdiff1d(np.arange(t.dims[mode]), t.idx[mode])
+        assert np.all(got[empty] == 0.0)
+
+
+@pytest.mark.parametrize("dims,nnz,R", [((30, 20, 25, 40), 20000, 16),
+                                        ((12, 9, 15, 8, 11), 8000, 32),
+                                        ((300, 200), 5000, 8)])
+def test_mttkrp_fp64_generic(gpu, oracle, dims, nnz, R):
+    t = cp.gen_uniform(dims, nnz, seed=5, values="normal")
+    e = engine_for(t, R, dense_generic=False)
+    F = rand_factors(t.dims, R, signed=True)
+    for m in range(t.order):
+        e.set_factor(m, F[m])
+    for n in range(t.order):
+        assert rel(e.mttkrp(n), oracle.mttkrp(t, F, n, threads=8)) < FP64_TOL
+
+
+@pytest.mark.parametrize("R", [16, 32, 64, 128])
+def test_mttkrp_tf32_tiles(gpu, oracle, R):
+    # 256^3 at fill ~0.9: every tile dense; partition on the given
+    # coordinates (no relabelling) so both sides see the same tiles.
+    t = cp.gen_config(2, scale=0.05)
+    e = engine_for(t, R, path="tf32", threshold=0.001, reorder="none")
+    st = e.stats()
+    assert st["tf32_path"] == 1 and st["dense_tiles"] > 0
+    F = rand_factors(t.dims, R)
+    for m in range(3):
+        e.set_factor(m, F[m])
+    for n in range(3):
+        got = e.mttkrp(n)
+        hyb, _ = oracle.mttkrp_hybrid3(t, F, n, thr=0.001, threads=8)
+        exact = oracle.mttkrp(t, F, n, threads=8)
+        assert rel(got, hyb) < 1e-5
+        assert np.abs(got - exact).max() / np.abs(exact).max() < 2e-3
+
+
+def test_mttkrp_tf32_mixed_partition(gpu, oracle):
+    t = cp.gen_config(3, scale=0.02)
+    e = engine_for(t, 32, path="tf32", threshold=0.03, reorder="none")
+    st = e.stats()
+    ref_stats = oracle.partition_stats3(t, thr=0.03)
+    assert st["dense_tiles"] == ref_stats["tiles"]
+    assert st["dense_nnz"] == ref_stats["dense_nnz"]
+    assert st["cutoff"] == ref_stats["cutoff"]
+    F = rand_factors(t.dims, 32)
+    for m in range(3):
+        e.set_factor(m, F[m])
+    for n in range(3):
+        hyb, _ = oracle.mttkrp_hybrid3(t, F, n, thr=0.03, threads=8)
+        assert rel(e.mttkrp(n), hyb) < 1e-5
+
+
+def test_als3_fp64_matches_oracle(gpu, oracle):
+    t = cp.gen_config(1)
+    e = engine_for(t, 16, path="fp64")
+    e.init_factors()
+    rep = e.als(10)
+    fits = np.array([r.fit for r in rep])
+    ref, lam_ref, F_ref = oracle.cp_als3(t, 16, 10, path="fp64", threads=8, want_factors=True)
+    assert np.max(np.abs(fits - ref)) < 1e-8
+    lam = e.lam()
+    assert np.allclose(np.sort(lam), np.sort(lam_ref), rtol=1e-6)
+    for m in range(3):
+        assert rel(e.factor(m), F_ref[m]) < 1e-6
+
+
+def test_als3_tf32_close_to_oracle(gpu, oracle):
+    t = cp.gen_config(1)
+    e = engine_for(t, 16, path="tf32")
+    e.init_factors()
+    fits = np.array([r.fit for r in e.als(5)])
+    ref_tf32, _, _ = oracle.cp_als3(t, 16, 5, path="tf32", threads=8)
+    ref_fp64, _, _ = oracle.cp_als3(t, 16, 5, path="fp64", threads=8)
+    assert np.max(np.abs(fits - ref_tf32)) < 1e-5
+    assert np.max(np.abs(fits - ref_fp64)) < 1e-4
+
+
+def test_als_generic_matches_oracle(gpu, oracle):
+    t = cp.gen_config(5, scale=0.02)
+    e = engine_for(t, 16, dense_generic=False)
+    e.init_factors()
+    fits = np.array([r.fit for r in e.als(5)])
+    ref, _, _ = oracle.cp_als_generic(t, 16, 5, dense_thr=0.0, threads=8)
+    assert np.max(np.abs(fits - ref)) < 1e-8
+
+
+def test_als_generic_pinv_solver(gpu, oracle):
+    t = cp.gen_uniform((40, 30, 20, 10), 8000, seed=2, values="poisson")
+    e = engine_for(t, 8, dense_generic=False, solver="pinv")
+    e.init_factors()
+    fits = np.array([r.fit for r in e.als(4)])
+    ref, _, _ = oracle.cp_als_generic(t, 8, 4, dense_thr=0.0, solver="pinv", threads=8)
+    assert np.max(np.abs(fits - ref)) < 1e-8
+
+
+def test_order3_generic_route(gpu, oracle):
+    # ALS_GENERIC_FORCE: order 3 through the N-order path (CADR with tie
+    # break, Cholesky, lambda = norms).
+    t = cp.gen_config(1, scale=0.2)
+    e = engine_for(t, 8, generic=True)
+    e.init_factors()
+    fits = np.array([r.fit for r in e.als(4)])
+    ref, _, _ = oracle.cp_als_generic(t, 8, 4, dense_thr=0.0, threads=8)
+    assert np.max(np.abs(fits - ref)) < 1e-8
