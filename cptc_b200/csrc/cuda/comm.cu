@@ -156,23 +156,25 @@ void slab_select(Engine& E, int n, const uint32_t* base, uint64_t nbase, DArray<
 }
 
 void slab_tiles(Engine& E) {
-  for (int m = 0; m < 3; ++m) E.tile_cnt[m] = E.tiles.ntiles;
-  if (E.nranks == 1 || E.tiles.ntiles == 0) return;
-  for (int m = 0; m < 3; ++m) {
-    TileInSlab pred{E.tiles.tile.p, m, (int)(E.row_lo(m) / 16), (int)((E.row_hi(m) + 15) / 16)};
-    DArray<uint32_t> out(E.tiles.ntiles);
+  UnitPool& U = E.units;
+  for (int t = 0; t < 3; ++t) U.cnt[t] = U.nunits;
+  if (E.nranks == 1 || U.nunits == 0) return;
+  for (int t = 0; t < 3; ++t) {
+    const int m = U.inner[t];
+    TileInSlab pred{U.unit.p, t, (int)(E.row_lo(m) / 16), (int)((E.row_hi(m) + 15) / 16)};
+    DArray<uint32_t> out(U.nunits);
     DArray<unsigned long long> cnt(1);
     size_t tb = 0;
-    CPTC_CUDA(cub::DeviceSelect::If(nullptr, tb, E.tile_order[m].p, out.p, cnt.p,
-                                    (int64_t)E.tiles.ntiles, pred, E.stream));
+    CPTC_CUDA(cub::DeviceSelect::If(nullptr, tb, U.order[t].p, out.p, cnt.p, (int64_t)U.nunits,
+                                    pred, E.stream));
     DArray<unsigned char> temp(tb);
-    CPTC_CUDA(cub::DeviceSelect::If(temp.p, tb, E.tile_order[m].p, out.p, cnt.p,
-                                    (int64_t)E.tiles.ntiles, pred, E.stream));
+    CPTC_CUDA(cub::DeviceSelect::If(temp.p, tb, U.order[t].p, out.p, cnt.p, (int64_t)U.nunits,
+                                    pred, E.stream));
     unsigned long long h = 0;
     CPTC_CUDA(cudaMemcpyAsync(&h, cnt.p, sizeof(h), cudaMemcpyDeviceToHost, E.stream));
     CPTC_CUDA(cudaStreamSynchronize(E.stream));
-    E.tile_order[m] = std::move(out);
-    E.tile_cnt[m] = h;
+    U.order[t] = std::move(out);
+    U.cnt[t] = h;
   }
 }
 

@@ -64,8 +64,9 @@ uint64_t Engine::device_bytes() const {
   for (int m = 0; m < N; ++m) b += idx[m].bytes() + F[m].bytes() + G[m].bytes();
   for (const View& v : views)
     b += v.gw.bytes() + v.oidx.bytes() + v.val.bytes() + v.rows.bytes() + v.task_row.bytes();
-  b += tiles.tile.bytes() + tiles.start.bytes() + tiles.lid.bytes() + tiles.val.bytes();
-  for (int m = 0; m < 3; ++m) b += tile_order[m].bytes();
+  b += units.unit.bytes() + units.start.bytes() + units.lid.bytes() + units.val.bytes() +
+       units.outer_idx.bytes();
+  for (int m = 0; m < 3; ++m) b += units.order[m].bytes();
   b += FtV.bytes() + FtF.bytes() + Ainv.bytes() + gpart.bytes() + dots.bytes() + lambda.bytes();
   return b;
 }
@@ -171,8 +172,8 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
   built = false;
   have_factors = false;
   views.clear();
-  tiles = TilePool{};
-  for (auto& t : tile_order) t.release();
+  units = UnitPool{};
+  dense_active = false;
   tf32 = false;
   avg_fill = 0.0;
   cutoff = 0;
@@ -199,35 +200,45 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
 
   DArray<uint32_t> sel;
   uint64_t nsel = nnz;
-  bool use_sel = false;
   if (!generic && opts.path != CPTC_PATH_FP64 && nnz > 0) {
-    partition_tiles3(*this, threshold, sel, nsel, tile_order);
-    avg_fill = tiles.ntiles ? (double)tiles.nnz / ((double)tiles.ntiles * 4096.0) : 0.0;
+    partition_tiles3(*this, threshold, sel, nsel);
+    avg_fill = units.nunits ? (double)units.nnz / ((double)units.nunits * 4096.0) : 0.0;
     if (opts.path == CPTC_PATH_TF32) tf32 = true;
-    else tf32 = (avg_fill >= fill_min) && tiles.ntiles > 0 && (R % 8 == 0);
-    if (tf32) {
-      CPTC_REQUIRE(R % 8 == 0, CPTC_E_UNSUP,
-                   "the TF32 tile path needs the rank to be a multiple of 8");
-      use_sel = true;
-    } else {
-      tiles = TilePool{};
-      for (auto& t : tile_order) t.release();
-      sel.release();
-      nsel = nnz;
-    }
+    else tf32 = (avg_fill >= fill_min) && units.nunits > 0 && (R % 8 == 0);
+    CPTC_REQUIRE(!tf32 || R % 8 == 0, CPTC_E_UNSUP,
+                 "the TF32 tile path needs the rank to be a multiple of 8");
+  } else if (generic && N >= 4 && opts.dense_generic && opts.dense_thr_generic > 0.0 &&
+             R % 8 == 0 && nnz > 0) {
+    // N-order dense units over the inner modes (src/generic.cu:1808-1840).
+    partition_units(*this, opts.dense_thr_generic, sel, nsel);
+    units.store_dups = false;
+    cutoff = (int)(4096.0 * opts.dense_thr_generic);
+    avg_fill = units.nunits ? (double)units.nnz / ((double)units.nunits * 4096.0) : 0.0;
+    tf32 = units.nunits > 0;
   }
+  if (!tf32) {
+    units = UnitPool{};
+    sel.release();
+    nsel = nnz;
+  }
+  dense_active = tf32;
   views.resize(N);
   alloc_workspace();
   comm_prepare(*this);
   slab_tiles(*this);
   for (int n = 0; n < N; ++n) {
+    // Residual-only views for modes the dense tiles cover as a target.
+    const bool covered = dense_active &&
+                         (n == units.inner[0] || n == units.inner[1] || n == units.inner[2]);
+    const uint32_t* base = covered ? sel.p : nullptr;
+    const uint64_t nbase = covered ? nsel : nnz;
     if (nranks > 1) {
       DArray<uint32_t> mine;
       uint64_t nmine = 0;
-      slab_select(*this, n, use_sel ? sel.p : nullptr, use_sel ? nsel : nnz, mine, nmine);
+      slab_select(*this, n, base, nbase, mine, nmine);
       build_view(*this, views[n], n, mine.p, nmine);
     } else {
-      build_view(*this, views[n], n, use_sel ? sel.p : nullptr, use_sel ? nsel : nnz);
+      build_view(*this, views[n], n, base, nbase);
     }
   }
   CPTC_CUDA(cudaStreamSynchronize(stream));
@@ -320,28 +331,39 @@ void Engine::mttkrp(int mode) {
 }
 
 void Engine::mttkrp_tiles(int mode) {
-  if (tf32 && tile_cnt[mode] > 0) {
-    // Order-3 roles (src/dense.cu:339-1075): mode 0 contracts j in TF32 and
-    // weights k-slabs; mode 1 contracts i, weights k; mode 2 contracts i,
-    // weights j.
-    TileArgs ta{};
-    ta.tile = tiles.tile.p;
-    ta.start = tiles.start.p;
-    ta.lid = tiles.lid.p;
-    ta.val = tiles.val.p;
-    ta.ntiles = tile_cnt[mode];
-    ta.R = R;
-    ta.tslot = mode;
-    ta.cslot = (mode == 0) ? 1 : 0;
-    ta.sslot = (mode == 2) ? 1 : 2;
-    for (int m = 0; m < 3; ++m) ta.dims[m] = dims[m];
-    ta.Fc = F[ta.cslot].p;
-    ta.Fs = F[ta.sslot].p;
-    ta.nouter = 0;
-    ta.store_dups = 1;
-    ta.out = FtV.p;
-    launch_mttkrp_tiles3(ta, tile_order[mode].p, stream);
+  if (!dense_active) return;
+  int ts = -1;
+  for (int q = 0; q < 3; ++q)
+    if (units.inner[q] == mode) ts = q;
+  if (ts < 0 || units.cnt[ts] == 0) return;
+  TileArgs ta{};
+  ta.tile = units.unit.p;
+  ta.start = units.start.p;
+  ta.lid = units.lid.p;
+  ta.val = units.val.p;
+  ta.ntiles = units.cnt[ts];
+  ta.R = R;
+  ta.tslot = ts;
+  if (!generic) {
+    // Order-3 roles (src/dense.cu:339-1075): mode 0 contracts j in TF32
+    // and weights k-slabs; mode 1 contracts i, weights k; mode 2 contracts
+    // i, weights j.
+    ta.cslot = (ts == 0) ? 1 : 0;
+    ta.sslot = (ts == 2) ? 1 : 2;
+  } else {
+    // N-order roles (src/generic.cu:486-487): fold slot t+1, weight t+2.
+    ta.cslot = (ts + 1) % 3;
+    ta.sslot = (ts + 2) % 3;
   }
+  for (int q = 0; q < 3; ++q) ta.dims[q] = dims[units.inner[q]];
+  ta.Fc = F[units.inner[ta.cslot]].p;
+  ta.Fs = F[units.inner[ta.sslot]].p;
+  ta.nouter = units.nouter;
+  ta.outer_idx = units.outer_idx.p;
+  for (int q = 0; q < units.nouter; ++q) ta.Fout[q] = F[units.outer[q]].p;
+  ta.store_dups = units.store_dups ? 1 : 0;
+  ta.out = FtV.p;
+  launch_mttkrp_tiles3(ta, units.order[ts].p, stream);
 }
 
 void Engine::mttkrp_sparse(int mode) {
@@ -634,9 +656,9 @@ int cptc_get_stats(cptc_ctx* c, cptc_stats* s) {
     s->nnz = e.nnz;
     s->rank = e.R;
     s->tf32_path = e.tf32 ? 1 : 0;
-    s->dense_nnz = e.tf32 ? e.tiles.nnz : 0;
-    s->sparse_nnz = e.views.empty() ? e.nnz : e.views[0].nnz;
-    s->dense_tiles = e.tf32 ? e.tiles.ntiles : 0;
+    s->dense_nnz = e.tf32 ? e.units.nnz : 0;
+    s->sparse_nnz = e.nnz - s->dense_nnz;
+    s->dense_tiles = e.tf32 ? e.units.nunits : 0;
     s->avg_fill = e.avg_fill;
     s->fill_min = e.fill_min;
     s->cutoff = e.cutoff;

@@ -39,28 +39,23 @@ struct View {
   uint64_t nrows = 0, ntasks = 0;
 };
 
-// Order-3 dense tiles: elements of tiles with at least `cutoff` nonzeros,
-// grouped by tile.  tile_info[t] = (b0, b1, b2) tile origins / 16.
-struct TilePool {
-  uint64_t ntiles = 0, nnz = 0;
-  DArray<int4> tile;        // x,y,z = tile block coords, w = element count
-  DArray<uint64_t> start;   // first element of each tile in the pool
-  DArray<uint16_t> lid;     // (li << 8) | (lj << 4) | lk
-  DArray<double> val;
-};
-
-// N-order dense units: a 16^3 tile over the inner modes with every outer
-// mode fixed (src/generic.cu:406-561).
+// Dense 16^3 tiles: order 3 (inner = modes 0,1,2, no outer modes) or the
+// N-order units (a tile over the inner modes with every outer mode fixed,
+// src/generic.cu:406-561).  Elements of tiles with at least `cutoff`
+// nonzeros, grouped by tile.
 struct UnitPool {
   uint64_t nunits = 0, nnz = 0;
   int inner[3] = {0, 1, 2};
   int nouter = 0;
   int outer[CPTC_MAX_ORDER] = {0};
-  DArray<uint4> unit;        // x,y,z inner tile coords, w = count
-  DArray<uint64_t> start;
-  DArray<uint32_t> outer_idx;  // nouter * nunits
-  DArray<uint16_t> lid;
+  bool store_dups = true;      // order-3 tiles store (last write wins)
+  DArray<int4> unit;           // x,y,z tile block coords of the inner modes, w = count
+  DArray<uint64_t> start;      // first element of each tile in the pool
+  DArray<uint32_t> outer_idx;  // nunits x nouter (unit-major)
+  DArray<uint16_t> lid;        // (l0 << 8) | (l1 << 4) | l2
   DArray<double> val;
+  DArray<uint32_t> order[3];   // visiting order per inner target slot
+  uint64_t cnt[3] = {0, 0, 0}; // tiles of this rank per inner target slot
 };
 
 struct Engine {
@@ -88,10 +83,8 @@ struct Engine {
   bool generic = false;  // N-order ALS semantics (Cholesky, lambda = norms)
   bool tf32 = false;
   std::vector<View> views;
-  TilePool tiles;
-  DArray<uint32_t> tile_order[3];
-  uint64_t tile_cnt[3] = {0, 0, 0};  // tiles of this rank per target mode
-  UnitPool units;
+  UnitPool units;               // dense tiles (order 3) or units (N-order)
+  bool dense_active = false;
   double avg_fill = 0.0, fill_min = 0.0;
   int cutoff = 0;
   double build_ms = 0.0;

@@ -48,8 +48,7 @@ struct TileArgs {
 // order: tile visiting order for this mode (sorted by target block).
 void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, cudaStream_t s);
 // Partition of Engine::tiles + residual selection (tiles.cu).
-void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64_t& nsel,
-                      DArray<uint32_t> tile_order[3]);
+void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64_t& nsel);
 // Views (views.cu).
 void build_view(Engine& E, View& v, int n, const uint32_t* d_sel, uint64_t nsel);
 

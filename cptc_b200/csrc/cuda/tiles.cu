@@ -286,13 +286,13 @@ __global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __res
 
 // Builds the dense tile pool (tiles with >= cutoff nonzeros) and the list of
 // residual elements.  Returns the residual selection in `sel` (device).
-void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64_t& nsel,
-                      DArray<uint32_t> tile_order[3]) {
+void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64_t& nsel) {
   cudaStream_t s = E.stream;
   const uint64_t n = E.nnz;
   const uint64_t nbj = (E.dims[1] + 15) / 16, nbk = (E.dims[2] + 15) / 16;
-  TilePool& P = E.tiles;
-  P = TilePool{};
+  UnitPool& P = E.units;
+  P = UnitPool{};
+  P.store_dups = true;
   const unsigned gb = grid_for(n, 256, 148 * 16);
   DArray<uint64_t> key_a(n), key_b(n);
   DArray<uint32_t> id_a(n), id_b(n);
@@ -409,14 +409,14 @@ void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64
   unsigned long long ntiles = 0;
   CPTC_CUDA(cudaMemcpyAsync(&ntiles, nt_d.p, sizeof(ntiles), cudaMemcpyDeviceToHost, s));
   CPTC_CUDA(cudaStreamSynchronize(s));
-  P.ntiles = ntiles;
-  P.tile.alloc(ntiles);
+  P.nunits = ntiles;
+  P.unit.alloc(ntiles);
   P.start.alloc(ntiles);
   if (ntiles > 0) {
     DArray<uint64_t> c64(ntiles);
     k_tiles_from_runs<<<grid_for(ntiles, 256, 148 * 16), 256, 0, s>>>(rsel.p, ntiles, ukeys.p,
                                                                       counts.p, nbj, nbk,
-                                                                      P.tile.p, c64.p);
+                                                                      P.unit.p, c64.p);
     CPTC_LAUNCH_CHECK();
     size_t xb = 0;
     CPTC_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, xb, c64.p, P.start.p, (int64_t)ntiles, s));
@@ -425,15 +425,15 @@ void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64
     // Per-mode visiting order: by target block (stable).
     for (int m = 0; m < 3; ++m) {
       DArray<uint32_t> ka(ntiles), kb(ntiles), ia(ntiles);
-      tile_order[m].alloc(ntiles);
-      k_tile_target_keys<<<grid_for(ntiles, 256, 148 * 16), 256, 0, s>>>(P.tile.p, ntiles, m,
+      P.order[m].alloc(ntiles);
+      k_tile_target_keys<<<grid_for(ntiles, 256, 148 * 16), 256, 0, s>>>(P.unit.p, ntiles, m,
                                                                           ka.p, ia.p);
       CPTC_LAUNCH_CHECK();
       size_t ob = 0;
-      CPTC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, ob, ka.p, kb.p, ia.p, tile_order[m].p,
+      CPTC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, ob, ka.p, kb.p, ia.p, P.order[m].p,
                                                 (int64_t)ntiles, 0, 32, s));
       if (ob > temp.bytes()) temp.alloc(ob);
-      CPTC_CUDA(cub::DeviceRadixSort::SortPairs(temp.p, ob, ka.p, kb.p, ia.p, tile_order[m].p,
+      CPTC_CUDA(cub::DeviceRadixSort::SortPairs(temp.p, ob, ka.p, kb.p, ia.p, P.order[m].p,
                                                 (int64_t)ntiles, 0, 32, s));
     }
   }

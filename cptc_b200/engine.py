@@ -115,7 +115,7 @@ class Engine:
               reorder: str = "default", reorder_rounds: int = 3,
               reorder_sample: int = 8_000_000, solver: str = "default", seed: int = 42,
               dense_generic: bool = True, dense_thr_generic: float = 0.03,
-              fill_min: float = 0.0) -> None:
+              dense_inner: tuple = (0, 1, 2), fill_min: float = 0.0) -> None:
         o = default_opts()
         o.path = PATHS[path]
         o.fill_min = float(fill_min)
@@ -127,6 +127,8 @@ class Engine:
         o.seed = int(seed)
         o.dense_generic = int(bool(dense_generic))
         o.dense_thr_generic = float(dense_thr_generic)
+        for q in range(3):
+            o.dense_inner[q] = int(dense_inner[q])
         self._check(self._lib.cptc_build(self._h, int(R), float(threshold), C.byref(o)), "build")
         self.R = int(R)
 

@@ -184,3 +184,44 @@ def test_order3_generic_route(gpu, oracle):
     fits = np.array([r.fit for r in e.als(4)])
     ref, _, _ = oracle.cp_als_generic(t, 8, 4, dense_thr=0.0, threads=8)
     assert np.max(np.abs(fits - ref)) < 1e-8
+
+
+@pytest.mark.parametrize("R,inner", [(16, (0, 1, 2)), (32, (0, 1, 2)), (16, (1, 2, 3)),
+                                     (8, (0, 2, 3))])
+def test_mttkrp_units_generic(gpu, oracle, R, inner):
+    # N-order dense units (16^3 over the inner modes, outer modes fixed) in
+    # TF32 with FP64 weighting, plus the FP64 residual; no relabelling so
+    # both sides form the same units.  Inner sets other than (0,1,2) are
+    # refused by the reference (its kernel fails its own self-test there).
+    t = cp.gen_config(5, scale=0.05)
+    e = engine_for(t, R, reorder="none", dense_thr_generic=0.03, dense_inner=inner)
+    st = e.stats()
+    assert st["tf32_path"] == 1 and st["dense_tiles"] > 0
+    F = rand_factors(t.dims, R)
+    for m in range(t.order):
+        e.set_factor(m, F[m])
+    inner_c = (C_INT * 3)(*inner)
+    for n in range(t.order):
+        got = e.mttkrp(n)
+        exact = oracle.mttkrp(t, F, n, threads=8)
+        if n in inner:
+            ref = units_oracle(oracle, t, F, inner, inner.index(n))
+            assert rel(got, ref) < 1e-5
+            assert np.abs(got - exact).max() / np.abs(exact).max() < 2e-3
+        else:
+            assert rel(got, exact) < FP64_TOL
+
+
+import ctypes as _C  # noqa: E402
+
+C_INT = _C.c_int
+
+
+def units_oracle(oracle, t, F, inner, tslot):
+    a = oracle._Args(t)
+    Fs, fp = oracle._fptrs(F)
+    out = np.zeros((t.dims[inner[tslot]], F[0].shape[1]))
+    inn = (_C.c_int * 3)(*inner)
+    oracle.lib().or_mttkrp_units(t.order, a.dims, a.nnz, a.ip, a.vp, F[0].shape[1], fp, inn,
+                                 tslot, 0.03, out.ctypes.data_as(oracle.DP), 8)
+    return out
