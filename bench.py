@@ -121,22 +121,39 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # tensor generation (rank 0 generates, other ranks read the shared copy)
 # ---------------------------------------------------------------------------
-def get_tensor(a, rank: int, world: int, barrier):
+def _cache_path(a) -> Path:
+    d = Path(tempfile.gettempdir()) / "cptc_bench_cache"
+    d.mkdir(exist_ok=True)
+    return d / f"cfg{a.config}_s{a.scale}.npz"
+
+
+def load_or_generate(a):
+    """The seeded workload; cached as .npz in the temp folder because
+    generating the 76.9M-nonzero tensor takes tens of seconds."""
     import cptc_b200 as cp
 
+    path = _cache_path(a)
+    if path.exists():
+        z = np.load(path)
+        dims = tuple(int(x) for x in z["dims"])
+        return cp.CooTensor(dims, [z[f"i{m}"] for m in range(len(dims))], z["vals"])
+    t = cp.gen_config(a.config, a.scale)
+    tmp = path.with_suffix(".tmp.npz")
+    np.savez(tmp, dims=np.array(t.dims, dtype=np.uint64), vals=t.vals,
+             **{f"i{m}": t.idx[m] for m in range(t.order)})
+    os.replace(tmp, path)
+    return t
+
+
+def get_tensor(a, rank: int, world: int, barrier):
     if world == 1:
-        return cp.gen_config(a.config, a.scale)
-    path = Path(tempfile.gettempdir()) / f"cptc_bench_cfg{a.config}_{a.scale}.npz"
+        return load_or_generate(a)
     if rank == 0:
-        t = cp.gen_config(a.config, a.scale)
-        np.savez(path, dims=np.array(t.dims, dtype=np.uint64), vals=t.vals,
-                 **{f"i{m}": t.idx[m] for m in range(t.order)})
+        t = load_or_generate(a)
         barrier()
         return t
     barrier()
-    z = np.load(path)
-    dims = tuple(int(x) for x in z["dims"])
-    return cp.CooTensor(dims, [z[f"i{m}"] for m in range(len(dims))], z["vals"])
+    return load_or_generate(a)
 
 
 def algorithmic_bytes(nnz: int, order: int, R: int, rows: int) -> int:
@@ -339,7 +356,7 @@ def run_reference(a):
     import cptc_b200 as cp
 
     binary = ROOT / "oracle" / "_ref" / "cptc_opt"
-    t = cp.gen_config(a.config, a.scale)
+    t = load_or_generate(a)
     if not binary.exists():
         # Oracle port on the host cores instead.
         from oracle import oracle as o
