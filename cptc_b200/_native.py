@@ -105,6 +105,9 @@ ENGINE_SYMBOLS = {
     "cptc_launch_count": (C.c_ulonglong, []),
     "cptc_als": (C.c_int, [C.c_void_p, C.c_int, ITER_CB, C.c_void_p]),
     "cptc_get_stats": (C.c_int, [C.c_void_p, C.POINTER(Stats)]),
+    "cptc_fit_terms": (C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
+    "cptc_get_relabel": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_uint32)]),
+    "cptc_residual": (C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
 }
 
 _host = None

@@ -1,0 +1,250 @@
+// cptc_opt — command-line driver with the reference's surface
+// (src/main.cu:22-680):
+//
+//   cptc_opt <tns> [iters=20] [R=32] [threshold=0.03]
+//
+// Order-3 tensors run the hybrid pipeline (CADR, dense 16^3 tiles in TF32 +
+// FP64 residual, or FP64 only, chosen by the fill-rate selector); any other
+// order, or ALS_GENERIC_FORCE=1, runs the N-order path.  Switches honoured:
+//   ALS_FORCE_WMMA, ALS_FORCE_CUDA, ALS_FILL_MIN, ALS_GENERIC_FORCE,
+//   ALS_EXPORT_FACTORS, ALS_PROFILE,
+//   GEN_DENSE, GEN_DENSE_THRESHOLD, GEN_DENSE_INNER, GEN_REORDER,
+//   GEN_REORDER_T, GEN_REORDER_SAMPLE, GEN_SOLVER, GEN_SEED, GEN_DUMP,
+//   GEN_PROFILE, CPTC_DEVICE.
+// Output lines keep the reference's formats ("[ALS] iter i/N time=<ms> ms
+// fit=<f>", "[GEN] iter ... fit=", "[ALS] Lambda:", export files).
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "cptc.h"
+
+namespace {
+
+const char* env(const char* k) { return std::getenv(k); }
+
+struct IterLog {
+  bool generic = false;
+  int iters = 0;
+  bool profile = false;
+  cptc_ctx* ctx = nullptr;
+};
+
+void on_iter(int it, double ms, double fit, const double* mode_ms, int nm, void* user) {
+  IterLog* L = (IterLog*)user;
+  if (!L->generic) {
+    std::printf("[ALS] iter %d/%d time=%g ms fit=%g\n", it, L->iters, ms, fit);
+    if (L->profile) {
+      std::printf("[ALS][profile] iter %d mttkrp=", it);
+      for (int m = 0; m < nm; ++m) std::printf("%s%g", m ? "/" : "", mode_ms[m]);
+      std::printf(" ms (iter=%g)\n", ms);
+    }
+  } else {
+    double t[3] = {0, 0, 0};
+    cptc_fit_terms(L->ctx, t);
+    std::printf("[GEN] iter %d/%d time=%g ms iprod=%g model2=%g fit=%g\n", it, L->iters, ms,
+                t[0], t[1], fit);
+    if (L->profile) {
+      std::printf("[GEN][profile] iter %d mttkrp=", it);
+      for (int m = 0; m < nm; ++m) std::printf("%s%g", m ? "/" : "", mode_ms[m]);
+      std::printf(" ms\n");
+    }
+  }
+  std::fflush(stdout);
+}
+
+int fail(cptc_ctx* c, const char* what, int rc) {
+  std::fprintf(stderr, "[cptc] %s failed (%d): %s\n", what, rc, c ? cptc_last_error(c) : "");
+  return 1;
+}
+
+int reorder_of(const char* s) {
+  if (!s) return CPTC_REORDER_DEFAULT;
+  if (!std::strcmp(s, "none")) return CPTC_REORDER_NONE;
+  if (!std::strcmp(s, "cadr")) return CPTC_REORDER_CADR;
+  if (!std::strcmp(s, "hits")) return CPTC_REORDER_HITS;
+  if (!std::strcmp(s, "auto")) return CPTC_REORDER_AUTO;
+  std::fprintf(stderr, "[GEN] unknown GEN_REORDER=%s -> falling back to cadr\n", s);
+  return CPTC_REORDER_CADR;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  std::string filename = "nell-2.tns";
+  int iters = 20, R = 32;
+  double threshold = 0.03;
+  if (argc > 1) filename = argv[1];
+  if (argc > 2) iters = std::atoi(argv[2]);
+  if (argc > 3) R = std::atoi(argv[3]);
+  if (argc > 4) threshold = std::atof(argv[4]);
+  if (iters <= 0) iters = 1;
+  if (R <= 0) R = 1;
+
+  const int order = cptc_tns_probe_order(filename.c_str());
+  if (order < 0) {
+    std::fprintf(stderr, "[Main] cannot determine tensor order of: %s\n", filename.c_str());
+    return 1;
+  }
+  const bool generic = (order != 3) || env("ALS_GENERIC_FORCE");
+
+  const auto t0 = std::chrono::steady_clock::now();
+  cptc_coo t{};
+  if (cptc_tns_read(filename.c_str(), order, &t) != 0) {
+    std::fprintf(stderr, "[Error] Cannot open file: %s\n", filename.c_str());
+    return 1;
+  }
+  const double load_ms =
+      std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  if (generic) {
+    std::printf("[Main] order-%d tensor -> generic N-order CP-ALS\n", order);
+    std::printf("[Main] Load time = %g ms | dims = ", load_ms);
+    for (int m = 0; m < order; ++m) std::printf("%s%llu", m ? " x " : "", (unsigned long long)t.dims[m]);
+    std::printf(" | NNZ = %llu\n", (unsigned long long)t.nnz);
+  } else {
+    std::printf("[Main] Load time = %g ms\n", load_ms);
+    std::printf("[Main] Tensor Dimensions: %llu x %llu x %llu | NNZ: %llu\n",
+                (unsigned long long)t.dims[0], (unsigned long long)t.dims[1],
+                (unsigned long long)t.dims[2], (unsigned long long)t.nnz);
+  }
+
+  cptc_opts o;
+  cptc_opts_default(&o);
+  o.generic = generic ? 1 : 0;
+  if (env("ALS_FORCE_WMMA")) o.path = CPTC_PATH_TF32;
+  else if (env("ALS_FORCE_CUDA")) o.path = CPTC_PATH_FP64;
+  if (env("ALS_FILL_MIN")) o.fill_min = std::atof(env("ALS_FILL_MIN"));
+  if (generic) {
+    o.reorder = reorder_of(env("GEN_REORDER"));
+    if (env("GEN_REORDER_T")) o.reorder_rounds = std::max(1, std::atoi(env("GEN_REORDER_T")));
+    if (env("GEN_REORDER_SAMPLE"))
+      o.reorder_sample = std::strtoull(env("GEN_REORDER_SAMPLE"), nullptr, 10);
+    if (env("GEN_SOLVER") && !std::strcmp(env("GEN_SOLVER"), "svd")) o.solver = CPTC_SOLVER_PINV;
+    if (env("GEN_SEED")) o.seed = (uint32_t)std::atoi(env("GEN_SEED"));
+    if (env("GEN_DENSE")) o.dense_generic = std::atoi(env("GEN_DENSE")) != 0;
+    if (env("GEN_DENSE_THRESHOLD")) o.dense_thr_generic = std::atof(env("GEN_DENSE_THRESHOLD"));
+    if (const char* s = env("GEN_DENSE_INNER")) {
+      int k = 0;
+      const char* q = s;
+      while (*q && k < 3) {
+        o.dense_inner[k++] = std::atoi(q);
+        while (*q && *q != ',') ++q;
+        if (*q == ',') ++q;
+      }
+    }
+  }
+
+  int dev = env("CPTC_DEVICE") ? std::atoi(env("CPTC_DEVICE")) : 0;
+  cptc_ctx* c = nullptr;
+  int rc = cptc_create(&c, dev, 0);
+  if (rc) return fail(c, "cptc_create", rc);
+  if ((rc = cptc_load_coo(c, &t))) return fail(c, "load", rc);
+  if ((rc = cptc_build(c, R, threshold, &o))) return fail(c, "build", rc);
+  cptc_stats st;
+  cptc_get_stats(c, &st);
+  std::printf("[Main] build (reorder + partition + views) = %g ms\n", st.build_ms);
+  if (!generic) {
+    std::printf("[Main] density check: dense_nnz=%llu sparse_nnz=%llu tiles=%llu avg_fill=%g "
+                "(threshold %g) -> %s\n",
+                (unsigned long long)st.dense_nnz, (unsigned long long)st.sparse_nnz,
+                (unsigned long long)st.dense_tiles, st.avg_fill, st.fill_min,
+                st.tf32_path ? "TF32 dense tiles + FP64 residual" : "FP64 only");
+    std::printf("[ALS] Starting CP-ALS: rank=%d, max_iters=%d\n", R, iters);
+  } else {
+    std::printf("[GEN] N-order CP-ALS: order=%d R=%d iters=%d nnz=%llu\n", order, R, iters,
+                (unsigned long long)t.nnz);
+    if (st.tf32_path)
+      std::printf("[GEN] dense: units=%llu dense_nnz=%llu cutoff=%d\n",
+                  (unsigned long long)st.dense_tiles, (unsigned long long)st.dense_nnz,
+                  st.cutoff);
+  }
+  if ((rc = cptc_init_factors(c))) return fail(c, "init_factors", rc);
+  IterLog L;
+  L.generic = generic;
+  L.iters = iters;
+  L.ctx = c;
+  L.profile = env(generic ? "GEN_PROFILE" : "ALS_PROFILE") != nullptr;
+  const auto ta = std::chrono::steady_clock::now();
+  if ((rc = cptc_als(c, iters, on_iter, &L))) return fail(c, "als", rc);
+  const double als_ms =
+      std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - ta).count();
+
+  std::vector<double> lam(R);
+  cptc_get_lambda(c, lam.data());
+  double res[2] = {0, 0};
+  cptc_residual(c, res);
+  const double xn = std::sqrt(res[1]);
+  const double rmse = t.nnz ? std::sqrt(std::max(res[0], 0.0) / (double)t.nnz) : 0.0;
+  if (!generic) {
+    std::printf("[ALS] Final RMSE=%g\n", rmse);
+    std::printf("[ALS] Lambda:");
+    for (int r = 0; r < R; ++r) std::printf(" %g", lam[r]);
+    std::printf("\n[ALS] Total time=%g ms\n", als_ms);
+  } else {
+    const double rn = std::sqrt(std::max(res[0], 0.0));
+    std::printf("[GEN] ALS total = %g ms\n", als_ms);
+    std::printf("[GEN] exact: ||X-Xhat||_F=%g RMSE=%g fit=%g (||X||_F=%g)\n", rn, rmse,
+                xn > 0 ? 1.0 - rn / xn : 0.0, xn);
+    std::printf("[GEN] lambda = ");
+    for (int r = 0; r < R; ++r) std::printf("%s%g", r ? " " : "", lam[r]);
+    std::printf("\n");
+  }
+
+  if (const char* exp = env("ALS_EXPORT_FACTORS"); exp && !generic) {
+    // src/main.cu:595-621: <p>.{0,1,2}.out (row-major, %.20lf) and <p>.lambda.out
+    for (int n = 0; n < 3; ++n) {
+      std::vector<double> f(t.dims[n] * (size_t)R);
+      cptc_get_factors(c, n, f.data());
+      std::string path = std::string(exp) + "." + std::to_string(n) + ".out";
+      FILE* fp = std::fopen(path.c_str(), "w");
+      if (!fp) continue;
+      std::fprintf(fp, "matrix\n2\n%llu %d\n", (unsigned long long)t.dims[n], R);
+      for (double v : f) std::fprintf(fp, "%.20lf\n", v);
+      std::fclose(fp);
+    }
+    FILE* lf = std::fopen((std::string(exp) + ".lambda.out").c_str(), "w");
+    if (lf) {
+      std::fprintf(lf, "vector\n1\n%d\n", R);
+      for (double v : lam) std::fprintf(lf, "%.20lf\n", v);
+      std::fclose(lf);
+    }
+    std::printf("[Main] factors exported to %s\n", exp);
+  }
+  if (const char* dump = env("GEN_DUMP"); dump && generic) {
+    // src/generic.cu:2253-2287: factors in the relabelled row order, 17 digits
+    std::string path = std::string(dump) + ".factors.txt";
+    FILE* fo = std::fopen(path.c_str(), "w");
+    if (fo) {
+      std::fprintf(fo, "# cpTC factor dump (factors are column-normalised; lambda holds the norms)\n");
+      std::fprintf(fo, "order %d\nrank %d\ndims", order, R);
+      for (int m = 0; m < order; ++m) std::fprintf(fo, " %llu", (unsigned long long)t.dims[m]);
+      std::fprintf(fo, "\n");
+      for (int m = 0; m < order; ++m) {
+        const size_t d = t.dims[m];
+        std::vector<double> f(d * R), g(d * R);
+        std::vector<uint32_t> perm(d);
+        cptc_get_factors(c, m, f.data());
+        cptc_get_relabel(c, m, perm.data());
+        for (size_t a = 0; a < d; ++a)
+          std::memcpy(g.data() + (size_t)perm[a] * R, f.data() + a * R, R * sizeof(double));
+        std::fprintf(fo, "mode %d %zu %d\n", m, d, R);
+        for (size_t i = 0; i < d; ++i) {
+          for (int r = 0; r < R; ++r) std::fprintf(fo, "%s%.17g", r ? " " : "", g[i * R + r]);
+          std::fprintf(fo, "\n");
+        }
+      }
+      std::fprintf(fo, "lambda %d\n", R);
+      for (int r = 0; r < R; ++r) std::fprintf(fo, "%s%.17g", r ? " " : "", lam[r]);
+      std::fprintf(fo, "\n");
+      std::fclose(fo);
+      std::printf("[GEN] factors dumped to %s\n", path.c_str());
+    }
+  }
+  cptc_destroy(c);
+  cptc_coo_free(&t);
+  return 0;
+}

@@ -109,21 +109,24 @@ __device__ __forceinline__ double warp_sum(double v) {
 // ---------------------------------------------------------------------------
 // Truncated pseudo-inverse of a symmetric positive semi-definite A (R <= 128)
 // by one-sided Jacobi (Hestenes 1958): W = A is rotated in column pairs
-// until its columns are mutually orthogonal, W = A V = U Sigma.  For PSD A,
-// U = V, so pinv(A) = sum_k s_k u_k u_k^T / sigma_k, s_k = sign(u_k^T A u_k)
-// (guards tiny negative eigenvalues from rounding).  sigma_k <= R*ulp(sigma
-// max) is dropped, the truncation rule of the reference (src/solver.cu:
-// 952-954).  Pairs follow a round-robin schedule: R/2 disjoint rotations per
-// step, one warp per pair, R-1 steps per sweep.  Only W lives in shared
-// memory (R*R doubles), so R = 128 fits one CTA.
+// until its columns are mutually orthogonal, W = A V = U Sigma.  A is PSD
+// (a Hadamard product of Gram matrices, Schur product theorem), so U = V and
+// pinv(A) = sum_k u_k u_k^T / sigma_k = sum_k w_k w_k^T / sigma_k^3.
+// sigma_k <= R*ulp(sigma_max) is dropped, the truncation rule of the
+// reference (src/solver.cu:952-954).  Convergence test and sweep cap follow
+// the reference's gesvdj settings (tolerance 1e-14, 15 sweeps,
+// src/solver.cu:837-838).  Pairs follow a round-robin schedule: R/2
+// disjoint rotations per step, one warp per pair, R-1 steps per sweep.  Only
+// W lives in shared memory (R*R doubles), so R = 128 fits one CTA.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) k_pinv_jacobi(const double* __restrict__ A, int R,
                                                       double* __restrict__ Ainv,
-                                                      int* __restrict__ status) {
+                                                      int* __restrict__ status,
+                                                      const int* __restrict__ gate) {
+  if (gate != nullptr && *gate == 0) return;  // the Cholesky inverse was accepted
   extern __shared__ double smem[];
   double* W = smem;                        // column-major, W[c*R + r]
-  double* sig = smem + R * R;              // R
-  double* sgn = sig + R;                   // R
+  double* wgt = smem + R * R;              // R
   __shared__ int rotated;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   for (int k = tid; k < R * R; k += blockDim.x) {
@@ -131,7 +134,7 @@ __global__ void __launch_bounds__(1024) k_pinv_jacobi(const double* __restrict__
     W[k] = A[r * R + c];
   }
   const int n = (R + 1) & ~1;  // players, with a dummy when R is odd
-  for (int sweep = 0; sweep < 40; ++sweep) {
+  for (int sweep = 0; sweep < 15; ++sweep) {
     if (tid == 0) rotated = 0;
     __syncthreads();
     for (int step = 0; step < n - 1; ++step) {
@@ -151,7 +154,7 @@ __global__ void __launch_bounds__(1024) k_pinv_jacobi(const double* __restrict__
         al = warp_sum(al);
         be = warp_sum(be);
         ga = warp_sum(ga);
-        if (fabs(ga) > 1e-15 * sqrt(al * be) && ga != 0.0) {
+        if (fabs(ga) > 1e-14 * sqrt(al * be) && ga != 0.0) {
           const double zeta = (be - al) / (2.0 * ga);
           const double t = (zeta >= 0.0 ? 1.0 : -1.0) / (fabs(zeta) + sqrt(1.0 + zeta * zeta));
           const double c = 1.0 / sqrt(1.0 + t * t), s = c * t;
@@ -168,61 +171,60 @@ __global__ void __launch_bounds__(1024) k_pinv_jacobi(const double* __restrict__
     if (!rotated) break;
     __syncthreads();
   }
-  // sigma_k = ||w_k||, sign from the Rayleigh quotient w_k^T A w_k.
   for (int k = warp; k < R; k += nwarps) {
-    double s2 = 0.0, rq = 0.0;
-    for (int i = lane; i < R; i += 32) {
-      const double wi = W[k * R + i];
-      s2 = fma(wi, wi, s2);
-      double aw = 0.0;
-      for (int j = 0; j < R; ++j) aw = fma(A[i * R + j], W[k * R + j], aw);
-      rq = fma(wi, aw, rq);
-    }
+    double s2 = 0.0;
+    for (int i = lane; i < R; i += 32) s2 = fma(W[k * R + i], W[k * R + i], s2);
     s2 = warp_sum(s2);
-    rq = warp_sum(rq);
-    if (lane == 0) {
-      sig[k] = sqrt(s2);
-      sgn[k] = rq < 0.0 ? -1.0 : 1.0;
-    }
+    if (lane == 0) wgt[k] = sqrt(s2);
   }
   __syncthreads();
   double smax = 0.0;
-  for (int k = 0; k < R; ++k) smax = fmax(smax, sig[k]);
+  for (int k = 0; k < R; ++k) smax = fmax(smax, wgt[k]);
   const double tol = (double)R * (nextafter(smax, smax + 1.0) - smax);
+  __syncthreads();
   for (int k = tid; k < R; k += blockDim.x) {
-    const double sk = sig[k];
-    // weight of u_k u_k^T = w_k w_k^T / sigma^2 in pinv: sign / sigma.
-    sgn[k] = (sk > tol && isfinite(sk)) ? sgn[k] / (sk * sk * sk) : 0.0;
+    const double sk = wgt[k];
+    wgt[k] = (sk > tol && isfinite(sk)) ? 1.0 / (sk * sk * sk) : 0.0;
   }
   __syncthreads();
   for (int o = tid; o < R * R; o += blockDim.x) {
     const int a = o / R, b = o % R;
     double s = 0.0;
-    for (int k = 0; k < R; ++k) s = fma(W[k * R + a] * sgn[k], W[k * R + b], s);
+    for (int k = 0; k < R; ++k) s = fma(W[k * R + a] * wgt[k], W[k * R + b], s);
     Ainv[o] = s;
     if (!isfinite(s)) atomicExch(status, 1);
   }
 }
 
 // ---------------------------------------------------------------------------
-// Inverse of A + eps*I by Cholesky, eps = 1e-12 * tr(A)/R + 1e-300 with the
-// reference's pivot rule (src/generic.cu:757-783): pivot s <= 0 -> sqrt(eps).
-// Right-looking factorisation in shared memory, then L^-1 column by column
-// and Ainv = L^-T L^-1.  Linv goes through `Ainv` as scratch row-major.
+// Inverse by Cholesky, right-looking in shared memory, then L^-1 column by
+// column (one thread per column) and Ainv = L^-T L^-1.
+//  ridge = 1: the reference's N-order rule (src/generic.cu:757-783): factor
+//    A + eps*I with eps = 1e-12 * tr(A)/R + 1e-300, pivot s <= 0 -> sqrt(eps).
+//  ridge = 0: plain Cholesky of A; if a pivot falls to <= 1e-11 * max diag
+//    (condition number beyond ~1e11) the factorisation is rejected, *fail is
+//    set and Ainv is left for the pseudo-inverse kernel that follows.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) k_chol_inverse(const double* __restrict__ A, int R,
-                                                       double* __restrict__ Ainv,
+                                                       int ridge, double* __restrict__ Ainv,
                                                        double* __restrict__ Linv,
-                                                       int* __restrict__ status) {
+                                                       int* __restrict__ status,
+                                                       int* __restrict__ fail) {
   extern __shared__ double L[];  // R*R row-major lower
-  __shared__ double eps_s;
+  __shared__ double eps_s, dmax_s;
+  __shared__ int bad;
   const int tid = threadIdx.x;
   for (int k = tid; k < R * R; k += blockDim.x) L[k] = A[k];
   __syncthreads();
   if (tid == 0) {
-    double tr = 0.0;
-    for (int i = 0; i < R; ++i) tr += L[i * R + i];
-    eps_s = 1e-12 * ((tr > 0.0) ? tr / (double)R : 1.0) + 1e-300;
+    double tr = 0.0, dm = 0.0;
+    for (int i = 0; i < R; ++i) {
+      tr += L[i * R + i];
+      dm = fmax(dm, L[i * R + i]);
+    }
+    eps_s = ridge ? 1e-12 * ((tr > 0.0) ? tr / (double)R : 1.0) + 1e-300 : 0.0;
+    dmax_s = dm;
+    bad = 0;
   }
   __syncthreads();
   const double eps = eps_s;
@@ -231,9 +233,17 @@ __global__ void __launch_bounds__(1024) k_chol_inverse(const double* __restrict_
   for (int j = 0; j < R; ++j) {
     if (tid == 0) {
       const double s = L[j * R + j];
-      L[j * R + j] = (s > 0.0) ? sqrt(s) : sqrt(eps);
+      if (ridge) {
+        L[j * R + j] = (s > 0.0) ? sqrt(s) : sqrt(eps);
+      } else if (!(s > 1e-11 * dmax_s)) {
+        bad = 1;
+        L[j * R + j] = 1.0;
+      } else {
+        L[j * R + j] = sqrt(s);
+      }
     }
     __syncthreads();
+    if (bad) break;
     const double d = L[j * R + j];
     for (int i = j + 1 + tid; i < R; i += blockDim.x) L[i * R + j] /= d;
     __syncthreads();
@@ -244,7 +254,11 @@ __global__ void __launch_bounds__(1024) k_chol_inverse(const double* __restrict_
     }
     __syncthreads();
   }
-  // Linv (lower): column c by forward substitution, one thread per column.
+  if (bad) {
+    if (tid == 0 && fail) *fail = 1;
+    return;
+  }
+  if (tid == 0 && fail) *fail = 0;
   for (int c = tid; c < R; c += blockDim.x) {
     for (int i = 0; i < R; ++i) {
       double s = (i == c) ? 1.0 : 0.0;
@@ -431,6 +445,29 @@ __global__ void k_sumsq_partial(const double* __restrict__ v, uint64_t n, double
   if (threadIdx.x == 0) part[blockIdx.x] = sh[0];
 }
 
+__global__ void k_residual_partial(ResidualArgs a, double* __restrict__ part) {
+  __shared__ double sh[256];
+  double s = 0.0;
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < a.nnz;
+       e += (uint64_t)gridDim.x * blockDim.x) {
+    double xhat = 0.0;
+    for (int r = 0; r < a.R; ++r) {
+      double p = a.lambda[r];
+      for (int m = 0; m < a.N; ++m) p *= a.F[m][(uint64_t)a.idx[m][e] * a.R + r];
+      xhat += p;
+    }
+    const double d = a.val[e] - xhat;
+    s = fma(d, d, s);
+  }
+  sh[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part[blockIdx.x] = sh[0];
+}
+
 __global__ void k_sum_serial(const double* __restrict__ part, int n, double* __restrict__ out) {
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     double s = 0.0;
@@ -473,26 +510,30 @@ void launch_hadamard(const double* const* Gs, int ng, int R, double* FtF, cudaSt
   CPTC_LAUNCH_CHECK();
 }
 
-void launch_sym_inverse(const double* A, int R, int pinv, double* Ainv, int* status,
+void launch_sym_inverse(const double* A, int R, int mode, double* Ainv, int* status,
                         cudaStream_t s) {
   CPTC_REQUIRE(R >= 1 && R <= 128, CPTC_E_UNSUP, "rank must be in [1, 128]");
-  if (pinv) {
-    const int n = (R + 1) & ~1;
-    int threads = 32 * (n / 2);
-    if (threads > 1024) threads = 1024;
-    if (threads < 64) threads = 64;
-    const size_t smem = ((size_t)R * R + 2 * R) * sizeof(double);
-    CPTC_CUDA(cudaFuncSetAttribute(k_pinv_jacobi, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)smem));
-    k_pinv_jacobi<<<1, threads, smem, s>>>(A, R, Ainv, status);
-  } else {
-    const size_t smem = (size_t)R * R * sizeof(double);
+  // Ainv holds 2*R*R doubles (+1 int flag after them): the second half is
+  // the L^-1 scratch of the Cholesky kernel.
+  double* Linv = Ainv + (size_t)R * R;
+  int* gate = reinterpret_cast<int*>(Ainv + 2 * (size_t)R * R);
+  const size_t csm = (size_t)R * R * sizeof(double);
+  if (mode != kInvPinv) {
     CPTC_CUDA(cudaFuncSetAttribute(k_chol_inverse, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)smem));
-    // Linv scratch: the upper half of Ainv's storage is not enough, so the
-    // caller's Ainv buffer holds 2*R*R doubles.
-    k_chol_inverse<<<1, 512, smem, s>>>(A, R, Ainv, Ainv + (size_t)R * R, status);
+                                   (int)csm));
+    k_chol_inverse<<<1, 512, csm, s>>>(A, R, mode == kInvCholRidge ? 1 : 0, Ainv, Linv, status,
+                                       mode == kInvAuto ? gate : nullptr);
+    CPTC_LAUNCH_CHECK();
+    if (mode == kInvCholRidge) return;
   }
+  const int n = (R + 1) & ~1;
+  int threads = 32 * (n / 2);
+  if (threads > 1024) threads = 1024;
+  if (threads < 64) threads = 64;
+  const size_t smem = ((size_t)R * R + R) * sizeof(double);
+  CPTC_CUDA(cudaFuncSetAttribute(k_pinv_jacobi, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+  k_pinv_jacobi<<<1, threads, smem, s>>>(A, R, Ainv, status, mode == kInvAuto ? gate : nullptr);
   CPTC_LAUNCH_CHECK();
 }
 
@@ -551,6 +592,15 @@ void launch_fit_final(const double* dot_part, int nblk, const double* lambda,
   GPtrs g{};
   for (int k = 0; k < ng; ++k) g.p[k] = Gs[k];
   k_fit_final<<<1, 1024, 0, s>>>(dot_part, nblk, lambda, g, ng, R, out);
+  CPTC_LAUNCH_CHECK();
+}
+
+void launch_residual(const ResidualArgs& a, double* part, int max_blocks, double* out,
+                     cudaStream_t s) {
+  const int nblk = (int)grid_for(a.nnz, 256, (unsigned)max_blocks);
+  k_residual_partial<<<nblk, 256, 0, s>>>(a, part);
+  CPTC_LAUNCH_CHECK();
+  k_sum_serial<<<1, 32, 0, s>>>(part, nblk, out);
   CPTC_LAUNCH_CHECK();
 }
 

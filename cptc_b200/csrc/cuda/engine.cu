@@ -147,7 +147,7 @@ void Engine::alloc_workspace() {
   for (int m = 0; m < N; ++m) maxd = std::max<uint64_t>(maxd, dims[m]);
   FtV.alloc(maxd * (uint64_t)R);
   FtF.alloc((uint64_t)R * R);
-  Ainv.alloc(2 * (uint64_t)R * R);
+  Ainv.alloc(2 * (uint64_t)R * R + 1);
   gpart_blocks = 148;
   gpart.alloc((uint64_t)gpart_blocks * R * R);
   dots.alloc((uint64_t)gpart_blocks * R);
@@ -403,10 +403,14 @@ void Engine::update_mode(int n) {
   cudaEventRecord(ev[2 * n], stream);
   mttkrp(n);
   cudaEventRecord(ev[2 * n + 1], stream);
-  int pinv = generic ? 0 : 1;
-  if (opts.solver == CPTC_SOLVER_CHOL) pinv = 0;
-  if (opts.solver == CPTC_SOLVER_PINV) pinv = 1;
-  launch_sym_inverse(FtF.p, R, pinv, Ainv.p, status.p, stream);
+  // Order 3: the reference solves with a truncated SVD pseudo-inverse; by
+  // default the same result is obtained by Cholesky when FtF is well
+  // conditioned (the pseudo-inverse kernel runs only when it is not).
+  // N-order: the reference's ridge Cholesky.
+  int inv = generic ? kInvCholRidge : kInvAuto;
+  if (opts.solver == CPTC_SOLVER_CHOL) inv = kInvCholRidge;
+  if (opts.solver == CPTC_SOLVER_PINV) inv = kInvPinv;
+  launch_sym_inverse(FtF.p, R, inv, Ainv.p, status.p, stream);
   comm_reduce_ftv(*this, n);
   const uint64_t lo = row_lo(n), rows = row_hi(n) - lo;
   const int nb = launch_apply_solve(FtV.p + lo * R, Ainv.p, lambda.p, generic ? 0 : 1, rows, R,
@@ -642,6 +646,47 @@ int cptc_profile_mttkrp(cptc_ctx* c, int mode, int reps, double* ms3) {
 }
 
 unsigned long long cptc_launch_count(void) { return cptc::g_launches; }
+
+int cptc_get_relabel(cptc_ctx* c, int mode, uint32_t* perm_out) {
+  return guarded(c, [&](Engine& e) {
+    CPTC_REQUIRE(e.built && mode >= 0 && mode < e.N && perm_out, CPTC_E_ARG, "call order");
+    if (e.perm[mode].empty())
+      for (uint64_t a = 0; a < e.dims[mode]; ++a) perm_out[a] = (uint32_t)a;
+    else
+      std::memcpy(perm_out, e.perm[mode].data(), e.dims[mode] * sizeof(uint32_t));
+  });
+}
+
+int cptc_fit_terms(cptc_ctx* c, double* out3) {
+  return guarded(c, [&](Engine& e) {
+    CPTC_REQUIRE(out3 != nullptr, CPTC_E_ARG, "null output");
+    out3[0] = e.last_iprod;
+    out3[1] = e.last_model2;
+    out3[2] = e.last_fit;
+  });
+}
+
+int cptc_residual(cptc_ctx* c, double* out2) {
+  return guarded(c, [&](Engine& e) {
+    CPTC_REQUIRE(e.built && e.have_factors && out2, CPTC_E_ARG, "call order");
+    CPTC_CUDA(cudaSetDevice(e.device));
+    cptc::ResidualArgs a{};
+    for (int m = 0; m < e.N; ++m) {
+      a.idx[m] = e.idx[m].p;
+      a.F[m] = e.F[m].p;
+    }
+    a.val = e.vals.p;
+    a.lambda = e.lambda.p;
+    a.nnz = e.nnz;
+    a.N = e.N;
+    a.R = e.R;
+    cptc::DArray<double> part(148 * 8);
+    cptc::launch_residual(a, part.p, 148 * 8, e.scal.p + 4, e.stream);
+    CPTC_CUDA(cudaMemcpyAsync(out2, e.scal.p + 4, sizeof(double), cudaMemcpyDeviceToHost, e.stream));
+    CPTC_CUDA(cudaStreamSynchronize(e.stream));
+    out2[1] = e.x_norm_sq;
+  });
+}
 
 int cptc_als(cptc_ctx* c, int iters, cptc_iter_cb cb, void* user) {
   return guarded(c, [&](Engine& e) { e.als(iters, cb, user); });

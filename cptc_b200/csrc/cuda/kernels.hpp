@@ -66,10 +66,13 @@ void launch_partial_sum(const double* part, int nblk, int len, double* out, cuda
 void launch_gram_reduce(const double* part, int nblk, int R, double* G, cudaStream_t s);
 // FtF = prod_{m in list} G_m (elementwise).
 void launch_hadamard(const double* const* Gs, int ng, int R, double* FtF, cudaStream_t s);
-// Ainv = truncated pseudo-inverse (pinv=1, tol R*ulp(smax)) or ridge-
-// Cholesky inverse (pinv=0) of the SPD R x R matrix A; status[0] != 0 on
-// failure.
-void launch_sym_inverse(const double* A, int R, int pinv, double* Ainv, int* status,
+// Ainv = inverse of the symmetric PSD R x R matrix A; status[0] != 0 on
+// non-finite results.  Ainv must hold 2*R*R + 1 doubles (scratch).
+//   kInvPinv:      truncated pseudo-inverse (Jacobi, tol R*ulp(smax))
+//   kInvCholRidge: ridge Cholesky of the N-order reference path
+//   kInvAuto:      Cholesky when well conditioned, else the pseudo-inverse
+enum { kInvPinv = 0, kInvCholRidge = 1, kInvAuto = 2 };
+void launch_sym_inverse(const double* A, int R, int mode, double* Ainv, int* status,
                         cudaStream_t s);
 // F[i,:] = (FtV[i,:] * Ainv) ./ (divide_lambda ? lambda : 1) for rows
 // [0, rows); partial Grams of the written rows into part; returns nblk.
@@ -91,6 +94,17 @@ int launch_col_dots(const double* F, const double* FtV, uint64_t rows, int R, do
 // out[0] = iprod = sum_r lambda_r dot_r, out[1] = model^2.
 void launch_fit_final(const double* dot_part, int nblk, const double* lambda,
                       const double* const* Gs, int ng, int R, double* out, cudaStream_t s);
+// part[b] = partial sums of (v - sum_r lambda_r prod_m F_m[i_m, r])^2.
+struct ResidualArgs {
+  const uint32_t* idx[CPTC_MAX_ORDER];
+  const double* val;
+  const double* F[CPTC_MAX_ORDER];
+  const double* lambda;
+  uint64_t nnz;
+  int N, R;
+};
+void launch_residual(const ResidualArgs& a, double* part, int max_blocks, double* out,
+                     cudaStream_t s);
 // out[0] = sum v^2 (two-stage, deterministic).
 void launch_sumsq(const double* v, uint64_t n, double* part, int max_blocks, double* out,
                   cudaStream_t s);

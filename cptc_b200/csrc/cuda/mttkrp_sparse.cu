@@ -64,9 +64,15 @@ __device__ __forceinline__ void load_row(const double* __restrict__ F, uint64_t 
   }
 }
 
+// Software pipeline per lane group: element words of batch b+1 are loaded
+// while batch b is processed, and the factor rows of sub-batch k+1 are
+// gathered before sub-batch k is consumed (two register buffers, selected
+// at compile time by the sub-batch parity, so U*GW/U must be even).
 template <int GW, int RPL, bool VEC, int U>
-__global__ void __launch_bounds__(256) k_mttkrp_view(MttkrpArgs a) {
+__global__ void __launch_bounds__(256, 2) k_mttkrp_view(MttkrpArgs a) {
   constexpr int GPW = 32 / GW;
+  constexpr int SUBS = GW / U;
+  static_assert(SUBS % 2 == 0, "an even number of sub-batches per batch");
   const int lane = threadIdx.x & 31;
   const int glane = lane % GW;
   const int gid = lane / GW;
@@ -98,39 +104,58 @@ __global__ void __launch_bounds__(256) k_mttkrp_view(MttkrpArgs a) {
       accr[k] = 0.0;
     }
   };
-
-  for (uint64_t b = p0; b < p1; b += GW) {
+  auto load_batch = [&](uint64_t b, uint32_t& w, uint32_t& o, double& v) {
     const uint64_t p = b + glane;
-    uint32_t w = 0, o0 = 0;
-    double v = 0.0;
+    w = 0u;
+    o = 0u;
+    v = 0.0;
     if (p < p1) {
       w = __ldcs(a.gw + p);
       v = __ldcs(a.val + p);
-      if (a.nout > 0) o0 = __ldcs(a.oidx + p);
+      if (a.nout > 0) o = __ldcs(a.oidx + p);
     }
-    if (p == p0) w = (w & ~kRowFlag) | kFibFlag;  // row state is set; open a fiber
-    const int cnt = (p1 - b < (uint64_t)GW) ? (int)(p1 - b) : GW;
-#pragma unroll 1
-    for (int j0 = 0; j0 < cnt; j0 += U) {
-      uint32_t wj[U], oj[U];
-      double vj[U], g[U][RPL];
+  };
+  auto gather = [&](uint32_t wsrc, int j0, int cnt, double (&g)[U][RPL]) {
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        wj[u] = __shfl_sync(gmask, w, j0 + u, GW);
-        oj[u] = __shfl_sync(gmask, o0, j0 + u, GW);
-        vj[u] = __shfl_sync(gmask, v, j0 + u, GW);
-        if (j0 + u < cnt) {
-          load_row<GW, RPL, VEC>(a.Fg, wj[u] & kIdxMask, R, glane, L, g[u]);
-        } else {
+    for (int u = 0; u < U; ++u) {
+      const uint32_t w = __shfl_sync(gmask, wsrc, j0 + u, GW);
+      if (j0 + u < cnt) {
+        load_row<GW, RPL, VEC>(a.Fg, w & kIdxMask, R, glane, L, g[u]);
+      } else {
 #pragma unroll
-          for (int k = 0; k < RPL; ++k) g[u][k] = 0.0;
-        }
+        for (int k = 0; k < RPL; ++k) g[u][k] = 0.0;
       }
+    }
+  };
+
+  uint32_t cw, co, nw = 0u, no = 0u;
+  double cv, nv = 0.0;
+  load_batch(p0, cw, co, cv);
+  if (glane == 0) cw = (cw & ~kRowFlag) | kFibFlag;  // row state is set; open a fiber
+  if (p0 + GW < p1) load_batch(p0 + GW, nw, no, nv);
+  double gA[U][RPL], gB[U][RPL];
+  gather(cw, 0, (p1 - p0 < (uint64_t)GW) ? (int)(p1 - p0) : GW, gA);
+
+  for (uint64_t b = p0; b < p1; b += GW) {
+    const int cnt = (p1 - b < (uint64_t)GW) ? (int)(p1 - b) : GW;
+    const bool has_next = b + GW < p1;
+    const int cnt_next = has_next ? ((p1 - b - GW < (uint64_t)GW) ? (int)(p1 - b - GW) : GW) : 0;
+#pragma unroll
+    for (int sb = 0; sb < SUBS; ++sb) {
+      const int j0 = sb * U;
+      if (j0 >= cnt) break;
+      double (&cur)[U][RPL] = (sb & 1) ? gB : gA;
+      double (&nxt)[U][RPL] = (sb & 1) ? gA : gB;
+      if (j0 + U < cnt) gather(cw, j0 + U, cnt, nxt);
+      else if (has_next) gather(nw, 0, cnt_next, nxt);
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        if (j0 + u >= cnt) break;
-        const uint32_t ww = wj[u];
+        const int j = j0 + u;
+        if (j >= cnt) break;
+        const uint32_t ww = __shfl_sync(gmask, cw, j, GW);
+        const double vj = __shfl_sync(gmask, cv, j, GW);
         if (ww & kFibFlag) {
+          const uint32_t oj = __shfl_sync(gmask, co, j, GW);
 #pragma unroll
           for (int k = 0; k < RPL; ++k) {
             accr[k] = fma(accf[k], ff[k], accr[k]);
@@ -145,9 +170,9 @@ __global__ void __launch_bounds__(256) k_mttkrp_view(MttkrpArgs a) {
 #pragma unroll
             for (int k = 0; k < RPL; ++k) ff[k] = 1.0;
           } else {
-            load_row<GW, RPL, VEC>(a.Fo[0], oj[u], R, glane, L, ff);
+            load_row<GW, RPL, VEC>(a.Fo[0], oj, R, glane, L, ff);
             for (int q = 1; q < a.nout; ++q) {
-              const uint32_t oq = a.oidx[(uint64_t)q * a.nnz + b + j0 + u];
+              const uint32_t oq = a.oidx[(uint64_t)q * a.nnz + b + j];
               double t[RPL];
               load_row<GW, RPL, VEC>(a.Fo[q], oq, R, glane, L, t);
 #pragma unroll
@@ -156,9 +181,13 @@ __global__ void __launch_bounds__(256) k_mttkrp_view(MttkrpArgs a) {
           }
         }
 #pragma unroll
-        for (int k = 0; k < RPL; ++k) accf[k] = fma(vj[u], g[u][k], accf[k]);
+        for (int k = 0; k < RPL; ++k) accf[k] = fma(vj, cur[u][k], accf[k]);
       }
     }
+    cw = nw;
+    co = no;
+    cv = nv;
+    if (b + 2 * GW < p1) load_batch(b + 2 * GW, nw, no, nv);
   }
 #pragma unroll
   for (int k = 0; k < RPL; ++k) accr[k] = fma(accf[k], ff[k], accr[k]);
@@ -179,16 +208,16 @@ void launch(const MttkrpArgs& a, cudaStream_t s) {
 void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
   if (a.nnz == 0 || a.ntasks == 0) return;
   switch (a.R) {
-    case 8: launch<8, 1, true, 8>(a, s); return;
+    case 8: launch<8, 1, true, 4>(a, s); return;
     case 16: launch<16, 1, true, 8>(a, s); return;
     case 32: launch<32, 1, true, 8>(a, s); return;
-    case 64: launch<32, 2, true, 8>(a, s); return;
-    case 128: launch<32, 4, true, 4>(a, s); return;
+    case 64: launch<32, 2, true, 4>(a, s); return;
+    case 128: launch<32, 4, true, 2>(a, s); return;
     default: break;
   }
   if (a.R <= 32) launch<32, 1, false, 8>(a, s);
-  else if (a.R <= 64) launch<32, 2, false, 8>(a, s);
-  else if (a.R <= 128) launch<32, 4, false, 4>(a, s);
+  else if (a.R <= 64) launch<32, 2, false, 4>(a, s);
+  else if (a.R <= 128) launch<32, 4, false, 2>(a, s);
   else throw CptcError(CPTC_E_UNSUP, "rank > 128 is not supported");
 }
 

@@ -191,6 +191,21 @@ class Engine:
                     "profile_mttkrp")
         return {"tiles_ms": ms[0], "sparse_ms": ms[1], "total_ms": ms[2]}
 
+    def fit_terms(self) -> dict:
+        out = (C.c_double * 3)()
+        self._check(self._lib.cptc_fit_terms(self._h, out), "fit_terms")
+        return {"iprod": out[0], "model2": out[1], "fit": out[2]}
+
+    def residual(self) -> dict:
+        """Exact sum of squared errors over the stored nonzeros, ||X||^2,
+        RMSE and exact fit with the current factors and lambda."""
+        out = (C.c_double * 2)()
+        self._check(self._lib.cptc_residual(self._h, out), "residual")
+        res2, x2 = out[0], out[1]
+        n = self._tensor.nnz
+        return {"res_sq": res2, "x_sq": x2, "rmse": (res2 / n) ** 0.5 if n else 0.0,
+                "fit": 1.0 - (max(res2, 0.0) ** 0.5) / (x2 ** 0.5) if x2 > 0 else 0.0}
+
     def als(self, iters: int, callback=None) -> list:
         reports = []
 

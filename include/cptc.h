@@ -154,6 +154,20 @@ int cptc_als(cptc_ctx* ctx, int iters, cptc_iter_cb cb, void* user);
 
 int cptc_get_stats(cptc_ctx* ctx, cptc_stats* out);
 
+/* The build's index relabelling of `mode`: perm_out[old] = new
+ * (dims[mode] entries; the identity when no relabelling ran). */
+int cptc_get_relabel(cptc_ctx* ctx, int mode, uint32_t* perm_out);
+
+/* Terms of the last iteration's Gram fit: out3 = {iprod, model^2, fit}
+ * (src/als.cu:668-715, src/generic.cu:2174-2214). */
+int cptc_fit_terms(cptc_ctx* ctx, double out3[3]);
+
+/* Exact residual over the stored nonzeros with the current factors and
+ * lambda: out2 = {sum (v - xhat)^2, sum v^2}.  Replaces
+ * compute_residual_and_norm_sq (src/common.cu:517-650) and
+ * g_exact_residual_kernel (src/generic.cu:936-967). */
+int cptc_residual(cptc_ctx* ctx, double out2[2]);
+
 #ifdef __cplusplus
 }
 #endif

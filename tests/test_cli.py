@@ -1,0 +1,72 @@
+"""The drop-in command-line driver (cptc_opt): reference argv, switches and
+output lines, checked against the reference's own printed fits."""
+import json
+import os
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import cptc_b200 as cp
+
+ROOT = Path(__file__).resolve().parent.parent
+CLI = ROOT / "cptc_b200" / "_lib" / "cptc_opt"
+GOLD = ROOT / "tests" / "golden"
+
+
+def golden_tensor(g, path):
+    t = cp.gen_config(g["cfg"], g["scale"])
+    t = cp.CooTensor(tuple(int(i.max()) + 1 for i in t.idx), t.idx, t.vals)
+    cp.write_tns(path, t)
+    return t
+
+
+def run(args, env_extra):
+    env = dict(os.environ, **env_extra)
+    r = subprocess.run([str(CLI)] + [str(a) for a in args], env=env, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stderr
+    return r.stdout
+
+
+def fits_of(out, tag):
+    return np.array([float(m.group(1)) for m in
+                     re.finditer(rf"\[{tag}\] iter \d+/\d+ time=[\d.eE+-]+ ms.*fit=([-\d.eE+]+)",
+                                 out)])
+
+
+def test_cli_binary_built():
+    assert CLI.exists()
+
+
+@pytest.mark.gpu
+def test_cli_order3_tf32_matches_reference(gpu, tmp_path):
+    g = json.loads((GOLD / "cfg1_R32_auto.json").read_text())
+    tns = tmp_path / "t.tns"
+    t = golden_tensor(g, tns)
+    exp = tmp_path / "exp"
+    out = run([tns, g["iters"], g["R"], g["threshold"]],
+              {"ALS_FORCE_WMMA": "1", "ALS_EXPORT_FACTORS": str(exp)})
+    fits = fits_of(out, "ALS")
+    assert len(fits) == g["iters"]
+    assert np.max(np.abs(fits - np.array(g["fits"]))) < 1e-5
+    assert "[ALS] Lambda:" in out and "[ALS] Final RMSE=" in out
+    head = (tmp_path / "exp.0.out").read_text().split("\n")[:3]
+    assert head == ["matrix", "2", f"{t.dims[0]} {g['R']}"]
+    lam = (tmp_path / "exp.lambda.out").read_text().split()
+    assert lam[:3] == ["vector", "1", str(g["R"])] and len(lam) == 3 + g["R"]
+
+
+@pytest.mark.gpu
+def test_cli_generic_matches_reference(gpu, tmp_path):
+    g = json.loads((GOLD / "cfg5s_R16_dense.json").read_text())
+    tns = tmp_path / "t.tns"
+    golden_tensor(g, tns)
+    out = run([tns, g["iters"], g["R"], g["threshold"]],
+              {"GEN_DENSE_THRESHOLD": "0.03", "GEN_DUMP": str(tmp_path / "d")})
+    fits = fits_of(out, "GEN")
+    assert np.max(np.abs(fits - np.array(g["fits"]))) < 1e-5
+    assert "[GEN] exact:" in out
+    assert (tmp_path / "d.factors.txt").read_text().startswith("# cpTC factor dump")

@@ -194,18 +194,18 @@ def test_mttkrp_units_generic(gpu, oracle, R, inner):
     # both sides form the same units.  Inner sets other than (0,1,2) are
     # refused by the reference (its kernel fails its own self-test there).
     t = cp.gen_config(5, scale=0.05)
-    e = engine_for(t, R, reorder="none", dense_thr_generic=0.03, dense_inner=inner)
+    thr = 0.03 if inner == (0, 1, 2) else 0.002  # other inner sets form fewer full units
+    e = engine_for(t, R, reorder="none", dense_thr_generic=thr, dense_inner=inner)
     st = e.stats()
     assert st["tf32_path"] == 1 and st["dense_tiles"] > 0
     F = rand_factors(t.dims, R)
     for m in range(t.order):
         e.set_factor(m, F[m])
-    inner_c = (C_INT * 3)(*inner)
     for n in range(t.order):
         got = e.mttkrp(n)
         exact = oracle.mttkrp(t, F, n, threads=8)
         if n in inner:
-            ref = units_oracle(oracle, t, F, inner, inner.index(n))
+            ref = units_oracle(oracle, t, F, inner, inner.index(n), thr)
             assert rel(got, ref) < 1e-5
             assert np.abs(got - exact).max() / np.abs(exact).max() < 2e-3
         else:
@@ -214,14 +214,12 @@ def test_mttkrp_units_generic(gpu, oracle, R, inner):
 
 import ctypes as _C  # noqa: E402
 
-C_INT = _C.c_int
 
-
-def units_oracle(oracle, t, F, inner, tslot):
+def units_oracle(oracle, t, F, inner, tslot, thr):
     a = oracle._Args(t)
     Fs, fp = oracle._fptrs(F)
     out = np.zeros((t.dims[inner[tslot]], F[0].shape[1]))
     inn = (_C.c_int * 3)(*inner)
     oracle.lib().or_mttkrp_units(t.order, a.dims, a.nnz, a.ip, a.vp, F[0].shape[1], fp, inn,
-                                 tslot, 0.03, out.ctypes.data_as(oracle.DP), 8)
+                                 tslot, thr, out.ctypes.data_as(oracle.DP), 8)
     return out
