@@ -194,12 +194,134 @@ __global__ void __launch_bounds__(256, 2) k_mttkrp_view(MttkrpArgs a) {
   write_row(row_began_here && last_row_ends_here);
 }
 
+// Order 3: every nonzero needs two factor rows, F_g[g] and F_o[o].  Both are
+// gathered inside a software pipeline: the rows of sub-batch k+1 are issued
+// before sub-batch k is consumed, and the element words of the next batch
+// are loaded one batch ahead, so no load result is waited on early; repeated
+// outer rows along a run hit L1.  Per nonzero acc += (v * F_g[g,r]) * F_o[o,r],
+// the reference's product v * F1 * F2 (src/sparse.cu:666-669).
+template <int GW, int RPL, bool VEC, int U>
+__global__ void __launch_bounds__(256, 2) k_mttkrp_view3(MttkrpArgs a) {
+  constexpr int GPW = 32 / GW;
+  constexpr int SUBS = GW / U;  // sub-batches per batch of GW elements
+  const int lane = threadIdx.x & 31;
+  const int glane = lane % GW;
+  const int gid = lane / GW;
+  const unsigned gmask = (GW == 32) ? 0xffffffffu : (((1u << GW) - 1u) << (gid * GW));
+  const uint64_t task =
+      ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + gid;
+  if (task >= a.ntasks) return;
+  const int R = a.R;
+  const Lanes<GW, RPL, VEC> L(glane, R);
+  const uint64_t p0 = task * (uint64_t)kTask;
+  const uint64_t p1 = (p0 + kTask < a.nnz) ? p0 + kTask : a.nnz;
+  const int nel = (int)(p1 - p0);
+  const int nsub = (nel + U - 1) / U;
+
+  uint32_t rowi = a.task_row[task];
+  uint32_t row = a.rows[rowi];
+  bool row_began_here = (a.gw[p0] & kRowFlag) != 0;
+  const bool last_row_ends_here = (p1 == a.nnz) || (a.gw[p1] & kRowFlag);
+
+  double acc[RPL];
+#pragma unroll
+  for (int k = 0; k < RPL; ++k) acc[k] = 0.0;
+
+  auto write_row = [&](bool owned) {
+    double* dst = a.out + (uint64_t)row * (uint64_t)R;
+#pragma unroll
+    for (int k = 0; k < RPL; ++k) {
+      if (!L.ok[k]) continue;
+      if (owned) dst[L.r[k]] += acc[k];
+      else atomicAdd(dst + L.r[k], acc[k]);
+      acc[k] = 0.0;
+    }
+  };
+  auto load_batch = [&](int b, uint32_t& w, uint32_t& o, double& v) {
+    const int e = b + glane;
+    if (e < nel) {
+      w = __ldcs(a.gw + p0 + e);
+      v = __ldcs(a.val + p0 + e);
+      o = __ldcs(a.oidx + p0 + e);
+    } else {
+      w = 0u;
+      o = 0u;
+      v = 0.0;
+    }
+  };
+
+  // Batch registers: bw/bo/bv[0] hold the batch being consumed, [1] the next.
+  uint32_t cw, co, nw = 0u, no = 0u;
+  double cv, nv = 0.0;
+  load_batch(0, cw, co, cv);
+  if (GW < nel) load_batch(GW, nw, no, nv);
+  if (glane == 0) cw &= ~kRowFlag;  // the row state at p0 is already set
+
+  double gA[U][RPL], fA[U][RPL], gB[U][RPL], fB[U][RPL];
+  // Issue the gathers of sub-batch k (elements k*U ..) into (g, f).  The
+  // sub-batch lies in the current batch when (k % SUBS) belongs to it; the
+  // first sub-batch of the next batch is gathered from the next-batch words.
+  auto gather = [&](int k, bool from_next, double (&g)[U][RPL], double (&f)[U][RPL]) {
+    const int j0 = (k % SUBS) * U;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t w = __shfl_sync(gmask, from_next ? nw : cw, j0 + u, GW);
+      const uint32_t o = __shfl_sync(gmask, from_next ? no : co, j0 + u, GW);
+      if (k * U + u < nel) {
+        load_row<GW, RPL, VEC>(a.Fg, w & kIdxMask, R, glane, L, g[u]);
+        load_row<GW, RPL, VEC>(a.Fo[0], o, R, glane, L, f[u]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < RPL; ++q) g[u][q] = f[u][q] = 0.0;
+      }
+    }
+  };
+  auto consume = [&](int k, const double (&g)[U][RPL], const double (&f)[U][RPL]) {
+    const int j0 = (k % SUBS) * U;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (k * U + u >= nel) break;
+      const uint32_t ww = __shfl_sync(gmask, cw, j0 + u, GW);
+      const double vj = __shfl_sync(gmask, cv, j0 + u, GW);
+      if (ww & kRowFlag) {
+        write_row(row_began_here);
+        row = a.rows[++rowi];
+        row_began_here = true;
+      }
+#pragma unroll
+      for (int q = 0; q < RPL; ++q) acc[q] = fma(vj * g[u][q], f[u][q], acc[q]);
+    }
+    // After the last sub-batch of a batch, rotate the batch registers.
+    if ((k % SUBS) == SUBS - 1) {
+      cw = nw;
+      co = no;
+      cv = nv;
+      const int nb = (k / SUBS + 2) * GW;
+      if (nb < nel) load_batch(nb, nw, no, nv);
+    }
+  };
+  auto next_is_new_batch = [&](int k) { return ((k + 1) % SUBS) == 0; };
+
+  gather(0, false, gA, fA);
+#pragma unroll 1
+  for (int k = 0; k < nsub; k += 2) {
+    if (k + 1 < nsub) gather(k + 1, next_is_new_batch(k), gB, fB);
+    consume(k, gA, fA);
+    if (k + 1 < nsub) {
+      if (k + 2 < nsub) gather(k + 2, next_is_new_batch(k + 1), gA, fA);
+      consume(k + 1, gB, fB);
+    }
+  }
+  write_row(row_began_here && last_row_ends_here);
+}
+
 template <int GW, int RPL, bool VEC, int U>
 void launch(const MttkrpArgs& a, cudaStream_t s) {
   constexpr int GPW = 32 / GW;
   const uint64_t warps = (a.ntasks + GPW - 1) / GPW;
   const unsigned blocks = (unsigned)((warps + 7) / 8);
-  k_mttkrp_view<GW, RPL, VEC, U><<<blocks, 256, 0, s>>>(a);
+  if (a.nout == 1) k_mttkrp_view3<GW, RPL, VEC, U><<<blocks, 256, 0, s>>>(a);
+  else k_mttkrp_view<GW, RPL, VEC, U><<<blocks, 256, 0, s>>>(a);
   CPTC_LAUNCH_CHECK();
 }
 
