@@ -46,6 +46,7 @@ def parse_args():
     p.add_argument("--path", default="auto", choices=["auto", "tf32", "fp64"])
     p.add_argument("--threshold", type=float, default=0.03)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--keep-tns", default="", help="reference arm: keep the .tns it writes here")
     return p.parse_args()
 
 
@@ -375,7 +376,7 @@ def run_reference(a):
         print(json.dumps(line), flush=True)
         return
     with tempfile.TemporaryDirectory() as d:
-        tns = Path(d) / "bench.tns"
+        tns = Path(a.keep_tns) if a.keep_tns else Path(d) / "bench.tns"
         cp.write_tns(tns, t)
         iters = a.warmup + a.steps
         env = dict(os.environ)
