@@ -63,7 +63,8 @@ uint64_t Engine::device_bytes() const {
   uint64_t b = vals.bytes();
   for (int m = 0; m < N; ++m) b += idx[m].bytes() + F[m].bytes() + G[m].bytes();
   for (const View& v : views)
-    b += v.gw.bytes() + v.oidx.bytes() + v.val.bytes() + v.rows.bytes() + v.task_row.bytes();
+    b += v.gw.bytes() + v.oidx.bytes() + v.val.bytes() + v.rec.bytes() + v.rows.bytes() +
+         v.task_row.bytes();
   b += units.unit.bytes() + units.start.bytes() + units.lid.bytes() + units.val.bytes() +
        units.outer_idx.bytes();
   for (int m = 0; m < 3; ++m) b += units.order[m].bytes();
@@ -369,6 +370,7 @@ void Engine::mttkrp_tiles(int mode) {
 void Engine::mttkrp_sparse(int mode) {
   const View& v = views[mode];
   MttkrpArgs a{};
+  a.rec = v.rec.p;
   a.gw = v.gw.p;
   a.oidx = v.oidx.p;
   a.val = v.val.p;

@@ -34,6 +34,9 @@ struct View {
   DArray<uint32_t> gw;           // element word (gathered index + flags)
   DArray<uint32_t> oidx;         // nout * nnz outer indices (SoA)
   DArray<double> val;
+  // Order 3: the same data as one 16-byte record per nonzero
+  // {word, outer index, value} (x, y = word, outer; zw = value bits).
+  DArray<uint4> rec;
   DArray<uint32_t> rows;         // non-empty target rows, in order
   DArray<uint32_t> task_row;     // index into `rows` of each task's first row
   uint64_t nrows = 0, ntasks = 0;

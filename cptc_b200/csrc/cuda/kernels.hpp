@@ -9,6 +9,7 @@
 namespace cptc {
 
 struct MttkrpArgs {
+  const uint4* rec;  // order-3 records (null otherwise)
   const uint32_t* gw;
   const uint32_t* oidx;
   const double* val;

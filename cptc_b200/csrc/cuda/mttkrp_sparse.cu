@@ -21,6 +21,8 @@
 //  * a row that starts and ends inside one task is written with a plain
 //    read-modify-write (it has no other writer in this launch); rows cut by
 //    a task boundary are combined with FP64 atomicAdd.
+#include <cstdlib>
+
 #include "engine.hpp"
 #include "kernels.hpp"
 
@@ -194,41 +196,42 @@ __global__ void __launch_bounds__(256, 2) k_mttkrp_view(MttkrpArgs a) {
   write_row(row_began_here && last_row_ends_here);
 }
 
-// Order 3: every nonzero needs two factor rows, F_g[g] and F_o[o].  Both are
-// gathered inside a software pipeline: the rows of sub-batch k+1 are issued
-// before sub-batch k is consumed, and the element words of the next batch
-// are loaded one batch ahead, so no load result is waited on early; repeated
-// outer rows along a run hit L1.  Per nonzero acc += (v * F_g[g,r]) * F_o[o,r],
-// the reference's product v * F1 * F2 (src/sparse.cu:666-669).
+// Order 3: one 16-byte record per nonzero {index word, outer index, value},
+// read by every lane of the group with a single uniform 128-bit load (no
+// shuffles); the two factor rows of the nonzero are 8/16-byte vector loads
+// across the group.  U nonzeros are in flight per group and the records of
+// the next U are loaded before the current U are consumed.  The kernel
+// keeps few registers so that many warps hide the gather latency.
+// Per nonzero acc += (v * F_g[g, r]) * F_o[o, r], the reference's product
+// v * F1 * F2 (src/sparse.cu:666-669).
 template <int GW, int RPL, bool VEC, int U>
-__global__ void __launch_bounds__(256, 2) k_mttkrp_view3(MttkrpArgs a) {
+__global__ void __launch_bounds__(256) k_mttkrp_rec3(const uint4* __restrict__ rec,
+                                                     const uint32_t* __restrict__ rows,
+                                                     const uint32_t* __restrict__ task_row,
+                                                     uint64_t nnz, uint64_t ntasks, int R,
+                                                     const double* __restrict__ Fg,
+                                                     const double* __restrict__ Fo,
+                                                     double* __restrict__ out) {
   constexpr int GPW = 32 / GW;
-  constexpr int SUBS = GW / U;  // sub-batches per batch of GW elements
   const int lane = threadIdx.x & 31;
   const int glane = lane % GW;
-  const int gid = lane / GW;
-  const unsigned gmask = (GW == 32) ? 0xffffffffu : (((1u << GW) - 1u) << (gid * GW));
   const uint64_t task =
-      ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + gid;
-  if (task >= a.ntasks) return;
-  const int R = a.R;
+      ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + lane / GW;
+  if (task >= ntasks) return;
   const Lanes<GW, RPL, VEC> L(glane, R);
   const uint64_t p0 = task * (uint64_t)kTask;
-  const uint64_t p1 = (p0 + kTask < a.nnz) ? p0 + kTask : a.nnz;
-  const int nel = (int)(p1 - p0);
-  const int nsub = (nel + U - 1) / U;
+  const uint64_t p1 = (p0 + kTask < nnz) ? p0 + kTask : nnz;
 
-  uint32_t rowi = a.task_row[task];
-  uint32_t row = a.rows[rowi];
-  bool row_began_here = (a.gw[p0] & kRowFlag) != 0;
-  const bool last_row_ends_here = (p1 == a.nnz) || (a.gw[p1] & kRowFlag);
+  uint32_t rowi = task_row[task];
+  uint32_t row = rows[rowi];
+  bool began = (rec[p0].x & kRowFlag) != 0;
+  const bool ends = (p1 == nnz) || (rec[p1].x & kRowFlag);
 
   double acc[RPL];
 #pragma unroll
   for (int k = 0; k < RPL; ++k) acc[k] = 0.0;
-
   auto write_row = [&](bool owned) {
-    double* dst = a.out + (uint64_t)row * (uint64_t)R;
+    double* dst = out + (uint64_t)row * (uint64_t)R;
 #pragma unroll
     for (int k = 0; k < RPL; ++k) {
       if (!L.ok[k]) continue;
@@ -237,82 +240,60 @@ __global__ void __launch_bounds__(256, 2) k_mttkrp_view3(MttkrpArgs a) {
       acc[k] = 0.0;
     }
   };
-  auto load_batch = [&](int b, uint32_t& w, uint32_t& o, double& v) {
-    const int e = b + glane;
-    if (e < nel) {
-      w = __ldcs(a.gw + p0 + e);
-      v = __ldcs(a.val + p0 + e);
-      o = __ldcs(a.oidx + p0 + e);
-    } else {
-      w = 0u;
-      o = 0u;
-      v = 0.0;
+  auto step = [&](const uint4& e, const double (&g)[RPL], const double (&f)[RPL], bool first) {
+    if ((e.x & kRowFlag) && !first) {
+      write_row(began);
+      row = rows[++rowi];
+      began = true;
     }
+    const double v = __hiloint2double((int)e.w, (int)e.z);
+#pragma unroll
+    for (int k = 0; k < RPL; ++k) acc[k] = fma(v * g[k], f[k], acc[k]);
   };
 
-  // Batch registers: bw/bo/bv[0] hold the batch being consumed, [1] the next.
-  uint32_t cw, co, nw = 0u, no = 0u;
-  double cv, nv = 0.0;
-  load_batch(0, cw, co, cv);
-  if (GW < nel) load_batch(GW, nw, no, nv);
-  if (glane == 0) cw &= ~kRowFlag;  // the row state at p0 is already set
-
-  double gA[U][RPL], fA[U][RPL], gB[U][RPL], fB[U][RPL];
-  // Issue the gathers of sub-batch k (elements k*U ..) into (g, f).  The
-  // sub-batch lies in the current batch when (k % SUBS) belongs to it; the
-  // first sub-batch of the next batch is gathered from the next-batch words.
-  auto gather = [&](int k, bool from_next, double (&g)[U][RPL], double (&f)[U][RPL]) {
-    const int j0 = (k % SUBS) * U;
+  uint64_t p = p0;
+  const uint64_t pfull = p0 + ((p1 - p0) / U) * U;
+  uint4 cur[U];
+  if (p < pfull) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const uint32_t w = __shfl_sync(gmask, from_next ? nw : cw, j0 + u, GW);
-      const uint32_t o = __shfl_sync(gmask, from_next ? no : co, j0 + u, GW);
-      if (k * U + u < nel) {
-        load_row<GW, RPL, VEC>(a.Fg, w & kIdxMask, R, glane, L, g[u]);
-        load_row<GW, RPL, VEC>(a.Fo[0], o, R, glane, L, f[u]);
-      } else {
-#pragma unroll
-        for (int q = 0; q < RPL; ++q) g[u][q] = f[u][q] = 0.0;
-      }
-    }
-  };
-  auto consume = [&](int k, const double (&g)[U][RPL], const double (&f)[U][RPL]) {
-    const int j0 = (k % SUBS) * U;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (k * U + u >= nel) break;
-      const uint32_t ww = __shfl_sync(gmask, cw, j0 + u, GW);
-      const double vj = __shfl_sync(gmask, cv, j0 + u, GW);
-      if (ww & kRowFlag) {
-        write_row(row_began_here);
-        row = a.rows[++rowi];
-        row_began_here = true;
-      }
-#pragma unroll
-      for (int q = 0; q < RPL; ++q) acc[q] = fma(vj * g[u][q], f[u][q], acc[q]);
-    }
-    // After the last sub-batch of a batch, rotate the batch registers.
-    if ((k % SUBS) == SUBS - 1) {
-      cw = nw;
-      co = no;
-      cv = nv;
-      const int nb = (k / SUBS + 2) * GW;
-      if (nb < nel) load_batch(nb, nw, no, nv);
-    }
-  };
-  auto next_is_new_batch = [&](int k) { return ((k + 1) % SUBS) == 0; };
-
-  gather(0, false, gA, fA);
-#pragma unroll 1
-  for (int k = 0; k < nsub; k += 2) {
-    if (k + 1 < nsub) gather(k + 1, next_is_new_batch(k), gB, fB);
-    consume(k, gA, fA);
-    if (k + 1 < nsub) {
-      if (k + 2 < nsub) gather(k + 2, next_is_new_batch(k + 1), gA, fA);
-      consume(k + 1, gB, fB);
-    }
+    for (int u = 0; u < U; ++u) cur[u] = __ldcs(rec + p + u);
   }
-  write_row(row_began_here && last_row_ends_here);
+#pragma unroll 1
+  for (; p < pfull; p += U) {
+    double g[U][RPL], f[U][RPL];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      load_row<GW, RPL, VEC>(Fg, cur[u].x & kIdxMask, R, glane, L, g[u]);
+      load_row<GW, RPL, VEC>(Fo, cur[u].y, R, glane, L, f[u]);
+    }
+    uint4 nxt[U];
+    if (p + U < pfull) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) nxt[u] = __ldcs(rec + p + U + u);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) step(cur[u], g[u], f[u], p + u == p0);
+#pragma unroll
+    for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+  }
+  for (; p < p1; ++p) {  // tail of fewer than U nonzeros
+    const uint4 e = __ldcs(rec + p);
+    double g[RPL], f[RPL];
+    load_row<GW, RPL, VEC>(Fg, e.x & kIdxMask, R, glane, L, g);
+    load_row<GW, RPL, VEC>(Fo, e.y, R, glane, L, f);
+    step(e, g, f, p == p0);
+  }
+  write_row(began && ends);
+}
+
+template <int GW, int RPL, bool VEC, int U>
+void launch_rec3(const MttkrpArgs& a, cudaStream_t s) {
+  constexpr int GPW = 32 / GW;
+  const uint64_t warps = (a.ntasks + GPW - 1) / GPW;
+  const unsigned blocks = (unsigned)((warps + 7) / 8);
+  k_mttkrp_rec3<GW, RPL, VEC, U><<<blocks, 256, 0, s>>>(a.rec, a.rows, a.task_row, a.nnz,
+                                                         a.ntasks, a.R, a.Fg, a.Fo[0], a.out);
+  CPTC_LAUNCH_CHECK();
 }
 
 template <int GW, int RPL, bool VEC, int U>
@@ -320,8 +301,7 @@ void launch(const MttkrpArgs& a, cudaStream_t s) {
   constexpr int GPW = 32 / GW;
   const uint64_t warps = (a.ntasks + GPW - 1) / GPW;
   const unsigned blocks = (unsigned)((warps + 7) / 8);
-  if (a.nout == 1) k_mttkrp_view3<GW, RPL, VEC, U><<<blocks, 256, 0, s>>>(a);
-  else k_mttkrp_view<GW, RPL, VEC, U><<<blocks, 256, 0, s>>>(a);
+  k_mttkrp_view<GW, RPL, VEC, U><<<blocks, 256, 0, s>>>(a);
   CPTC_LAUNCH_CHECK();
 }
 
@@ -329,6 +309,36 @@ void launch(const MttkrpArgs& a, cudaStream_t s) {
 
 void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
   if (a.nnz == 0 || a.ntasks == 0) return;
+  if (a.rec != nullptr) {
+    // Order 3: group width x ranks per lane, U nonzeros in flight per group
+    // (CPTC_REC3_U overrides U for tuning: 1, 2 or 4).
+    static const int tuneU = [] {
+      const char* e = std::getenv("CPTC_REC3_U");
+      return e ? std::atoi(e) : 0;
+    }();
+#define CPTC_REC3(GW_, RPL_, UDEF)                                          \
+  do {                                                                      \
+    const int u_ = tuneU ? tuneU : (UDEF);                                  \
+    if (u_ == 1) launch_rec3<GW_, RPL_, true, 1>(a, s);                     \
+    else if (u_ == 4) launch_rec3<GW_, RPL_, true, 4>(a, s);                \
+    else launch_rec3<GW_, RPL_, true, 2>(a, s);                             \
+    return;                                                                 \
+  } while (0)
+    switch (a.R) {
+      case 8: CPTC_REC3(8, 1, 4);
+      case 16: CPTC_REC3(8, 2, 4);
+      case 32: CPTC_REC3(16, 2, 4);
+      case 64: CPTC_REC3(16, 4, 2);
+      case 128: CPTC_REC3(32, 4, 2);
+      default: break;
+    }
+#undef CPTC_REC3
+    if (a.R <= 32) launch_rec3<32, 1, false, 4>(a, s);
+    else if (a.R <= 64) launch_rec3<32, 2, false, 2>(a, s);
+    else if (a.R <= 128) launch_rec3<32, 4, false, 2>(a, s);
+    else throw CptcError(CPTC_E_UNSUP, "rank > 128 is not supported");
+    return;
+  }
   switch (a.R) {
     case 8: launch<8, 1, true, 4>(a, s); return;
     case 16: launch<16, 1, true, 8>(a, s); return;

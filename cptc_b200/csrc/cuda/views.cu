@@ -76,6 +76,15 @@ __global__ void k_gather_view(IdxPtrs idx, const double* __restrict__ vals,
   if ((threadIdx.x & 31) == 0 && fibs) atomicAdd(nfib, fibs);
 }
 
+__global__ void k_pack_records(const uint32_t* __restrict__ gw, const uint32_t* __restrict__ oidx,
+                               const double* __restrict__ val, uint64_t n, uint4* __restrict__ rec) {
+  for (uint64_t p = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; p < n;
+       p += (uint64_t)gridDim.x * blockDim.x) {
+    const unsigned long long vb = __double_as_longlong(val[p]);
+    rec[p] = make_uint4(gw[p], oidx[p], (uint32_t)vb, (uint32_t)(vb >> 32));
+  }
+}
+
 __global__ void k_rows_from_pos(const uint32_t* __restrict__ pos, uint64_t nrows,
                                 const uint32_t* __restrict__ tsrc, const uint32_t* __restrict__ perm,
                                 uint32_t* __restrict__ rows) {
@@ -207,6 +216,18 @@ void build_view_order(Engine& E, View& v, int n, const int* order, int nother,
   k_task_rows<<<grid_for(v.ntasks, 256, 148 * 16), 256, 0, s>>>(pos.p, v.nrows, v.ntasks,
                                                                  v.task_row.p);
   CPTC_LAUNCH_CHECK();
+  if (v.nout == 1) {
+    // Order 3: one 16-byte record per nonzero for the MTTKRP stream; the
+    // separate arrays are released (only the row-start flags are read
+    // elsewhere, from the records).
+    v.rec.alloc(nsel);
+    k_pack_records<<<gb, 256, 0, s>>>(v.gw.p, v.oidx.p, v.val.p, nsel, v.rec.p);
+    CPTC_LAUNCH_CHECK();
+    CPTC_CUDA(cudaStreamSynchronize(s));
+    v.oidx.release();
+    v.val.release();
+    v.gw.release();
+  }
   CPTC_CUDA(cudaStreamSynchronize(s));
 }
 
