@@ -142,12 +142,15 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
 }
 
 // Block of 4 warps, persistent over a contiguous range of the visiting
-// order.  Warp w owns n-tiles w, w+4, ... (R/8 n-tiles of 8 ranks); when
-// R < 32 the warps also split the 16 slabs and combine through shared
-// memory.  Per tile: zero + scatter the 16^3 tile in (s, t, c) layout, load
-// the c-slot rows (TF32) and the s-slot rows times the outer weights (FP64),
-// then 16 slabs x 2 k-steps of m16n8k8 with the FP64 epilogue in registers.
-template <int NTMAX>
+// order.  Slot roles (target TS, TF32-contracted CS, FP64-weighted SS) are
+// compile-time constants.  Warp w owns n-tiles w, w+4, ... (R/8 n-tiles of 8
+// ranks); when R < 32 the warps also split the 16 slabs and combine through
+// shared memory.  Per tile: zero + scatter the 16^3 tile in (s, t, c)
+// layout, load the c-slot rows (TF32) and the s-slot rows times the outer
+// weights (FP64), then 16 slabs x 2 k-steps of m16n8k8 with the FP64
+// epilogue in registers.  Row loops are (warp, lane)-strided: no integer
+// division in the kernel.
+template <int TS, int CS, int SS, int NTMAX>
 __global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __restrict__ order,
                                                uint64_t per_block) {
   extern __shared__ __align__(16) unsigned char smraw[];
@@ -160,36 +163,39 @@ __global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __res
   double* wS = accS + 16 * R;                                   // R (outer weights)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
-  const int ts = a.tslot, cs = a.cslot, ss = a.sslot;
-  const int NT = R / 8;
+  const int NT = R >> 3;
   const int ntstep = NT >= 4 ? 4 : NT;
   const int SG = 4 / ntstep;
   const int my_sg = warp / ntstep;
-  const int nt0 = warp % ntstep;
+  const int nt0 = warp - my_sg * ntstep;
+  const uint64_t dimT = a.dims[TS], dimC = a.dims[CS], dimS = a.dims[SS];
 
   const uint64_t k0 = (uint64_t)blockIdx.x * per_block;
   uint64_t k1 = k0 + per_block;
   if (k1 > a.ntiles) k1 = a.ntiles;
   if (k0 >= k1) return;
 
-  for (int i = tid; i < 16 * R; i += 128) accS[i] = 0.0;
+  for (int t = warp; t < 16; t += 4)
+    for (int r = lane; r < R; r += 32) accS[t * R + r] = 0.0;
   int cur_tb = -1;
 
   auto flush = [&](int tb) {
-    for (int i = tid; i < 16 * R; i += 128) {
-      const int t = i / R, r = i % R;
+    for (int t = warp; t < 16; t += 4) {
       const uint64_t row = (uint64_t)tb * 16 + t;
-      const double v = accS[i];
-      if (row < a.dims[ts] && v != 0.0) atomicAdd(a.out + row * (uint64_t)R + r, v);
-      accS[i] = 0.0;
+      for (int r = lane; r < R; r += 32) {
+        const double v = accS[t * R + r];
+        if (row < dimT && v != 0.0) atomicAdd(a.out + row * (uint64_t)R + r, v);
+        accS[t * R + r] = 0.0;
+      }
     }
   };
 
   for (uint64_t k = k0; k < k1; ++k) {
     const uint32_t ti = order[k];
     const int4 T = a.tile[ti];
-    const int blk[3] = {T.x, T.y, T.z};
-    const int tb = blk[ts], cb = blk[cs], sb = blk[ss];
+    const int tb = TS == 0 ? T.x : TS == 1 ? T.y : T.z;
+    const int cb = CS == 0 ? T.x : CS == 1 ? T.y : T.z;
+    const int sb = SS == 0 ? T.x : SS == 1 ? T.y : T.z;
     __syncthreads();  // previous tile's shared-memory reads are done
     if (tb != cur_tb) {
       if (cur_tb >= 0) flush(cur_tb);
@@ -206,21 +212,26 @@ __global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __res
       }
     }
     __syncthreads();
-    for (int i = tid; i < 16 * R; i += 128) {
-      const int c = i / R, r = i % R;
+    for (int c = warp; c < 16; c += 4) {
       const uint64_t cg = (uint64_t)cb * 16 + c, sg = (uint64_t)sb * 16 + c;
-      fB[c * Rs + r] = (cg < a.dims[cs]) ? (float)a.Fc[cg * R + r] : 0.0f;
-      double f2 = (sg < a.dims[ss]) ? a.Fs[sg * R + r] : 0.0;
-      if (a.nouter > 0) f2 *= wS[r];
-      F2s[c * R + r] = f2;
+      const bool cok = cg < dimC, sok = sg < dimS;
+      for (int r = lane; r < R; r += 32) {
+        fB[c * Rs + r] = cok ? (float)a.Fc[cg * R + r] : 0.0f;
+        double f2 = sok ? a.Fs[sg * R + r] : 0.0;
+        if (a.nouter > 0) f2 *= wS[r];
+        F2s[c * R + r] = f2;
+      }
     }
     const uint64_t st = a.start[ti];
     for (int j = tid; j < T.w; j += 128) {
       const uint32_t l = a.lid[st + j];
-      const int loc[3] = {(int)(l >> 8), (int)((l >> 4) & 15), (int)(l & 15)};
+      const int l0 = (int)(l >> 8), l1 = (int)((l >> 4) & 15), l2 = (int)(l & 15);
+      const int lt = TS == 0 ? l0 : TS == 1 ? l1 : l2;
+      const int lc = CS == 0 ? l0 : CS == 1 ? l1 : l2;
+      const int ls = SS == 0 ? l0 : SS == 1 ? l1 : l2;
       double v = a.val[st + j];
       v = v > FLT_MAX ? FLT_MAX : (v < -FLT_MAX ? -FLT_MAX : v);
-      float* dst = X + loc[ss] * kSs + loc[ts] * kSt + loc[cs];
+      float* dst = X + ls * kSs + lt * kSt + lc;
       if (a.store_dups) *dst = (float)v;
       else atomicAdd(dst, (float)v);
     }
@@ -272,10 +283,17 @@ __global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __res
       const int nt = nt0 + q * ntstep;
       if (nt >= NT) break;
       const int r = nt * 8 + 2 * t4;
-      atomicAdd(&accS[g * R + r], acc[q][0]);
-      atomicAdd(&accS[g * R + r + 1], acc[q][1]);
-      atomicAdd(&accS[(g + 8) * R + r], acc[q][2]);
-      atomicAdd(&accS[(g + 8) * R + r + 1], acc[q][3]);
+      if (SG == 1) {  // this warp alone owns these columns
+        accS[g * R + r] += acc[q][0];
+        accS[g * R + r + 1] += acc[q][1];
+        accS[(g + 8) * R + r] += acc[q][2];
+        accS[(g + 8) * R + r + 1] += acc[q][3];
+      } else {
+        atomicAdd(&accS[g * R + r], acc[q][0]);
+        atomicAdd(&accS[g * R + r + 1], acc[q][1]);
+        atomicAdd(&accS[(g + 8) * R + r], acc[q][2]);
+        atomicAdd(&accS[(g + 8) * R + r + 1], acc[q][3]);
+      }
     }
   }
   __syncthreads();
@@ -455,16 +473,30 @@ void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, cudaStream_t
   const uint64_t per = (a.ntiles + blocks - 1) / blocks;
   blocks = (a.ntiles + per - 1) / per;
   const int NT = R / 8;
-#define CPTC_TILES(NTM)                                                                      \
-  do {                                                                                       \
-    CPTC_CUDA(cudaFuncSetAttribute(k_tiles<NTM>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                   (int)smem));                                              \
-    k_tiles<NTM><<<(unsigned)blocks, 128, smem, s>>>(a, order, per);                         \
+  const int ntm = NT <= 4 ? 1 : NT <= 8 ? 2 : NT <= 12 ? 3 : 4;
+  const int roles = a.tslot * 100 + a.cslot * 10 + a.sslot;
+#define CPTC_TILES(TS_, CS_, SS_, NTM)                                                     \
+  do {                                                                                     \
+    auto kern = k_tiles<TS_, CS_, SS_, NTM>;                                               \
+    CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                                   (int)smem));                                            \
+    kern<<<(unsigned)blocks, 128, smem, s>>>(a, order, per);                               \
   } while (0)
-  if (NT <= 4) CPTC_TILES(1);
-  else if (NT <= 8) CPTC_TILES(2);
-  else if (NT <= 12) CPTC_TILES(3);
-  else CPTC_TILES(4);
+#define CPTC_TILES_R(TS_, CS_, SS_)          \
+  do {                                       \
+    if (ntm == 1) CPTC_TILES(TS_, CS_, SS_, 1); \
+    else if (ntm == 2) CPTC_TILES(TS_, CS_, SS_, 2); \
+    else if (ntm == 3) CPTC_TILES(TS_, CS_, SS_, 3); \
+    else CPTC_TILES(TS_, CS_, SS_, 4);       \
+  } while (0)
+  switch (roles) {
+    case 12: CPTC_TILES_R(0, 1, 2); break;   // order-3 mode 0; N-order slot 0
+    case 102: CPTC_TILES_R(1, 0, 2); break;  // order-3 mode 1
+    case 201: CPTC_TILES_R(2, 0, 1); break;  // order-3 mode 2
+    case 120: CPTC_TILES_R(1, 2, 0); break;  // N-order slot 1 (slot 2 is 201)
+    default: throw CptcError(CPTC_E_ARG, "unsupported tile slot roles");
+  }
+#undef CPTC_TILES_R
 #undef CPTC_TILES
   CPTC_LAUNCH_CHECK();
 }
