@@ -327,7 +327,7 @@ void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
     switch (a.R) {
       case 8: CPTC_REC3(8, 1, 4);
       case 16: CPTC_REC3(8, 2, 4);
-      case 32: CPTC_REC3(16, 2, 4);
+      case 32: CPTC_REC3(16, 2, 2);
       case 64: CPTC_REC3(16, 4, 2);
       case 128: CPTC_REC3(32, 4, 2);
       default: break;

@@ -468,7 +468,13 @@ void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, cudaStream_t
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  uint64_t blocks = (uint64_t)sms * 4;
+  // As many CTAs as the SMs hold at once (shared memory is the limit):
+  // each CTA walks its tiles one after another, so latency is hidden by the
+  // number of CTAs in flight.
+  int per_sm = (int)((228 * 1024) / (smem + 1024));
+  if (per_sm < 1) per_sm = 1;
+  if (per_sm > 16) per_sm = 16;
+  uint64_t blocks = (uint64_t)sms * per_sm;
   if (blocks > a.ntiles) blocks = a.ntiles;
   const uint64_t per = (a.ntiles + blocks - 1) / blocks;
   blocks = (a.ntiles + per - 1) / per;
