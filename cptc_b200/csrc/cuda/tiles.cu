@@ -486,6 +486,8 @@ void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, cudaStream_t
     auto kern = k_tiles<TS_, CS_, SS_, NTM>;                                               \
     CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                                    (int)smem));                                            \
+    CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,   \
+                                   100));                                                  \
     kern<<<(unsigned)blocks, 128, smem, s>>>(a, order, per);                               \
   } while (0)
 #define CPTC_TILES_R(TS_, CS_, SS_)          \
