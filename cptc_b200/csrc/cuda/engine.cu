@@ -227,6 +227,10 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
   alloc_workspace();
   comm_prepare(*this);
   slab_tiles(*this);
+  if (dense_active) {
+    units.blocks = tile_blocks_for(R, device);
+    for (int t = 0; t < 3; ++t) tile_cuts(*this, t);
+  }
   for (int n = 0; n < N; ++n) {
     // Residual-only views for modes the dense tiles cover as a target.
     const bool covered = dense_active &&
@@ -364,7 +368,7 @@ void Engine::mttkrp_tiles(int mode) {
   for (int q = 0; q < units.nouter; ++q) ta.Fout[q] = F[units.outer[q]].p;
   ta.store_dups = units.store_dups ? 1 : 0;
   ta.out = FtV.p;
-  launch_mttkrp_tiles3(ta, units.order[ts].p, stream);
+  launch_mttkrp_tiles3(ta, units.order[ts].p, units.cut[ts].p, units.blocks, stream);
 }
 
 void Engine::mttkrp_sparse(int mode) {
@@ -378,6 +382,7 @@ void Engine::mttkrp_sparse(int mode) {
   a.task_row = v.task_row.p;
   a.nnz = v.nnz;
   a.ntasks = v.ntasks;
+  a.task = v.task;
   a.nout = v.nout;
   a.R = R;
   a.Fg = F[v.gmode].p;

@@ -18,8 +18,14 @@ constexpr uint32_t kFibFlag = 0x40000000u;
 constexpr uint32_t kIdxMask = 0x3FFFFFFFu;
 constexpr uint64_t kMaxGatherDim = (1ull << 30);
 
-// Elements of one warp task in the sparse MTTKRP (multiple of 32).
+// Nonzeros of one lane-group task in the sparse MTTKRP: 1024, smaller for
+// small views so that every SM gets work (a power of two >= 64).
 constexpr int kTask = 1024;
+inline uint32_t task_size_for(uint64_t nnz) {
+  uint32_t t = kTask;
+  while (t > 64 && nnz / t < 148ull * 64) t >>= 1;
+  return t;
+}
 
 // Sorted view of the nonzeros for one target mode, in the order
 // (target, outer modes..., gathered mode).  The rows of the outer modes are
@@ -40,6 +46,7 @@ struct View {
   DArray<uint32_t> rows;         // non-empty target rows, in order
   DArray<uint32_t> task_row;     // index into `rows` of each task's first row
   uint64_t nrows = 0, ntasks = 0;
+  uint32_t task = kTask;         // nonzeros per task
 };
 
 // Dense 16^3 tiles: order 3 (inner = modes 0,1,2, no outer modes) or the
@@ -59,6 +66,10 @@ struct UnitPool {
   DArray<double> val;
   DArray<uint32_t> order[3];   // visiting order per inner target slot
   uint64_t cnt[3] = {0, 0, 0}; // tiles of this rank per inner target slot
+  // CTA ranges over each visiting order with balanced nonzero counts
+  // (blocks + 1 cut points), computed for `blocks` CTAs at build time.
+  DArray<uint32_t> cut[3];
+  uint32_t blocks = 0;
 };
 
 struct Engine {

@@ -16,6 +16,7 @@ struct MttkrpArgs {
   const uint32_t* rows;
   const uint32_t* task_row;
   uint64_t nnz, ntasks;
+  uint32_t task;
   int nout, R;
   const double* Fg;
   const double* Fo[CPTC_MAX_ORDER];
@@ -46,8 +47,14 @@ struct TileArgs {
   int store_dups;           // 1: last write wins (order-3), 0: duplicates sum
   double* out;
 };
-// order: tile visiting order for this mode (sorted by target block).
-void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, cudaStream_t s);
+// order: tile visiting order for this mode (sorted by target block);
+// cut: blocks+1 CTA range starts over `order` (balanced by nonzeros).
+void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, const uint32_t* cut,
+                          uint32_t blocks, cudaStream_t s);
+// CTAs the tile kernel runs for rank R (shared-memory occupancy x SMs).
+uint32_t tile_blocks_for(int R, int device);
+// Balanced CTA ranges over E.units.order[slot] (fills E.units.cut[slot]).
+void tile_cuts(Engine& E, int slot);
 // Partition of Engine::tiles + residual selection (tiles.cu).
 void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64_t& nsel);
 // Views (views.cu).

@@ -84,8 +84,8 @@ __global__ void __launch_bounds__(256, 2) k_mttkrp_view(MttkrpArgs a) {
   if (task >= a.ntasks) return;
   const int R = a.R;
   const Lanes<GW, RPL, VEC> L(glane, R);
-  const uint64_t p0 = task * (uint64_t)kTask;
-  const uint64_t p1 = (p0 + kTask < a.nnz) ? p0 + kTask : a.nnz;
+  const uint64_t p0 = task * (uint64_t)a.task;
+  const uint64_t p1 = (p0 + a.task < a.nnz) ? p0 + a.task : a.nnz;
 
   uint32_t rowi = a.task_row[task];
   uint32_t row = a.rows[rowi];
@@ -208,7 +208,8 @@ template <int GW, int RPL, bool VEC, int U>
 __global__ void __launch_bounds__(256) k_mttkrp_rec3(const uint4* __restrict__ rec,
                                                      const uint32_t* __restrict__ rows,
                                                      const uint32_t* __restrict__ task_row,
-                                                     uint64_t nnz, uint64_t ntasks, int R,
+                                                     uint64_t nnz, uint64_t ntasks,
+                                                     uint32_t tsize, int R,
                                                      const double* __restrict__ Fg,
                                                      const double* __restrict__ Fo,
                                                      double* __restrict__ out) {
@@ -219,8 +220,8 @@ __global__ void __launch_bounds__(256) k_mttkrp_rec3(const uint4* __restrict__ r
       ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + lane / GW;
   if (task >= ntasks) return;
   const Lanes<GW, RPL, VEC> L(glane, R);
-  const uint64_t p0 = task * (uint64_t)kTask;
-  const uint64_t p1 = (p0 + kTask < nnz) ? p0 + kTask : nnz;
+  const uint64_t p0 = task * (uint64_t)tsize;
+  const uint64_t p1 = (p0 + tsize < nnz) ? p0 + tsize : nnz;
 
   uint32_t rowi = task_row[task];
   uint32_t row = rows[rowi];
@@ -292,7 +293,8 @@ void launch_rec3(const MttkrpArgs& a, cudaStream_t s) {
   const uint64_t warps = (a.ntasks + GPW - 1) / GPW;
   const unsigned blocks = (unsigned)((warps + 7) / 8);
   k_mttkrp_rec3<GW, RPL, VEC, U><<<blocks, 256, 0, s>>>(a.rec, a.rows, a.task_row, a.nnz,
-                                                         a.ntasks, a.R, a.Fg, a.Fo[0], a.out);
+                                                         a.ntasks, a.task, a.R, a.Fg, a.Fo[0],
+                                                         a.out);
   CPTC_LAUNCH_CHECK();
 }
 

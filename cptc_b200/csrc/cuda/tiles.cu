@@ -152,7 +152,7 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
 // division in the kernel.
 template <int TS, int CS, int SS, int NTMAX>
 __global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __restrict__ order,
-                                               uint64_t per_block) {
+                                               const uint32_t* __restrict__ cut) {
   extern __shared__ __align__(16) unsigned char smraw[];
   const int R = a.R;
   const int Rs = R + 8;                                         // fB row stride (floats)
@@ -170,9 +170,8 @@ __global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __res
   const int nt0 = warp - my_sg * ntstep;
   const uint64_t dimT = a.dims[TS], dimC = a.dims[CS], dimS = a.dims[SS];
 
-  const uint64_t k0 = (uint64_t)blockIdx.x * per_block;
-  uint64_t k1 = k0 + per_block;
-  if (k1 > a.ntiles) k1 = a.ntiles;
+  const uint64_t k0 = cut[blockIdx.x];
+  const uint64_t k1 = cut[blockIdx.x + 1];
   if (k0 >= k1) return;
 
   for (int t = warp; t < 16; t += 4)
@@ -458,26 +457,83 @@ void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64
   CPTC_CUDA(cudaStreamSynchronize(s));
 }
 
-void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, cudaStream_t s) {
+namespace {
+
+size_t tile_smem(int R) {
+  return (size_t)kTileFloats * 4 + (size_t)16 * (R + 8) * 4 + (size_t)(2 * 16 * R + R) * 8;
+}
+
+// Weight of a tile in the CTA balance: its nonzeros plus a fixed cost of
+// 512 for zeroing the tile and the 16 slab products.
+__global__ void k_tile_weights(const int4* __restrict__ tile, const uint32_t* __restrict__ order,
+                               uint64_t n, unsigned long long* __restrict__ w) {
+  for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < n;
+       k += (uint64_t)gridDim.x * blockDim.x)
+    w[k] = (unsigned long long)tile[order[k]].w + 512ull;
+}
+
+// cut[c] = first k whose inclusive prefix exceeds c * total / blocks.
+__global__ void k_tile_cuts(const unsigned long long* __restrict__ pre, uint64_t n,
+                            uint32_t blocks, uint32_t* __restrict__ cut) {
+  const unsigned long long total = n ? pre[n - 1] : 0ull;
+  for (uint32_t c = blockIdx.x * blockDim.x + threadIdx.x; c <= blocks;
+       c += gridDim.x * blockDim.x) {
+    if (c == 0) { cut[0] = 0; continue; }
+    if (c == blocks) { cut[c] = (uint32_t)n; continue; }
+    const unsigned long long target = (total * c) / blocks;
+    uint64_t lo = 0, hi = n;  // first k with pre[k] > target
+    while (lo < hi) {
+      const uint64_t mid = (lo + hi) >> 1;
+      if (pre[mid] <= target) lo = mid + 1;
+      else hi = mid;
+    }
+    cut[c] = (uint32_t)lo;
+  }
+}
+
+}  // namespace
+
+uint32_t tile_blocks_for(int R, int device) {
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  // As many CTAs as the SMs hold at once (shared memory is the limit): each
+  // CTA walks its tiles one after another, so latency is hidden by the
+  // number of CTAs in flight.
+  int per_sm = (int)((228 * 1024) / (tile_smem(R) + 1024));
+  if (per_sm < 1) per_sm = 1;
+  if (per_sm > 16) per_sm = 16;
+  return (uint32_t)(sms * per_sm);
+}
+
+void tile_cuts(Engine& E, int slot) {
+  UnitPool& U = E.units;
+  const uint64_t n = U.cnt[slot];
+  U.cut[slot].alloc((uint64_t)U.blocks + 1);
+  if (n == 0) {
+    CPTC_CUDA(cudaMemsetAsync(U.cut[slot].p, 0, ((uint64_t)U.blocks + 1) * 4, E.stream));
+    return;
+  }
+  DArray<unsigned long long> w(n), pre(n);
+  k_tile_weights<<<grid_for(n, 256, 148 * 16), 256, 0, E.stream>>>(U.unit.p, U.order[slot].p, n,
+                                                                   w.p);
+  CPTC_LAUNCH_CHECK();
+  size_t tb = 0;
+  CPTC_CUDA(cub::DeviceScan::InclusiveSum(nullptr, tb, w.p, pre.p, (int64_t)n, E.stream));
+  DArray<unsigned char> temp(tb);
+  CPTC_CUDA(cub::DeviceScan::InclusiveSum(temp.p, tb, w.p, pre.p, (int64_t)n, E.stream));
+  k_tile_cuts<<<grid_for((uint64_t)U.blocks + 1, 256), 256, 0, E.stream>>>(pre.p, n, U.blocks,
+                                                                          U.cut[slot].p);
+  CPTC_LAUNCH_CHECK();
+  CPTC_CUDA(cudaStreamSynchronize(E.stream));
+}
+
+void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, const uint32_t* cut,
+                          uint32_t blocks, cudaStream_t s) {
   if (a.ntiles == 0) return;
   CPTC_REQUIRE(a.R % 8 == 0 && a.R <= 128, CPTC_E_UNSUP,
                "the TF32 tile path needs R a multiple of 8, <= 128");
   const int R = a.R;
-  const size_t smem = (size_t)kTileFloats * 4 + (size_t)16 * (R + 8) * 4 +
-                      (size_t)(2 * 16 * R + R) * 8;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // As many CTAs as the SMs hold at once (shared memory is the limit):
-  // each CTA walks its tiles one after another, so latency is hidden by the
-  // number of CTAs in flight.
-  int per_sm = (int)((228 * 1024) / (smem + 1024));
-  if (per_sm < 1) per_sm = 1;
-  if (per_sm > 16) per_sm = 16;
-  uint64_t blocks = (uint64_t)sms * per_sm;
-  if (blocks > a.ntiles) blocks = a.ntiles;
-  const uint64_t per = (a.ntiles + blocks - 1) / blocks;
-  blocks = (a.ntiles + per - 1) / per;
+  const size_t smem = tile_smem(R);
   const int NT = R / 8;
   const int ntm = NT <= 4 ? 1 : NT <= 8 ? 2 : NT <= 12 ? 3 : 4;
   const int roles = a.tslot * 100 + a.cslot * 10 + a.sslot;
@@ -488,7 +544,7 @@ void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, cudaStream_t
                                    (int)smem));                                            \
     CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,   \
                                    100));                                                  \
-    kern<<<(unsigned)blocks, 128, smem, s>>>(a, order, per);                               \
+    kern<<<blocks, 128, smem, s>>>(a, order, cut);                                         \
   } while (0)
 #define CPTC_TILES_R(TS_, CS_, SS_)          \
   do {                                       \

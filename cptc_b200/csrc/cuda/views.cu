@@ -93,12 +93,12 @@ __global__ void k_rows_from_pos(const uint32_t* __restrict__ pos, uint64_t nrows
     rows[k] = tsrc[perm[pos[k]]];
 }
 
-// task_row[k] = index of the last row start at or before element k*kTask.
+// task_row[k] = index of the last row start at or before element k*task.
 __global__ void k_task_rows(const uint32_t* __restrict__ pos, uint64_t nrows, uint64_t ntasks,
-                            uint32_t* __restrict__ task_row) {
+                            uint32_t task, uint32_t* __restrict__ task_row) {
   for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < ntasks;
        k += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t e0 = k * (uint64_t)kTask;
+    const uint64_t e0 = k * (uint64_t)task;
     uint64_t lo = 0, hi = nrows;  // first pos > e0
     while (lo < hi) {
       const uint64_t mid = (lo + hi) >> 1;
@@ -211,10 +211,11 @@ void build_view_order(Engine& E, View& v, int n, const int* order, int nother,
   k_rows_from_pos<<<grid_for(v.nrows, 256, 148 * 16), 256, 0, s>>>(pos.p, v.nrows, E.idx[n].p,
                                                                     perm_a.p, v.rows.p);
   CPTC_LAUNCH_CHECK();
-  v.ntasks = (nsel + kTask - 1) / kTask;
+  v.task = task_size_for(nsel);
+  v.ntasks = (nsel + v.task - 1) / v.task;
   v.task_row.alloc(v.ntasks);
   k_task_rows<<<grid_for(v.ntasks, 256, 148 * 16), 256, 0, s>>>(pos.p, v.nrows, v.ntasks,
-                                                                 v.task_row.p);
+                                                                 v.task, v.task_row.p);
   CPTC_LAUNCH_CHECK();
   if (v.nout == 1) {
     // Order 3: one 16-byte record per nonzero for the MTTKRP stream; the
