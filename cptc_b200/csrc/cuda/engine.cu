@@ -39,6 +39,12 @@ void gather_rows_host(const std::vector<double>& in, const std::vector<uint32_t>
 
 }  // namespace
 
+double b200_fill_min(int R) {
+  if (R <= 32) return 0.07;
+  if (R >= 128) return 0.04;
+  return 0.07 - 0.03 * (double)(R - 32) / 96.0;
+}
+
 Engine::Engine(int dev) : device(dev) {
   int n = 0;
   CPTC_CUDA(cudaGetDeviceCount(&n));
@@ -194,10 +200,13 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
     CPTC_CUDA(cudaStreamSynchronize(stream));
   }
 
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  fill_min = opts.fill_min > 0.0 ? opts.fill_min
-                                 : std::max(0.08, 0.11 / std::sqrt((double)sms / 24.0));
+  // Fill-rate selector re-derived on B200 (the reference's rule,
+  // max(0.08, 0.11/sqrt(SMs/24)) from src/main.cu:369-381, was calibrated on
+  // a 24-SM RTX 4060).  Measured per-tile cost a + b*nnz of the TF32 tile
+  // kernel against c*nnz of the FP64 kernel on configs 2-4 gives the
+  // break-even fill a / (4096 (c - b)): ~0.07 at R <= 32 falling to ~0.04 at
+  // R = 128 (table in DESIGN.md).
+  fill_min = opts.fill_min > 0.0 ? opts.fill_min : b200_fill_min(R);
 
   DArray<uint32_t> sel;
   uint64_t nsel = nnz;

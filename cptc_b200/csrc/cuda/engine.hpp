@@ -72,6 +72,9 @@ struct UnitPool {
   uint32_t blocks = 0;
 };
 
+// Default fill-rate threshold of the dense-tile path on B200 for rank R.
+double b200_fill_min(int R);
+
 struct Engine {
   int device = 0;
   cudaStream_t stream = nullptr;
