@@ -107,6 +107,9 @@ ENGINE_SYMBOLS = {
     "cptc_get_stats": (C.c_int, [C.c_void_p, C.POINTER(Stats)]),
     "cptc_fit_terms": (C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
     "cptc_get_relabel": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_uint32)]),
+    "cptc_residual_noalloc": (C.c_int, [C.c_int, C.c_uint64, C.POINTER(C.c_void_p), C.c_void_p,
+                                        C.c_int, C.POINTER(C.c_void_p), C.c_void_p, C.c_void_p,
+                                        C.c_void_p]),
     "cptc_residual": (C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
 }
 

@@ -33,6 +33,7 @@ CUDA_SRCS = [
     "cuda/als_kernels.cu",
     "cuda/comm.cu",
     "cuda/engine.cu",
+    "cuda/noalloc.cu",
 ]
 
 

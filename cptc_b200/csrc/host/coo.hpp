@@ -14,4 +14,7 @@ bool coo_alloc(cptc_coo* t, int order, uint64_t nnz);
 // Number of worker threads for host loops (CPTC_HOST_THREADS, else all cores).
 int host_threads();
 
+// Sets the thread-local message returned by cptc_host_last_error().
+void set_host_error(const char* msg);
+
 }  // namespace cptc

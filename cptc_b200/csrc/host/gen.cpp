@@ -27,6 +27,8 @@ static int host_fail(int code, const std::string& msg) {
   return code;
 }
 
+void set_host_error(const char* msg) { g_host_err = msg ? msg : ""; }
+
 int host_threads() {
   if (const char* e = std::getenv("CPTC_HOST_THREADS")) {
     const int n = std::atoi(e);

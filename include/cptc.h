@@ -168,6 +168,36 @@ int cptc_fit_terms(cptc_ctx* ctx, double out3[3]);
  * g_exact_residual_kernel (src/generic.cu:936-967). */
 int cptc_residual(cptc_ctx* ctx, double out2[2]);
 
+/* Residual sum of squares of a CP model against a sparse tensor,
+ *   d_out[0] = sum_e (v_e - sum_r lambda_r prod_m F_m[i_m(e), r])^2,
+ * computed on buffers the caller already holds on the current device,
+ * WITHOUT ALLOCATING: no cudaMalloc, no cudaFree, no allocating library
+ * routine.  It is for callers that cannot let a library allocate device
+ * memory: processes whose device memory belongs to their own pool or to a
+ * reservation made at start-up (a serving process that pre-allocates
+ * everything, a framework that permits no allocation outside its caching
+ * allocator), and tight loops that cannot afford the device-wide
+ * synchronisation a cudaFree implies.  It has no counterpart in the
+ * reference; cptc_residual is the allocating equivalent.
+ *   d_idx[m]     host array of `order` device pointers: u32 indices, nnz each
+ *   d_vals       device, nnz doubles
+ *   d_factors[m] host array of `order` device pointers: row-major I_m x R
+ *   d_lambda     device, R doubles;  d_out  device, 1 double (written)
+ *   stream       cudaStream_t on the current device (NULL = default stream)
+ * Limits: 1 <= order <= 8 and 1 <= R <= 128, else CPTC_E_UNSUP and a
+ * message in cptc_host_last_error(); nnz is unrestricted.  The per-block
+ * partial sums live in a fixed array inside the library, 2048 doubles
+ * (16 KiB) on every GPU that loads it, held until the process exits.  The
+ * first call on each device sets up that device's address of the array
+ * (cudaGetSymbolAddress, with the device current): make that first call
+ * before any stream capture.  All calls share the array, which keeps the
+ * last call's contents; each call writes every slot it later reads, so no
+ * clearing is needed.  Calls that overlap on the GPU (concurrent streams,
+ * or host threads sharing a device) race on the array: serialise them. */
+int cptc_residual_noalloc(int order, uint64_t nnz, const uint32_t* const* d_idx,
+                          const double* d_vals, int R, const double* const* d_factors,
+                          const double* d_lambda, double* d_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
