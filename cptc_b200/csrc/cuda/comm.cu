@@ -68,24 +68,13 @@ void comm_prepare(Engine& E) {
     CPTC_CUDA(cudaMemsetAsync(h.p, 0, E.dims[m] * sizeof(unsigned), E.stream));
     k_row_hist<<<grid_for(E.nnz, 256, 148 * 16), 256, 0, E.stream>>>(E.idx[m].p, E.nnz, h.p);
     CPTC_LAUNCH_CHECK();
-    std::vector<unsigned> hh(E.dims[m]);
+    std::vector<uint32_t> hh(E.dims[m]);
     CPTC_CUDA(cudaMemcpyAsync(hh.data(), h.p, E.dims[m] * sizeof(unsigned),
                               cudaMemcpyDeviceToHost, E.stream));
     CPTC_CUDA(cudaStreamSynchronize(E.stream));
-    // Cut at equal nonzero shares, rounded to a multiple of 16 rows.
     std::vector<uint64_t> cuts(E.nranks + 1, 0);
-    cuts[E.nranks] = E.dims[m];
-    uint64_t acc = 0, r = 1;
-    for (uint64_t i = 0; i < E.dims[m] && r < (uint64_t)E.nranks; ++i) {
-      acc += hh[i];
-      while (r < (uint64_t)E.nranks && acc * E.nranks >= r * E.nnz) {
-        uint64_t c = ((i + 1) + 15) / 16 * 16;
-        if (c > E.dims[m]) c = E.dims[m];
-        if (c < cuts[r - 1]) c = cuts[r - 1];
-        cuts[r++] = c;
-      }
-    }
-    for (; r < (uint64_t)E.nranks; ++r) cuts[r] = E.dims[m];
+    CPTC_REQUIRE(cptc_slab_cuts(hh.data(), E.dims[m], E.nnz, E.nranks, cuts.data()) == 0,
+                 CPTC_E_ARG, "slab cuts");
     E.slab[m] = cuts;
   }
 }

@@ -28,13 +28,32 @@ __global__ void k_relabel(uint32_t* __restrict__ idx, uint64_t n, const uint32_t
     idx[e] = map[idx[e]];
 }
 
-// Rows of a relabelled matrix back to original order: out[a] = in[map[a]].
-void gather_rows_host(const std::vector<double>& in, const std::vector<uint32_t>& map, int R,
-                      double* out) {
-  const int64_t n = (int64_t)map.size();
-#pragma omp parallel for schedule(static)
-  for (int64_t a = 0; a < n; ++a)
-    std::memcpy(out + a * R, in.data() + (uint64_t)map[a] * R, R * sizeof(double));
+// Row permutation between the caller's labels and the relabelled space,
+// on the device.  to_relabelled: out[map[a]] = in[a]; otherwise
+// out[a] = in[map[a]] (map[old] = new).  One thread per (row, column pair).
+__global__ void k_permute_rows(const double* __restrict__ in, const uint32_t* __restrict__ map,
+                               uint64_t rows, int R, int to_relabelled, double* __restrict__ out) {
+  const int h = R >> 1;  // R is even for every vector-width path; odd R uses h = 0
+  if (h > 0 && (R & 1) == 0) {
+    const uint64_t n = rows * (uint64_t)h;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < n;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+      const uint64_t a = e / h, c = e - a * h;
+      const uint64_t b = map[a];
+      const uint64_t src = to_relabelled ? a : b, dst = to_relabelled ? b : a;
+      reinterpret_cast<double2*>(out)[dst * h + c] =
+          reinterpret_cast<const double2*>(in)[src * h + c];
+    }
+  } else {
+    const uint64_t n = rows * (uint64_t)R;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < n;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+      const uint64_t a = e / R, c = e - a * R;
+      const uint64_t b = map[a];
+      const uint64_t src = to_relabelled ? a : b, dst = to_relabelled ? b : a;
+      out[dst * R + c] = in[src * R + c];
+    }
+  }
 }
 
 }  // namespace
@@ -140,10 +159,12 @@ void Engine::reorder() {
     perm.resize(N);
   }
   for (int m = 0; m < N; ++m) {
+    dperm[m].release();
     if (perm[m].empty()) continue;
-    DArray<uint32_t> map(dims[m]);
-    CPTC_CUDA(cudaMemcpyAsync(map.p, perm[m].data(), dims[m] * 4, cudaMemcpyHostToDevice, stream));
-    k_relabel<<<grid_for(nnz, 256, 148 * 16), 256, 0, stream>>>(idx[m].p, nnz, map.p);
+    dperm[m].alloc(dims[m]);
+    CPTC_CUDA(cudaMemcpyAsync(dperm[m].p, perm[m].data(), dims[m] * 4, cudaMemcpyHostToDevice,
+                              stream));
+    k_relabel<<<grid_for(nnz, 256, 148 * 16), 256, 0, stream>>>(idx[m].p, nnz, dperm[m].p);
     CPTC_LAUNCH_CHECK();
     CPTC_CUDA(cudaStreamSynchronize(stream));
   }
@@ -301,20 +322,39 @@ void Engine::init_factors() {
   grams_valid = false;
 }
 
+// Host factors in the caller's labels <-> device factors in relabelled rows.
+// The rows are permuted on the device (through `stage`), so a transfer is one
+// copy at PCIe speed (DMA when the caller's buffer is pinned).
+double* Engine::stage_rows() {
+  uint64_t maxd = 0;
+  for (int m = 0; m < N; ++m) maxd = std::max<uint64_t>(maxd, dims[m]);
+  if (stage.n < maxd * (uint64_t)R) stage.alloc(maxd * (uint64_t)R);
+  return stage.p;
+}
+
+void Engine::permute_rows(const double* in, int m, bool to_relabelled, double* out) {
+  const uint64_t n = dims[m] * (uint64_t)R;
+  k_permute_rows<<<grid_for(n / 2 + 1, 256, 148 * 16), 256, 0, stream>>>(
+      in, dperm[m].p, dims[m], R, to_relabelled ? 1 : 0, out);
+  CPTC_LAUNCH_CHECK();
+}
+
 void Engine::set_factor(int m, const double* host) {
   CPTC_REQUIRE(built && m >= 0 && m < N && host, CPTC_E_ARG, "bad mode or call order");
-  std::vector<double> h(dims[m] * (uint64_t)R);
-  for (uint64_t a = 0; a < dims[m]; ++a) {
-    const uint64_t nw = perm[m].empty() ? a : perm[m][a];
-    std::memcpy(h.data() + nw * R, host + a * R, R * sizeof(double));
+  const uint64_t bytes = dims[m] * (uint64_t)R * sizeof(double);
+  if (dperm[m].p) {
+    double* st = stage_rows();
+    CPTC_CUDA(cudaMemcpyAsync(st, host, bytes, cudaMemcpyHostToDevice, stream));
+    permute_rows(st, m, true, F[m].p);
+  } else {
+    CPTC_CUDA(cudaMemcpyAsync(F[m].p, host, bytes, cudaMemcpyHostToDevice, stream));
   }
-  CPTC_CUDA(cudaMemcpyAsync(F[m].p, h.data(), h.size() * 8, cudaMemcpyHostToDevice, stream));
-  CPTC_CUDA(cudaStreamSynchronize(stream));
   if (!have_factors) {
     std::vector<double> one(R, 1.0);
     CPTC_CUDA(cudaMemcpyAsync(lambda.p, one.data(), R * 8, cudaMemcpyHostToDevice, stream));
-    CPTC_CUDA(cudaStreamSynchronize(stream));
   }
+  // The caller may reuse `host` once this returns.
+  CPTC_CUDA(cudaStreamSynchronize(stream));
   have_factors = true;
   grams_valid = false;
 }
@@ -322,19 +362,19 @@ void Engine::set_factor(int m, const double* host) {
 void Engine::get_factor(int m, double* host) {
   CPTC_REQUIRE(built && have_factors && m >= 0 && m < N && host, CPTC_E_ARG,
                "bad mode or call order");
-  std::vector<double> h(dims[m] * (uint64_t)R);
-  CPTC_CUDA(cudaMemcpyAsync(h.data(), F[m].p, h.size() * 8, cudaMemcpyDeviceToHost, stream));
-  CPTC_CUDA(cudaStreamSynchronize(stream));
-  if (perm[m].empty()) std::memcpy(host, h.data(), h.size() * 8);
-  else gather_rows_host(h, perm[m], R, host);
+  fetch_rows(F[m].p, m, host);
 }
 
 void Engine::fetch_rows(const double* dev, int m, double* host) {
-  std::vector<double> h(dims[m] * (uint64_t)R);
-  CPTC_CUDA(cudaMemcpyAsync(h.data(), dev, h.size() * 8, cudaMemcpyDeviceToHost, stream));
+  const uint64_t bytes = dims[m] * (uint64_t)R * sizeof(double);
+  const double* src = dev;
+  if (dperm[m].p) {
+    double* st = stage_rows();
+    permute_rows(dev, m, false, st);
+    src = st;
+  }
+  CPTC_CUDA(cudaMemcpyAsync(host, src, bytes, cudaMemcpyDeviceToHost, stream));
   CPTC_CUDA(cudaStreamSynchronize(stream));
-  if (perm[m].empty()) std::memcpy(host, h.data(), h.size() * 8);
-  else gather_rows_host(h, perm[m], R, host);
 }
 
 // FtV = MTTKRP of `mode` (relabelled rows): zero, dense tiles, residual.
@@ -427,7 +467,6 @@ void Engine::update_mode(int n) {
   if (opts.solver == CPTC_SOLVER_CHOL) inv = kInvCholRidge;
   if (opts.solver == CPTC_SOLVER_PINV) inv = kInvPinv;
   launch_sym_inverse(FtF.p, R, inv, Ainv.p, status.p, stream);
-  comm_reduce_ftv(*this, n);
   const uint64_t lo = row_lo(n), rows = row_hi(n) - lo;
   const int nb = launch_apply_solve(FtV.p + lo * R, Ainv.p, lambda.p, generic ? 0 : 1, rows, R,
                                     F[n].p + lo * R, gpart.p, gpart_blocks, stream);
@@ -604,7 +643,9 @@ int cptc_get_factors(cptc_ctx* c, int mode, double* host) {
 int cptc_get_lambda(cptc_ctx* c, double* host) {
   return guarded(c, [&](Engine& e) {
     CPTC_REQUIRE(e.built && e.have_factors && host, CPTC_E_ARG, "no factors yet");
-    CPTC_CUDA(cudaMemcpy(host, e.lambda.p, e.R * sizeof(double), cudaMemcpyDeviceToHost));
+    CPTC_CUDA(cudaMemcpyAsync(host, e.lambda.p, e.R * sizeof(double), cudaMemcpyDeviceToHost,
+                              e.stream));
+    CPTC_CUDA(cudaStreamSynchronize(e.stream));
   });
 }
 

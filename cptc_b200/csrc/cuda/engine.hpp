@@ -90,6 +90,8 @@ struct Engine {
 
   // Relabelling: perm[m][old] = new (host); identity when empty.
   std::vector<std::vector<uint32_t>> perm;
+  DArray<uint32_t> dperm[CPTC_MAX_ORDER];  // device copy of perm (unset when identity)
+  DArray<double> stage;                    // max_m I_m x R rows for host transfers
   std::vector<std::vector<uint32_t>> host_idx;  // original coordinates
   std::string reorder_note;
 
@@ -135,6 +137,8 @@ struct Engine {
   void set_factor(int m, const double* host);
   void get_factor(int m, double* host);
   void fetch_rows(const double* dev, int m, double* host);
+  double* stage_rows();
+  void permute_rows(const double* in, int m, bool to_relabelled, double* out);
   void mttkrp(int mode);  // into FtV (relabelled rows), stream-ordered
   void mttkrp_tiles(int mode);   // dense-tile TF32 part only (accumulates)
   void mttkrp_sparse(int mode);  // FP64 view part only (accumulates)

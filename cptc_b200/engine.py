@@ -154,8 +154,14 @@ class Engine:
                                                F.ctypes.data_as(C.POINTER(C.c_double))),
                     "set_factors")
 
-    def factor(self, mode: int) -> np.ndarray:
-        out = np.empty((self._dims()[mode], self.R), dtype=np.float64)
+    def factor(self, mode: int, out: np.ndarray = None) -> np.ndarray:
+        """Factor `mode` in the tensor's own labels.  `out`, when given, is a
+        C-contiguous float64 (I_mode, R) array to fill (e.g. pinned memory)."""
+        shape = (self._dims()[mode], self.R)
+        if out is None:
+            out = np.empty(shape, dtype=np.float64)
+        elif out.shape != shape or out.dtype != np.float64 or not out.flags.c_contiguous:
+            raise ValueError(f"out must be a C-contiguous float64 array of shape {shape}")
         self._check(self._lib.cptc_get_factors(self._h, int(mode),
                                                out.ctypes.data_as(C.POINTER(C.c_double))),
                     "get_factors")
@@ -164,8 +170,11 @@ class Engine:
     def factors(self) -> list:
         return [self.factor(m) for m in range(len(self._dims()))]
 
-    def lam(self) -> np.ndarray:
-        out = np.empty(self.R, dtype=np.float64)
+    def lam(self, out: np.ndarray = None) -> np.ndarray:
+        if out is None:
+            out = np.empty(self.R, dtype=np.float64)
+        elif out.shape != (self.R,) or out.dtype != np.float64:
+            raise ValueError(f"out must be a float64 array of shape ({self.R},)")
         self._check(self._lib.cptc_get_lambda(self._h, out.ctypes.data_as(C.POINTER(C.c_double))),
                     "get_lambda")
         return out

@@ -1,0 +1,174 @@
+"""Worker code for the multi-rank tests (imported by spawned processes).
+
+`slab_als3` restates, with numpy on CPU ranks, what the engine does on G GPUs
+for the order-3 ALS: every rank keeps all factors, computes the MTTKRP rows of
+its own row slab (nonzeros selected by the slab of the target mode), solves
+them, all-reduces the partial Gram of its unnormalised rows (the column norms
+are its diagonal), normalises, and broadcasts its slab rows to the others.
+The fit all-reduces per-column dot products of the last mode.  Run with gloo
+it exercises the partition (cptc_slab_cuts, the same host function the engine
+calls) and the order and payload of the collectives on the host.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+
+import numpy as np
+
+
+def np_mttkrp(idx, vals, dims, F, n):
+    R = F[0].shape[1]
+    out = np.zeros((dims[n], R))
+    prod = np.repeat(vals[:, None], R, axis=1)
+    for m in range(len(dims)):
+        if m != n:
+            prod = prod * F[m][idx[m]]
+    np.add.at(out, idx[n], prod)
+    return out
+
+
+def truncated_pinv(A, R):
+    w, V = np.linalg.eigh(A)
+    tol = R * np.spacing(np.abs(w).max())
+    keep = np.abs(w) > tol
+    return (V[:, keep] / w[keep]) @ V[:, keep].T
+
+
+def slab_als3(t, R, iters, rank, world, dist):
+    """The engine's distributed order-3 ALS on `world` CPU ranks (see module doc)."""
+    import torch
+
+    import cptc_b200 as cp
+    from oracle import oracle as o
+
+    perm = [o.cadr_perm(t.dims[m], t.idx[m]) for m in range(3)]
+    idx = [perm[m][t.idx[m]].astype(np.int64) for m in range(3)]
+    relab = cp.CooTensor(t.dims, [i.astype(np.uint32) for i in idx], t.vals)
+    cuts = cp.mode_slabs(relab, world)
+    F = [f.copy() for f in o.init_factors3(t.dims, R)]
+    lam = np.ones(R)
+    G = [f.T @ f for f in F]
+    X2 = float(t.vals @ t.vals)
+    fits = []
+
+    def allreduce(x):
+        v = torch.from_numpy(np.ascontiguousarray(x))
+        dist.all_reduce(v)
+        return v.numpy()
+
+    for _ in range(iters):
+        for n in range(3):
+            p, q = [m for m in range(3) if m != n]
+            FtF = G[p] * G[q]
+            lo, hi = int(cuts[n][rank]), int(cuts[n][rank + 1])
+            mine = (idx[n] >= lo) & (idx[n] < hi)
+            M = np_mttkrp([i[mine] for i in idx], t.vals[mine], t.dims, F, n)
+            A = truncated_pinv(FtF, R)
+            Fl = M[lo:hi] @ A.T / lam
+            Gs = allreduce(Fl.T @ Fl)
+            nr = np.sqrt(np.diag(Gs))
+            zero = nr < 1e-14
+            scale = np.where(zero, 0.0, 1.0 / np.where(zero, 1.0, nr))
+            lam = np.where(zero, 0.0, lam * nr)
+            Fl = Fl * scale
+            G[n] = Gs * np.outer(scale, scale)
+            Fn = np.zeros((t.dims[n], R))
+            Fn[lo:hi] = Fl
+            # all-gather of the slab rows: one broadcast per owner
+            for r in range(world):
+                a, b = int(cuts[n][r]), int(cuts[n][r + 1])
+                if b > a:
+                    blk = torch.from_numpy(np.ascontiguousarray(Fn[a:b]))
+                    dist.broadcast(blk, src=r)
+                    Fn[a:b] = blk.numpy()
+            F[n] = Fn
+        lo, hi = int(cuts[2][rank]), int(cuts[2][rank + 1])
+        dots = allreduce(np.einsum("kr,kr->r", F[2][lo:hi], M[lo:hi]))
+        iprod = float(lam @ dots)
+        model2 = float(lam @ (G[0] * G[1] * G[2]) @ lam)
+        fits.append(1 - np.sqrt(max(X2 - 2 * iprod + model2, 0.0)) / np.sqrt(X2))
+    return np.array(fits), F, lam, cuts
+
+
+def cpu_worker(rank, world, port, spec, q):
+    """Entry point of one spawned gloo rank: runs slab_als3 and reports."""
+    import torch.distributed as dist
+
+    import cptc_b200 as cp
+
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        t = cp.gen_uniform(spec["dims"], spec["nnz"], seed=spec["seed"], values=spec["values"])
+        fits, F, lam, cuts = slab_als3(t, spec["R"], spec["iters"], rank, world, dist)
+        q.put((rank, fits, F, lam, [c.tolist() for c in cuts]))
+    except Exception as e:  # report instead of hanging the other ranks' test
+        q.put((rank, repr(e), None, None, None))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def gpu_main(argv=None):
+    """One torchrun rank of the engine's NCCL row-slab ALS; rank 0 writes
+    fits, lambda and factors (original labels) to --out as .npz."""
+    import argparse
+
+    import torch
+    import torch.distributed as dist
+
+    import cptc_b200 as cp
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", required=True)
+    ap.add_argument("--case", required=True)
+    a = ap.parse_args(argv)
+    spec = GPU_CASES[a.case]
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    try:
+        t = make_case(spec)
+        e = cp.Engine(local)
+        obj = [cp.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        e.comm_init(obj[0], rank, world)
+        e.load(t)
+        e.build(spec["R"], **spec["build"])
+        e.init_factors()
+        reps = e.als(spec["iters"])
+        st = e.stats()
+        F = e.factors()
+        lam = e.lam()
+        M0 = e.mttkrp(0)
+        dist.barrier()
+        if rank == 0:
+            np.savez(a.out, fits=np.array([r.fit for r in reps]), lam=lam, M0=M0,
+                     tf32=int(st["tf32_path"]), **{f"F{m}": f for m, f in enumerate(F)})
+        e.close()
+    finally:
+        dist.destroy_process_group()
+
+
+GPU_CASES = {
+    "fp64_o3": dict(gen=("uniform", (600, 500, 400), 400_000, 3, "lognormal"), R=16, iters=4,
+                    build=dict(path="fp64")),
+    "hybrid_o3": dict(gen=("config", 4, 0.05, 0), R=32, iters=3, build=dict(path="tf32")),
+    "generic_o4": dict(gen=("config", 5, 0.2, 0), R=16, iters=3, build=dict(generic=True)),
+}
+
+
+def make_case(spec):
+    import cptc_b200 as cp
+
+    g = spec["gen"]
+    if g[0] == "uniform":
+        return cp.gen_uniform(g[1], g[2], seed=g[3], values=g[4])
+    return cp.gen_config(g[1], scale=g[2], seed=g[3])
+
+
+if __name__ == "__main__":
+    gpu_main()
