@@ -47,6 +47,7 @@ def parse_args():
     p.add_argument("--threshold", type=float, default=0.03)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--keep-tns", default="", help="reference arm: keep the .tns it writes here")
+    p.add_argument("--ref-log", default="", help="reference arm: save cpTC's stdout here")
     return p.parse_args()
 
 
@@ -162,6 +163,14 @@ def algorithmic_bytes(nnz: int, order: int, R: int, rows: int) -> int:
     N-1 indices and N-1 gathered factor rows per nonzero, output written
     once."""
     return nnz * (8 + 4 * (order - 1) + 8 * R * (order - 1)) + 8 * R * rows
+
+
+def tile_tflops(st, R: int, tile_ms) -> float | None:
+    """TF32 MMA rate of the dense-tile kernel: 8192*R flops per tile per mode."""
+    ms = float(np.mean(tile_ms)) if len(tile_ms) else 0.0
+    if not st["tf32_path"] or ms <= 0.0:
+        return None
+    return st["dense_tiles"] * 8192.0 * R / (ms / 1000.0) / 1e12
 
 
 def measured_peaks() -> dict:
@@ -289,12 +298,16 @@ def run_engine(a):
 
     sp = [p["sparse_ms"] for p in prof]
     tl = [p["tiles_ms"] for p in prof]
-    dominant = "k_mttkrp_view (FP64 sparse MTTKRP)"
+    dominant = "k_mttkrp_rec3" if t.order == 3 else "k_mttkrp_view"
     nnz_view = st["sparse_nnz"]
-    algo = sum(algorithmic_bytes(nnz_view, t.order, a.rank, t.dims[n]) for n in range(t.order))
-    ktime = sum(sp) / 1000.0
+    # Per launch (one mode): bytes as SURVEY 8(d) counts them (every factor-row
+    # gather) and the compulsory bytes (each stored byte once).
+    algo = [algorithmic_bytes(nnz_view, t.order, a.rank, t.dims[n]) for n in range(t.order)]
+    comp = 16 * nnz_view + 8 * a.rank * sum(t.dims)
+    algo_launch = float(np.mean(algo))
+    ktime = float(np.mean(sp)) / 1000.0
     peaks = measured_peaks()
-    achieved = algo / ktime / 1e9 if ktime > 0 else None
+    achieved = algo_launch / ktime / 1e9 if ktime > 0 else None
     traffic = None
     prof_file = ROOT / "profiles" / "traffic.json"
     if prof_file.exists():
@@ -302,6 +315,8 @@ def run_engine(a):
             traffic = json.loads(prof_file.read_text()).get(f"cfg{a.config}_R{a.rank}")
         except Exception:
             traffic = None
+        if traffic is not None and a.scale != 1.0:
+            traffic = None  # recorded for the full-size workload only
 
     value = dev_s / a.steps
     line = {
@@ -345,9 +360,15 @@ def run_engine(a):
             "frac": (achieved / peaks["hbm_gbs"]) if achieved else None,
             "peak_src": peaks["src"],
             "traffic": traffic,
-            "algorithmic_bytes_per_iter": algo,
+            "algorithmic_bytes_per_launch": algo_launch,
+            "bytes_note": "algorithmic bytes count every factor-row gather (SURVEY 8(d)); "
+                          "most gathers hit L1/L2, so frac can exceed 1; compulsory_frac "
+                          "counts each stored byte once",
+            "compulsory_bytes_per_launch": comp,
+            "compulsory_frac": (comp / ktime / 1e9 / peaks["hbm_gbs"]) if ktime > 0 else None,
             "sparse_kernel_ms_per_mode": sp,
             "tile_kernel_ms_per_mode": tl,
+            "tile_tflops": tile_tflops(st, a.rank, tl),
         },
     }
     if not a.no_cpu_baseline:
@@ -395,6 +416,8 @@ def run_reference(a):
         r = subprocess.run([str(binary), str(tns), str(iters), str(a.rank), str(a.threshold)],
                            capture_output=True, text=True, env=env, timeout=1800)
         out = r.stdout
+    if a.ref_log:
+        Path(a.ref_log).write_text(out + "\n--- stderr ---\n" + r.stderr)
     if r.returncode != 0:
         print(json.dumps({"impl": "reference", "unavailable":
                           f"cpTC exited {r.returncode}: {r.stderr.strip()[-200:]}"}))
@@ -414,10 +437,11 @@ def run_reference(a):
             "dtype": "f64+tf32", "data": "synthetic (same generator and seed)",
             "config": {"workload": workload_name(a), "rank": a.rank, "nnz": t.nnz,
                        "selector_line": selector[:300], "final_fit": fits[-1] if fits else None},
-            "cpu_baseline": {"kind": "reference", "cores": 0, "value": v, "unit": UNIT,
+            "cpu_baseline": {"kind": "reference", "cores": 1, "value": v, "unit": UNIT,
                              "sample": "zhixianzhu/cpTC sources rebuilt for sm_100a "
-                                       "(oracle/build_ref.sh), per-iteration time it prints "
-                                       "([ALS] iter ... time=), after warm-up"},
+                                       "(oracle/build_ref.sh), one host thread driving one "
+                                       "B200; mean of the per-iteration times it prints "
+                                       "([ALS] iter ... time=) after the warm-up iterations"},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

@@ -14,7 +14,8 @@
 //  * the view is sorted by (target, outer modes, gathered mode): along a
 //    fiber of equal outer indices the outer rows are loaded once and the
 //    fiber sum  sum_e v_e F_g[g_e]  is multiplied by them at the fiber end,
-//    so ~1/fiber-length of the second gather disappears;
+//    so ~1/fiber-length of the second gather disappears (N-order kernel,
+//    and the order-3 record kernel at R >= 64 where it measures faster);
 //  * element words/values are streamed with evict-first loads so the factor
 //    matrices stay resident in L1/L2; gathers of U elements are issued
 //    before any of them is consumed;
@@ -287,6 +288,132 @@ __global__ void __launch_bounds__(256) k_mttkrp_rec3(const uint4* __restrict__ r
   write_row(began && ends);
 }
 
+// Order 3 with fiber reuse: the view is sorted by (target, outer, gathered),
+// so consecutive nonzeros of one fiber share the outer factor row.  The
+// outer row is loaded only for a fiber's first nonzero (the load is still
+// issued with the batch, predicated on the fiber flag) and the fiber sum
+// sum_e v_e F_g[g_e, r] is multiplied by it once, at the fiber's end:
+// acc += (sum_e v_e F_g[g_e, r]) * F_o[o, r].  On config 4 fibers hold 4.4 to
+// 5.8 nonzeros, so ~40% of the factor-row requests disappear.  MINB is the
+// minimum resident CTAs per SM asked of the register allocator.
+template <int GW, int RPL, bool VEC, int U, int MINB>
+__global__ void __launch_bounds__(256, MINB) k_mttkrp_rec3f(const uint4* __restrict__ rec,
+                                                           const uint32_t* __restrict__ rows,
+                                                           const uint32_t* __restrict__ task_row,
+                                                           uint64_t nnz, uint64_t ntasks,
+                                                           uint32_t tsize, int R,
+                                                           const double* __restrict__ Fg,
+                                                           const double* __restrict__ Fo,
+                                                           double* __restrict__ out) {
+  constexpr int GPW = 32 / GW;
+  const int lane = threadIdx.x & 31;
+  const int glane = lane % GW;
+  const uint64_t task =
+      ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + lane / GW;
+  if (task >= ntasks) return;
+  const Lanes<GW, RPL, VEC> L(glane, R);
+  const uint64_t p0 = task * (uint64_t)tsize;
+  const uint64_t p1 = (p0 + tsize < nnz) ? p0 + tsize : nnz;
+
+  uint32_t rowi = task_row[task];
+  uint32_t row = rows[rowi];
+  bool began = (rec[p0].x & kRowFlag) != 0;
+  const bool ends = (p1 == nnz) || (rec[p1].x & kRowFlag);
+
+  double acc[RPL], fs[RPL], fo[RPL];
+#pragma unroll
+  for (int k = 0; k < RPL; ++k) acc[k] = fs[k] = fo[k] = 0.0;
+  auto write_row = [&](bool owned) {
+    double* dst = out + (uint64_t)row * (uint64_t)R;
+#pragma unroll
+    for (int k = 0; k < RPL; ++k) {
+      if (!L.ok[k]) continue;
+      if (owned) dst[L.r[k]] += acc[k];
+      else atomicAdd(dst + L.r[k], acc[k]);
+      acc[k] = 0.0;
+    }
+  };
+  // Nonzero e with gathered row g; f holds the outer row when e opens a fiber.
+  auto step = [&](const uint4& e, const double (&g)[RPL], const double (&f)[RPL], bool first) {
+    if (((e.x & kFibFlag) != 0) && !first) {
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) {
+        acc[k] = fma(fs[k], fo[k], acc[k]);
+        fs[k] = 0.0;
+      }
+      if (e.x & kRowFlag) {
+        write_row(began);
+        row = rows[++rowi];
+        began = true;
+      }
+    }
+    if (((e.x & kFibFlag) != 0) || first) {
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) fo[k] = f[k];
+    }
+    const double v = __hiloint2double((int)e.w, (int)e.z);
+#pragma unroll
+    for (int k = 0; k < RPL; ++k) fs[k] = fma(v, g[k], fs[k]);
+  };
+
+  uint64_t p = p0;
+  const uint64_t pfull = p0 + ((p1 - p0) / U) * U;
+  uint4 cur[U];
+  if (p < pfull) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) cur[u] = __ldcs(rec + p + u);
+  }
+#pragma unroll 1
+  for (; p < pfull; p += U) {
+    double g[U][RPL], f[U][RPL];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      load_row<GW, RPL, VEC>(Fg, cur[u].x & kIdxMask, R, glane, L, g[u]);
+      if ((cur[u].x & kFibFlag) || p + u == p0) {
+        load_row<GW, RPL, VEC>(Fo, cur[u].y, R, glane, L, f[u]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < RPL; ++k) f[u][k] = 0.0;
+      }
+    }
+    uint4 nxt[U];
+    if (p + U < pfull) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) nxt[u] = __ldcs(rec + p + U + u);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) step(cur[u], g[u], f[u], p + u == p0);
+#pragma unroll
+    for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+  }
+  for (; p < p1; ++p) {  // tail of fewer than U nonzeros
+    const uint4 e = __ldcs(rec + p);
+    double g[RPL], f[RPL];
+    load_row<GW, RPL, VEC>(Fg, e.x & kIdxMask, R, glane, L, g);
+    if ((e.x & kFibFlag) || p == p0) {
+      load_row<GW, RPL, VEC>(Fo, e.y, R, glane, L, f);
+    } else {
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) f[k] = 0.0;
+    }
+    step(e, g, f, p == p0);
+  }
+#pragma unroll
+  for (int k = 0; k < RPL; ++k) acc[k] = fma(fs[k], fo[k], acc[k]);
+  write_row(began && ends);
+}
+
+template <int GW, int RPL, bool VEC, int U, int MINB>
+void launch_rec3f(const MttkrpArgs& a, cudaStream_t s) {
+  constexpr int GPW = 32 / GW;
+  const uint64_t warps = (a.ntasks + GPW - 1) / GPW;
+  const unsigned blocks = (unsigned)((warps + 7) / 8);
+  k_mttkrp_rec3f<GW, RPL, VEC, U, MINB><<<blocks, 256, 0, s>>>(a.rec, a.rows, a.task_row, a.nnz,
+                                                                a.ntasks, a.task, a.R, a.Fg,
+                                                                a.Fo[0], a.out);
+  CPTC_LAUNCH_CHECK();
+}
+
 template <int GW, int RPL, bool VEC, int U>
 void launch_rec3(const MttkrpArgs& a, cudaStream_t s) {
   constexpr int GPW = 32 / GW;
@@ -312,29 +439,19 @@ void launch(const MttkrpArgs& a, cudaStream_t s) {
 void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
   if (a.nnz == 0 || a.ntasks == 0) return;
   if (a.rec != nullptr) {
-    // Order 3: group width x ranks per lane, U nonzeros in flight per group
-    // (CPTC_REC3_U overrides U for tuning: 1, 2 or 4).
-    static const int tuneU = [] {
-      const char* e = std::getenv("CPTC_REC3_U");
-      return e ? std::atoi(e) : 0;
-    }();
-#define CPTC_REC3(GW_, RPL_, UDEF)                                          \
-  do {                                                                      \
-    const int u_ = tuneU ? tuneU : (UDEF);                                  \
-    if (u_ == 1) launch_rec3<GW_, RPL_, true, 1>(a, s);                     \
-    else if (u_ == 4) launch_rec3<GW_, RPL_, true, 4>(a, s);                \
-    else launch_rec3<GW_, RPL_, true, 2>(a, s);                             \
-    return;                                                                 \
-  } while (0)
+    // Record-kernel variant per rank, measured on config 4 (B200, ms per
+    // mode of the FP64 residual): R=32 plain 1.11 vs fiber reuse 1.27-2.04
+    // (the kernel is latency-bound there and fiber reuse costs registers,
+    // hence resident warps); R=64 fiber 2.28 vs plain 2.74; R=128 fiber with
+    // one nonzero in flight per warp 3.80 vs plain 5.00.
     switch (a.R) {
-      case 8: CPTC_REC3(8, 1, 4);
-      case 16: CPTC_REC3(8, 2, 4);
-      case 32: CPTC_REC3(16, 2, 2);
-      case 64: CPTC_REC3(16, 4, 2);
-      case 128: CPTC_REC3(32, 4, 2);
+      case 8: launch_rec3<8, 1, true, 4>(a, s); return;
+      case 16: launch_rec3<8, 2, true, 4>(a, s); return;
+      case 32: launch_rec3<16, 2, true, 2>(a, s); return;
+      case 64: launch_rec3f<16, 4, true, 2, 1>(a, s); return;
+      case 128: launch_rec3f<32, 4, true, 1, 1>(a, s); return;
       default: break;
     }
-#undef CPTC_REC3
     if (a.R <= 32) launch_rec3<32, 1, false, 4>(a, s);
     else if (a.R <= 64) launch_rec3<32, 2, false, 2>(a, s);
     else if (a.R <= 128) launch_rec3<32, 4, false, 2>(a, s);
