@@ -5,8 +5,7 @@ sm_100a CUDA behind a C ABI (include/cptc.h), with this package as the
 Python face.  Native libraries are built in-tree by ``python -m
 cptc_b200.build``.
 """
-from .tensor import (CooTensor, gen_config, gen_uniform, mode_slabs, probe_order, read_tns,
-                     slab_cuts, write_tns)
+from .tensor import CooTensor, gen_config, gen_uniform, probe_order, read_tns, write_tns
 from .engine import CptcError, Engine, IterReport, comm_unique_id
 
 __all__ = [
@@ -14,12 +13,10 @@ __all__ = [
     "CptcError",
     "Engine",
     "IterReport",
-    "mode_slabs",
     "comm_unique_id",
     "gen_config",
     "gen_uniform",
     "probe_order",
     "read_tns",
-    "slab_cuts",
     "write_tns",
 ]

@@ -84,8 +84,6 @@ HOST_SYMBOLS = {
     "cptc_gen_uniform": (C.c_int, [C.c_int, C.POINTER(C.c_uint64), C.c_uint64, C.c_uint64,
                                    C.c_int, C.POINTER(Coo)]),
     "cptc_host_last_error": (C.c_char_p, []),
-    "cptc_slab_cuts": (C.c_int, [C.POINTER(C.c_uint32), C.c_uint64, C.c_uint64, C.c_int,
-                                 C.POINTER(C.c_uint64)]),
 }
 
 ENGINE_SYMBOLS = {

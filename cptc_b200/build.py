@@ -24,7 +24,7 @@ LIB = PKG / "_lib"
 OBJ = PKG / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-HOST_SRCS = ["host/gen.cpp", "host/tns.cpp", "host/reorder.cpp", "host/slab.cpp"]
+HOST_SRCS = ["host/gen.cpp", "host/tns.cpp", "host/reorder.cpp"]
 CUDA_SRCS = [
     "cuda/views.cu",
     "cuda/mttkrp_sparse.cu",

@@ -1,17 +1,25 @@
-// Multi-GPU plumbing of the engine: one process per GPU, mode-n rows split
-// into contiguous slabs of equal nonzero count, NCCL over NVLink for the two
-// collectives of a mode update (Gram all-reduce, factor all-gather).
+// Multi-GPU plumbing of the engine: one process per GPU, NCCL over NVLink.
+//
+// Work and ownership are split separately.  The nonzeros of every mode are
+// shared out by count: each rank walks an equal range of the view's
+// nonzero-balanced tasks and an equal-weight range of the dense tiles, so a
+// Zipf head row (or a 16-row block holding half of all nonzeros) is spread
+// over all ranks.  Rows are owned in equal-size slabs: after the MTTKRP the
+// partial results are reduce-scattered into the slabs, each rank solves and
+// normalises its slab (Gram partials all-reduced), and the slabs are
+// all-gathered into every rank's replica of the factor.
 #pragma once
 #include "engine.hpp"
 
 namespace cptc {
 
-// Computes the row slabs of every mode for this rank (single rank: whole
-// modes).  Slab cuts are multiples of 16 so dense tiles have one owner.
+// Row slabs of every mode (single rank: whole modes).
 void comm_prepare(Engine& E);
 void comm_destroy(Engine& E);
 void comm_init(Engine& E, const unsigned char id[128], int rank, int nranks);
 int comm_unique_id(unsigned char out[128]);
+// Rows per slab of mode m (slab r = rows [r * s, min((r + 1) * s, I_m))).
+uint64_t slab_rows(const Engine& E, int m);
 
 // Sum of the per-block Gram partials over blocks and ranks into gpart[0];
 // returns the number of partial blocks left for launch_norm_finalize.
@@ -19,13 +27,11 @@ void comm_allreduce_gram(Engine& E, int nblk);
 int comm_gram_blocks(const Engine& E, int nblk);
 void comm_allreduce_dots(Engine& E, int nblk);
 int comm_dot_blocks(const Engine& E, int nblk);
-// Every rank's slab of F[n] (or FtV) to every rank.
+// Partial MTTKRP rows of every rank summed into each rank's slab of FtV.
+void comm_reduce_scatter_ftv(Engine& E, int n);
+// Every rank's slab of F[n] to every rank (in place).
 void comm_allgather_factor(Engine& E, int n);
+// The full reduced FtV on every rank (reduce-scatter + all-gather).
 void comm_reduce_ftv(Engine& E, int n);
-// Elements of `base` (all when null) whose mode-n index lies in this rank's
-// slab; and the per-mode tile lists restricted to this rank's row blocks.
-void slab_select(Engine& E, int n, const uint32_t* base, uint64_t nbase, DArray<uint32_t>& out,
-                 uint64_t& nout);
-void slab_tiles(Engine& E);
 
 }  // namespace cptc

@@ -170,9 +170,15 @@ void Engine::reorder() {
   }
 }
 
+// Factor-shaped buffers hold nranks equal slabs (padding rows past I_m are
+// never read as factor rows); FtV is shared by all modes.
+uint64_t Engine::padded_rows(int m) const {
+  return nranks > 1 ? slab_rows(*this, m) * (uint64_t)nranks : dims[m];
+}
+
 void Engine::alloc_workspace() {
   uint64_t maxd = 0;
-  for (int m = 0; m < N; ++m) maxd = std::max<uint64_t>(maxd, dims[m]);
+  for (int m = 0; m < N; ++m) maxd = std::max<uint64_t>(maxd, padded_rows(m));
   FtV.alloc(maxd * (uint64_t)R);
   FtF.alloc((uint64_t)R * R);
   Ainv.alloc(2 * (uint64_t)R * R + 1);
@@ -183,7 +189,8 @@ void Engine::alloc_workspace() {
   status.alloc(1);
   lambda.alloc(R);
   for (int m = 0; m < N; ++m) {
-    F[m].alloc(dims[m] * (uint64_t)R);
+    F[m].alloc(padded_rows(m) * (uint64_t)R);
+    CPTC_CUDA(cudaMemsetAsync(F[m].p, 0, padded_rows(m) * (uint64_t)R * sizeof(double), stream));
     G[m].alloc((uint64_t)R * R);
   }
 }
@@ -254,9 +261,9 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
   }
   dense_active = tf32;
   views.resize(N);
-  alloc_workspace();
   comm_prepare(*this);
-  slab_tiles(*this);
+  alloc_workspace();
+  for (int t = 0; t < 3; ++t) units.cnt[t] = units.nunits;
   if (dense_active) {
     units.blocks = tile_blocks_for(R, device);
     for (int t = 0; t < 3; ++t) tile_cuts(*this, t);
@@ -267,14 +274,11 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
                          (n == units.inner[0] || n == units.inner[1] || n == units.inner[2]);
     const uint32_t* base = covered ? sel.p : nullptr;
     const uint64_t nbase = covered ? nsel : nnz;
-    if (nranks > 1) {
-      DArray<uint32_t> mine;
-      uint64_t nmine = 0;
-      slab_select(*this, n, base, nbase, mine, nmine);
-      build_view(*this, views[n], n, mine.p, nmine);
-    } else {
-      build_view(*this, views[n], n, base, nbase);
-    }
+    build_view(*this, views[n], n, base, nbase);
+    // This rank's share: an equal range of the nonzero-balanced tasks.
+    View& v = views[n];
+    v.t0 = v.ntasks * (uint64_t)rank / (uint64_t)nranks;
+    v.t1 = v.ntasks * (uint64_t)(rank + 1) / (uint64_t)nranks;
   }
   CPTC_CUDA(cudaStreamSynchronize(stream));
   build_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
@@ -379,7 +383,7 @@ void Engine::fetch_rows(const double* dev, int m, double* host) {
 
 // FtV = MTTKRP of `mode` (relabelled rows): zero, dense tiles, residual.
 void Engine::mttkrp(int mode) {
-  CPTC_CUDA(cudaMemsetAsync(FtV.p, 0, dims[mode] * (uint64_t)R * sizeof(double), stream));
+  CPTC_CUDA(cudaMemsetAsync(FtV.p, 0, padded_rows(mode) * (uint64_t)R * sizeof(double), stream));
   mttkrp_tiles(mode);
   mttkrp_sparse(mode);
 }
@@ -417,7 +421,8 @@ void Engine::mttkrp_tiles(int mode) {
   for (int q = 0; q < units.nouter; ++q) ta.Fout[q] = F[units.outer[q]].p;
   ta.store_dups = units.store_dups ? 1 : 0;
   ta.out = FtV.p;
-  launch_mttkrp_tiles3(ta, units.order[ts].p, units.cut[ts].p, units.blocks, stream);
+  launch_mttkrp_tiles3(ta, units.order[ts].p, units.cut[ts].p + (uint64_t)rank * units.blocks,
+                       units.blocks, stream);
 }
 
 void Engine::mttkrp_sparse(int mode) {
@@ -430,7 +435,8 @@ void Engine::mttkrp_sparse(int mode) {
   a.rows = v.rows.p;
   a.task_row = v.task_row.p;
   a.nnz = v.nnz;
-  a.ntasks = v.ntasks;
+  a.task0 = v.t0;
+  a.ntasks = v.t1;
   a.task = v.task;
   a.nout = v.nout;
   a.R = R;
@@ -459,6 +465,7 @@ void Engine::update_mode(int n) {
   cudaEventRecord(ev[2 * n], stream);
   mttkrp(n);
   cudaEventRecord(ev[2 * n + 1], stream);
+  comm_reduce_scatter_ftv(*this, n);
   // Order 3: the reference solves with a truncated SVD pseudo-inverse; by
   // default the same result is obtained by Cholesky when FtF is well
   // conditioned (the pseudo-inverse kernel runs only when it is not).

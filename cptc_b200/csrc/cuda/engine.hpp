@@ -47,6 +47,7 @@ struct View {
   DArray<uint32_t> task_row;     // index into `rows` of each task's first row
   uint64_t nrows = 0, ntasks = 0;
   uint32_t task = kTask;         // nonzeros per task
+  uint64_t t0 = 0, t1 = 0;       // tasks [t0, t1) are this rank's share
 };
 
 // Dense 16^3 tiles: order 3 (inner = modes 0,1,2, no outer modes) or the
@@ -65,9 +66,10 @@ struct UnitPool {
   DArray<uint16_t> lid;        // (l0 << 8) | (l1 << 4) | l2
   DArray<double> val;
   DArray<uint32_t> order[3];   // visiting order per inner target slot
-  uint64_t cnt[3] = {0, 0, 0}; // tiles of this rank per inner target slot
-  // CTA ranges over each visiting order with balanced nonzero counts
-  // (blocks + 1 cut points), computed for `blocks` CTAs at build time.
+  uint64_t cnt[3] = {0, 0, 0}; // tiles per inner target slot
+  // CTA ranges over each visiting order with balanced nonzero counts:
+  // nranks * blocks + 1 cut points; rank r launches `blocks` CTAs on
+  // cut[r * blocks .. (r + 1) * blocks].
   DArray<uint32_t> cut[3];
   uint32_t blocks = 0;
 };
@@ -138,6 +140,7 @@ struct Engine {
   void get_factor(int m, double* host);
   void fetch_rows(const double* dev, int m, double* host);
   double* stage_rows();
+  uint64_t padded_rows(int m) const;
   void permute_rows(const double* in, int m, bool to_relabelled, double* out);
   void mttkrp(int mode);  // into FtV (relabelled rows), stream-ordered
   void mttkrp_tiles(int mode);   // dense-tile TF32 part only (accumulates)

@@ -15,7 +15,8 @@ struct MttkrpArgs {
   const double* val;
   const uint32_t* rows;
   const uint32_t* task_row;
-  uint64_t nnz, ntasks;
+  uint64_t nnz;
+  uint64_t task0, ntasks;  // this launch walks tasks [task0, ntasks)
   uint32_t task;
   int nout, R;
   const double* Fg;

@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(256, 2) k_mttkrp_view(MttkrpArgs a) {
   const int gid = lane / GW;
   const unsigned gmask = (GW == 32) ? 0xffffffffu : (((1u << GW) - 1u) << (gid * GW));
   const uint64_t task =
-      ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + gid;
+      a.task0 + ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + gid;
   if (task >= a.ntasks) return;
   const int R = a.R;
   const Lanes<GW, RPL, VEC> L(glane, R);
@@ -209,7 +209,8 @@ template <int GW, int RPL, bool VEC, int U>
 __global__ void __launch_bounds__(256) k_mttkrp_rec3(const uint4* __restrict__ rec,
                                                      const uint32_t* __restrict__ rows,
                                                      const uint32_t* __restrict__ task_row,
-                                                     uint64_t nnz, uint64_t ntasks,
+                                                     uint64_t nnz, uint64_t task0,
+                                                     uint64_t ntasks,
                                                      uint32_t tsize, int R,
                                                      const double* __restrict__ Fg,
                                                      const double* __restrict__ Fo,
@@ -218,7 +219,7 @@ __global__ void __launch_bounds__(256) k_mttkrp_rec3(const uint4* __restrict__ r
   const int lane = threadIdx.x & 31;
   const int glane = lane % GW;
   const uint64_t task =
-      ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + lane / GW;
+      task0 + ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + lane / GW;
   if (task >= ntasks) return;
   const Lanes<GW, RPL, VEC> L(glane, R);
   const uint64_t p0 = task * (uint64_t)tsize;
@@ -300,7 +301,8 @@ template <int GW, int RPL, bool VEC, int U, int MINB>
 __global__ void __launch_bounds__(256, MINB) k_mttkrp_rec3f(const uint4* __restrict__ rec,
                                                            const uint32_t* __restrict__ rows,
                                                            const uint32_t* __restrict__ task_row,
-                                                           uint64_t nnz, uint64_t ntasks,
+                                                           uint64_t nnz, uint64_t task0,
+                                                           uint64_t ntasks,
                                                            uint32_t tsize, int R,
                                                            const double* __restrict__ Fg,
                                                            const double* __restrict__ Fo,
@@ -309,7 +311,7 @@ __global__ void __launch_bounds__(256, MINB) k_mttkrp_rec3f(const uint4* __restr
   const int lane = threadIdx.x & 31;
   const int glane = lane % GW;
   const uint64_t task =
-      ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + lane / GW;
+      task0 + ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + lane / GW;
   if (task >= ntasks) return;
   const Lanes<GW, RPL, VEC> L(glane, R);
   const uint64_t p0 = task * (uint64_t)tsize;
@@ -406,10 +408,11 @@ __global__ void __launch_bounds__(256, MINB) k_mttkrp_rec3f(const uint4* __restr
 template <int GW, int RPL, bool VEC, int U, int MINB>
 void launch_rec3f(const MttkrpArgs& a, cudaStream_t s) {
   constexpr int GPW = 32 / GW;
-  const uint64_t warps = (a.ntasks + GPW - 1) / GPW;
+  const uint64_t warps = (a.ntasks - a.task0 + GPW - 1) / GPW;
   const unsigned blocks = (unsigned)((warps + 7) / 8);
   k_mttkrp_rec3f<GW, RPL, VEC, U, MINB><<<blocks, 256, 0, s>>>(a.rec, a.rows, a.task_row, a.nnz,
-                                                                a.ntasks, a.task, a.R, a.Fg,
+                                                                a.task0, a.ntasks, a.task, a.R,
+                                                                a.Fg,
                                                                 a.Fo[0], a.out);
   CPTC_LAUNCH_CHECK();
 }
@@ -417,18 +420,18 @@ void launch_rec3f(const MttkrpArgs& a, cudaStream_t s) {
 template <int GW, int RPL, bool VEC, int U>
 void launch_rec3(const MttkrpArgs& a, cudaStream_t s) {
   constexpr int GPW = 32 / GW;
-  const uint64_t warps = (a.ntasks + GPW - 1) / GPW;
+  const uint64_t warps = (a.ntasks - a.task0 + GPW - 1) / GPW;
   const unsigned blocks = (unsigned)((warps + 7) / 8);
   k_mttkrp_rec3<GW, RPL, VEC, U><<<blocks, 256, 0, s>>>(a.rec, a.rows, a.task_row, a.nnz,
-                                                         a.ntasks, a.task, a.R, a.Fg, a.Fo[0],
-                                                         a.out);
+                                                         a.task0, a.ntasks, a.task, a.R, a.Fg,
+                                                         a.Fo[0], a.out);
   CPTC_LAUNCH_CHECK();
 }
 
 template <int GW, int RPL, bool VEC, int U>
 void launch(const MttkrpArgs& a, cudaStream_t s) {
   constexpr int GPW = 32 / GW;
-  const uint64_t warps = (a.ntasks + GPW - 1) / GPW;
+  const uint64_t warps = (a.ntasks - a.task0 + GPW - 1) / GPW;
   const unsigned blocks = (unsigned)((warps + 7) / 8);
   k_mttkrp_view<GW, RPL, VEC, U><<<blocks, 256, 0, s>>>(a);
   CPTC_LAUNCH_CHECK();
@@ -437,7 +440,7 @@ void launch(const MttkrpArgs& a, cudaStream_t s) {
 }  // namespace
 
 void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
-  if (a.nnz == 0 || a.ntasks == 0) return;
+  if (a.nnz == 0 || a.ntasks <= a.task0) return;
   if (a.rec != nullptr) {
     // Record-kernel variant per rank, measured on config 4 (B200, ms per
     // mode of the FP64 residual): R=32 plain 1.11 vs fiber reuse 1.27-2.04

@@ -508,9 +508,12 @@ uint32_t tile_blocks_for(int R, int device) {
 void tile_cuts(Engine& E, int slot) {
   UnitPool& U = E.units;
   const uint64_t n = U.cnt[slot];
-  U.cut[slot].alloc((uint64_t)U.blocks + 1);
+  // One set of `blocks` CTA ranges per rank, cut over the whole visiting
+  // order: rank r takes the r-th equal-weight share of the tiles.
+  const uint32_t total = U.blocks * (uint32_t)E.nranks;
+  U.cut[slot].alloc((uint64_t)total + 1);
   if (n == 0) {
-    CPTC_CUDA(cudaMemsetAsync(U.cut[slot].p, 0, ((uint64_t)U.blocks + 1) * 4, E.stream));
+    CPTC_CUDA(cudaMemsetAsync(U.cut[slot].p, 0, ((uint64_t)total + 1) * 4, E.stream));
     return;
   }
   DArray<unsigned long long> w(n), pre(n);
@@ -521,8 +524,8 @@ void tile_cuts(Engine& E, int slot) {
   CPTC_CUDA(cub::DeviceScan::InclusiveSum(nullptr, tb, w.p, pre.p, (int64_t)n, E.stream));
   DArray<unsigned char> temp(tb);
   CPTC_CUDA(cub::DeviceScan::InclusiveSum(temp.p, tb, w.p, pre.p, (int64_t)n, E.stream));
-  k_tile_cuts<<<grid_for((uint64_t)U.blocks + 1, 256), 256, 0, E.stream>>>(pre.p, n, U.blocks,
-                                                                          U.cut[slot].p);
+  k_tile_cuts<<<grid_for((uint64_t)total + 1, 256), 256, 0, E.stream>>>(pre.p, n, total,
+                                                                      U.cut[slot].p);
   CPTC_LAUNCH_CHECK();
   CPTC_CUDA(cudaStreamSynchronize(E.stream));
 }

@@ -97,21 +97,3 @@ def write_tns(path: str, t: CooTensor) -> None:
 def probe_order(path: str) -> int:
     return int(N.host_lib().cptc_tns_probe_order(str(path).encode()))
 
-
-def slab_cuts(counts: np.ndarray, nnz: int, nranks: int) -> np.ndarray:
-    """Row-slab cuts of one mode for `nranks` GPUs (nranks + 1 entries, inner
-    cuts multiples of 16).  counts[i] = nonzeros with index i along the mode."""
-    counts = np.ascontiguousarray(counts, dtype=np.uint32)
-    out = np.zeros(nranks + 1, dtype=np.uint64)
-    rc = N.host_lib().cptc_slab_cuts(counts.ctypes.data_as(C.POINTER(C.c_uint32)), counts.size,
-                                     int(nnz), int(nranks),
-                                     out.ctypes.data_as(C.POINTER(C.c_uint64)))
-    if rc != 0:
-        raise ValueError(N.host_lib().cptc_host_last_error().decode())
-    return out
-
-
-def mode_slabs(t: CooTensor, nranks: int) -> list:
-    """slab_cuts for every mode of `t`, as the engine computes them."""
-    return [slab_cuts(np.bincount(t.idx[m], minlength=t.dims[m]), t.nnz, nranks)
-            for m in range(t.order)]

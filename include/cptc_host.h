@@ -65,17 +65,6 @@ int cptc_gen_uniform(int order, const uint64_t* dims, uint64_t nnz,
 /* Last host-side error message (thread-local). */
 const char* cptc_host_last_error(void);
 
-/* Row-slab partition of one mode for `nranks` GPUs: cuts_out[0..nranks]
- * with cuts_out[0] = 0, cuts_out[nranks] = dim, non-decreasing, every inner
- * cut a multiple of 16 rows (so a 16-row dense tile never straddles two
- * ranks) placed at the first row where the running nonzero count reaches
- * r/nranks of nnz.  Rank r owns rows [cuts_out[r], cuts_out[r+1]) of the
- * mode: it computes those MTTKRP rows and broadcasts them after the solve.
- * counts[i] = nonzeros whose index along the mode is i (dim entries).  The
- * reference runs on one GPU and has no counterpart; the engine computes
- * its cuts with this function. */
-int cptc_slab_cuts(const uint32_t* counts, uint64_t dim, uint64_t nnz, int nranks,
-                   uint64_t* cuts_out);
 
 #ifdef __cplusplus
 }

@@ -1,13 +1,17 @@
 """Worker code for the multi-rank tests (imported by spawned processes).
 
-`slab_als3` restates, with numpy on CPU ranks, what the engine does on G GPUs
-for the order-3 ALS: every rank keeps all factors, computes the MTTKRP rows of
-its own row slab (nonzeros selected by the slab of the target mode), solves
-them, all-reduces the partial Gram of its unnormalised rows (the column norms
-are its diagonal), normalises, and broadcasts its slab rows to the others.
-The fit all-reduces per-column dot products of the last mode.  Run with gloo
-it exercises the partition (cptc_slab_cuts, the same host function the engine
-calls) and the order and payload of the collectives on the host.
+`shard_als3` restates, with numpy on CPU ranks, what the engine does on G GPUs
+for the order-3 ALS.  Work and ownership are split separately:
+  * work: the nonzeros of each mode, sorted by target row, are cut into G
+    equal-count chunks (the engine gives each rank an equal range of its
+    nonzero-balanced tasks and an equal-weight range of the dense tiles), so
+    a heavy row is shared by several ranks;
+  * ownership: rows in G equal slabs (ceil(I/G) rows each).
+Per mode: partial MTTKRP of the rank's chunk -> reduce-scatter into the slabs
+-> solve of the own slab -> all-reduce of the partial Gram (column norms are
+its diagonal) -> normalisation -> all-gather of the slabs.  The fit
+all-reduces per-column dot products of the last mode.  Run with gloo it checks
+the order and payload of the collectives on the host.
 """
 from __future__ import annotations
 
@@ -35,37 +39,55 @@ def truncated_pinv(A, R):
     return (V[:, keep] / w[keep]) @ V[:, keep].T
 
 
-def slab_als3(t, R, iters, rank, world, dist):
+def shard_als3(t, R, iters, rank, world, dist):
     """The engine's distributed order-3 ALS on `world` CPU ranks (see module doc)."""
     import torch
 
-    import cptc_b200 as cp
     from oracle import oracle as o
 
     perm = [o.cadr_perm(t.dims[m], t.idx[m]) for m in range(3)]
     idx = [perm[m][t.idx[m]].astype(np.int64) for m in range(3)]
-    relab = cp.CooTensor(t.dims, [i.astype(np.uint32) for i in idx], t.vals)
-    cuts = cp.mode_slabs(relab, world)
     F = [f.copy() for f in o.init_factors3(t.dims, R)]
     lam = np.ones(R)
     G = [f.T @ f for f in F]
     X2 = float(t.vals @ t.vals)
     fits = []
+    srows = [-(-d // world) for d in t.dims]
+    # this rank's nonzeros per target mode: an equal share of the row-sorted order
+    chunk = []
+    for n in range(3):
+        order = np.argsort(idx[n], kind="stable")
+        a, b = t.nnz * rank // world, t.nnz * (rank + 1) // world
+        chunk.append(order[a:b])
 
     def allreduce(x):
         v = torch.from_numpy(np.ascontiguousarray(x))
         dist.all_reduce(v)
         return v.numpy()
 
+    def reduce_scatter_rows(M, s):
+        # padded to world * s rows; gloo has no reduce_scatter: all-reduce, keep own slab
+        P = np.zeros((world * s, R))
+        P[:M.shape[0]] = M
+        return allreduce(P)[rank * s:(rank + 1) * s]
+
+    def allgather_rows(Fl, s, dim):
+        parts = [torch.zeros((s, R), dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(Fl)))
+        return np.concatenate([p.numpy() for p in parts])[:dim]
+
     for _ in range(iters):
         for n in range(3):
             p, q = [m for m in range(3) if m != n]
             FtF = G[p] * G[q]
-            lo, hi = int(cuts[n][rank]), int(cuts[n][rank + 1])
-            mine = (idx[n] >= lo) & (idx[n] < hi)
+            mine = chunk[n]
             M = np_mttkrp([i[mine] for i in idx], t.vals[mine], t.dims, F, n)
+            s = srows[n]
+            lo, hi = min(rank * s, t.dims[n]), min((rank + 1) * s, t.dims[n])
+            Ms = reduce_scatter_rows(M, s)          # own slab, padded to s rows
             A = truncated_pinv(FtF, R)
-            Fl = M[lo:hi] @ A.T / lam
+            Fl = np.zeros((s, R))
+            Fl[:hi - lo] = Ms[:hi - lo] @ A.T / lam
             Gs = allreduce(Fl.T @ Fl)
             nr = np.sqrt(np.diag(Gs))
             zero = nr < 1e-14
@@ -73,26 +95,28 @@ def slab_als3(t, R, iters, rank, world, dist):
             lam = np.where(zero, 0.0, lam * nr)
             Fl = Fl * scale
             G[n] = Gs * np.outer(scale, scale)
-            Fn = np.zeros((t.dims[n], R))
-            Fn[lo:hi] = Fl
-            # all-gather of the slab rows: one broadcast per owner
-            for r in range(world):
-                a, b = int(cuts[n][r]), int(cuts[n][r + 1])
-                if b > a:
-                    blk = torch.from_numpy(np.ascontiguousarray(Fn[a:b]))
-                    dist.broadcast(blk, src=r)
-                    Fn[a:b] = blk.numpy()
-            F[n] = Fn
-        lo, hi = int(cuts[2][rank]), int(cuts[2][rank + 1])
-        dots = allreduce(np.einsum("kr,kr->r", F[2][lo:hi], M[lo:hi]))
+            F[n] = allgather_rows(Fl, s, t.dims[n])
+        dots = allreduce(np.einsum("kr,kr->r", F[2][lo:hi], Ms[:hi - lo]))
         iprod = float(lam @ dots)
         model2 = float(lam @ (G[0] * G[1] * G[2]) @ lam)
         fits.append(1 - np.sqrt(max(X2 - 2 * iprod + model2, 0.0)) / np.sqrt(X2))
-    return np.array(fits), F, lam, cuts
+    return np.array(fits), F, lam, [c.size for c in chunk]
+
+
+def make_cpu_case(spec):
+    """Seeded tensor of a CPU test; spec["heavy"] = f moves the first f of the
+    nonzeros into row 0 of every mode (a head row larger than a rank's share)."""
+    import cptc_b200 as cp
+
+    t = cp.gen_uniform(spec["dims"], spec["nnz"], seed=spec["seed"], values=spec["values"])
+    k = int(spec.get("heavy", 0.0) * t.nnz)
+    for m in range(t.order):
+        t.idx[m][:k] = 0
+    return t
 
 
 def cpu_worker(rank, world, port, spec, q):
-    """Entry point of one spawned gloo rank: runs slab_als3 and reports."""
+    """Entry point of one spawned gloo rank: runs shard_als3 and reports."""
     import torch.distributed as dist
 
     import cptc_b200 as cp
@@ -101,9 +125,9 @@ def cpu_worker(rank, world, port, spec, q):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
-        t = cp.gen_uniform(spec["dims"], spec["nnz"], seed=spec["seed"], values=spec["values"])
-        fits, F, lam, cuts = slab_als3(t, spec["R"], spec["iters"], rank, world, dist)
-        q.put((rank, fits, F, lam, [c.tolist() for c in cuts]))
+        t = make_cpu_case(spec)
+        fits, F, lam, shares = shard_als3(t, spec["R"], spec["iters"], rank, world, dist)
+        q.put((rank, fits, F, lam, shares))
     except Exception as e:  # report instead of hanging the other ranks' test
         q.put((rank, repr(e), None, None, None))
         raise

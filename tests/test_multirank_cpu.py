@@ -1,10 +1,11 @@
-"""The multi-GPU row-slab path on CPU ranks (gloo), no GPU needed.
+"""The multi-GPU partition and collectives on CPU ranks (gloo), no GPU needed.
 
-The slab cuts come from cptc_slab_cuts, the host function the engine uses to
-partition each mode; the distributed ALS restatement in tests/multirank.py
-runs the engine's sequence of collectives (partial-Gram all-reduce, one
-broadcast per slab owner, dot-product all-reduce) over world-size 2 and 3
-gloo groups and must reproduce the single-process ALS.
+tests/multirank.py restates the engine's distributed ALS (nonzeros shared out
+by count, partial MTTKRP reduce-scattered into equal row slabs, Gram
+all-reduce, slab all-gather) over world-size 2 and 3 gloo groups; it must
+reproduce the single-process ALS, and every rank must end with the same
+factors.  The tensor has a Zipf-like head row so that one row is split
+between ranks.
 """
 import multiprocessing as mp
 import socket
@@ -14,7 +15,7 @@ import pytest
 
 import cptc_b200 as cp
 
-from multirank import cpu_worker
+from multirank import cpu_worker, make_cpu_case
 from test_oracle import np_als3
 
 
@@ -24,45 +25,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_slab_cuts_properties():
-    rng = np.random.default_rng(3)
-    for dim, world in ((1000, 2), (1000, 8), (37, 4), (5, 3), (16, 2), (300, 7)):
-        counts = rng.zipf(1.3, dim).astype(np.uint32) % 5000
-        nnz = int(counts.sum())
-        cuts = cp.slab_cuts(counts, nnz, world).astype(np.int64)
-        assert cuts[0] == 0 and cuts[-1] == dim and len(cuts) == world + 1
-        assert np.all(np.diff(cuts) >= 0)
-        inner = cuts[1:-1]
-        assert np.all((inner % 16 == 0) | (inner == dim))
-        # rank r starts at the first 16-row boundary at or after the row where
-        # the running count reaches r/world of nnz
-        csum = np.concatenate([[0], np.cumsum(counts, dtype=np.int64)])
-        for r in range(1, world):
-            row = int(np.argmax(csum[1:] * world >= r * nnz))
-            want = min(-(-(row + 1) // 16) * 16, dim)
-            assert cuts[r] == max(want, cuts[r - 1])
-
-
-def test_slab_cuts_rejects_bad_arguments():
-    with pytest.raises(ValueError):
-        cp.slab_cuts(np.ones(4, np.uint32), 4, 0)
-
-
-def test_mode_slabs_balance_uniform_tensor():
-    t = cp.gen_uniform((512, 640, 384), 200_000, seed=5)
-    for world in (2, 4, 8):
-        for m, cuts in enumerate(cp.mode_slabs(t, world)):
-            share = [np.count_nonzero((t.idx[m] >= a) & (t.idx[m] < b))
-                     for a, b in zip(cuts[:-1], cuts[1:])]
-            assert sum(share) == t.nnz
-            # each slab is within one 16-row block of its equal share
-            per_row = t.nnz / t.dims[m]
-            assert max(share) <= t.nnz / world + 32 * per_row
-
-
-@pytest.mark.parametrize("world", [2, 3])
-def test_slab_als_matches_single_process(world):
-    spec = dict(dims=(90, 70, 50), nnz=12_000, seed=21, values="lognormal", R=8, iters=4)
+def _run(world, spec):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -72,8 +35,8 @@ def test_slab_als_matches_single_process(world):
     out = {}
     try:
         for _ in range(world):
-            rank, fits, F, lam, cuts = q.get(timeout=240)
-            out[rank] = (fits, F, lam, cuts)
+            rank, fits, F, lam, shares = q.get(timeout=240)
+            out[rank] = (fits, F, lam, shares)
     finally:
         for p in procs:
             p.join(timeout=60)
@@ -81,14 +44,38 @@ def test_slab_als_matches_single_process(world):
                 p.kill()
     for r in range(world):
         assert not isinstance(out[r][0], str), out[r][0]
-    t = cp.gen_uniform(spec["dims"], spec["nnz"], seed=spec["seed"], values=spec["values"])
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_als_matches_single_process(world):
+    spec = dict(dims=(90, 70, 50), nnz=12_000, seed=21, values="lognormal", R=8, iters=4)
+    out = _run(world, spec)
+    t = make_cpu_case(spec)
     ref = np_als3(t, spec["R"], spec["iters"])
-    fits0, F0, lam0, cuts0 = out[0]
+    fits0, F0, lam0, shares0 = out[0]
     assert np.max(np.abs(fits0 - ref)) < 1e-10
-    # every slab is non-trivial and every rank ends with identical factors
-    assert all(len(set(c)) == world + 1 for c in cuts0)
     for r in range(1, world):
-        fits, F, lam, _ = out[r]
+        fits, F, lam, shares = out[r]
         assert np.array_equal(fits, fits0) and np.array_equal(lam, lam0)
         for a, b in zip(F, F0):
             assert np.array_equal(a, b)
+    # nonzeros are shared out by count: shares differ by at most one
+    for m in range(3):
+        sizes = [out[r][3][m] for r in range(world)]
+        assert sum(sizes) == spec["nnz"] and max(sizes) - min(sizes) <= 1
+
+
+def test_sharded_als_with_a_split_head_row():
+    # 45% of the nonzeros in row 0 of every mode (like config 4's head block):
+    # with 3 ranks that row is computed in pieces by two ranks and summed by
+    # the reduce-scatter
+    spec = dict(dims=(60, 50, 40), nnz=9_000, seed=5, values="lognormal", R=8, iters=3,
+                heavy=0.45)
+    t = make_cpu_case(spec)
+    assert np.bincount(t.idx[0]).max() / t.nnz > 1 / 3
+    out = _run(3, spec)
+    ref = np_als3(t, spec["R"], spec["iters"])
+    assert np.max(np.abs(out[0][0] - ref)) < 1e-10
+    for a, b in zip(out[2][1], out[0][1]):
+        assert np.array_equal(a, b)
