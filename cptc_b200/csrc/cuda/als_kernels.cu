@@ -78,12 +78,25 @@ __global__ void __launch_bounds__(256) k_gram_partial(const double* __restrict__
   store_partial<TM>(part + (uint64_t)blockIdx.x * R * R, R, a0, b0, acc);
 }
 
-__global__ void k_partial_sum(const double* __restrict__ part, int nblk, int len,
-                              double* __restrict__ out) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < len; i += gridDim.x * blockDim.x) {
-    double s = 0.0;
-    for (int b = 0; b < nblk; ++b) s += part[(uint64_t)b * len + i];
-    out[i] = s;
+// out[i] = sum_b part[b * len + i] for b < nblk, in a fixed order: warp w of
+// the block adds partials w, w + 8, w + 16, ... for 32 consecutive entries
+// (coalesced), then the 8 warp sums are added in warp order.  One block per
+// 32 entries, so an R x R Gram (R = 128: 512 blocks) is reduced across the GPU.
+__global__ void __launch_bounds__(256) k_partial_sum(const double* __restrict__ part, int nblk,
+                                                     int len, double* __restrict__ out) {
+  __shared__ double sh[8][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int i = blockIdx.x * 32 + lane;
+  double s = 0.0;
+  if (i < len)
+    for (int b = w; b < nblk; b += 8) s += part[(uint64_t)b * len + i];
+  sh[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && i < len) {
+    double t = 0.0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += sh[k][lane];
+    out[i] = t;
   }
 }
 
@@ -197,83 +210,80 @@ __global__ void __launch_bounds__(1024) k_pinv_jacobi(const double* __restrict__
 }
 
 // ---------------------------------------------------------------------------
-// Inverse by Cholesky, right-looking in shared memory, then L^-1 column by
-// column (one thread per column) and Ainv = L^-T L^-1.
-//  ridge = 1: the reference's N-order rule (src/generic.cu:757-783): factor
-//    A + eps*I with eps = 1e-12 * tr(A)/R + 1e-300, pivot s <= 0 -> sqrt(eps).
-//  ridge = 0: plain Cholesky of A; if a pivot falls to <= 1e-11 * max diag
-//    (condition number beyond ~1e11) the factorisation is rejected, *fail is
-//    set and Ainv is left for the pseudo-inverse kernel that follows.
+// FtF = Hadamard product of the Gram matrices Gs (written out for the
+// pseudo-inverse kernel) and its inverse by the symmetric sweep operator
+// (Gauss-Jordan elimination in place; Goodnight 1979): for pivot j with
+// d = M[j][j],  M[i][k] -= M[i][j] M[j][k] / d,  M[i][j] = M[i][j] / d,
+// M[j][j] = -1 / d;  after all R pivots M = -A^-1.  The pivot d of step j is
+// the Schur complement that a Cholesky factorisation would take the square
+// root of, so the reference's rules carry over unchanged:
+//  ridge = 1 (N-order path, src/generic.cu:757-783): A + eps*I with
+//    eps = 1e-12 * tr(A)/R + 1e-300, a pivot d <= 0 becomes eps;
+//  ridge = 0: a pivot d <= 1e-11 * max diag (condition beyond ~1e11) rejects
+//    the inverse: *fail is set and the pseudo-inverse kernel that follows
+//    computes Ainv instead.
+// All R*R entries are updated in parallel per pivot (warp = row, lane =
+// column), two barriers per pivot.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) k_chol_inverse(const double* __restrict__ A, int R,
-                                                       int ridge, double* __restrict__ Ainv,
-                                                       double* __restrict__ Linv,
-                                                       int* __restrict__ status,
-                                                       int* __restrict__ fail) {
-  extern __shared__ double L[];  // R*R row-major lower
+__global__ void __launch_bounds__(1024) k_sweep_inverse(GPtrs g, int ng, int R, int ridge,
+                                                        double* __restrict__ FtF,
+                                                        double* __restrict__ Ainv,
+                                                        int* __restrict__ status,
+                                                        int* __restrict__ fail) {
+  extern __shared__ double M[];  // R*R row-major, then the pivot row (R)
+  double* prow = M + R * R;
   __shared__ double eps_s, dmax_s;
-  __shared__ int bad;
-  const int tid = threadIdx.x;
-  for (int k = tid; k < R * R; k += blockDim.x) L[k] = A[k];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  const int RR = R * R;
+  for (int k = tid; k < RR; k += blockDim.x) {
+    double v = 1.0;
+    for (int q = 0; q < ng; ++q) v *= g.p[q][k];
+    FtF[k] = v;
+    M[k] = v;
+  }
   __syncthreads();
   if (tid == 0) {
     double tr = 0.0, dm = 0.0;
     for (int i = 0; i < R; ++i) {
-      tr += L[i * R + i];
-      dm = fmax(dm, L[i * R + i]);
+      tr += M[i * R + i];
+      dm = fmax(dm, M[i * R + i]);
     }
     eps_s = ridge ? 1e-12 * ((tr > 0.0) ? tr / (double)R : 1.0) + 1e-300 : 0.0;
     dmax_s = dm;
-    bad = 0;
   }
   __syncthreads();
-  const double eps = eps_s;
-  for (int i = tid; i < R; i += blockDim.x) L[i * R + i] += eps;
-  __syncthreads();
+  const double eps = eps_s, dmax = dmax_s;
+  if (ridge)
+    for (int i = tid; i < R; i += blockDim.x) M[i * R + i] += eps;
   for (int j = 0; j < R; ++j) {
-    if (tid == 0) {
-      const double s = L[j * R + j];
-      if (ridge) {
-        L[j * R + j] = (s > 0.0) ? sqrt(s) : sqrt(eps);
-      } else if (!(s > 1e-11 * dmax_s)) {
-        bad = 1;
-        L[j * R + j] = 1.0;
-      } else {
-        L[j * R + j] = sqrt(s);
+    __syncthreads();
+    for (int k = tid; k < R; k += blockDim.x) prow[k] = M[j * R + k];
+    __syncthreads();
+    double d = prow[j];
+    if (ridge) {
+      if (!(d > 0.0)) d = eps;
+    } else if (!(d > 1e-11 * dmax)) {
+      if (tid == 0 && fail) *fail = 1;
+      return;  // every thread sees the same d: uniform exit
+    }
+    const double inv = 1.0 / d;
+    for (int i = wid; i < R; i += nw) {
+      const double pi = prow[i];
+      for (int k = lane; k < R; k += 32) {
+        double v;
+        if (i == j) v = (k == j) ? -inv : prow[k] * inv;
+        else if (k == j) v = pi * inv;
+        else v = M[i * R + k] - pi * prow[k] * inv;
+        M[i * R + k] = v;
       }
     }
-    __syncthreads();
-    if (bad) break;
-    const double d = L[j * R + j];
-    for (int i = j + 1 + tid; i < R; i += blockDim.x) L[i * R + j] /= d;
-    __syncthreads();
-    const int m = R - j - 1;
-    for (int k = tid; k < m * m; k += blockDim.x) {
-      const int i = j + 1 + k / m, c = j + 1 + k % m;
-      if (c <= i) L[i * R + c] -= L[i * R + j] * L[c * R + j];
-    }
-    __syncthreads();
-  }
-  if (bad) {
-    if (tid == 0 && fail) *fail = 1;
-    return;
-  }
-  if (tid == 0 && fail) *fail = 0;
-  for (int c = tid; c < R; c += blockDim.x) {
-    for (int i = 0; i < R; ++i) {
-      double s = (i == c) ? 1.0 : 0.0;
-      for (int k = c; k < i; ++k) s -= L[i * R + k] * Linv[k * R + c];
-      Linv[i * R + c] = (i < c) ? 0.0 : s / L[i * R + i];
-    }
   }
   __syncthreads();
-  for (int o = tid; o < R * R; o += blockDim.x) {
-    const int a = o / R, b = o % R;
-    const int k0 = a > b ? a : b;
-    double s = 0.0;
-    for (int k = k0; k < R; ++k) s = fma(Linv[k * R + a], Linv[k * R + b], s);
-    Ainv[o] = s;
-    if (!isfinite(s)) atomicExch(status, 1);
+  if (tid == 0 && fail) *fail = 0;
+  for (int k = tid; k < RR; k += blockDim.x) {
+    const double v = -M[k];
+    Ainv[k] = v;
+    if (!isfinite(v)) atomicExch(status, 1);
   }
 }
 
@@ -495,7 +505,7 @@ int launch_gram_partial(const double* F, uint64_t rows, int R, double* part, int
 }
 
 void launch_partial_sum(const double* part, int nblk, int len, double* out, cudaStream_t s) {
-  k_partial_sum<<<grid_for((uint64_t)len, 256), 256, 0, s>>>(part, nblk, len, out);
+  k_partial_sum<<<(unsigned)((len + 31) / 32), 256, 0, s>>>(part, nblk, len, out);
   CPTC_LAUNCH_CHECK();
 }
 
@@ -510,21 +520,27 @@ void launch_hadamard(const double* const* Gs, int ng, int R, double* FtF, cudaSt
   CPTC_LAUNCH_CHECK();
 }
 
-void launch_sym_inverse(const double* A, int R, int mode, double* Ainv, int* status,
-                        cudaStream_t s) {
+void launch_sym_inverse(const double* const* Gs, int ng, int R, int mode, double* FtF,
+                        double* Ainv, int* status, cudaStream_t s) {
   CPTC_REQUIRE(R >= 1 && R <= 128, CPTC_E_UNSUP, "rank must be in [1, 128]");
-  // Ainv holds 2*R*R doubles (+1 int flag after them): the second half is
-  // the L^-1 scratch of the Cholesky kernel.
-  double* Linv = Ainv + (size_t)R * R;
+  CPTC_REQUIRE(ng >= 1 && ng <= CPTC_MAX_ORDER, CPTC_E_ARG, "bad Gram count");
+  // Ainv holds 2*R*R doubles (+1 int flag after them): the flag gates the
+  // pseudo-inverse kernel on the sweep's outcome.
   int* gate = reinterpret_cast<int*>(Ainv + 2 * (size_t)R * R);
-  const size_t csm = (size_t)R * R * sizeof(double);
+  GPtrs g{};
+  for (int k = 0; k < ng; ++k) g.p[k] = Gs[k];
   if (mode != kInvPinv) {
-    CPTC_CUDA(cudaFuncSetAttribute(k_chol_inverse, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)csm));
-    k_chol_inverse<<<1, 512, csm, s>>>(A, R, mode == kInvCholRidge ? 1 : 0, Ainv, Linv, status,
-                                       mode == kInvAuto ? gate : nullptr);
+    const size_t ssm = ((size_t)R * R + R) * sizeof(double);
+    CPTC_CUDA(cudaFuncSetAttribute(k_sweep_inverse, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)ssm));
+    const int threads = 32 * (R < 32 ? R : 32);
+    k_sweep_inverse<<<1, threads, ssm, s>>>(g, ng, R, mode == kInvCholRidge ? 1 : 0, FtF, Ainv,
+                                           status, mode == kInvAuto ? gate : nullptr);
     CPTC_LAUNCH_CHECK();
     if (mode == kInvCholRidge) return;
+  } else {
+    k_hadamard<<<grid_for((uint64_t)R * R, 256), 256, 0, s>>>(g, ng, R, FtF);
+    CPTC_LAUNCH_CHECK();
   }
   const int n = (R + 1) & ~1;
   int threads = 32 * (n / 2);
@@ -533,7 +549,7 @@ void launch_sym_inverse(const double* A, int R, int mode, double* Ainv, int* sta
   const size_t smem = ((size_t)R * R + R) * sizeof(double);
   CPTC_CUDA(cudaFuncSetAttribute(k_pinv_jacobi, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem));
-  k_pinv_jacobi<<<1, threads, smem, s>>>(A, R, Ainv, status, mode == kInvAuto ? gate : nullptr);
+  k_pinv_jacobi<<<1, threads, smem, s>>>(FtF, R, Ainv, status, mode == kInvAuto ? gate : nullptr);
   CPTC_LAUNCH_CHECK();
 }
 

@@ -72,24 +72,22 @@ void comm_prepare(Engine& E) {
   }
 }
 
-void comm_allreduce_gram(Engine& E, int nblk) {
-  if (E.nranks == 1) return;
+const double* comm_reduce_gram(Engine& E, int nblk) {
   const int RR = E.R * E.R;
-  if (E.comm_buf.n < (size_t)RR) E.comm_buf.alloc(RR);
-  launch_partial_sum(E.gpart.p, nblk, RR, E.comm_buf.p, E.stream);
-  CPTC_NCCL(ncclAllReduce(E.comm_buf.p, E.gpart.p, RR, ncclDouble, ncclSum, comm_of(E), E.stream));
+  double* out = E.comm_buf.p;
+  launch_partial_sum(E.gpart.p, nblk, RR, out, E.stream);
+  if (E.nranks > 1)
+    CPTC_NCCL(ncclAllReduce(out, out, RR, ncclDouble, ncclSum, comm_of(E), E.stream));
+  return out;
 }
 
-int comm_gram_blocks(const Engine& E, int nblk) { return E.nranks == 1 ? nblk : 1; }
-
-void comm_allreduce_dots(Engine& E, int nblk) {
-  if (E.nranks == 1) return;
-  if (E.comm_buf.n < (size_t)E.R * E.R) E.comm_buf.alloc((size_t)E.R * E.R);
-  launch_partial_sum(E.dots.p, nblk, E.R, E.comm_buf.p, E.stream);
-  CPTC_NCCL(ncclAllReduce(E.comm_buf.p, E.dots.p, E.R, ncclDouble, ncclSum, comm_of(E), E.stream));
+const double* comm_reduce_dots(Engine& E, int nblk) {
+  double* out = E.comm_buf.p + (size_t)E.R * E.R;
+  launch_partial_sum(E.dots.p, nblk, E.R, out, E.stream);
+  if (E.nranks > 1)
+    CPTC_NCCL(ncclAllReduce(out, out, E.R, ncclDouble, ncclSum, comm_of(E), E.stream));
+  return out;
 }
-
-int comm_dot_blocks(const Engine& E, int nblk) { return E.nranks == 1 ? nblk : 1; }
 
 void comm_reduce_scatter_ftv(Engine& E, int n) {
   if (E.nranks == 1) return;

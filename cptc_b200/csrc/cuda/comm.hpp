@@ -21,12 +21,11 @@ int comm_unique_id(unsigned char out[128]);
 // Rows per slab of mode m (slab r = rows [r * s, min((r + 1) * s, I_m))).
 uint64_t slab_rows(const Engine& E, int m);
 
-// Sum of the per-block Gram partials over blocks and ranks into gpart[0];
-// returns the number of partial blocks left for launch_norm_finalize.
-void comm_allreduce_gram(Engine& E, int nblk);
-int comm_gram_blocks(const Engine& E, int nblk);
-void comm_allreduce_dots(Engine& E, int nblk);
-int comm_dot_blocks(const Engine& E, int nblk);
+// Sum of the nblk per-block Gram partials (R x R) over blocks and ranks, in
+// a fixed order; returns the device address of the single summed Gram.
+const double* comm_reduce_gram(Engine& E, int nblk);
+// The same for the per-block column dot products (R) of the fit.
+const double* comm_reduce_dots(Engine& E, int nblk);
 // Partial MTTKRP rows of every rank summed into each rank's slab of FtV.
 void comm_reduce_scatter_ftv(Engine& E, int n);
 // Every rank's slab of F[n] to every rank (in place).

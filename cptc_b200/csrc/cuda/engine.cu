@@ -185,6 +185,7 @@ void Engine::alloc_workspace() {
   gpart_blocks = 148;
   gpart.alloc((uint64_t)gpart_blocks * R * R);
   dots.alloc((uint64_t)gpart_blocks * R);
+  comm_buf.alloc((uint64_t)R * R + R);
   scal.alloc(8);
   status.alloc(1);
   lambda.alloc(R);
@@ -461,7 +462,6 @@ void Engine::update_mode(int n) {
   int ng = 0;
   for (int m = 0; m < N; ++m)
     if (m != n) gs[ng++] = G[m].p;
-  launch_hadamard(gs, ng, R, FtF.p, stream);
   cudaEventRecord(ev[2 * n], stream);
   mttkrp(n);
   cudaEventRecord(ev[2 * n + 1], stream);
@@ -473,13 +473,12 @@ void Engine::update_mode(int n) {
   int inv = generic ? kInvCholRidge : kInvAuto;
   if (opts.solver == CPTC_SOLVER_CHOL) inv = kInvCholRidge;
   if (opts.solver == CPTC_SOLVER_PINV) inv = kInvPinv;
-  launch_sym_inverse(FtF.p, R, inv, Ainv.p, status.p, stream);
+  launch_sym_inverse(gs, ng, R, inv, FtF.p, Ainv.p, status.p, stream);
   const uint64_t lo = row_lo(n), rows = row_hi(n) - lo;
   const int nb = launch_apply_solve(FtV.p + lo * R, Ainv.p, lambda.p, generic ? 0 : 1, rows, R,
                                     F[n].p + lo * R, gpart.p, gpart_blocks, stream);
-  comm_allreduce_gram(*this, nb);
-  launch_norm_finalize(gpart.p, comm_gram_blocks(*this, nb), R, generic ? 1 : 0, lambda.p,
-                       G[n].p, colscale(), stream);
+  const double* gsum = comm_reduce_gram(*this, nb);
+  launch_norm_finalize(gsum, 1, R, generic ? 1 : 0, lambda.p, G[n].p, colscale(), stream);
   launch_scale_cols(F[n].p + lo * R, rows, R, colscale(), stream);
   comm_allgather_factor(*this, n);
 }
@@ -506,10 +505,10 @@ void Engine::als(int iters, cptc_iter_cb cb, void* user) {
     const uint64_t lo = row_lo(last), rows = row_hi(last) - lo;
     const int nb = launch_col_dots(F[last].p + lo * R, FtV.p + lo * R, rows, R, dots.p,
                                    gpart_blocks, stream);
-    comm_allreduce_dots(*this, nb);
+    const double* dsum = comm_reduce_dots(*this, nb);
     const double* gs[CPTC_MAX_ORDER];
     for (int m = 0; m < N; ++m) gs[m] = G[m].p;
-    launch_fit_final(dots.p, comm_dot_blocks(*this, nb), lambda.p, gs, N, R, scal.p, stream);
+    launch_fit_final(dsum, 1, lambda.p, gs, N, R, scal.p, stream);
     CPTC_CUDA(cudaMemcpyAsync(h_scal, scal.p, 2 * sizeof(double), cudaMemcpyDeviceToHost, stream));
     int h_status = 0;
     CPTC_CUDA(cudaMemcpyAsync(h_scal + 4, status.p, sizeof(int), cudaMemcpyDeviceToHost, stream));

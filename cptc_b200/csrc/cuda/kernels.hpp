@@ -75,14 +75,15 @@ void launch_partial_sum(const double* part, int nblk, int len, double* out, cuda
 void launch_gram_reduce(const double* part, int nblk, int R, double* G, cudaStream_t s);
 // FtF = prod_{m in list} G_m (elementwise).
 void launch_hadamard(const double* const* Gs, int ng, int R, double* FtF, cudaStream_t s);
-// Ainv = inverse of the symmetric PSD R x R matrix A; status[0] != 0 on
-// non-finite results.  Ainv must hold 2*R*R + 1 doubles (scratch).
+// FtF = prod of the ng Grams Gs (elementwise, written out) and Ainv = its
+// inverse; status[0] != 0 on non-finite results.  Ainv must hold
+// 2*R*R + 1 doubles (scratch).
 //   kInvPinv:      truncated pseudo-inverse (Jacobi, tol R*ulp(smax))
-//   kInvCholRidge: ridge Cholesky of the N-order reference path
-//   kInvAuto:      Cholesky when well conditioned, else the pseudo-inverse
+//   kInvCholRidge: ridge rule of the N-order reference path (sweep inverse)
+//   kInvAuto:      sweep inverse when well conditioned, else the pseudo-inverse
 enum { kInvPinv = 0, kInvCholRidge = 1, kInvAuto = 2 };
-void launch_sym_inverse(const double* A, int R, int mode, double* Ainv, int* status,
-                        cudaStream_t s);
+void launch_sym_inverse(const double* const* Gs, int ng, int R, int mode, double* FtF,
+                        double* Ainv, int* status, cudaStream_t s);
 // F[i,:] = (FtV[i,:] * Ainv) ./ (divide_lambda ? lambda : 1) for rows
 // [0, rows); partial Grams of the written rows into part; returns nblk.
 int launch_apply_solve(const double* FtV, const double* Ainv, const double* lambda,
