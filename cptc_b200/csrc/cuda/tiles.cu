@@ -23,6 +23,7 @@
 //    consecutive tiles of the same 16 output rows in shared memory and
 //    issues the FP64 atomics once per row block instead of once per tile.
 #include <cfloat>
+#include <cstdlib>
 
 #include <cub/cub.cuh>
 
@@ -127,6 +128,7 @@ __global__ void k_tile_target_keys(const int4* __restrict__ tile, uint64_t n, in
 constexpr int kSt = 20;               // t stride (floats) of the slab layout
 constexpr int kSs = 16 * kSt;         // s stride
 constexpr int kTileFloats = 16 * kSs; // 5120 floats = 20 KB
+constexpr int kScU = 4;               // nonzeros per thread per scatter round
 
 __device__ __forceinline__ uint32_t tf32_bits(float x) {
   return __float_as_uint(x) & 0xFFFFE000u;  // low 13 mantissa bits ignored
@@ -143,31 +145,38 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
 
 // Block of 4 warps, persistent over a contiguous range of the visiting
 // order.  Slot roles (target TS, TF32-contracted CS, FP64-weighted SS) are
-// compile-time constants.  Warp w owns n-tiles w, w+4, ... (R/8 n-tiles of 8
-// ranks); when R < 32 the warps also split the 16 slabs and combine through
-// shared memory.  Per tile: zero + scatter the 16^3 tile in (s, t, c)
-// layout, load the c-slot rows (TF32) and the s-slot rows times the outer
-// weights (FP64), then 16 slabs x 2 k-steps of m16n8k8 with the FP64
-// epilogue in registers.  Row loops are (warp, lane)-strided: no integer
-// division in the kernel.
-template <int TS, int CS, int SS, int NTMAX>
-__global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __restrict__ order,
-                                               const uint32_t* __restrict__ cut) {
+// compile-time constants.  The R/8 n-tiles (8 ranks each) are cut into
+// ng = ceil(NT/NW) groups of NW; the 4 warps are (n-tile group, slab group)
+// pairs, each slab group taking every SG-th of the 16 slabs (SG = 4/ng).  A
+// warp loads an A fragment (a 16x8 piece of one slab) once and uses it for
+// all NW of its n-tiles, so each slab is read ng times per tile (R=32: once).
+// Per tile: zero + scatter the 16^3 tile in (s, t, c) layout as TF32 bit
+// patterns, load the c-slot rows (TF32) and the s-slot rows times the outer
+// weights (FP64), then per slab 2 k-steps of m16n8k8 and the FP64 epilogue.
+// The FP64 results stay in registers across consecutive tiles of the same
+// target block; when the block changes they are added into shared memory
+// slab group by slab group (fixed order) and flushed with FP64 atomics.
+// Row loops are (warp, lane)-strided: no integer division in the kernel.
+template <int TS, int CS, int SS, int NW, int MINB>
+__global__ void __launch_bounds__(128, MINB) k_tiles(TileArgs a,
+                                                     const uint32_t* __restrict__ order,
+                                                     const uint32_t* __restrict__ cut) {
   extern __shared__ __align__(16) unsigned char smraw[];
   const int R = a.R;
   const int Rs = R + 8;                                         // fB row stride (floats)
-  float* X = reinterpret_cast<float*>(smraw);                  // kTileFloats
-  float* fB = X + kTileFloats;                                  // 16 * Rs
+  float* X = reinterpret_cast<float*>(smraw);                  // kTileFloats (TF32)
+  float* fB = X + kTileFloats;                                  // 16 * Rs (TF32)
   double* F2s = reinterpret_cast<double*>(fB + 16 * Rs);       // 16 * R
   double* accS = F2s + 16 * R;                                  // 16 * R
   double* wS = accS + 16 * R;                                   // R (outer weights)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
   const int NT = R >> 3;
-  const int ntstep = NT >= 4 ? 4 : NT;
-  const int SG = 4 / ntstep;
-  const int my_sg = warp / ntstep;
-  const int nt0 = warp - my_sg * ntstep;
+  const int ng = (NT + NW - 1) / NW;
+  const int SG = 4 / ng;
+  const bool active = warp < ng * SG;
+  const int ntg = warp % ng, my_sg = warp / ng;
+  const int nt_base = ntg * NW;
   const uint64_t dimT = a.dims[TS], dimC = a.dims[CS], dimS = a.dims[SS];
 
   const uint64_t k0 = cut[blockIdx.x];
@@ -176,9 +185,34 @@ __global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __res
 
   for (int t = warp; t < 16; t += 4)
     for (int r = lane; r < R; r += 32) accS[t * R + r] = 0.0;
+  double acc[NW][4];
+#pragma unroll
+  for (int q = 0; q < NW; ++q)
+#pragma unroll
+    for (int x = 0; x < 4; ++x) acc[q][x] = 0.0;
   int cur_tb = -1;
 
+  // Called by all threads at the same point.
   auto flush = [&](int tb) {
+    for (int sgi = 0; sgi < SG; ++sgi) {
+      if (active && my_sg == sgi) {
+#pragma unroll
+        for (int q = 0; q < NW; ++q) {
+          const int nt = nt_base + q;
+          if (nt >= NT) break;
+          const int r = nt * 8 + 2 * t4;
+          accS[g * R + r] += acc[q][0];
+          accS[g * R + r + 1] += acc[q][1];
+          accS[(g + 8) * R + r] += acc[q][2];
+          accS[(g + 8) * R + r + 1] += acc[q][3];
+        }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int q = 0; q < NW; ++q)
+#pragma unroll
+      for (int x = 0; x < 4; ++x) acc[q][x] = 0.0;
     for (int t = warp; t < 16; t += 4) {
       const uint64_t row = (uint64_t)tb * 16 + t;
       for (int r = lane; r < R; r += 32) {
@@ -189,9 +223,19 @@ __global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __res
     }
   };
 
+  // Tile metadata is fetched one tile ahead (three dependent loads).
+  uint32_t ti_next = order[k0];
+  int4 T_next = a.tile[ti_next];
+  uint64_t st_next = a.start[ti_next];
   for (uint64_t k = k0; k < k1; ++k) {
-    const uint32_t ti = order[k];
-    const int4 T = a.tile[ti];
+    const uint32_t ti = ti_next;
+    const int4 T = T_next;
+    const uint64_t st = st_next;
+    if (k + 1 < k1) {
+      ti_next = order[k + 1];
+      T_next = a.tile[ti_next];
+      st_next = a.start[ti_next];
+    }
     const int tb = TS == 0 ? T.x : TS == 1 ? T.y : T.z;
     const int cb = CS == 0 ? T.x : CS == 1 ? T.y : T.z;
     const int sb = SS == 0 ? T.x : SS == 1 ? T.y : T.z;
@@ -211,87 +255,102 @@ __global__ void __launch_bounds__(128) k_tiles(TileArgs a, const uint32_t* __res
       }
     }
     __syncthreads();
-    for (int c = warp; c < 16; c += 4) {
+    // Factor rows of the tile; every load of this thread is issued before
+    // the first is used (the c loop is unrolled).
+#pragma unroll
+    for (int ci = 0; ci < 4; ++ci) {
+      const int c = warp + 4 * ci;
       const uint64_t cg = (uint64_t)cb * 16 + c, sg = (uint64_t)sb * 16 + c;
       const bool cok = cg < dimC, sok = sg < dimS;
       for (int r = lane; r < R; r += 32) {
-        fB[c * Rs + r] = cok ? (float)a.Fc[cg * R + r] : 0.0f;
+        fB[c * Rs + r] = cok ? __uint_as_float(tf32_bits((float)a.Fc[cg * R + r])) : 0.0f;
         double f2 = sok ? a.Fs[sg * R + r] : 0.0;
         if (a.nouter > 0) f2 *= wS[r];
         F2s[c * R + r] = f2;
       }
     }
-    const uint64_t st = a.start[ti];
-    for (int j = tid; j < T.w; j += 128) {
-      const uint32_t l = a.lid[st + j];
-      const int l0 = (int)(l >> 8), l1 = (int)((l >> 4) & 15), l2 = (int)(l & 15);
-      const int lt = TS == 0 ? l0 : TS == 1 ? l1 : l2;
-      const int lc = CS == 0 ? l0 : CS == 1 ? l1 : l2;
-      const int ls = SS == 0 ? l0 : SS == 1 ? l1 : l2;
-      double v = a.val[st + j];
-      v = v > FLT_MAX ? FLT_MAX : (v < -FLT_MAX ? -FLT_MAX : v);
-      float* dst = X + ls * kSs + lt * kSt + lc;
-      if (a.store_dups) *dst = (float)v;
-      else atomicAdd(dst, (float)v);
-    }
-    __syncthreads();
-
-    uint32_t bf[NTMAX][2][2];
-    double acc[NTMAX][4];
+    // Scatter of the tile's nonzeros, kScU per thread loaded at once.  Order-3
+    // tiles store each cell once (duplicates: last write wins) and keep TF32
+    // bit patterns; N-order units sum duplicates in FP32 and are truncated to
+    // TF32 after the scatter.
+    for (int j0 = 0; j0 < T.w; j0 += 128 * kScU) {
+      uint32_t lq[kScU];
+      double vq[kScU];
 #pragma unroll
-    for (int q = 0; q < NTMAX; ++q) {
-      const int nt = nt0 + q * ntstep;
+      for (int u = 0; u < kScU; ++u) {
+        const int j = j0 + u * 128 + tid;
+        if (j < T.w) {
+          lq[u] = a.lid[st + j];
+          vq[u] = a.val[st + j];
+        }
+      }
 #pragma unroll
-      for (int x = 0; x < 4; ++x) acc[q][x] = 0.0;
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        bf[q][ks][0] = bf[q][ks][1] = 0u;
-        if (nt < NT) {
-          bf[q][ks][0] = tf32_bits(fB[(ks * 8 + t4) * Rs + nt * 8 + g]);
-          bf[q][ks][1] = tf32_bits(fB[(ks * 8 + t4 + 4) * Rs + nt * 8 + g]);
+      for (int u = 0; u < kScU; ++u) {
+        const int j = j0 + u * 128 + tid;
+        if (j < T.w) {
+          const uint32_t l = lq[u];
+          const int l0 = (int)(l >> 8), l1 = (int)((l >> 4) & 15), l2 = (int)(l & 15);
+          const int lt = TS == 0 ? l0 : TS == 1 ? l1 : l2;
+          const int lc = CS == 0 ? l0 : CS == 1 ? l1 : l2;
+          const int ls = SS == 0 ? l0 : SS == 1 ? l1 : l2;
+          double v = vq[u];
+          v = v > FLT_MAX ? FLT_MAX : (v < -FLT_MAX ? -FLT_MAX : v);
+          float* dst = X + ls * kSs + lt * kSt + lc;
+          if (a.store_dups) *dst = __uint_as_float(tf32_bits((float)v));
+          else atomicAdd(dst, (float)v);
         }
       }
     }
-    for (int s = my_sg; s < 16; s += SG) {
-      uint32_t af[2][4];
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        const float* base = X + s * kSs + ks * 8;
-        af[ks][0] = tf32_bits(base[g * kSt + t4]);
-        af[ks][1] = tf32_bits(base[(g + 8) * kSt + t4]);
-        af[ks][2] = tf32_bits(base[g * kSt + t4 + 4]);
-        af[ks][3] = tf32_bits(base[(g + 8) * kSt + t4 + 4]);
+    __syncthreads();
+    if (!a.store_dups) {
+      for (int i = tid; i < kTileFloats / 4; i += 128) {
+        float4 x = reinterpret_cast<float4*>(X)[i];
+        x.x = __uint_as_float(tf32_bits(x.x));
+        x.y = __uint_as_float(tf32_bits(x.y));
+        x.z = __uint_as_float(tf32_bits(x.z));
+        x.w = __uint_as_float(tf32_bits(x.w));
+        reinterpret_cast<float4*>(X)[i] = x;
       }
-#pragma unroll
-      for (int q = 0; q < NTMAX; ++q) {
-        const int nt = nt0 + q * ntstep;
-        if (nt >= NT) break;
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-        mma_tf32(d, af[0], bf[q][0][0], bf[q][0][1]);
-        mma_tf32(d, af[1], bf[q][1][0], bf[q][1][1]);
-        const int r = nt * 8 + 2 * t4;
-        const double w0 = F2s[s * R + r], w1 = F2s[s * R + r + 1];
-        acc[q][0] = fma((double)d[0], w0, acc[q][0]);
-        acc[q][1] = fma((double)d[1], w1, acc[q][1]);
-        acc[q][2] = fma((double)d[2], w0, acc[q][2]);
-        acc[q][3] = fma((double)d[3], w1, acc[q][3]);
-      }
+      __syncthreads();
     }
+
+    if (active) {
+      uint32_t bf[NW][2][2];
 #pragma unroll
-    for (int q = 0; q < NTMAX; ++q) {
-      const int nt = nt0 + q * ntstep;
-      if (nt >= NT) break;
-      const int r = nt * 8 + 2 * t4;
-      if (SG == 1) {  // this warp alone owns these columns
-        accS[g * R + r] += acc[q][0];
-        accS[g * R + r + 1] += acc[q][1];
-        accS[(g + 8) * R + r] += acc[q][2];
-        accS[(g + 8) * R + r + 1] += acc[q][3];
-      } else {
-        atomicAdd(&accS[g * R + r], acc[q][0]);
-        atomicAdd(&accS[g * R + r + 1], acc[q][1]);
-        atomicAdd(&accS[(g + 8) * R + r], acc[q][2]);
-        atomicAdd(&accS[(g + 8) * R + r + 1], acc[q][3]);
+      for (int q = 0; q < NW; ++q) {
+        const int nt = nt_base + q;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          bf[q][ks][0] = bf[q][ks][1] = 0u;
+          if (nt < NT) {
+            bf[q][ks][0] = __float_as_uint(fB[(ks * 8 + t4) * Rs + nt * 8 + g]);
+            bf[q][ks][1] = __float_as_uint(fB[(ks * 8 + t4 + 4) * Rs + nt * 8 + g]);
+          }
+        }
+      }
+      for (int s = my_sg; s < 16; s += SG) {
+        uint32_t af[2][4];
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          const float* base = X + s * kSs + ks * 8;
+          af[ks][0] = __float_as_uint(base[g * kSt + t4]);
+          af[ks][1] = __float_as_uint(base[(g + 8) * kSt + t4]);
+          af[ks][2] = __float_as_uint(base[g * kSt + t4 + 4]);
+          af[ks][3] = __float_as_uint(base[(g + 8) * kSt + t4 + 4]);
+        }
+#pragma unroll
+        for (int q = 0; q < NW; ++q) {
+          const int nt = nt_base + q;
+          if (nt >= NT) break;
+          float d[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_tf32(d, af[0], bf[q][0][0], bf[q][0][1]);
+          mma_tf32(d, af[1], bf[q][1][0], bf[q][1][1]);
+          const double2 w = *reinterpret_cast<const double2*>(F2s + s * R + nt * 8 + 2 * t4);
+          acc[q][0] = fma((double)d[0], w.x, acc[q][0]);
+          acc[q][1] = fma((double)d[1], w.y, acc[q][1]);
+          acc[q][2] = fma((double)d[2], w.x, acc[q][2]);
+          acc[q][3] = fma((double)d[3], w.y, acc[q][3]);
+        }
       }
     }
   }
@@ -538,11 +597,15 @@ void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, const uint32
   const int R = a.R;
   const size_t smem = tile_smem(R);
   const int NT = R / 8;
-  const int ntm = NT <= 4 ? 1 : NT <= 8 ? 2 : NT <= 12 ? 3 : 4;
+  const int ntm = NT < 4 ? NT : 4;  // n-tiles per warp
   const int roles = a.tslot * 100 + a.cslot * 10 + a.sslot;
+  static const int minb = [] {
+    const char* e = std::getenv("CPTC_TILES_MINB");
+    return e ? std::atoi(e) : 4;
+  }();
 #define CPTC_TILES(TS_, CS_, SS_, NTM)                                                     \
   do {                                                                                     \
-    auto kern = k_tiles<TS_, CS_, SS_, NTM>;                                               \
+    auto kern = (minb == 5) ? k_tiles<TS_, CS_, SS_, NTM, 5> : k_tiles<TS_, CS_, SS_, NTM, 4>; \
     CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                                    (int)smem));                                            \
     CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,   \
