@@ -23,7 +23,6 @@
 //    consecutive tiles of the same 16 output rows in shared memory and
 //    issues the FP64 atomics once per row block instead of once per tile.
 #include <cfloat>
-#include <cstdlib>
 
 #include <cub/cub.cuh>
 
@@ -599,13 +598,11 @@ void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, const uint32
   const int NT = R / 8;
   const int ntm = NT < 4 ? NT : 4;  // n-tiles per warp
   const int roles = a.tslot * 100 + a.cslot * 10 + a.sslot;
-  static const int minb = [] {
-    const char* e = std::getenv("CPTC_TILES_MINB");
-    return e ? std::atoi(e) : 4;
-  }();
+  // 4 resident CTAs per SM (<= 128 registers): measured against 5 (96
+  // registers, spills at 4 n-tiles per warp) on config 4, 4 is faster.
 #define CPTC_TILES(TS_, CS_, SS_, NTM)                                                     \
   do {                                                                                     \
-    auto kern = (minb == 5) ? k_tiles<TS_, CS_, SS_, NTM, 5> : k_tiles<TS_, CS_, SS_, NTM, 4>; \
+    auto kern = k_tiles<TS_, CS_, SS_, NTM, 4>;                                            \
     CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                                    (int)smem));                                            \
     CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,   \
