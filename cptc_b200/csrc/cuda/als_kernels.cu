@@ -222,44 +222,75 @@ __global__ void __launch_bounds__(1024) k_pinv_jacobi(const double* __restrict__
 //  ridge = 0: a pivot d <= 1e-11 * max diag (condition beyond ~1e11) rejects
 //    the inverse: *fail is set and the pseudo-inverse kernel that follows
 //    computes Ainv instead.
-// All R*R entries are updated in parallel per pivot (warp = row, lane =
-// column), two barriers per pivot.
+// One CTA; all R*R entries are updated in parallel per pivot from registers,
+// one barrier per pivot.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) k_sweep_inverse(GPtrs g, int ng, int R, int ridge,
+template <int NWARP, int RM, int RC>
+__global__ void __launch_bounds__(NWARP * 32) k_sweep_inverse(GPtrs g, int ng, int R, int ridge,
                                                         double* __restrict__ FtF,
                                                         double* __restrict__ Ainv,
                                                         int* __restrict__ status,
                                                         int* __restrict__ fail) {
-  extern __shared__ double M[];  // R*R row-major, then the pivot row (R)
-  double* prow = M + R * R;
+  // The matrix lives in registers: thread (warp w, lane l) holds entries
+  // (w + NWARP*m, l + 32c), m < RM, c < RC.  Per pivot the warp owning row j writes
+  // it to shared memory (two buffers, so one barrier per pivot suffices) and
+  // every thread updates its own entries: no shared-memory read-modify-write.
+  __shared__ double prow[2][128];
+  __shared__ double diag[128];
   __shared__ double eps_s, dmax_s;
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
-  const int RR = R * R;
-  for (int k = tid; k < RR; k += blockDim.x) {
-    double v = 1.0;
-    for (int q = 0; q < ng; ++q) v *= g.p[q][k];
-    FtF[k] = v;
-    M[k] = v;
-  }
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  double M[RM][RC];
+#pragma unroll
+  for (int m = 0; m < RM; ++m)
+#pragma unroll
+    for (int c = 0; c < RC; ++c) {
+      const int i = w + NWARP * m, k = lane + 32 * c;
+      double v = 0.0;
+      if (i < R && k < R) {
+        v = 1.0;
+#pragma unroll
+        for (int q = 0; q < CPTC_MAX_ORDER; ++q)
+          if (q < ng) v *= g.p[q][i * R + k];
+        FtF[i * R + k] = v;
+        if (i == k) diag[i] = v;
+      }
+      M[m][c] = v;
+    }
   __syncthreads();
   if (tid == 0) {
     double tr = 0.0, dm = 0.0;
     for (int i = 0; i < R; ++i) {
-      tr += M[i * R + i];
-      dm = fmax(dm, M[i * R + i]);
+      tr += diag[i];
+      dm = fmax(dm, diag[i]);
     }
     eps_s = ridge ? 1e-12 * ((tr > 0.0) ? tr / (double)R : 1.0) + 1e-300 : 0.0;
     dmax_s = dm;
   }
   __syncthreads();
   const double eps = eps_s, dmax = dmax_s;
-  if (ridge)
-    for (int i = tid; i < R; i += blockDim.x) M[i * R + i] += eps;
+  if (ridge) {
+#pragma unroll
+    for (int m = 0; m < RM; ++m)
+#pragma unroll
+      for (int c = 0; c < RC; ++c)
+        if (w + NWARP * m == lane + 32 * c && w + NWARP * m < R) M[m][c] += eps;
+  }
   for (int j = 0; j < R; ++j) {
+    double* pr = prow[j & 1];
+    if (w == (j % NWARP)) {
+      // Select chain over the compile-time row index (a runtime index would
+      // move M to local memory).
+      const int mj = j / NWARP;
+#pragma unroll
+      for (int c = 0; c < RC; ++c) {
+        double val = M[0][c];
+#pragma unroll
+        for (int m = 1; m < RM; ++m) val = (m == mj) ? M[m][c] : val;
+        if (lane + 32 * c < R) pr[lane + 32 * c] = val;
+      }
+    }
     __syncthreads();
-    for (int k = tid; k < R; k += blockDim.x) prow[k] = M[j * R + k];
-    __syncthreads();
-    double d = prow[j];
+    double d = pr[j];
     if (ridge) {
       if (!(d > 0.0)) d = eps;
     } else if (!(d > 1e-11 * dmax)) {
@@ -267,24 +298,39 @@ __global__ void __launch_bounds__(1024) k_sweep_inverse(GPtrs g, int ng, int R, 
       return;  // every thread sees the same d: uniform exit
     }
     const double inv = 1.0 / d;
-    for (int i = wid; i < R; i += nw) {
-      const double pi = prow[i];
-      for (int k = lane; k < R; k += 32) {
+    double pks[RC];
+#pragma unroll
+    for (int c = 0; c < RC; ++c) {
+      const int k = lane + 32 * c;
+      pks[c] = (k < R) ? pr[k] * inv : 0.0;
+    }
+#pragma unroll
+    for (int m = 0; m < RM; ++m) {
+      const int i = w + NWARP * m;
+      const double pi = (i < R) ? pr[i] : 0.0;
+#pragma unroll
+      for (int c = 0; c < RC; ++c) {
+        const int k = lane + 32 * c;
         double v;
-        if (i == j) v = (k == j) ? -inv : prow[k] * inv;
+        if (i == j) v = (k == j) ? -inv : pks[c];
         else if (k == j) v = pi * inv;
-        else v = M[i * R + k] - pi * prow[k] * inv;
-        M[i * R + k] = v;
+        else v = fma(-pi, pks[c], M[m][c]);
+        M[m][c] = v;
       }
     }
   }
-  __syncthreads();
   if (tid == 0 && fail) *fail = 0;
-  for (int k = tid; k < RR; k += blockDim.x) {
-    const double v = -M[k];
-    Ainv[k] = v;
-    if (!isfinite(v)) atomicExch(status, 1);
-  }
+#pragma unroll
+  for (int m = 0; m < RM; ++m)
+#pragma unroll
+    for (int c = 0; c < RC; ++c) {
+      const int i = w + NWARP * m, k = lane + 32 * c;
+      if (i < R && k < R) {
+        const double v = -M[m][c];
+        Ainv[i * R + k] = v;
+        if (!isfinite(v)) atomicExch(status, 1);
+      }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -530,12 +576,14 @@ void launch_sym_inverse(const double* const* Gs, int ng, int R, int mode, double
   GPtrs g{};
   for (int k = 0; k < ng; ++k) g.p[k] = Gs[k];
   if (mode != kInvPinv) {
-    const size_t ssm = ((size_t)R * R + R) * sizeof(double);
-    CPTC_CUDA(cudaFuncSetAttribute(k_sweep_inverse, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)ssm));
-    const int threads = 32 * (R < 32 ? R : 32);
-    k_sweep_inverse<<<1, threads, ssm, s>>>(g, ng, R, mode == kInvCholRidge ? 1 : 0, FtF, Ainv,
-                                           status, mode == kInvAuto ? gate : nullptr);
+    // (warps, rows per warp, 32-column slices per lane): the R x R matrix
+    // stays in registers (R = 128: 32 doubles per thread, 512 threads).
+    const int rdg = mode == kInvCholRidge ? 1 : 0;
+    int* fl = mode == kInvAuto ? gate : nullptr;
+    if (R <= 32) k_sweep_inverse<32, 1, 1><<<1, 1024, 0, s>>>(g, ng, R, rdg, FtF, Ainv, status, fl);
+    else if (R <= 64) k_sweep_inverse<16, 4, 2><<<1, 512, 0, s>>>(g, ng, R, rdg, FtF, Ainv, status, fl);
+    else if (R <= 96) k_sweep_inverse<16, 6, 3><<<1, 512, 0, s>>>(g, ng, R, rdg, FtF, Ainv, status, fl);
+    else k_sweep_inverse<16, 8, 4><<<1, 512, 0, s>>>(g, ng, R, rdg, FtF, Ainv, status, fl);
     CPTC_LAUNCH_CHECK();
     if (mode == kInvCholRidge) return;
   } else {

@@ -70,17 +70,24 @@ Engine::Engine(int dev) : device(dev) {
   CPTC_REQUIRE(dev >= 0 && dev < n, CPTC_E_ARG, "no such CUDA device");
   CPTC_CUDA(cudaSetDevice(dev));
   CPTC_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  CPTC_CUDA(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
   for (auto& e : ev) CPTC_CUDA(cudaEventCreate(&e));
+  CPTC_CUDA(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming));
+  CPTC_CUDA(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming));
   CPTC_CUDA(cudaMallocHost((void**)&h_scal, 8 * sizeof(double)));
 }
 
 Engine::~Engine() {
   cudaSetDevice(device);
   if (stream) cudaStreamSynchronize(stream);
+  if (side) cudaStreamSynchronize(side);
   comm_destroy(*this);
   for (auto& e : ev)
     if (e) cudaEventDestroy(e);
+  if (ev_fork) cudaEventDestroy(ev_fork);
+  if (ev_join) cudaEventDestroy(ev_join);
   if (h_scal) cudaFreeHost(h_scal);
+  if (side) cudaStreamDestroy(side);
   if (stream) cudaStreamDestroy(stream);
 }
 
@@ -385,8 +392,11 @@ void Engine::fetch_rows(const double* dev, int m, double* host) {
 // FtV = MTTKRP of `mode` (relabelled rows): zero, dense tiles, residual.
 void Engine::mttkrp(int mode) {
   CPTC_CUDA(cudaMemsetAsync(FtV.p, 0, padded_rows(mode) * (uint64_t)R * sizeof(double), stream));
-  mttkrp_tiles(mode);
+  // The residual kernel first: its many short CTAs rebalance around an SM
+  // that the side stream's inverse may hold; the persistent tile grid is
+  // launched once that SM is free again.
   mttkrp_sparse(mode);
+  mttkrp_tiles(mode);
 }
 
 void Engine::mttkrp_tiles(int mode) {
@@ -462,18 +472,25 @@ void Engine::update_mode(int n) {
   int ng = 0;
   for (int m = 0; m < N; ++m)
     if (m != n) gs[ng++] = G[m].p;
+  // Order 3: the reference solves with a truncated SVD pseudo-inverse; by
+  // default the same result is obtained by the sweep inverse when FtF is
+  // well conditioned (the pseudo-inverse kernel runs only when it is not).
+  // N-order: the reference's ridge rule.  The inverse needs only the other
+  // modes' Grams, so it runs on the side stream during this mode's MTTKRP;
+  // it is launched first so that its single CTA is placed before the
+  // MTTKRP fills the GPU.
+  int inv = generic ? kInvCholRidge : kInvAuto;
+  if (opts.solver == CPTC_SOLVER_CHOL) inv = kInvCholRidge;
+  if (opts.solver == CPTC_SOLVER_PINV) inv = kInvPinv;
+  CPTC_CUDA(cudaEventRecord(ev_fork, stream));
+  CPTC_CUDA(cudaStreamWaitEvent(side, ev_fork, 0));
+  launch_sym_inverse(gs, ng, R, inv, FtF.p, Ainv.p, status.p, side);
+  CPTC_CUDA(cudaEventRecord(ev_join, side));
   cudaEventRecord(ev[2 * n], stream);
   mttkrp(n);
   cudaEventRecord(ev[2 * n + 1], stream);
   comm_reduce_scatter_ftv(*this, n);
-  // Order 3: the reference solves with a truncated SVD pseudo-inverse; by
-  // default the same result is obtained by Cholesky when FtF is well
-  // conditioned (the pseudo-inverse kernel runs only when it is not).
-  // N-order: the reference's ridge Cholesky.
-  int inv = generic ? kInvCholRidge : kInvAuto;
-  if (opts.solver == CPTC_SOLVER_CHOL) inv = kInvCholRidge;
-  if (opts.solver == CPTC_SOLVER_PINV) inv = kInvPinv;
-  launch_sym_inverse(gs, ng, R, inv, FtF.p, Ainv.p, status.p, stream);
+  CPTC_CUDA(cudaStreamWaitEvent(stream, ev_join, 0));
   const uint64_t lo = row_lo(n), rows = row_hi(n) - lo;
   const int nb = launch_apply_solve(FtV.p + lo * R, Ainv.p, lambda.p, generic ? 0 : 1, rows, R,
                                     F[n].p + lo * R, gpart.p, gpart_blocks, stream);

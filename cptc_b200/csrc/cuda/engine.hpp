@@ -80,6 +80,10 @@ double b200_fill_min(int R);
 struct Engine {
   int device = 0;
   cudaStream_t stream = nullptr;
+  // Side stream for the R x R inverse of a mode update, which needs only the
+  // other modes' Grams and so runs beside that mode's MTTKRP.
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   std::string err;
 
   // Tensor (device COO, relabelled in place by the build).
