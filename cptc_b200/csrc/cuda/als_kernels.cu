@@ -454,14 +454,15 @@ __global__ void __launch_bounds__(256) k_col_dots(const double* __restrict__ F,
 }
 
 __global__ void k_fit_final(const double* __restrict__ dot_part, int nblk,
-                            const double* __restrict__ lambda, GPtrs g, int ng, int R,
-                            double* __restrict__ out) {
+                            const double* __restrict__ scale, const double* __restrict__ lambda,
+                            GPtrs g, int ng, int R, double* __restrict__ out) {
   __shared__ double sh[1024];
   const int tid = threadIdx.x;
   double ip = 0.0, m2 = 0.0;
   for (int r = tid; r < R; r += blockDim.x) {
     double d = 0.0;
     for (int b = 0; b < nblk; ++b) d += dot_part[(uint64_t)b * R + r];
+    if (scale) d *= scale[r];
     ip += lambda[r] * d;
   }
   for (int i = tid; i < R * R; i += blockDim.x) {
@@ -651,11 +652,11 @@ int launch_col_dots(const double* F, const double* FtV, uint64_t rows, int R, do
   return nblk;
 }
 
-void launch_fit_final(const double* dot_part, int nblk, const double* lambda,
+void launch_fit_final(const double* dot_part, int nblk, const double* scale, const double* lambda,
                       const double* const* Gs, int ng, int R, double* out, cudaStream_t s) {
   GPtrs g{};
   for (int k = 0; k < ng; ++k) g.p[k] = Gs[k];
-  k_fit_final<<<1, 1024, 0, s>>>(dot_part, nblk, lambda, g, ng, R, out);
+  k_fit_final<<<1, 1024, 0, s>>>(dot_part, nblk, scale, lambda, g, ng, R, out);
   CPTC_LAUNCH_CHECK();
 }
 

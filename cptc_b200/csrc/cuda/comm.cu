@@ -34,6 +34,7 @@ int comm_unique_id(unsigned char out[128]) {
 void comm_init(Engine& E, const unsigned char idb[128], int rank, int nranks) {
   CPTC_REQUIRE(nranks >= 1 && rank >= 0 && rank < nranks, CPTC_E_ARG, "bad rank / nranks");
   CPTC_CUDA(cudaSetDevice(E.device));
+  E.release_graph();  // it may hold NCCL calls on the old communicator
   comm_destroy(E);
   if (nranks == 1) {
     E.nranks = 1;
@@ -72,20 +73,20 @@ void comm_prepare(Engine& E) {
   }
 }
 
-const double* comm_reduce_gram(Engine& E, int nblk) {
+const double* comm_reduce_gram_gather(Engine& E, int n, int nblk, int ndots) {
   const int RR = E.R * E.R;
   double* out = E.comm_buf.p;
   launch_partial_sum(E.gpart.p, nblk, RR, out, E.stream);
-  if (E.nranks > 1)
-    CPTC_NCCL(ncclAllReduce(out, out, RR, ncclDouble, ncclSum, comm_of(E), E.stream));
-  return out;
-}
-
-const double* comm_reduce_dots(Engine& E, int nblk) {
-  double* out = E.comm_buf.p + (size_t)E.R * E.R;
-  launch_partial_sum(E.dots.p, nblk, E.R, out, E.stream);
-  if (E.nranks > 1)
-    CPTC_NCCL(ncclAllReduce(out, out, E.R, ncclDouble, ncclSum, comm_of(E), E.stream));
+  if (ndots > 0) launch_partial_sum(E.dots.p, ndots, E.R, out + RR, E.stream);
+  if (E.nranks > 1) {
+    const uint64_t cnt = slab_rows(E, n) * (uint64_t)E.R;
+    double* F = E.F[n].p;
+    CPTC_NCCL(ncclGroupStart());
+    CPTC_NCCL(ncclAllReduce(out, out, RR + (ndots > 0 ? E.R : 0), ncclDouble, ncclSum, comm_of(E),
+                            E.stream));
+    CPTC_NCCL(ncclAllGather(F + (uint64_t)E.rank * cnt, F, cnt, ncclDouble, comm_of(E), E.stream));
+    CPTC_NCCL(ncclGroupEnd());
+  }
   return out;
 }
 
@@ -103,8 +104,6 @@ static void allgather_slabs(Engine& E, int n, double* base) {
   CPTC_NCCL(ncclAllGather(base + (uint64_t)E.rank * cnt, base, cnt, ncclDouble, comm_of(E),
                           E.stream));
 }
-
-void comm_allgather_factor(Engine& E, int n) { allgather_slabs(E, n, E.F[n].p); }
 
 void comm_reduce_ftv(Engine& E, int n) {
   comm_reduce_scatter_ftv(E, n);

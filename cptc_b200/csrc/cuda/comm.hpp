@@ -21,15 +21,14 @@ int comm_unique_id(unsigned char out[128]);
 // Rows per slab of mode m (slab r = rows [r * s, min((r + 1) * s, I_m))).
 uint64_t slab_rows(const Engine& E, int m);
 
-// Sum of the nblk per-block Gram partials (R x R) over blocks and ranks, in
-// a fixed order; returns the device address of the single summed Gram.
-const double* comm_reduce_gram(Engine& E, int nblk);
-// The same for the per-block column dot products (R) of the fit.
-const double* comm_reduce_dots(Engine& E, int nblk);
+// Sums, in a fixed order over blocks and ranks, the nblk per-block Gram
+// partials (R x R) and, when ndots > 0, the ndots per-block column dot
+// products (R, stored after the Gram); with several ranks the all-reduce is
+// grouped with the all-gather of this rank's solved slab of F[n] into every
+// rank's replica.  Returns the device address of the summed Gram.
+const double* comm_reduce_gram_gather(Engine& E, int n, int nblk, int ndots);
 // Partial MTTKRP rows of every rank summed into each rank's slab of FtV.
 void comm_reduce_scatter_ftv(Engine& E, int n);
-// Every rank's slab of F[n] to every rank (in place).
-void comm_allgather_factor(Engine& E, int n);
 // The full reduced FtV on every rank (reduce-scatter + all-gather).
 void comm_reduce_ftv(Engine& E, int n);
 

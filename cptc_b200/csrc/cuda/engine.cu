@@ -14,6 +14,7 @@
 #include "../host/coo.hpp"
 #include "../host/reorder.hpp"
 #include "comm.hpp"
+#include <cstdlib>
 #include "kernels.hpp"
 
 namespace cptc {
@@ -81,6 +82,7 @@ Engine::~Engine() {
   cudaSetDevice(device);
   if (stream) cudaStreamSynchronize(stream);
   if (side) cudaStreamSynchronize(side);
+  release_graph();  // before the communicator its NCCL nodes use
   comm_destroy(*this);
   for (auto& e : ev)
     if (e) cudaEventDestroy(e);
@@ -109,6 +111,7 @@ void Engine::load(const cptc_coo* t) {
                "tensor order must be in [2, 8]");
   CPTC_REQUIRE(t->nnz < (1ull << 32), CPTC_E_UNSUP, "more than 2^32-1 nonzeros");
   CPTC_CUDA(cudaSetDevice(device));
+  release_graph();
   built = false;
   have_factors = false;
   views.clear();
@@ -193,6 +196,7 @@ void Engine::alloc_workspace() {
   gpart.alloc((uint64_t)gpart_blocks * R * R);
   dots.alloc((uint64_t)gpart_blocks * R);
   comm_buf.alloc((uint64_t)R * R + R);
+  cscale.alloc(R);
   scal.alloc(8);
   status.alloc(1);
   lambda.alloc(R);
@@ -212,6 +216,7 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
   else cptc_opts_default(&opts);
   R = R_;
   generic = (N != 3) || opts.generic;
+  release_graph();
   built = false;
   have_factors = false;
   views.clear();
@@ -467,7 +472,7 @@ void Engine::gram_of(int m) {
 // divide by lambda, norm < 1e-14 zeroes the column, lambda *= norm.
 // N-order semantics (src/generic.cu:2109-2170): ridge Cholesky (default),
 // lambda = norms with norm < 1e-14 -> 1.
-void Engine::update_mode(int n) {
+void Engine::update_mode(int n, bool last) {
   const double* gs[CPTC_MAX_ORDER];
   int ng = 0;
   for (int m = 0; m < N; ++m)
@@ -486,23 +491,87 @@ void Engine::update_mode(int n) {
   CPTC_CUDA(cudaStreamWaitEvent(side, ev_fork, 0));
   launch_sym_inverse(gs, ng, R, inv, FtF.p, Ainv.p, status.p, side);
   CPTC_CUDA(cudaEventRecord(ev_join, side));
-  cudaEventRecord(ev[2 * n], stream);
+  // Per-mode MTTKRP timing; while the iteration is being captured the
+  // records must be External so that the graph performs them.
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  CPTC_CUDA(cudaStreamIsCapturing(stream, &cs));
+  const unsigned rf = (cs == cudaStreamCaptureStatusActive) ? cudaEventRecordExternal
+                                                            : cudaEventRecordDefault;
+  CPTC_CUDA(cudaEventRecordWithFlags(ev[2 * n], stream, rf));
   mttkrp(n);
-  cudaEventRecord(ev[2 * n + 1], stream);
+  CPTC_CUDA(cudaEventRecordWithFlags(ev[2 * n + 1], stream, rf));
   comm_reduce_scatter_ftv(*this, n);
   CPTC_CUDA(cudaStreamWaitEvent(stream, ev_join, 0));
   const uint64_t lo = row_lo(n), rows = row_hi(n) - lo;
   const int nb = launch_apply_solve(FtV.p + lo * R, Ainv.p, lambda.p, generic ? 0 : 1, rows, R,
                                     F[n].p + lo * R, gpart.p, gpart_blocks, stream);
-  const double* gsum = comm_reduce_gram(*this, nb);
+  // The last mode also yields the fit's column dot products, taken on the
+  // solved (not yet normalised) rows and scaled with the column scales.
+  const int nd = last ? launch_col_dots(F[n].p + lo * R, FtV.p + lo * R, rows, R, dots.p,
+                                        gpart_blocks, stream)
+                      : 0;
+  // One all-reduce (Gram partials, dot products) grouped with the all-gather
+  // of the solved slab; every rank then normalises the whole factor.
+  const double* gsum = comm_reduce_gram_gather(*this, n, nb, nd);
   launch_norm_finalize(gsum, 1, R, generic ? 1 : 0, lambda.p, G[n].p, colscale(), stream);
-  launch_scale_cols(F[n].p + lo * R, rows, R, colscale(), stream);
-  comm_allgather_factor(*this, n);
+  launch_scale_cols(F[n].p, dims[n], R, colscale(), stream);
+  if (last) {
+    const double* gall[CPTC_MAX_ORDER];
+    for (int m = 0; m < N; ++m) gall[m] = G[m].p;
+    launch_fit_final(gsum + (size_t)R * R, 1, colscale(), lambda.p, gall, N, R, scal.p, stream);
+  }
 }
 
-double* Engine::colscale() {
-  if (!cscale.p) cscale.alloc(R);
-  return cscale.p;
+double* Engine::colscale() { return cscale.p; }
+
+void Engine::release_graph() {
+  if (iter_exec) cudaGraphExecDestroy(iter_exec);
+  if (iter_graph) cudaGraphDestroy(iter_graph);
+  iter_exec = nullptr;
+  iter_graph = nullptr;
+}
+
+// One ALS iteration on the stream: every mode update, then the fit and the
+// solve status copied to pinned host memory.
+void Engine::enqueue_iteration() {
+  for (int n = 0; n < N; ++n) update_mode(n, n == N - 1);
+  CPTC_CUDA(cudaMemcpyAsync(h_scal, scal.p, 2 * sizeof(double), cudaMemcpyDeviceToHost, stream));
+  CPTC_CUDA(cudaMemcpyAsync(h_scal + 4, status.p, sizeof(int), cudaMemcpyDeviceToHost, stream));
+}
+
+// The iteration is captured once into a CUDA graph (kernels, the side
+// stream's inverse, NCCL calls, the readback) and replayed with one launch,
+// so host launch overhead does not gap the GPU between the short solve
+// kernels; set CPTC_GRAPH=0 to launch it stream-ordered instead.
+void Engine::launch_iteration() {
+  static const bool use_graph = [] {
+    const char* e = std::getenv("CPTC_GRAPH");
+    return !(e && e[0] == '0');
+  }();
+  // The iteration's start and end events are recorded outside the graph:
+  // the host waits on the end event for the fit.
+  CPTC_CUDA(cudaEventRecord(ev[2 * CPTC_MAX_ORDER], stream));
+  if (!use_graph) {
+    enqueue_iteration();
+    CPTC_CUDA(cudaEventRecord(ev[2 * CPTC_MAX_ORDER + 1], stream));
+    return;
+  }
+  if (!iter_exec) {
+    CPTC_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
+    try {
+      enqueue_iteration();
+    } catch (...) {
+      cudaGraph_t g = nullptr;
+      cudaStreamEndCapture(stream, &g);
+      if (g) cudaGraphDestroy(g);
+      cudaGetLastError();
+      throw;
+    }
+    CPTC_CUDA(cudaStreamEndCapture(stream, &iter_graph));
+    CPTC_CUDA(cudaGraphInstantiate(&iter_exec, iter_graph, 0));
+  }
+  CPTC_CUDA(cudaGraphLaunch(iter_exec, stream));
+  CPTC_CUDA(cudaEventRecord(ev[2 * CPTC_MAX_ORDER + 1], stream));
 }
 
 void Engine::als(int iters, cptc_iter_cb cb, void* user) {
@@ -515,21 +584,10 @@ void Engine::als(int iters, cptc_iter_cb cb, void* user) {
   CPTC_CUDA(cudaMemsetAsync(status.p, 0, sizeof(int), stream));
   const double xn = std::sqrt(x_norm_sq);
   for (int it = 0; it < iters; ++it) {
-    cudaEventRecord(ev[2 * CPTC_MAX_ORDER], stream);
-    for (int n = 0; n < N; ++n) update_mode(n);
-    // Gram fit from the last mode's MTTKRP and factor.
-    const int last = N - 1;
-    const uint64_t lo = row_lo(last), rows = row_hi(last) - lo;
-    const int nb = launch_col_dots(F[last].p + lo * R, FtV.p + lo * R, rows, R, dots.p,
-                                   gpart_blocks, stream);
-    const double* dsum = comm_reduce_dots(*this, nb);
-    const double* gs[CPTC_MAX_ORDER];
-    for (int m = 0; m < N; ++m) gs[m] = G[m].p;
-    launch_fit_final(dsum, 1, lambda.p, gs, N, R, scal.p, stream);
-    CPTC_CUDA(cudaMemcpyAsync(h_scal, scal.p, 2 * sizeof(double), cudaMemcpyDeviceToHost, stream));
+    // Gram fit from the last mode's MTTKRP and factor (computed inside the
+    // last mode's update).
+    launch_iteration();
     int h_status = 0;
-    CPTC_CUDA(cudaMemcpyAsync(h_scal + 4, status.p, sizeof(int), cudaMemcpyDeviceToHost, stream));
-    cudaEventRecord(ev[2 * CPTC_MAX_ORDER + 1], stream);
     CPTC_CUDA(cudaEventSynchronize(ev[2 * CPTC_MAX_ORDER + 1]));
     std::memcpy(&h_status, h_scal + 4, sizeof(int));
     CPTC_REQUIRE(h_status == 0, CPTC_E_NUMERIC, "non-finite values in the R x R solve");

@@ -84,6 +84,10 @@ struct Engine {
   // other modes' Grams and so runs beside that mode's MTTKRP.
   cudaStream_t side = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  // One ALS iteration captured as a CUDA graph (rebuilt after load, build
+  // and communicator changes).
+  cudaGraph_t iter_graph = nullptr;
+  cudaGraphExec_t iter_exec = nullptr;
   std::string err;
 
   // Tensor (device COO, relabelled in place by the build).
@@ -144,6 +148,9 @@ struct Engine {
   void get_factor(int m, double* host);
   void fetch_rows(const double* dev, int m, double* host);
   double* stage_rows();
+  void release_graph();
+  void enqueue_iteration();
+  void launch_iteration();
   uint64_t padded_rows(int m) const;
   void permute_rows(const double* in, int m, bool to_relabelled, double* out);
   void mttkrp(int mode);  // into FtV (relabelled rows), stream-ordered
@@ -159,7 +166,7 @@ struct Engine {
  private:
   void reorder();
   void alloc_workspace();
-  void update_mode(int n);
+  void update_mode(int n, bool last);
   void gram_of(int m);
 };
 

@@ -101,8 +101,9 @@ void launch_scale_cols(double* F, uint64_t rows, int R, const double* scale, cud
 // dots[r] partials of sum_i F[i,r] * FtV[i,r]; returns nblk.
 int launch_col_dots(const double* F, const double* FtV, uint64_t rows, int R, double* part,
                     int max_blocks, cudaStream_t s);
-// out[0] = iprod = sum_r lambda_r dot_r, out[1] = model^2.
-void launch_fit_final(const double* dot_part, int nblk, const double* lambda,
+// out[0] = iprod = sum_r lambda_r dot_r (dot_r * scale[r] when scale is
+// given), out[1] = model^2.
+void launch_fit_final(const double* dot_part, int nblk, const double* scale, const double* lambda,
                       const double* const* Gs, int ng, int R, double* out, cudaStream_t s);
 // part[b] = partial sums of (v - sum_r lambda_r prod_m F_m[i_m, r])^2.
 struct ResidualArgs {

@@ -8,10 +8,11 @@ for the order-3 ALS.  Work and ownership are split separately:
     a heavy row is shared by several ranks;
   * ownership: rows in G equal slabs (ceil(I/G) rows each).
 Per mode: partial MTTKRP of the rank's chunk -> reduce-scatter into the slabs
--> solve of the own slab -> all-reduce of the partial Gram (column norms are
-its diagonal) -> normalisation -> all-gather of the slabs.  The fit
-all-reduces per-column dot products of the last mode.  Run with gloo it checks
-the order and payload of the collectives on the host.
+-> solve of the own slab -> one all-reduce of the partial Gram (column norms
+are its diagonal; the last mode appends the fit's column dot products) beside
+the all-gather of the unnormalised slabs -> every rank normalises the whole
+factor.  Run with gloo it checks the order and payload of the collectives on
+the host.
 """
 from __future__ import annotations
 
@@ -88,15 +89,22 @@ def shard_als3(t, R, iters, rank, world, dist):
             A = truncated_pinv(FtF, R)
             Fl = np.zeros((s, R))
             Fl[:hi - lo] = Ms[:hi - lo] @ A.T / lam
-            Gs = allreduce(Fl.T @ Fl)
+            # one all-reduce (Gram partials, and for the last mode the fit's
+            # column dots of the unnormalised rows) beside the all-gather of
+            # the unnormalised slab; every rank then normalises the factor
+            payload = [(Fl.T @ Fl).ravel()]
+            if n == 2:
+                payload.append(np.einsum("kr,kr->r", Fl[:hi - lo], Ms[:hi - lo]))
+            red = allreduce(np.concatenate(payload))
+            Gs = red[:R * R].reshape(R, R)
+            Fn = allgather_rows(Fl, s, t.dims[n])
             nr = np.sqrt(np.diag(Gs))
             zero = nr < 1e-14
             scale = np.where(zero, 0.0, 1.0 / np.where(zero, 1.0, nr))
             lam = np.where(zero, 0.0, lam * nr)
-            Fl = Fl * scale
+            F[n] = Fn * scale
             G[n] = Gs * np.outer(scale, scale)
-            F[n] = allgather_rows(Fl, s, t.dims[n])
-        dots = allreduce(np.einsum("kr,kr->r", F[2][lo:hi], Ms[:hi - lo]))
+        dots = red[R * R:] * scale
         iprod = float(lam @ dots)
         model2 = float(lam @ (G[0] * G[1] * G[2]) @ lam)
         fits.append(1 - np.sqrt(max(X2 - 2 * iprod + model2, 0.0)) / np.sqrt(X2))
