@@ -281,6 +281,7 @@ def run_engine(a):
 
     # ---- roofline of the dominant kernel -----------------------------------
     prof = [eng.profile_mttkrp(n, reps=3) for n in range(t.order)]
+    rank_mode_ms = None
 
     if dist is not None:
         import torch
@@ -288,6 +289,11 @@ def run_engine(a):
         v = torch.tensor([dev_s, e2e_s], dtype=torch.float64)
         dist.all_reduce(v, op=dist.ReduceOp.MAX)
         dev_s, e2e_s = float(v[0]), float(v[1])
+        # per-rank MTTKRP times (the iteration waits for the slowest rank)
+        mm = torch.tensor(mode_ms, dtype=torch.float64)
+        gathered = [torch.zeros_like(mm) for _ in range(world)]
+        dist.all_gather(gathered, mm)
+        rank_mode_ms = [[round(float(x), 4) for x in g] for g in gathered]
 
     if rank != 0:
         eng.close()
@@ -345,6 +351,7 @@ def run_engine(a):
             "l2": "views (1.2 GB/mode) stream from HBM each MTTKRP; no flush needed",
             "build_s": build_s,
             "mttkrp_ms_per_mode": mode_ms,
+            "mttkrp_ms_per_mode_by_rank": rank_mode_ms if world > 1 else None,
             "final_fit": fits[-1],
         },
         "e2e": {"value": e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
