@@ -211,8 +211,10 @@ void build_view_order(Engine& E, View& v, int n, const int* order, int nother,
   k_rows_from_pos<<<grid_for(v.nrows, 256, 148 * 16), 256, 0, s>>>(pos.p, v.nrows, E.idx[n].p,
                                                                     perm_a.p, v.rows.p);
   CPTC_LAUNCH_CHECK();
-  // Each rank walks 1/nranks of the tasks: size them for that share.
-  v.task = task_size_for(nsel / (uint64_t)E.nranks);
+  // Sized for the whole view: on 8 GPUs, sizing for a rank's share (256
+  // instead of 1024 on config 4) measured slower (more row-boundary atomics
+  // and task set-up than the occupancy it gains).
+  v.task = task_size_for(nsel);
   v.ntasks = (nsel + v.task - 1) / v.task;
   v.task_row.alloc(v.ntasks);
   k_task_rows<<<grid_for(v.ntasks, 256, 148 * 16), 256, 0, s>>>(pos.p, v.nrows, v.ntasks,
