@@ -437,13 +437,15 @@ def run_reference(a):
             fits.append(float(parts["fit"]))
     timed = times[a.warmup:]
     v = float(np.mean(timed)) / 1000.0
+    med = float(np.median(timed)) if timed else None
     selector = next((ln for ln in out.splitlines() if "avg_fill=" in ln), "")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
             "higher_is_better": False, "n_gpus": 1, "steps": len(timed), "warmup": a.warmup,
             "ms_per_step": v * 1000.0, "scaling": "strong", "vs_baseline": None,
             "dtype": "f64+tf32", "data": "synthetic (same generator and seed)",
             "config": {"workload": workload_name(a), "rank": a.rank, "nnz": t.nnz,
-                       "selector_line": selector[:300], "final_fit": fits[-1] if fits else None},
+                       "selector_line": selector[:300], "final_fit": fits[-1] if fits else None,
+                       "median_ms_per_step": med, "max_ms_per_step": max(timed) if timed else None},
             "cpu_baseline": {"kind": "reference", "cores": 1, "value": v, "unit": UNIT,
                              "sample": "zhixianzhu/cpTC sources rebuilt for sm_100a "
                                        "(oracle/build_ref.sh), one host thread driving one "

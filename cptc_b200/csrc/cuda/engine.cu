@@ -557,6 +557,8 @@ void Engine::launch_iteration() {
     return;
   }
   if (!iter_exec) {
+    // Kernels enqueued during capture are counted when the graph runs.
+    const unsigned long long l0 = g_launches;
     CPTC_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
     try {
       enqueue_iteration();
@@ -565,12 +567,16 @@ void Engine::launch_iteration() {
       cudaStreamEndCapture(stream, &g);
       if (g) cudaGraphDestroy(g);
       cudaGetLastError();
+      g_launches = l0;
       throw;
     }
+    iter_kernels = g_launches - l0;
+    g_launches = l0;
     CPTC_CUDA(cudaStreamEndCapture(stream, &iter_graph));
     CPTC_CUDA(cudaGraphInstantiate(&iter_exec, iter_graph, 0));
   }
   CPTC_CUDA(cudaGraphLaunch(iter_exec, stream));
+  g_launches += iter_kernels;
   CPTC_CUDA(cudaEventRecord(ev[2 * CPTC_MAX_ORDER + 1], stream));
 }
 

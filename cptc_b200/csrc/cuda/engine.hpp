@@ -88,6 +88,7 @@ struct Engine {
   // and communicator changes).
   cudaGraph_t iter_graph = nullptr;
   cudaGraphExec_t iter_exec = nullptr;
+  unsigned long long iter_kernels = 0;  // this library's kernels in the graph
   std::string err;
 
   // Tensor (device COO, relabelled in place by the build).

@@ -110,9 +110,12 @@ const char* cptc_last_error(const cptc_ctx* ctx);
 
 /* Multi-GPU (one process per GPU): rank 0 calls cptc_comm_unique_id and
  * shares the 128 bytes; every rank then calls cptc_comm_init before
- * cptc_build.  Mode-n rows are split into nranks contiguous slabs of equal
- * nonzero count; each mode update ends with an all-reduce of the R x R Gram
- * partials and an all-gather of the updated factor slab. */
+ * cptc_build, and afterwards calls every function of this header in the
+ * same order as the other ranks (they may issue collectives).  Each rank
+ * computes an equal share of every mode's nonzeros; the partial MTTKRP is
+ * reduce-scattered into equal row slabs, each rank solves its slab, and one
+ * grouped call all-reduces the R x R Gram and all-gathers the slabs into
+ * every rank's factor replica.  The reference runs on one GPU. */
 int cptc_comm_unique_id(unsigned char out_id[128]);
 int cptc_comm_init(cptc_ctx* ctx, const unsigned char id[128], int rank, int nranks);
 
@@ -146,7 +149,8 @@ int cptc_mttkrp_timed(cptc_ctx* ctx, int mode, int reps, double* ms);
  * ms3[1] FP64 view kernel, ms3[2] the whole MTTKRP (zero + both). */
 int cptc_profile_mttkrp(cptc_ctx* ctx, int mode, int reps, double ms3[3]);
 
-/* Number of kernels this library has launched since it was loaded. */
+/* Number of kernels this library has launched since it was loaded (a
+ * replayed CUDA graph of an ALS iteration counts the kernels it holds). */
 unsigned long long cptc_launch_count(void);
 
 /* Runs `iters` CP-ALS iterations; cb (nullable) is called after each. */
