@@ -304,7 +304,7 @@ def run_engine(a):
 
     sp = [p["sparse_ms"] for p in prof]
     tl = [p["tiles_ms"] for p in prof]
-    dominant = "k_mttkrp_rec3" if t.order == 3 else "k_mttkrp_view"
+    dominant = "k_mttkrp_rec3s" if t.order == 3 else "k_mttkrp_view"
     nnz_view = st["sparse_nnz"]
     # Per launch (one mode): bytes as SURVEY 8(d) counts them (every factor-row
     # gather) and the compulsory bytes (each stored byte once).

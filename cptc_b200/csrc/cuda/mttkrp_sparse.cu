@@ -16,14 +16,13 @@
 //    fiber sum  sum_e v_e F_g[g_e]  is multiplied by them at the fiber end,
 //    so ~1/fiber-length of the second gather disappears (N-order kernel,
 //    and the order-3 record kernel at R >= 64 where it measures faster);
-//  * element words/values are streamed with evict-first loads so the factor
-//    matrices stay resident in L1/L2; gathers of U elements are issued
-//    before any of them is consumed;
+//  * order 3: the record stream is staged through shared memory by cp.async
+//    (L2 only), N-order: element words/values are streamed with evict-first
+//    loads, so the factor matrices stay resident in L1/L2; gathers of U
+//    elements are issued before any of them is consumed;
 //  * a row that starts and ends inside one task is written with a plain
 //    read-modify-write (it has no other writer in this launch); rows cut by
 //    a task boundary are combined with FP64 atomicAdd.
-#include <cstdlib>
-
 #include "engine.hpp"
 #include "kernels.hpp"
 
@@ -289,38 +288,64 @@ __global__ void __launch_bounds__(256) k_mttkrp_rec3(const uint4* __restrict__ r
   write_row(began && ends);
 }
 
-// Order 3 with fiber reuse: the view is sorted by (target, outer, gathered),
-// so consecutive nonzeros of one fiber share the outer factor row.  The
-// outer row is loaded only for a fiber's first nonzero (the load is still
-// issued with the batch, predicated on the fiber flag) and the fiber sum
-// sum_e v_e F_g[g_e, r] is multiplied by it once, at the fiber's end:
-// acc += (sum_e v_e F_g[g_e, r]) * F_o[o, r].  On config 4 fibers hold 4.4 to
-// 5.8 nonzeros, so ~40% of the factor-row requests disappear.  MINB is the
-// minimum resident CTAs per SM asked of the register allocator.
-template <int GW, int RPL, bool VEC, int U, int MINB>
-__global__ void __launch_bounds__(256, MINB) k_mttkrp_rec3f(const uint4* __restrict__ rec,
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Order 3 with the record stream staged through shared memory: each lane
+// group double-buffers chunks of 2*GW records, copied with cp.async (16
+// bytes per lane, L2 only, so the stream leaves L1 to the factor rows) one
+// chunk ahead; no registers hold prefetched records.  The factor rows are
+// register loads, U nonzeros issued together (staging them in shared memory
+// as well measured 2x slower: it triples traffic on the L1/shared path).
+// Same arithmetic and row/atomic rules as k_mttkrp_rec3.  MINB: minimum
+// resident CTAs per SM asked of the register allocator.
+template <int GW, int RPL, int U, int MINB, bool FIB>
+__global__ void __launch_bounds__(256, MINB) k_mttkrp_rec3s(const uint4* __restrict__ rec,
                                                            const uint32_t* __restrict__ rows,
                                                            const uint32_t* __restrict__ task_row,
                                                            uint64_t nnz, uint64_t task0,
-                                                           uint64_t ntasks,
-                                                           uint32_t tsize, int R,
+                                                           uint64_t ntasks, uint32_t tsize, int R,
                                                            const double* __restrict__ Fg,
                                                            const double* __restrict__ Fo,
                                                            double* __restrict__ out) {
   constexpr int GPW = 32 / GW;
-  const int lane = threadIdx.x & 31;
-  const int glane = lane % GW;
-  const uint64_t task =
-      task0 + ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + lane / GW;
+  constexpr int CH = 2 * GW;  // records per chunk: two per lane
+  static_assert(CH % U == 0, "chunk holds whole batches");
+  __shared__ __align__(16) uint4 sbuf[8 * GPW][2][CH];
+  const int lane = threadIdx.x & 31, glane = lane % GW, gw = lane / GW;
+  const int warp = threadIdx.x >> 5;
+  const int grp = warp * GPW + gw;
+  const unsigned gmask = (GW == 32) ? 0xffffffffu : (((1u << GW) - 1u) << (gw * GW));
+  const uint64_t task = task0 + ((uint64_t)blockIdx.x * 8 + warp) * GPW + gw;
   if (task >= ntasks) return;
-  const Lanes<GW, RPL, VEC> L(glane, R);
+  const Lanes<GW, RPL, true> L(glane, R);
   const uint64_t p0 = task * (uint64_t)tsize;
   const uint64_t p1 = (p0 + tsize < nnz) ? p0 + tsize : nnz;
+  const int n = (int)(p1 - p0);
+  uint4 (*buf)[CH] = sbuf[grp];
 
   uint32_t rowi = task_row[task];
   uint32_t row = rows[rowi];
   bool began = (rec[p0].x & kRowFlag) != 0;
   const bool ends = (p1 == nnz) || (rec[p1].x & kRowFlag);
+
+  auto fetch = [&](int c) {  // chunk c -> buffer c & 1 (records past the task end skipped)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int q = c * CH + h * GW + glane;
+      if (q < n) cp_async16(&buf[c & 1][h * GW + glane], rec + p0 + q);
+    }
+    cp_async_commit();
+  };
 
   double acc[RPL], fs[RPL], fo[RPL];
 #pragma unroll
@@ -335,85 +360,102 @@ __global__ void __launch_bounds__(256, MINB) k_mttkrp_rec3f(const uint4* __restr
       acc[k] = 0.0;
     }
   };
-  // Nonzero e with gathered row g; f holds the outer row when e opens a fiber.
-  auto step = [&](const uint4& e, const double (&g)[RPL], const double (&f)[RPL], bool first) {
-    if (((e.x & kFibFlag) != 0) && !first) {
+  // One nonzero: row change, then acc += (v*g)*f; with FIB the view's sort
+  // order (target, outer, gathered) is used: the outer row is loaded only
+  // for a fiber's first nonzero and the fiber sum sum v*g is multiplied by
+  // it once, at the fiber end (acc += (sum_e v_e g_e) * f).
+  auto step = [&](uint32_t ex, const uint4& e, const double (&g)[RPL], const double (&f)[RPL],
+                  bool first) {
+    const bool fib = (ex & kFibFlag) != 0;
+    if (FIB && fib && !first) {
 #pragma unroll
       for (int k = 0; k < RPL; ++k) {
         acc[k] = fma(fs[k], fo[k], acc[k]);
         fs[k] = 0.0;
       }
-      if (e.x & kRowFlag) {
-        write_row(began);
-        row = rows[++rowi];
-        began = true;
-      }
     }
-    if (((e.x & kFibFlag) != 0) || first) {
-#pragma unroll
-      for (int k = 0; k < RPL; ++k) fo[k] = f[k];
+    if ((ex & kRowFlag) && !first) {
+      write_row(began);
+      row = rows[++rowi];
+      began = true;
     }
     const double v = __hiloint2double((int)e.w, (int)e.z);
+    if (FIB) {
+      if (fib || first) {
 #pragma unroll
-    for (int k = 0; k < RPL; ++k) fs[k] = fma(v, g[k], fs[k]);
-  };
-
-  uint64_t p = p0;
-  const uint64_t pfull = p0 + ((p1 - p0) / U) * U;
-  uint4 cur[U];
-  if (p < pfull) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) cur[u] = __ldcs(rec + p + u);
-  }
-#pragma unroll 1
-  for (; p < pfull; p += U) {
-    double g[U][RPL], f[U][RPL];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      load_row<GW, RPL, VEC>(Fg, cur[u].x & kIdxMask, R, glane, L, g[u]);
-      if ((cur[u].x & kFibFlag) || p + u == p0) {
-        load_row<GW, RPL, VEC>(Fo, cur[u].y, R, glane, L, f[u]);
-      } else {
-#pragma unroll
-        for (int k = 0; k < RPL; ++k) f[u][k] = 0.0;
+        for (int k = 0; k < RPL; ++k) fo[k] = f[k];
       }
-    }
-    uint4 nxt[U];
-    if (p + U < pfull) {
 #pragma unroll
-      for (int u = 0; u < U; ++u) nxt[u] = __ldcs(rec + p + U + u);
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) step(cur[u], g[u], f[u], p + u == p0);
-#pragma unroll
-    for (int u = 0; u < U; ++u) cur[u] = nxt[u];
-  }
-  for (; p < p1; ++p) {  // tail of fewer than U nonzeros
-    const uint4 e = __ldcs(rec + p);
-    double g[RPL], f[RPL];
-    load_row<GW, RPL, VEC>(Fg, e.x & kIdxMask, R, glane, L, g);
-    if ((e.x & kFibFlag) || p == p0) {
-      load_row<GW, RPL, VEC>(Fo, e.y, R, glane, L, f);
+      for (int k = 0; k < RPL; ++k) fs[k] = fma(v, g[k], fs[k]);
     } else {
 #pragma unroll
-      for (int k = 0; k < RPL; ++k) f[k] = 0.0;
+      for (int k = 0; k < RPL; ++k) acc[k] = fma(v * g[k], f[k], acc[k]);
     }
-    step(e, g, f, p == p0);
-  }
+  };
+
+  const int nch = (n + CH - 1) / CH;
+  fetch(0);
+  if (nch > 1) fetch(1);
+  else cp_async_commit();
+#pragma unroll 1
+  for (int c = 0; c < nch; ++c) {
+    cp_async_wait<1>();  // chunk c has landed (chunk c + 1 may be in flight)
+    __syncwarp(gmask);
+    const int q0 = c * CH;
+    const int qe = (q0 + CH < n) ? q0 + CH : n;
+    const uint4* cb = buf[c & 1];
+    int q = q0;
+#pragma unroll 1
+    for (; q + U <= qe; q += U) {
+      double g[U][RPL], f[U][RPL];
+      uint32_t ex[U];
 #pragma unroll
-  for (int k = 0; k < RPL; ++k) acc[k] = fma(fs[k], fo[k], acc[k]);
+      for (int u = 0; u < U; ++u) {
+        const uint4 e = cb[q - q0 + u];
+        ex[u] = e.x;
+        load_row<GW, RPL, true>(Fg, e.x & kIdxMask, R, glane, L, g[u]);
+        if (!FIB || (e.x & kFibFlag) || q + u == 0) {
+          load_row<GW, RPL, true>(Fo, e.y, R, glane, L, f[u]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < RPL; ++k) f[u][k] = 0.0;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) step(ex[u], cb[q - q0 + u], g[u], f[u], q + u == 0);
+    }
+    for (; q < qe; ++q) {
+      const uint4 e = cb[q - q0];
+      double g[RPL], f[RPL];
+      load_row<GW, RPL, true>(Fg, e.x & kIdxMask, R, glane, L, g);
+      if (!FIB || (e.x & kFibFlag) || q == 0) {
+        load_row<GW, RPL, true>(Fo, e.y, R, glane, L, f);
+      } else {
+#pragma unroll
+        for (int k = 0; k < RPL; ++k) f[k] = 0.0;
+      }
+      step(e.x, e, g, f, q == 0);
+    }
+    __syncwarp(gmask);  // every lane is done with buffer c & 1
+    if (c + 2 < nch) fetch(c + 2);
+    else cp_async_commit();
+  }
+  cp_async_wait<0>();
+  if (FIB) {
+#pragma unroll
+    for (int k = 0; k < RPL; ++k) acc[k] = fma(fs[k], fo[k], acc[k]);
+  }
   write_row(began && ends);
 }
 
-template <int GW, int RPL, bool VEC, int U, int MINB>
-void launch_rec3f(const MttkrpArgs& a, cudaStream_t s) {
+template <int GW, int RPL, int U, int MINB, bool FIB = false>
+void launch_rec3s(const MttkrpArgs& a, cudaStream_t s) {
   constexpr int GPW = 32 / GW;
   const uint64_t warps = (a.ntasks - a.task0 + GPW - 1) / GPW;
   const unsigned blocks = (unsigned)((warps + 7) / 8);
-  k_mttkrp_rec3f<GW, RPL, VEC, U, MINB><<<blocks, 256, 0, s>>>(a.rec, a.rows, a.task_row, a.nnz,
+  k_mttkrp_rec3s<GW, RPL, U, MINB, FIB><<<blocks, 256, 0, s>>>(a.rec, a.rows, a.task_row, a.nnz,
                                                                 a.task0, a.ntasks, a.task, a.R,
-                                                                a.Fg,
-                                                                a.Fo[0], a.out);
+                                                                a.Fg, a.Fo[0], a.out);
   CPTC_LAUNCH_CHECK();
 }
 
@@ -442,17 +484,18 @@ void launch(const MttkrpArgs& a, cudaStream_t s) {
 void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
   if (a.nnz == 0 || a.ntasks <= a.task0) return;
   if (a.rec != nullptr) {
-    // Record-kernel variant per rank, measured on config 4 (B200, ms per
-    // mode of the FP64 residual): R=32 plain 1.11 vs fiber reuse 1.27-2.04
-    // (the kernel is latency-bound there and fiber reuse costs registers,
-    // hence resident warps); R=64 fiber 2.28 vs plain 2.74; R=128 fiber with
-    // one nonzero in flight per warp 3.80 vs plain 5.00.
+    // Record kernel per rank, measured on config 4 (B200, ms per mode of the
+    // FP64 residual): staging the record stream through shared memory with
+    // cp.async beats register prefetch at every rank (R=16 0.70 -> 0.58,
+    // R=32 1.10 -> 0.95, R=64 2.27 -> 1.82 with fiber reuse, R=128
+    // 3.75 -> 3.49 with fiber reuse); fiber reuse costs registers and loses
+    // at R <= 32, where the kernel is latency-bound.
     switch (a.R) {
-      case 8: launch_rec3<8, 1, true, 4>(a, s); return;
-      case 16: launch_rec3<8, 2, true, 4>(a, s); return;
-      case 32: launch_rec3<16, 2, true, 2>(a, s); return;
-      case 64: launch_rec3f<16, 4, true, 2, 1>(a, s); return;
-      case 128: launch_rec3f<32, 4, true, 1, 1>(a, s); return;
+      case 8: launch_rec3s<8, 1, 4, 1>(a, s); return;
+      case 16: launch_rec3s<8, 2, 2, 4>(a, s); return;
+      case 32: launch_rec3s<16, 2, 2, 4>(a, s); return;
+      case 64: launch_rec3s<16, 4, 2, 1, true>(a, s); return;
+      case 128: launch_rec3s<32, 4, 1, 1, true>(a, s); return;
       default: break;
     }
     if (a.R <= 32) launch_rec3<32, 1, false, 4>(a, s);
