@@ -273,9 +273,12 @@ def run_engine(a):
         for m in range(t.order):
             eng.set_factor(m, host_F[m])
         eng.als(1)
-        for m in range(t.order):
-            eng.factor(m, out=host_F[m])
-        eng.lam(out=host_lam)
+        # the factors are replicated on every rank after the all-gather: one
+        # rank reads the step's result back (reads issue no collective)
+        if rank == 0:
+            for m in range(t.order):
+                eng.factor(m, out=host_F[m])
+            eng.lam(out=host_lam)
     e2e_s = (time.perf_counter() - te0) / a.steps
     d2h = sum(f.nbytes for f in host_F) + host_lam.nbytes + 16
 
