@@ -73,9 +73,11 @@ Engine::Engine(int dev) : device(dev) {
   CPTC_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   CPTC_CUDA(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
   for (auto& e : ev) CPTC_CUDA(cudaEventCreate(&e));
+  for (auto& e : ev1) CPTC_CUDA(cudaEventCreate(&e));
+  evc = ev;
   CPTC_CUDA(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming));
   CPTC_CUDA(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming));
-  CPTC_CUDA(cudaMallocHost((void**)&h_scal, 8 * sizeof(double)));
+  CPTC_CUDA(cudaMallocHost((void**)&h_scal, 16 * sizeof(double)));
 }
 
 Engine::~Engine() {
@@ -85,6 +87,8 @@ Engine::~Engine() {
   release_graph();  // before the communicator its NCCL nodes use
   comm_destroy(*this);
   for (auto& e : ev)
+    if (e) cudaEventDestroy(e);
+  for (auto& e : ev1)
     if (e) cudaEventDestroy(e);
   if (ev_fork) cudaEventDestroy(ev_fork);
   if (ev_join) cudaEventDestroy(ev_join);
@@ -278,7 +282,7 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
   alloc_workspace();
   for (int t = 0; t < 3; ++t) units.cnt[t] = units.nunits;
   if (dense_active) {
-    units.blocks = tile_blocks_for(R, device);
+    units.blocks = tile_blocks_for(R, device, units.nunits / (uint64_t)nranks);
     for (int t = 0; t < 3; ++t) tile_cuts(*this, t);
   }
   for (int n = 0; n < N; ++n) {
@@ -497,9 +501,9 @@ void Engine::update_mode(int n, bool last) {
   CPTC_CUDA(cudaStreamIsCapturing(stream, &cs));
   const unsigned rf = (cs == cudaStreamCaptureStatusActive) ? cudaEventRecordExternal
                                                             : cudaEventRecordDefault;
-  CPTC_CUDA(cudaEventRecordWithFlags(ev[2 * n], stream, rf));
+  CPTC_CUDA(cudaEventRecordWithFlags(evc[2 * n], stream, rf));
   mttkrp(n);
-  CPTC_CUDA(cudaEventRecordWithFlags(ev[2 * n + 1], stream, rf));
+  CPTC_CUDA(cudaEventRecordWithFlags(evc[2 * n + 1], stream, rf));
   comm_reduce_scatter_ftv(*this, n);
   CPTC_CUDA(cudaStreamWaitEvent(stream, ev_join, 0));
   const uint64_t lo = row_lo(n), rows = row_hi(n) - lo;
@@ -525,59 +529,96 @@ void Engine::update_mode(int n, bool last) {
 double* Engine::colscale() { return cscale.p; }
 
 void Engine::release_graph() {
-  if (iter_exec) cudaGraphExecDestroy(iter_exec);
-  if (iter_graph) cudaGraphDestroy(iter_graph);
-  iter_exec = nullptr;
-  iter_graph = nullptr;
+  for (int k = 0; k < 2; ++k) {
+    if (iter_exec[k]) cudaGraphExecDestroy(iter_exec[k]);
+    if (iter_graph[k]) cudaGraphDestroy(iter_graph[k]);
+    iter_exec[k] = nullptr;
+    iter_graph[k] = nullptr;
+  }
 }
 
 // One ALS iteration on the stream: every mode update, then the fit and the
-// solve status copied to pinned host memory.
-void Engine::enqueue_iteration() {
+// solve status copied to readback slot `slot` of the pinned host buffer.
+void Engine::enqueue_iteration(int slot) {
+  evc = slot ? ev1 : ev;
   for (int n = 0; n < N; ++n) update_mode(n, n == N - 1);
-  CPTC_CUDA(cudaMemcpyAsync(h_scal, scal.p, 2 * sizeof(double), cudaMemcpyDeviceToHost, stream));
-  CPTC_CUDA(cudaMemcpyAsync(h_scal + 4, status.p, sizeof(int), cudaMemcpyDeviceToHost, stream));
+  double* hs = h_scal + 8 * slot;
+  CPTC_CUDA(cudaMemcpyAsync(hs, scal.p, 2 * sizeof(double), cudaMemcpyDeviceToHost, stream));
+  CPTC_CUDA(cudaMemcpyAsync(hs + 4, status.p, sizeof(int), cudaMemcpyDeviceToHost, stream));
+  evc = ev;
 }
 
 // The iteration is captured once into a CUDA graph (kernels, the side
 // stream's inverse, NCCL calls, the readback) and replayed with one launch,
 // so host launch overhead does not gap the GPU between the short solve
 // kernels; set CPTC_GRAPH=0 to launch it stream-ordered instead.
-void Engine::launch_iteration() {
+void Engine::launch_iteration(int slot) {
   static const bool use_graph = [] {
     const char* e = std::getenv("CPTC_GRAPH");
     return !(e && e[0] == '0');
   }();
+  cudaEvent_t* E = slot ? ev1 : ev;
   // The iteration's start and end events are recorded outside the graph:
   // the host waits on the end event for the fit.
-  CPTC_CUDA(cudaEventRecord(ev[2 * CPTC_MAX_ORDER], stream));
+  CPTC_CUDA(cudaEventRecord(E[2 * CPTC_MAX_ORDER], stream));
   if (!use_graph) {
-    enqueue_iteration();
-    CPTC_CUDA(cudaEventRecord(ev[2 * CPTC_MAX_ORDER + 1], stream));
+    enqueue_iteration(slot);
+    CPTC_CUDA(cudaEventRecord(E[2 * CPTC_MAX_ORDER + 1], stream));
     return;
   }
-  if (!iter_exec) {
+  if (!iter_exec[slot]) {
     // Kernels enqueued during capture are counted when the graph runs.
     const unsigned long long l0 = g_launches;
     CPTC_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
     try {
-      enqueue_iteration();
+      enqueue_iteration(slot);
     } catch (...) {
       cudaGraph_t g = nullptr;
       cudaStreamEndCapture(stream, &g);
       if (g) cudaGraphDestroy(g);
       cudaGetLastError();
       g_launches = l0;
+      evc = ev;
       throw;
     }
     iter_kernels = g_launches - l0;
     g_launches = l0;
-    CPTC_CUDA(cudaStreamEndCapture(stream, &iter_graph));
-    CPTC_CUDA(cudaGraphInstantiate(&iter_exec, iter_graph, 0));
+    CPTC_CUDA(cudaStreamEndCapture(stream, &iter_graph[slot]));
+    CPTC_CUDA(cudaGraphInstantiate(&iter_exec[slot], iter_graph[slot], 0));
   }
-  CPTC_CUDA(cudaGraphLaunch(iter_exec, stream));
+  CPTC_CUDA(cudaGraphLaunch(iter_exec[slot], stream));
   g_launches += iter_kernels;
-  CPTC_CUDA(cudaEventRecord(ev[2 * CPTC_MAX_ORDER + 1], stream));
+  CPTC_CUDA(cudaEventRecord(E[2 * CPTC_MAX_ORDER + 1], stream));
+}
+
+// Waits for iteration `it` (readback slot `slot`), checks the solve status,
+// computes the fit and reports it.
+void Engine::finish_iteration(int it, int slot, cptc_iter_cb cb, void* user) {
+  cudaEvent_t* E = slot ? ev1 : ev;
+  const double* hs = h_scal + 8 * slot;
+  CPTC_CUDA(cudaEventSynchronize(E[2 * CPTC_MAX_ORDER + 1]));
+  int h_status = 0;
+  std::memcpy(&h_status, hs + 4, sizeof(int));
+  if (h_status != 0) {
+    cudaStreamSynchronize(stream);  // the next iteration may be in flight
+    throw CptcError(CPTC_E_NUMERIC, "non-finite values in the R x R solve");
+  }
+  const double xn = std::sqrt(x_norm_sq);
+  const double iprod = hs[0], model2 = hs[1];
+  const double res2 = std::max(x_norm_sq - 2.0 * iprod + model2, 0.0);
+  const double fit = (xn > 0.0) ? 1.0 - std::sqrt(res2) / xn : 0.0;
+  float ms_it = 0.f;
+  cudaEventElapsedTime(&ms_it, E[2 * CPTC_MAX_ORDER], E[2 * CPTC_MAX_ORDER + 1]);
+  double mode_ms[CPTC_MAX_ORDER] = {0};
+  for (int n = 0; n < N; ++n) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, E[2 * n], E[2 * n + 1]);
+    mode_ms[n] = t;
+  }
+  last_iprod = iprod;
+  last_model2 = model2;
+  last_fit = fit;
+  if (cb) cb(it + 1, (double)ms_it, fit, mode_ms, N, user);
 }
 
 void Engine::als(int iters, cptc_iter_cb cb, void* user) {
@@ -588,31 +629,14 @@ void Engine::als(int iters, cptc_iter_cb cb, void* user) {
     grams_valid = true;
   }
   CPTC_CUDA(cudaMemsetAsync(status.p, 0, sizeof(int), stream));
-  const double xn = std::sqrt(x_norm_sq);
+  // One iteration stays in flight: iteration it + 1 is launched before the
+  // fit of iteration it is read, so the GPU does not wait for the host
+  // between iterations (the iterations do not depend on host decisions).
   for (int it = 0; it < iters; ++it) {
-    // Gram fit from the last mode's MTTKRP and factor (computed inside the
-    // last mode's update).
-    launch_iteration();
-    int h_status = 0;
-    CPTC_CUDA(cudaEventSynchronize(ev[2 * CPTC_MAX_ORDER + 1]));
-    std::memcpy(&h_status, h_scal + 4, sizeof(int));
-    CPTC_REQUIRE(h_status == 0, CPTC_E_NUMERIC, "non-finite values in the R x R solve");
-    const double iprod = h_scal[0], model2 = h_scal[1];
-    const double res2 = std::max(x_norm_sq - 2.0 * iprod + model2, 0.0);
-    const double fit = (xn > 0.0) ? 1.0 - std::sqrt(res2) / xn : 0.0;
-    float ms_it = 0.f;
-    cudaEventElapsedTime(&ms_it, ev[2 * CPTC_MAX_ORDER], ev[2 * CPTC_MAX_ORDER + 1]);
-    double mode_ms[CPTC_MAX_ORDER] = {0};
-    for (int n = 0; n < N; ++n) {
-      float t = 0.f;
-      cudaEventElapsedTime(&t, ev[2 * n], ev[2 * n + 1]);
-      mode_ms[n] = t;
-    }
-    last_iprod = iprod;
-    last_model2 = model2;
-    last_fit = fit;
-    if (cb) cb(it + 1, (double)ms_it, fit, mode_ms, N, user);
+    launch_iteration(it & 1);
+    if (it > 0) finish_iteration(it - 1, (it - 1) & 1, cb, user);
   }
+  if (iters > 0) finish_iteration(iters - 1, (iters - 1) & 1, cb, user);
 }
 
 }  // namespace cptc

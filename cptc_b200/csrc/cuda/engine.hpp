@@ -86,8 +86,12 @@ struct Engine {
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   // One ALS iteration captured as a CUDA graph (rebuilt after load, build
   // and communicator changes).
-  cudaGraph_t iter_graph = nullptr;
-  cudaGraphExec_t iter_exec = nullptr;
+  // Two of them, for two iterations in flight (slot = iteration parity),
+  // each with its own timing events (ev, ev1) and readback slot in h_scal.
+  cudaGraph_t iter_graph[2] = {nullptr, nullptr};
+  cudaGraphExec_t iter_exec[2] = {nullptr, nullptr};
+  cudaEvent_t ev1[2 * CPTC_MAX_ORDER + 2] = {};
+  cudaEvent_t* evc = nullptr;  // events of the iteration being enqueued
   unsigned long long iter_kernels = 0;  // this library's kernels in the graph
   std::string err;
 
@@ -127,7 +131,7 @@ struct Engine {
   DArray<double> lambda;
   DArray<double> FtV, FtF, Ainv, gpart, dots, scal, cscale;
   DArray<int> status;
-  double* h_scal = nullptr;  // pinned, 8 doubles
+  double* h_scal = nullptr;  // pinned, 16 doubles: two readback slots of 8
   int gpart_blocks = 0;
   double last_iprod = 0.0, last_model2 = 0.0, last_fit = 0.0;
 
@@ -150,8 +154,9 @@ struct Engine {
   void fetch_rows(const double* dev, int m, double* host);
   double* stage_rows();
   void release_graph();
-  void enqueue_iteration();
-  void launch_iteration();
+  void enqueue_iteration(int slot);
+  void launch_iteration(int slot);
+  void finish_iteration(int it, int slot, cptc_iter_cb cb, void* user);
   uint64_t padded_rows(int m) const;
   void permute_rows(const double* in, int m, bool to_relabelled, double* out);
   void mttkrp(int mode);  // into FtV (relabelled rows), stream-ordered

@@ -47,13 +47,14 @@ struct TileArgs {
   const double* Fout[CPTC_MAX_ORDER];
   int store_dups;           // 1: last write wins (order-3), 0: duplicates sum
   double* out;
+  int stage_max;  // nonzeros of the next tile staged ahead (0: none)
 };
 // order: tile visiting order for this mode (sorted by target block);
 // cut: blocks+1 CTA range starts over `order` (balanced by nonzeros).
 void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, const uint32_t* cut,
                           uint32_t blocks, cudaStream_t s);
 // CTAs the tile kernel runs for rank R (shared-memory occupancy x SMs).
-uint32_t tile_blocks_for(int R, int device);
+uint32_t tile_blocks_for(int R, int device, uint64_t ntiles);
 // Balanced CTA ranges over E.units.order[slot] (fills E.units.cut[slot]).
 void tile_cuts(Engine& E, int slot);
 // Partition of Engine::tiles + residual selection (tiles.cu).

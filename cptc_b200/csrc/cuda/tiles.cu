@@ -128,6 +128,22 @@ constexpr int kSt = 20;               // t stride (floats) of the slab layout
 constexpr int kSs = 16 * kSt;         // s stride
 constexpr int kTileFloats = 16 * kSs; // 5120 floats = 20 KB
 constexpr int kScU = 4;               // nonzeros per thread per scatter round
+constexpr int kStage = 1024;          // nonzeros of the next tile staged by cp.async
+
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* smem_dst, const void* gsrc) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(sa), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
 
 __device__ __forceinline__ uint32_t tf32_bits(float x) {
   return __float_as_uint(x) & 0xFFFFE000u;  // low 13 mantissa bits ignored
@@ -168,6 +184,8 @@ __global__ void __launch_bounds__(128, MINB) k_tiles(TileArgs a,
   double* F2s = reinterpret_cast<double*>(fB + 16 * Rs);       // 16 * R
   double* accS = F2s + 16 * R;                                  // 16 * R
   double* wS = accS + 16 * R;                                   // R (outer weights)
+  double* sv = wS + R;                                          // kStage staged values
+  uint32_t* sl = reinterpret_cast<uint32_t*>(sv + kStage);     // staged local ids (words)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
   const int NT = R >> 3;
@@ -222,10 +240,24 @@ __global__ void __launch_bounds__(128, MINB) k_tiles(TileArgs a,
     }
   };
 
+  // The first kStage nonzeros of a tile are copied into shared memory with
+  // cp.async while the previous tile is on the tensor cores: values as
+  // 8-byte copies, local ids as the aligned 4-byte words that hold them.
+  auto stage = [&](uint64_t st, int cnt) {
+    const int c = cnt < a.stage_max ? cnt : a.stage_max;
+    const uint64_t w0 = st >> 1;
+    const int nw = (int)(((st + (uint64_t)c + 1) >> 1) - w0);
+    const uint32_t* lw = reinterpret_cast<const uint32_t*>(a.lid);
+    for (int j = tid; j < nw; j += 128) cp_async4(sl + j, lw + w0 + j);
+    for (int j = tid; j < c; j += 128) cp_async8(sv + j, a.val + st + j);
+    cp_async_commit();
+  };
+
   // Tile metadata is fetched one tile ahead (three dependent loads).
   uint32_t ti_next = order[k0];
   int4 T_next = a.tile[ti_next];
   uint64_t st_next = a.start[ti_next];
+  stage(st_next, T_next.w);
   for (uint64_t k = k0; k < k1; ++k) {
     const uint32_t ti = ti_next;
     const int4 T = T_next;
@@ -253,7 +285,8 @@ __global__ void __launch_bounds__(128, MINB) k_tiles(TileArgs a,
         wS[r] = w;
       }
     }
-    __syncthreads();
+    cp_async_wait_all();  // this tile's staged nonzeros (own copies) ...
+    __syncthreads();      // ... and everyone else's
     // Factor rows of the tile; every load of this thread is issued before
     // the first is used (the c loop is unrolled).
 #pragma unroll
@@ -279,8 +312,13 @@ __global__ void __launch_bounds__(128, MINB) k_tiles(TileArgs a,
       for (int u = 0; u < kScU; ++u) {
         const int j = j0 + u * 128 + tid;
         if (j < T.w) {
-          lq[u] = a.lid[st + j];
-          vq[u] = a.val[st + j];
+          if (j < a.stage_max) {
+            lq[u] = reinterpret_cast<const uint16_t*>(sl)[(st & 1) + j];
+            vq[u] = sv[j];
+          } else {
+            lq[u] = a.lid[st + j];
+            vq[u] = a.val[st + j];
+          }
         }
       }
 #pragma unroll
@@ -312,6 +350,8 @@ __global__ void __launch_bounds__(128, MINB) k_tiles(TileArgs a,
       }
       __syncthreads();
     }
+    // Everyone is past the scatter: the staging buffer takes the next tile.
+    if (k + 1 < k1) stage(st_next, T_next.w);
 
     if (active) {
       uint32_t bf[NW][2][2];
@@ -462,7 +502,7 @@ void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64
   }
   P.nnz = dense_nnz;
   nsel = n - dense_nnz;
-  P.lid.alloc(dense_nnz);
+  P.lid.alloc(dense_nnz + 8);  // the tile kernel copies whole 4-byte words
   P.val.alloc(dense_nnz);
   sel.alloc(nsel);
   k_scatter_split<<<gb, 256, 0, s>>>(id_b.p, flag.p, dpos.p, n, E.idx[0].p, E.idx[1].p,
@@ -518,7 +558,8 @@ void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64
 namespace {
 
 size_t tile_smem(int R) {
-  return (size_t)kTileFloats * 4 + (size_t)16 * (R + 8) * 4 + (size_t)(2 * 16 * R + R) * 8;
+  return (size_t)kTileFloats * 4 + (size_t)16 * (R + 8) * 4 + (size_t)(2 * 16 * R + R) * 8 +
+         (size_t)kStage * 8 + (size_t)(kStage / 2 + 2) * 4;
 }
 
 // Weight of a tile in the CTA balance: its nonzeros plus a fixed cost of
@@ -551,16 +592,33 @@ __global__ void k_tile_cuts(const unsigned long long* __restrict__ pre, uint64_t
 
 }  // namespace
 
-uint32_t tile_blocks_for(int R, int device) {
+uint32_t tile_blocks_for(int R, int device, uint64_t ntiles) {
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  // As many CTAs as the SMs hold at once (shared memory is the limit): each
-  // CTA walks its tiles one after another, so latency is hidden by the
-  // number of CTAs in flight.
-  int per_sm = (int)((228 * 1024) / (tile_smem(R) + 1024));
+  // A whole number of waves of the CTAs the SMs hold at once (registers
+  // and shared memory both limit it; all role instances share the same
+  // resources), about 16 tiles per CTA, 1 to 8 waves: the static CTA ranges
+  // are balanced by nonzero count, and when tile costs vary (config 4's
+  // Zipf tiles) several short waves let the block scheduler even out the
+  // rest (config 4, R=32: 0.91 ms per mode at 1 wave, 0.70 at 8; config 2's
+  // uniform tiles: 0.09 at 1 wave, 0.11 at 4).
+  const size_t smem = tile_smem(R);
+  const int NT = R / 8;
+  const int ntm = NT < 4 ? NT : 4;
+  auto kern = ntm == 1 ? k_tiles<0, 1, 2, 1, 4>
+              : ntm == 2 ? k_tiles<0, 1, 2, 2, 4>
+              : ntm == 3 ? k_tiles<0, 1, 2, 3, 4>
+                         : k_tiles<0, 1, 2, 4, 4>;
+  CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+  int per_sm = 0;
+  CPTC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem));
   if (per_sm < 1) per_sm = 1;
-  if (per_sm > 16) per_sm = 16;
-  return (uint32_t)(sms * per_sm);
+  const uint64_t wave = (uint64_t)sms * per_sm;
+  uint64_t waves = ntiles / (wave * 16);
+  if (waves < 1) waves = 1;
+  if (waves > 8) waves = 8;
+  return (uint32_t)(wave * waves);
 }
 
 void tile_cuts(Engine& E, int slot) {
@@ -588,8 +646,10 @@ void tile_cuts(Engine& E, int slot) {
   CPTC_CUDA(cudaStreamSynchronize(E.stream));
 }
 
-void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, const uint32_t* cut,
+void launch_mttkrp_tiles3(const TileArgs& a_in, const uint32_t* order, const uint32_t* cut,
                           uint32_t blocks, cudaStream_t s) {
+  TileArgs a = a_in;
+  a.stage_max = kStage;
   if (a.ntiles == 0) return;
   CPTC_REQUIRE(a.R % 8 == 0 && a.R <= 128, CPTC_E_UNSUP,
                "the TF32 tile path needs R a multiple of 8, <= 128");

@@ -210,7 +210,7 @@ void partition_units(Engine& E, double threshold, DArray<uint32_t>& sel, uint64_
   CPTC_CUDA(cudaStreamSynchronize(s));
   U.nnz = last_pos + last_flag;
   nsel = n - U.nnz;
-  U.lid.alloc(U.nnz);
+  U.lid.alloc(U.nnz + 8);  // the tile kernel copies whole 4-byte words
   U.val.alloc(U.nnz);
   sel.alloc(nsel);
   k_scatter_units<<<gb, 256, 0, s>>>(id_a.p, flag.p, dpos.p, n, ka, E.vals.p, U.lid.p, U.val.p,

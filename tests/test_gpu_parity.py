@@ -99,8 +99,9 @@ def test_mttkrp_fp64_generic(gpu, oracle, dims, nnz, R):
 
 @pytest.mark.parametrize("R", [16, 32, 64, 128])
 def test_mttkrp_tf32_tiles(gpu, oracle, R):
-    # 256^3 at fill ~0.9: every tile dense; partition on the given
-    # coordinates (no relabelling) so both sides see the same tiles.
+    # config 2's 256^3 layout at 5% of its nonzeros, every tile taken as
+    # dense (threshold 0.001); partition on the given coordinates (no
+    # relabelling) so both sides see the same tiles.
     t = cp.gen_config(2, scale=0.05)
     e = engine_for(t, R, path="tf32", threshold=0.001, reorder="none")
     st = e.stats()
@@ -114,6 +115,24 @@ def test_mttkrp_tf32_tiles(gpu, oracle, R):
         exact = oracle.mttkrp(t, F, n, threads=8)
         assert rel(got, hyb) < 1e-5
         assert np.abs(got - exact).max() / np.abs(exact).max() < 2e-3
+
+
+@pytest.mark.parametrize("R", [16, 32, 128])
+def test_mttkrp_tf32_full_tiles(gpu, oracle, R):
+    # 64^3 at fill ~0.9: 64 tiles of ~3,700 nonzeros each, more than the
+    # tile kernel stages in shared memory ahead of time (the rest of each
+    # tile is read directly)
+    t = cp.gen_uniform((64, 64, 64), 235_000, seed=8, values="lognormal")
+    e = engine_for(t, R, path="tf32", threshold=0.03, reorder="none")
+    st = e.stats()
+    assert st["tf32_path"] == 1 and st["dense_tiles"] == 64
+    assert st["dense_nnz"] / st["dense_tiles"] > 2048
+    F = rand_factors(t.dims, R)
+    for m in range(3):
+        e.set_factor(m, F[m])
+    for n in range(3):
+        hyb, _ = oracle.mttkrp_hybrid3(t, F, n, thr=0.03, threads=8)
+        assert rel(e.mttkrp(n), hyb) < 1e-5
 
 
 def test_mttkrp_tf32_mixed_partition(gpu, oracle):
