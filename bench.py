@@ -423,6 +423,11 @@ def run_reference(a):
         cp.write_tns(tns, t)
         iters = a.warmup + a.steps
         env = dict(os.environ)
+        if t.order != 3:
+            # config 5's switches: HITS relabelling (3 rounds), dense units
+            # at cutoff 0.03
+            env.update({"GEN_REORDER": "hits", "GEN_REORDER_T": "3",
+                        "GEN_DENSE_THRESHOLD": str(a.threshold)})
         r = subprocess.run([str(binary), str(tns), str(iters), str(a.rank), str(a.threshold)],
                            capture_output=True, text=True, env=env, timeout=1800)
         out = r.stdout
@@ -434,7 +439,7 @@ def run_reference(a):
         return
     times, fits = [], []
     for ln in out.splitlines():
-        if ln.startswith("[ALS] iter "):
+        if ln.startswith("[ALS] iter ") or ln.startswith("[GEN] iter "):
             parts = dict(kv.split("=") for kv in ln.split() if "=" in kv)
             times.append(float(parts["time"]))
             fits.append(float(parts["fit"]))

@@ -449,6 +449,7 @@ void Engine::mttkrp_sparse(int mode) {
   const View& v = views[mode];
   MttkrpArgs a{};
   a.rec = v.rec.p;
+  a.recw = v.recw;
   a.gw = v.gw.p;
   a.oidx = v.oidx.p;
   a.val = v.val.p;

@@ -40,9 +40,11 @@ struct View {
   DArray<uint32_t> gw;           // element word (gathered index + flags)
   DArray<uint32_t> oidx;         // nout * nnz outer indices (SoA)
   DArray<double> val;
-  // Order 3: the same data as one 16-byte record per nonzero
-  // {word, outer index, value} (x, y = word, outer; zw = value bits).
+  // The same data as records: order 3 one 16-byte record per nonzero
+  // {word, outer index, value} (x, y = word, outer; zw = value bits);
+  // orders 4-6 two uint4 {word, o0, o1, o2} {o3, 0, value}.
   DArray<uint4> rec;
+  int recw = 0;                  // uint4 per record (0: SoA arrays only)
   DArray<uint32_t> rows;         // non-empty target rows, in order
   DArray<uint32_t> task_row;     // index into `rows` of each task's first row
   uint64_t nrows = 0, ntasks = 0;

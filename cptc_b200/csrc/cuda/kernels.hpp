@@ -9,7 +9,10 @@
 namespace cptc {
 
 struct MttkrpArgs {
-  const uint4* rec;  // order-3 records (null otherwise)
+  const uint4* rec;  // records (null: the SoA arrays below): order 3 one
+                     // uint4 {word, outer, value}; orders 4-6 two uint4
+                     // {word, o0, o1, o2}{o3, 0, value}
+  int recw;          // uint4 per record (1 or 2)
   const uint32_t* gw;
   const uint32_t* oidx;
   const double* val;

@@ -30,6 +30,10 @@ namespace cptc {
 
 namespace {
 
+struct FoPtrs {
+  const double* p[4];
+};
+
 template <int GW, int RPL, bool VEC>
 struct Lanes {
   int r[RPL];
@@ -459,6 +463,176 @@ void launch_rec3s(const MttkrpArgs& a, cudaStream_t s) {
   CPTC_LAUNCH_CHECK();
 }
 
+// Orders 4-6 (NOUT = 2..4 outer modes): 32-byte records {word, o0, o1, o2}
+// {o3, 0, value} staged through shared memory by cp.async as in
+// k_mttkrp_rec3s (one record per lane per chunk).  The outer rows of a
+// fiber are loaded with the batch, only for the fiber's first nonzero, and
+// multiplied together; per fiber acc += (sum_e v_e g_e) * prod_q F_q[o_q] —
+// the association of k_mttkrp_view, whose outer-row loads at a fiber start
+// wait on a shuffle and a further index load.
+template <int GW, int RPL, int U, int NOUT>
+__global__ void __launch_bounds__(256) k_mttkrp_recns(const uint4* __restrict__ rec,
+                                                     const uint32_t* __restrict__ rows,
+                                                     const uint32_t* __restrict__ task_row,
+                                                     uint64_t nnz, uint64_t task0,
+                                                     uint64_t ntasks, uint32_t tsize, int R,
+                                                     const double* __restrict__ Fg, FoPtrs fo_p,
+                                                     double* __restrict__ out) {
+  constexpr int GPW = 32 / GW;
+  constexpr int CH = GW;  // records per chunk: one per lane
+  static_assert(CH % U == 0, "chunk holds whole batches");
+  __shared__ __align__(16) uint4 sbuf[8 * GPW][2][2 * CH];
+  const int lane = threadIdx.x & 31, glane = lane % GW, gw = lane / GW;
+  const int warp = threadIdx.x >> 5;
+  const int grp = warp * GPW + gw;
+  const unsigned gmask = (GW == 32) ? 0xffffffffu : (((1u << GW) - 1u) << (gw * GW));
+  const uint64_t task = task0 + ((uint64_t)blockIdx.x * 8 + warp) * GPW + gw;
+  if (task >= ntasks) return;
+  const Lanes<GW, RPL, true> L(glane, R);
+  const uint64_t p0 = task * (uint64_t)tsize;
+  const uint64_t p1 = (p0 + tsize < nnz) ? p0 + tsize : nnz;
+  const int n = (int)(p1 - p0);
+  uint4 (*buf)[2 * CH] = sbuf[grp];
+
+  uint32_t rowi = task_row[task];
+  uint32_t row = rows[rowi];
+  bool began = (rec[2 * p0].x & kRowFlag) != 0;
+  const bool ends = (p1 == nnz) || (rec[2 * p1].x & kRowFlag);
+
+  auto fetch = [&](int c) {
+    const int q = c * CH + glane;
+    if (q < n) {
+      cp_async16(&buf[c & 1][2 * glane], rec + 2 * (p0 + q));
+      cp_async16(&buf[c & 1][2 * glane + 1], rec + 2 * (p0 + q) + 1);
+    }
+    cp_async_commit();
+  };
+
+  double acc[RPL], fs[RPL], fo[RPL];
+#pragma unroll
+  for (int k = 0; k < RPL; ++k) acc[k] = fs[k] = fo[k] = 0.0;
+  auto write_row = [&](bool owned) {
+    double* dst = out + (uint64_t)row * (uint64_t)R;
+#pragma unroll
+    for (int k = 0; k < RPL; ++k) {
+      if (!L.ok[k]) continue;
+      if (owned) dst[L.r[k]] += acc[k];
+      else atomicAdd(dst + L.r[k], acc[k]);
+      acc[k] = 0.0;
+    }
+  };
+  auto outer_rows = [&](const uint4& r0, const uint4& r1, double (&f)[RPL]) {
+    const uint32_t o[4] = {r0.y, r0.z, r0.w, r1.x};
+    load_row<GW, RPL, true>(fo_p.p[0], o[0], R, glane, L, f);
+#pragma unroll
+    for (int q = 1; q < NOUT; ++q) {
+      double t[RPL];
+      load_row<GW, RPL, true>(fo_p.p[q], o[q], R, glane, L, t);
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) f[k] *= t[k];
+    }
+  };
+  auto step = [&](const uint4& r0, const uint4& r1, const double (&g)[RPL],
+                  const double (&f)[RPL], bool first) {
+    const bool fib = (r0.x & kFibFlag) != 0;
+    if (fib && !first) {
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) {
+        acc[k] = fma(fs[k], fo[k], acc[k]);
+        fs[k] = 0.0;
+      }
+    }
+    if ((r0.x & kRowFlag) && !first) {
+      write_row(began);
+      row = rows[++rowi];
+      began = true;
+    }
+    if (fib || first) {
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) fo[k] = f[k];
+    }
+    const double v = __hiloint2double((int)r1.w, (int)r1.z);
+#pragma unroll
+    for (int k = 0; k < RPL; ++k) fs[k] = fma(v, g[k], fs[k]);
+  };
+
+  const int nch = (n + CH - 1) / CH;
+  fetch(0);
+  if (nch > 1) fetch(1);
+  else cp_async_commit();
+#pragma unroll 1
+  for (int c = 0; c < nch; ++c) {
+    cp_async_wait<1>();
+    __syncwarp(gmask);
+    const int q0 = c * CH;
+    const int qe = (q0 + CH < n) ? q0 + CH : n;
+    const uint4* cb = buf[c & 1];
+    int q = q0;
+#pragma unroll 1
+    for (; q + U <= qe; q += U) {
+      double g[U][RPL], f[U][RPL];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint4 r0 = cb[2 * (q - q0 + u)], r1 = cb[2 * (q - q0 + u) + 1];
+        load_row<GW, RPL, true>(Fg, r0.x & kIdxMask, R, glane, L, g[u]);
+        if ((r0.x & kFibFlag) || q + u == 0) {
+          outer_rows(r0, r1, f[u]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < RPL; ++k) f[u][k] = 0.0;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        step(cb[2 * (q - q0 + u)], cb[2 * (q - q0 + u) + 1], g[u], f[u], q + u == 0);
+    }
+    for (; q < qe; ++q) {
+      const uint4 r0 = cb[2 * (q - q0)], r1 = cb[2 * (q - q0) + 1];
+      double g[RPL], f[RPL];
+      load_row<GW, RPL, true>(Fg, r0.x & kIdxMask, R, glane, L, g);
+      if ((r0.x & kFibFlag) || q == 0) {
+        outer_rows(r0, r1, f);
+      } else {
+#pragma unroll
+        for (int k = 0; k < RPL; ++k) f[k] = 0.0;
+      }
+      step(r0, r1, g, f, q == 0);
+    }
+    __syncwarp(gmask);
+    if (c + 2 < nch) fetch(c + 2);
+    else cp_async_commit();
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int k = 0; k < RPL; ++k) acc[k] = fma(fs[k], fo[k], acc[k]);
+  write_row(began && ends);
+}
+
+template <int GW, int RPL, int U, int NOUT>
+void launch_recns(const MttkrpArgs& a, cudaStream_t s) {
+  constexpr int GPW = 32 / GW;
+  const uint64_t warps = (a.ntasks - a.task0 + GPW - 1) / GPW;
+  const unsigned blocks = (unsigned)((warps + 7) / 8);
+  FoPtrs fo{};
+  for (int q = 0; q < NOUT; ++q) fo.p[q] = a.Fo[q];
+  k_mttkrp_recns<GW, RPL, U, NOUT><<<blocks, 256, 0, s>>>(a.rec, a.rows, a.task_row, a.nnz,
+                                                           a.task0, a.ntasks, a.task, a.R, a.Fg,
+                                                           fo, a.out);
+  CPTC_LAUNCH_CHECK();
+}
+
+template <int NOUT>
+void launch_recns_r(const MttkrpArgs& a, cudaStream_t s) {
+  switch (a.R) {
+    case 8: launch_recns<8, 1, 2, NOUT>(a, s); return;
+    case 16: launch_recns<8, 2, 2, NOUT>(a, s); return;
+    case 32: launch_recns<16, 2, 2, NOUT>(a, s); return;
+    case 64: launch_recns<16, 4, 2, NOUT>(a, s); return;
+    case 128: launch_recns<32, 4, 1, NOUT>(a, s); return;
+    default: throw CptcError(CPTC_E_UNSUP, "N-order records are built for R in {8,16,32,64,128}");
+  }
+}
+
 template <int GW, int RPL, bool VEC, int U>
 void launch_rec3(const MttkrpArgs& a, cudaStream_t s) {
   constexpr int GPW = 32 / GW;
@@ -483,6 +657,14 @@ void launch(const MttkrpArgs& a, cudaStream_t s) {
 
 void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
   if (a.nnz == 0 || a.ntasks <= a.task0) return;
+  if (a.rec != nullptr && a.recw == 2) {
+    switch (a.nout) {
+      case 2: launch_recns_r<2>(a, s); return;
+      case 3: launch_recns_r<3>(a, s); return;
+      case 4: launch_recns_r<4>(a, s); return;
+      default: throw CptcError(CPTC_E_UNSUP, "32-byte records hold 2 to 4 outer modes");
+    }
+  }
   if (a.rec != nullptr) {
     // Record kernel per rank, measured on config 4 (B200, ms per mode of the
     // FP64 residual): staging the record stream through shared memory with

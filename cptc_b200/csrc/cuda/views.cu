@@ -76,6 +76,20 @@ __global__ void k_gather_view(IdxPtrs idx, const double* __restrict__ vals,
   if ((threadIdx.x & 31) == 0 && fibs) atomicAdd(nfib, fibs);
 }
 
+// Orders 4-6: two uint4 per nonzero, {word, o0, o1, o2} {o3, 0, value}.
+__global__ void k_pack_records2(const uint32_t* __restrict__ gw, const uint32_t* __restrict__ oidx,
+                                const double* __restrict__ val, uint64_t n, int nout,
+                                uint4* __restrict__ rec) {
+  for (uint64_t p = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; p < n;
+       p += (uint64_t)gridDim.x * blockDim.x) {
+    uint32_t o[4] = {0u, 0u, 0u, 0u};
+    for (int q = 0; q < nout; ++q) o[q] = oidx[(uint64_t)q * n + p];
+    const unsigned long long vb = __double_as_longlong(val[p]);
+    rec[2 * p] = make_uint4(gw[p], o[0], o[1], o[2]);
+    rec[2 * p + 1] = make_uint4(o[3], 0u, (uint32_t)vb, (uint32_t)(vb >> 32));
+  }
+}
+
 __global__ void k_pack_records(const uint32_t* __restrict__ gw, const uint32_t* __restrict__ oidx,
                                const double* __restrict__ val, uint64_t n, uint4* __restrict__ rec) {
   for (uint64_t p = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; p < n;
@@ -231,6 +245,19 @@ void build_view_order(Engine& E, View& v, int n, const int* order, int nother,
     v.oidx.release();
     v.val.release();
     v.gw.release();
+    v.recw = 1;
+  } else if (v.nout >= 2 && v.nout <= 4 &&
+             (E.R == 8 || E.R == 16 || E.R == 32 || E.R == 64 || E.R == 128)) {
+    // Orders 4-6 at the ranks the staged record kernel is built for: two
+    // uint4 per nonzero (32 bytes), the separate arrays released.
+    v.rec.alloc(2 * nsel);
+    k_pack_records2<<<gb, 256, 0, s>>>(v.gw.p, v.oidx.p, v.val.p, nsel, v.nout, v.rec.p);
+    CPTC_LAUNCH_CHECK();
+    CPTC_CUDA(cudaStreamSynchronize(s));
+    v.oidx.release();
+    v.val.release();
+    v.gw.release();
+    v.recw = 2;
   }
   CPTC_CUDA(cudaStreamSynchronize(s));
 }

@@ -135,6 +135,23 @@ def test_mttkrp_tf32_full_tiles(gpu, oracle, R):
         assert rel(e.mttkrp(n), hyb) < 1e-5
 
 
+@pytest.mark.parametrize("R", [8, 32])
+def test_mttkrp_tf32_ragged_dims(gpu, oracle, R):
+    # dims that are not multiples of 16: the last tile block of every mode
+    # is partial, so the kernel's row guards decide which rows exist
+    # (the reference's GEN_SELFTEST covers the same edge, src/generic.cu:1420-1426)
+    t = cp.gen_uniform((50, 37, 45), 40_000, seed=14, values="lognormal")
+    e = engine_for(t, R, path="tf32", threshold=0.01, reorder="none")
+    st = e.stats()
+    assert st["tf32_path"] == 1 and st["dense_tiles"] == 4 * 3 * 3
+    F = rand_factors(t.dims, R)
+    for m in range(3):
+        e.set_factor(m, F[m])
+    for n in range(3):
+        hyb, _ = oracle.mttkrp_hybrid3(t, F, n, thr=0.01, threads=8)
+        assert rel(e.mttkrp(n), hyb) < 1e-5
+
+
 def test_mttkrp_tf32_mixed_partition(gpu, oracle):
     t = cp.gen_config(3, scale=0.02)
     e = engine_for(t, 32, path="tf32", threshold=0.03, reorder="none")
@@ -242,3 +259,22 @@ def units_oracle(oracle, t, F, inner, tslot, thr):
     oracle.lib().or_mttkrp_units(t.order, a.dims, a.nnz, a.ip, a.vp, F[0].shape[1], fp, inn,
                                  tslot, thr, out.ctypes.data_as(oracle.DP), 8)
     return out
+
+
+@pytest.mark.parametrize("order", [3, 4])
+def test_exact_residual(gpu, order):
+    # cptc_residual: sum over the stored nonzeros of (v - xhat)^2 with the
+    # current factors and lambda, against numpy in the caller's labels
+    dims = (60, 50, 40) if order == 3 else (30, 20, 25, 15)
+    t = cp.gen_uniform(dims, 20_000, seed=31, values="lognormal")
+    e = engine_for(t, 16, path="fp64")
+    e.init_factors()
+    e.als(2)
+    F, lam = e.factors(), e.lam()
+    xhat = np.ones((t.nnz, 16)) * lam
+    for m in range(t.order):
+        xhat = xhat * F[m][t.idx[m]]
+    want = float(np.sum((t.vals - xhat.sum(axis=1)) ** 2))
+    got = e.residual()
+    assert abs(got["res_sq"] - want) <= 1e-10 * want
+    assert abs(got["x_sq"] - float(t.vals @ t.vals)) <= 1e-12 * got["x_sq"]
