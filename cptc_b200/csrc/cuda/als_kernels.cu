@@ -560,13 +560,6 @@ void launch_gram_reduce(const double* part, int nblk, int R, double* G, cudaStre
   launch_partial_sum(part, nblk, R * R, G, s);
 }
 
-void launch_hadamard(const double* const* Gs, int ng, int R, double* FtF, cudaStream_t s) {
-  GPtrs g{};
-  for (int k = 0; k < ng; ++k) g.p[k] = Gs[k];
-  k_hadamard<<<grid_for((uint64_t)R * R, 256), 256, 0, s>>>(g, ng, R, FtF);
-  CPTC_LAUNCH_CHECK();
-}
-
 void launch_sym_inverse(const double* const* Gs, int ng, int R, int mode, double* FtF,
                         double* Ainv, int* status, cudaStream_t s) {
   CPTC_REQUIRE(R >= 1 && R <= 128, CPTC_E_UNSUP, "rank must be in [1, 128]");

@@ -77,8 +77,6 @@ int launch_gram_partial(const double* F, uint64_t rows, int R, double* part, int
 void launch_partial_sum(const double* part, int nblk, int len, double* out, cudaStream_t s);
 // G = sum of nblk partials (fixed order).
 void launch_gram_reduce(const double* part, int nblk, int R, double* G, cudaStream_t s);
-// FtF = prod_{m in list} G_m (elementwise).
-void launch_hadamard(const double* const* Gs, int ng, int R, double* FtF, cudaStream_t s);
 // FtF = prod of the ng Grams Gs (elementwise, written out) and Ainv = its
 // inverse; status[0] != 0 on non-finite results.  Ainv must hold
 // 2*R*R + 1 doubles (scratch).
