@@ -381,7 +381,7 @@ def run_engine(a):
             "tile_tflops": tile_tflops(st, a.rank, tl),
         },
     }
-    if not a.no_cpu_baseline:
+    if not a.no_cpu_baseline and world == 1:  # measured at N=1 only
         line["cpu_baseline"] = cpu_baseline(t, a.rank)
     print(json.dumps(line), flush=True)
     eng.close()
