@@ -11,7 +11,8 @@ explicit L2 flush is needed between steps.
   python bench.py [--gpus N --steps K --warmup W --rank R]
   python bench.py --impl reference ...   # cpTC's own build (oracle/_ref)
 
-One JSON line on rank 0 (fields documented in DESIGN.md).
+One JSON line on rank 0: metric, value, unit, e2e, roofline, cpu_baseline,
+clocks, gpu_launches and the workload config.
 """
 from __future__ import annotations
 
@@ -309,7 +310,7 @@ def run_engine(a):
     tl = [p["tiles_ms"] for p in prof]
     dominant = "k_mttkrp_rec3s" if t.order == 3 else "k_mttkrp_view"
     nnz_view = st["sparse_nnz"]
-    # Per launch (one mode): bytes as SURVEY 8(d) counts them (every factor-row
+    # Per launch (one mode): the benchmark's algorithmic bytes (every factor-row
     # gather) and the compulsory bytes (each stored byte once).
     algo = [algorithmic_bytes(nnz_view, t.order, a.rank, t.dims[n]) for n in range(t.order)]
     comp = 16 * nnz_view + 8 * a.rank * sum(t.dims)
@@ -371,7 +372,7 @@ def run_engine(a):
             "peak_src": peaks["src"],
             "traffic": traffic,
             "algorithmic_bytes_per_launch": algo_launch,
-            "bytes_note": "algorithmic bytes count every factor-row gather (SURVEY 8(d)); "
+            "bytes_note": "algorithmic bytes count every factor-row gather; "
                           "most gathers hit L1/L2, so frac can exceed 1; compulsory_frac "
                           "counts each stored byte once",
             "compulsory_bytes_per_launch": comp,

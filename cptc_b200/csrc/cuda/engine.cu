@@ -249,8 +249,9 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
   // max(0.08, 0.11/sqrt(SMs/24)) from src/main.cu:369-381, was calibrated on
   // a 24-SM RTX 4060).  Measured per-tile cost a + b*nnz of the TF32 tile
   // kernel against c*nnz of the FP64 kernel on configs 2-4 gives the
-  // break-even fill a / (4096 (c - b)): ~0.07 at R <= 32 falling to ~0.04 at
-  // R = 128 (table in DESIGN.md).
+  // break-even fill a / (4096 (c - b)): R=16 a~4.1 ns, b~0.0053, c~0.0195
+  // -> 0.068; R=32 a~6, b~0.005, c~0.029 -> 0.061; R=128 a~20, b~0.012,
+  // c~0.13 -> 0.041 (ns per tile / per nonzero).
   fill_min = opts.fill_min > 0.0 ? opts.fill_min : b200_fill_min(R);
 
   DArray<uint32_t> sel;

@@ -14,7 +14,8 @@
 //  * mma.sync m16n8k8 TF32: a tile slab is a single 16x16x(R) product, far
 //    below the 128-row M of tcgen05.mma, and the kernel is bound by loading
 //    the tile pool and building the tile in shared memory, not by the
-//    tensor pipe (see DESIGN.md for the ncu evidence);
+//    tensor pipe (ncu on config 4: tensor pipe ~10% active, issue- and
+//    latency-bound while the tile is built);
 //  * the tile is scattered into shared memory in a per-mode (s, t, c) layout
 //    with a row stride of 20 floats, which makes every A-fragment load
 //    bank-conflict free; F1 (TF32) and F2 (FP64) rows of the tile sit in

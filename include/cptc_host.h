@@ -51,7 +51,10 @@ int cptc_tns_probe_order(const char* path);
 /* Writes `t` as 1-based .tns text, values with %.17g (exact round trip). */
 int cptc_tns_write(const char* path, const cptc_coo* t);
 
-/* Synthetic workloads of the benchmark (cfg 1..5), scaled
+/* Synthetic workloads of the benchmark (cfg 1..5: 128^3 planted rank 8;
+ * 256^3 block-dense planted rank 32; 512^3 dense blocks + uniform residual;
+ * 12092x9184x28818 Zipf(1.1) lognormal; 183x24x1140x1717 Zipf(1.2)
+ * Poisson+1), scaled
  * to round(nnz * nnz_scale) nonzeros with the same dims. Every tensor is a
  * pure function of (cfg, nnz_scale, seed): coordinates are the first nnz
  * distinct draws of a counter-based RNG, sorted by linear index. */

@@ -1,8 +1,8 @@
 #!/bin/bash
 # Builds the reference CP-ALS program (zhixianzhu/cpTC) from its own sources,
 # unmodified, for sm_100a, into oracle/_ref/cptc_opt.  Test and baseline
-# infrastructure only.  Needs the reference tree (REF_DIR, default
-# /root/reference); the GPU box uses the prebuilt binary.
+# infrastructure only.  Needs the reference tree (REF_DIR); machines without
+# it use the prebuilt binary.
 #   - MAGMA is replaced by oracle/refstub/magma_v2.h (only dead code uses it)
 #   - oracle/refstub/preinclude.h adds <cstdint> for include/generic.hpp
 set -euo pipefail
