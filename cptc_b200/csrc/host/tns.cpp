@@ -5,9 +5,16 @@
 // and tabs separate fields; a line whose coordinates are not all digit
 // strings or whose value does not parse is skipped; indices are 1-based and
 // an index of 0 maps to 0; dims[m] = largest 0-based index + 1.
-// The file is parsed by all host threads on newline-aligned chunks and the
-// nonzeros keep file order.
+// The file is mapped read-only and parsed by all host threads on
+// newline-aligned chunks (a last line without a newline is parsed from a
+// small padded copy, so no parse reads past the mapping); the per-thread
+// results are copied into the output arrays in parallel, and the nonzeros
+// keep file order.
+#include <fcntl.h>
 #include <omp.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <cstdio>
@@ -20,20 +27,6 @@
 namespace cptc {
 
 static thread_local std::string g_tns_err;
-
-static bool read_file(const char* path, std::vector<char>& buf) {
-  FILE* f = std::fopen(path, "rb");
-  if (!f) return false;
-  std::fseek(f, 0, SEEK_END);
-  const long sz = std::ftell(f);
-  std::fseek(f, 0, SEEK_SET);
-  buf.resize((size_t)(sz > 0 ? sz : 0) + 1);
-  const size_t got = sz > 0 ? std::fread(buf.data(), 1, (size_t)sz, f) : 0;
-  std::fclose(f);
-  buf.resize(got + 1);
-  buf[got] = '\n';  // sentinel: every line ends with '\n'
-  return true;
-}
 
 static inline bool is_blank(char c) { return c == ' ' || c == '\t'; }
 
@@ -66,6 +59,16 @@ struct Part {
 };
 
 static void parse_range(const char* p, const char* end, int N, Part& out) {
+  // Lines in the range bound the nonzeros: reserve once.
+  size_t lines = 0;
+  for (const char* c = p; c < end;) {
+    const char* nl = (const char*)std::memchr(c, '\n', (size_t)(end - c));
+    ++lines;
+    if (!nl) break;
+    c = nl + 1;
+  }
+  for (int m = 0; m < N; ++m) out.idx[m].reserve(lines);
+  out.val.reserve(lines);
   uint32_t ix[CPTC_MAX_ORDER];
   while (p < end) {
     const char* nl = (const char*)std::memchr(p, '\n', (size_t)(end - p));
@@ -116,44 +119,82 @@ int cptc_tns_probe_order(const char* path) {
 int cptc_tns_read(const char* path, int order_hint, cptc_coo* out) {
   if (!out) return -2;
   std::memset(out, 0, sizeof(*out));
-  std::vector<char> buf;
-  if (!read_file(path, buf)) return -1;
-  const char* b = buf.data();
-  const char* e = b + buf.size();
-  const int N = order_hint > 0 ? order_hint : probe_order(b, e);
+  const int fd = ::open(path, O_RDONLY);
+  if (fd < 0) return -1;
+  struct stat st;
+  if (::fstat(fd, &st) != 0) {
+    ::close(fd);
+    return -1;
+  }
+  const size_t fsz = (size_t)st.st_size;
+  const char* map = nullptr;
+  if (fsz > 0) {
+    void* mp = ::mmap(nullptr, fsz, PROT_READ, MAP_PRIVATE, fd, 0);
+    if (mp == MAP_FAILED) {
+      ::close(fd);
+      return -1;
+    }
+    map = (const char*)mp;
+    ::madvise(mp, fsz, MADV_SEQUENTIAL);
+  }
+  ::close(fd);
+  struct Unmap {
+    const char* p;
+    size_t n;
+    ~Unmap() {
+      if (p) ::munmap((void*)p, n);
+    }
+  } unmap{map, fsz};
+  // Everything up to the last newline is parsed in place; a final line
+  // without a newline goes through a copy that ends with one.
+  size_t body = fsz;
+  while (body > 0 && map[body - 1] != '\n') --body;
+  std::vector<char> tail(map + body, map + fsz);
+  tail.push_back('\n');
+  const char* b = map;
+  const char* e = map + body;
+  int N = order_hint;
+  if (N <= 0) {
+    N = probe_order(b, e);
+    if (N < 0) N = probe_order(tail.data(), tail.data() + tail.size());
+  }
   if (N < 1 || N > CPTC_MAX_ORDER) return -2;
 
-  const int nt = std::max(1, std::min(host_threads(), (int)(buf.size() >> 20) + 1));
+  const int nt = std::max(1, std::min(host_threads(), (int)(body >> 20) + 1));
   std::vector<const char*> cut(nt + 1);
   cut[0] = b;
   cut[nt] = e;
   for (int t = 1; t < nt; ++t) {
-    const char* c = b + (buf.size() * (size_t)t) / (size_t)nt;
+    const char* c = b + (body * (size_t)t) / (size_t)nt;
     if (c < cut[t - 1]) c = cut[t - 1];
     const char* nl = (const char*)std::memchr(c, '\n', (size_t)(e - c));
     cut[t] = nl ? nl + 1 : e;
   }
-  std::vector<Part> parts(nt);
+  std::vector<Part> parts(nt + 1);
 #pragma omp parallel for num_threads(nt) schedule(static, 1)
   for (int t = 0; t < nt; ++t) parse_range(cut[t], cut[t + 1], N, parts[t]);
+  parse_range(tail.data(), tail.data() + tail.size(), N, parts[nt]);
 
   uint64_t nnz = 0;
-  for (auto& p : parts) nnz += p.val.size();
+  std::vector<uint64_t> off(parts.size() + 1, 0);
+  for (size_t t = 0; t < parts.size(); ++t) off[t + 1] = off[t] + parts[t].val.size();
+  nnz = off[parts.size()];
   if (!coo_alloc(out, N, nnz)) {
     cptc_coo_free(out);
     return -3;
   }
-  uint64_t off = 0;
-  for (auto& p : parts) {
-    for (int m = 0; m < N; ++m) {
-      if (!p.val.empty())
-        std::memcpy(out->idx[m] + off, p.idx[m].data(), p.val.size() * sizeof(uint32_t));
-      out->dims[m] = std::max<uint64_t>(out->dims[m], p.mx[m] + 1);
-    }
-    if (!p.val.empty())
-      std::memcpy(out->vals + off, p.val.data(), p.val.size() * sizeof(double));
-    off += p.val.size();
+  // Parallel copy: the output pages are first touched by many threads.
+#pragma omp parallel for num_threads(nt) schedule(dynamic, 1)
+  for (int t = 0; t < (int)parts.size(); ++t) {
+    const Part& p = parts[t];
+    if (p.val.empty()) continue;
+    for (int m = 0; m < N; ++m)
+      std::memcpy(out->idx[m] + off[t], p.idx[m].data(), p.val.size() * sizeof(uint32_t));
+    std::memcpy(out->vals + off[t], p.val.data(), p.val.size() * sizeof(double));
   }
+  for (const Part& p : parts)
+    for (int m = 0; m < N; ++m)
+      if (!p.val.empty()) out->dims[m] = std::max<uint64_t>(out->dims[m], p.mx[m] + 1);
   for (int m = 0; m < N; ++m)
     if (out->dims[m] == 0) out->dims[m] = 1;
   return 0;
