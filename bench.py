@@ -166,6 +166,9 @@ def algorithmic_bytes(nnz: int, order: int, R: int, rows: int) -> int:
     return nnz * (8 + 4 * (order - 1) + 8 * R * (order - 1)) + 8 * R * rows
 
 
+TF32_NOMINAL_TFLOPS = 1100.0  # B200 dense TF32, nominal
+
+
 def tile_tflops(st, R: int, tile_ms) -> float | None:
     """TF32 MMA rate of the dense-tile kernel: 8192*R flops per tile per mode."""
     ms = float(np.mean(tile_ms)) if len(tile_ms) else 0.0
@@ -380,6 +383,9 @@ def run_engine(a):
             "sparse_kernel_ms_per_mode": sp,
             "tile_kernel_ms_per_mode": tl,
             "tile_tflops": tile_tflops(st, a.rank, tl),
+            # no measured TF32 peak exists for this pool: nominal dense TF32
+            "tile_tf32_frac_of_nominal": (tile_tflops(st, a.rank, tl) / TF32_NOMINAL_TFLOPS
+                                          if tile_tflops(st, a.rank, tl) else None),
         },
     }
     if not a.no_cpu_baseline and world == 1:  # measured at N=1 only
