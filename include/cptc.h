@@ -130,13 +130,18 @@ int cptc_build(cptc_ctx* ctx, int R, double threshold, const cptc_opts* opts);
  * space; N-order: mt19937(seed) carried through the relabelling), lambda=1. */
 int cptc_init_factors(cptc_ctx* ctx);
 
-/* Factors in the caller's original index space, row-major I_n x R. */
+/* Factors in the caller's original index space, row-major I_n x R.  The
+ * copy is complete when cptc_set_factors returns (the buffer may be reused;
+ * pinned memory makes it a single DMA).  With several ranks every rank sets
+ * the same factors (each holds a replica). */
 int cptc_set_factors(cptc_ctx* ctx, int mode, const double* host);
 int cptc_get_factors(cptc_ctx* ctx, int mode, double* host);
 int cptc_get_lambda(cptc_ctx* ctx, double* host_R);
 
 /* One MTTKRP of `mode` on the current factors (the path selected by
- * cptc_build), result in original index space (I_mode x R, host). */
+ * cptc_build), result in original index space (I_mode x R, host).  With
+ * several ranks it is collective: every rank calls it and receives the
+ * whole result. */
 int cptc_mttkrp(cptc_ctx* ctx, int mode, double* host_out);
 
 /* Device-resident MTTKRP into the context's FtV buffer; *ms = device time of
@@ -145,15 +150,20 @@ int cptc_mttkrp(cptc_ctx* ctx, int mode, double* host_out);
 int cptc_mttkrp_timed(cptc_ctx* ctx, int mode, int reps, double* ms);
 
 /* Device times (ms, mean of `reps` back-to-back launches on the context's
- * stream) of one mode's MTTKRP parts: ms3[0] dense-tile TF32 kernel,
- * ms3[1] FP64 view kernel, ms3[2] the whole MTTKRP (zero + both). */
+ * stream) of one mode's MTTKRP parts on this rank's share: ms3[0] dense-tile
+ * TF32 kernel, ms3[1] FP64 residual kernel, ms3[2] the whole MTTKRP (zero +
+ * both). */
 int cptc_profile_mttkrp(cptc_ctx* ctx, int mode, int reps, double ms3[3]);
 
 /* Number of kernels this library has launched since it was loaded (a
  * replayed CUDA graph of an ALS iteration counts the kernels it holds). */
 unsigned long long cptc_launch_count(void);
 
-/* Runs `iters` CP-ALS iterations; cb (nullable) is called after each. */
+/* Runs `iters` CP-ALS iterations; cb (nullable) is called once per
+ * iteration, in order, with that iteration's device time, fit and per-mode
+ * MTTKRP times.  Iteration k+1 is already on the GPU when the callback of
+ * iteration k runs (the iterations do not depend on the host), and all
+ * iterations have finished when cptc_als returns. */
 int cptc_als(cptc_ctx* ctx, int iters, cptc_iter_cb cb, void* user);
 
 int cptc_get_stats(cptc_ctx* ctx, cptc_stats* out);
