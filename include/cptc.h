@@ -110,8 +110,9 @@ const char* cptc_last_error(const cptc_ctx* ctx);
 
 /* Multi-GPU (one process per GPU): rank 0 calls cptc_comm_unique_id and
  * shares the 128 bytes; every rank then calls cptc_comm_init before
- * cptc_build, and afterwards calls every function of this header in the
- * same order as the other ranks (they may issue collectives).  Each rank
+ * cptc_build.  cptc_comm_init, cptc_als and cptc_mttkrp are collective:
+ * every rank calls them, in the same order; the other functions are local
+ * (for example one rank alone may read the replicated factors).  Each rank
  * computes an equal share of every mode's nonzeros; the partial MTTKRP is
  * reduce-scattered into equal row slabs, each rank solves its slab, and one
  * grouped call all-reduces the R x R Gram and all-gathers the slabs into
