@@ -84,6 +84,21 @@ def test_mttkrp_empty_rows_and_heavy_row(gpu, oracle):
         assert np.all(got[empty] == 0.0)
 
 
+@pytest.mark.parametrize("order,R", [(4, 8), (4, 128), (5, 64), (6, 8), (6, 32), (6, 128)])
+def test_mttkrp_fp64_nway_records(gpu, oracle, order, R):
+    # orders 4-6 at the ranks with 32-byte records (o3 is used at order 6),
+    # every mode as the target, against the oracle's COO MTTKRP
+    dims = (17, 23, 11, 29, 13, 19)[:order]
+    t = cp.gen_uniform(dims, 12_000, seed=40 + order, values="normal")
+    e = engine_for(t, R, dense_generic=False, reorder="none")
+    F = rand_factors(t.dims, R, signed=True)
+    for m in range(order):
+        e.set_factor(m, F[m])
+    for n in range(order):
+        ref = oracle.mttkrp(t, F, n, threads=8)
+        assert rel(e.mttkrp(n), ref) < FP64_TOL, (order, R, n)
+
+
 @pytest.mark.parametrize("dims,nnz,R", [((30, 20, 25, 40), 20000, 16),
                                         ((12, 9, 15, 8, 11), 8000, 32),
                                         ((300, 200), 5000, 8)])
