@@ -5,7 +5,8 @@ sm_100a CUDA behind a C ABI (include/cptc.h), with this package as the
 Python face.  Native libraries are built in-tree by ``python -m
 cptc_b200.build``.
 """
-from .tensor import CooTensor, gen_config, gen_uniform, probe_order, read_tns, write_tns
+from .tensor import (CooTensor, gen_config, gen_uniform, probe_order, read_bin, read_tns,
+                     read_tns_cached, write_bin, write_tns)
 from .engine import CptcError, Engine, IterReport, comm_unique_id
 
 __all__ = [
@@ -17,6 +18,9 @@ __all__ = [
     "gen_config",
     "gen_uniform",
     "probe_order",
+    "read_bin",
     "read_tns",
+    "read_tns_cached",
+    "write_bin",
     "write_tns",
 ]

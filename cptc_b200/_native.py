@@ -1,6 +1,6 @@
 """ctypes bindings of the native libraries (declarations in include/*.h).
 
-libcptc_host.so — host-only: generators, .tns reader/writer.
+libcptc_host.so — host-only: generators, .tns reader/writer, binary cache.
 libcptc.so      — the CUDA engine (also exports the host symbols).
 
 Loading fails loudly: there is no Python or CPU fallback for the engine.
@@ -80,6 +80,11 @@ HOST_SYMBOLS = {
     "cptc_tns_read": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(Coo)]),
     "cptc_tns_probe_order": (C.c_int, [C.c_char_p]),
     "cptc_tns_write": (C.c_int, [C.c_char_p, C.POINTER(Coo)]),
+    "cptc_bin_write": (C.c_int, [C.c_char_p, C.POINTER(Coo), C.c_uint64, C.c_int64]),
+    "cptc_bin_read": (C.c_int, [C.c_char_p, C.POINTER(Coo), C.POINTER(C.c_uint64),
+                                C.POINTER(C.c_int64)]),
+    "cptc_tns_read_cached": (C.c_int, [C.c_char_p, C.c_int, C.c_char_p, C.POINTER(Coo),
+                                       C.POINTER(C.c_int)]),
     "cptc_gen_config": (C.c_int, [C.c_int, C.c_double, C.c_uint64, C.POINTER(Coo)]),
     "cptc_gen_uniform": (C.c_int, [C.c_int, C.POINTER(C.c_uint64), C.c_uint64, C.c_uint64,
                                    C.c_int, C.POINTER(Coo)]),

@@ -1,6 +1,6 @@
 """Builds the native parts of cptc_b200 in-tree.
 
-  cptc_b200/_lib/libcptc_host.so  host-only library (generators, .tns I/O)
+  cptc_b200/_lib/libcptc_host.so  host-only library (generators, .tns I/O, binary cache)
   cptc_b200/_lib/libcptc.so       the CUDA engine (sm_100a) with the C ABI
   cptc_b200/_lib/cptc_opt         the command-line driver
 
@@ -24,7 +24,7 @@ LIB = PKG / "_lib"
 OBJ = PKG / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-HOST_SRCS = ["host/gen.cpp", "host/tns.cpp", "host/reorder.cpp"]
+HOST_SRCS = ["host/gen.cpp", "host/tns.cpp", "host/bincache.cpp", "host/reorder.cpp"]
 CUDA_SRCS = [
     "cuda/views.cu",
     "cuda/mttkrp_sparse.cu",

@@ -10,7 +10,8 @@
 //   ALS_EXPORT_FACTORS, ALS_PROFILE,
 //   GEN_DENSE, GEN_DENSE_THRESHOLD, GEN_DENSE_INNER, GEN_REORDER,
 //   GEN_REORDER_T, GEN_REORDER_SAMPLE, GEN_SOLVER, GEN_SEED, GEN_DUMP,
-//   GEN_PROFILE, CPTC_DEVICE.
+//   GEN_PROFILE, CPTC_DEVICE, CPTC_TNS_CACHE (binary copy of the parsed
+//   tensor beside the .tns, used while the text is unchanged).
 // Output lines keep the reference's formats ("[ALS] iter i/N time=<ms> ms
 // fit=<f>", "[GEN] iter ... fit=", "[ALS] Lambda:", export files).
 #include <chrono>
@@ -94,7 +95,16 @@ int main(int argc, char** argv) {
 
   const auto t0 = std::chrono::steady_clock::now();
   cptc_coo t{};
-  if (cptc_tns_read(filename.c_str(), order, &t) != 0) {
+  // CPTC_TNS_CACHE=1 keeps a binary copy beside the text (<tns>.cptcbin);
+  // any other non-empty value names the copy.
+  const char* cache = env("CPTC_TNS_CACHE");
+  const bool use_cache = cache && *cache && std::strcmp(cache, "0") != 0;
+  int from_cache = 0;
+  const int lrc = use_cache ? cptc_tns_read_cached(filename.c_str(), order,
+                                                   std::strcmp(cache, "1") ? cache : nullptr,
+                                                   &t, &from_cache)
+                            : cptc_tns_read(filename.c_str(), order, &t);
+  if (lrc != 0) {
     std::fprintf(stderr, "[Error] Cannot open file: %s\n", filename.c_str());
     return 1;
   }
@@ -111,6 +121,8 @@ int main(int argc, char** argv) {
                 (unsigned long long)t.dims[0], (unsigned long long)t.dims[1],
                 (unsigned long long)t.dims[2], (unsigned long long)t.nnz);
   }
+  if (use_cache)
+    std::printf("[Main] binary cache: %s\n", from_cache ? "read" : "written from the text");
 
   cptc_opts o;
   cptc_opts_default(&o);

@@ -101,12 +101,46 @@ def gen_uniform(dims, nnz: int, seed: int = 0, values: str = "uniform") -> CooTe
     return _take(s)
 
 
-def read_tns(path: str, order: int = 0) -> CooTensor:
+def read_tns(path: str, order: int = 0, cache=None) -> CooTensor:
+    """Reads a FROSTT .tns file.  cache=True keeps a binary copy beside it
+    (path + ".cptcbin"), a string names the copy; the copy is used while the
+    text's size and modification time are those it was made from."""
+    if cache:
+        return read_tns_cached(path, order, None if cache is True else cache)[0]
     lib = N.host_lib()
     s = N.Coo()
     rc = lib.cptc_tns_read(str(path).encode(), int(order), C.byref(s))
     if rc != 0:
         raise RuntimeError(f"cptc_tns_read({path}) failed with {rc}")
+    return _take(s)
+
+
+def read_tns_cached(path: str, order: int = 0, cache_path=None) -> tuple:
+    """(tensor, True if the binary cache was used)."""
+    lib = N.host_lib()
+    s = N.Coo()
+    hit = C.c_int(0)
+    cp = str(cache_path).encode() if cache_path else None
+    rc = lib.cptc_tns_read_cached(str(path).encode(), int(order), cp, C.byref(s), C.byref(hit))
+    if rc != 0:
+        raise RuntimeError(f"cptc_tns_read_cached({path}) failed with {rc}")
+    return _take(s), bool(hit.value)
+
+
+def write_bin(path: str, t: CooTensor, src_size: int = 0, src_mtime_ns: int = 0) -> None:
+    lib = N.host_lib()
+    s = t.as_struct()
+    if lib.cptc_bin_write(str(path).encode(), C.byref(s), int(src_size), int(src_mtime_ns)) != 0:
+        raise RuntimeError(f"cptc_bin_write({path}): {lib.cptc_host_last_error().decode()}")
+
+
+def read_bin(path: str) -> CooTensor:
+    lib = N.host_lib()
+    s = N.Coo()
+    rc = lib.cptc_bin_read(str(path).encode(), C.byref(s), None, None)
+    if rc != 0:
+        raise RuntimeError(f"cptc_bin_read({path}) failed with {rc}: "
+                           f"{lib.cptc_host_last_error().decode()}")
     return _take(s)
 
 

@@ -51,6 +51,33 @@ int cptc_tns_probe_order(const char* path);
 /* Writes `t` as 1-based .tns text, values with %.17g (exact round trip). */
 int cptc_tns_write(const char* path, const cptc_coo* t);
 
+/* Binary tensor cache (no counterpart in the reference, which parses the
+ * text on every run: src/tensor.cu:39-271, src/generic.cu:1023-1155).
+ * The file holds the arrays of `t` as they are in memory plus the size and
+ * modification time (ns) of the .tns they came from, and a hash of the
+ * arrays; it is written under a temporary name and renamed into place.
+ * Returns 0 or -1 (cannot create / write). */
+int cptc_bin_write(const char* path, const cptc_coo* t, uint64_t src_size,
+                   int64_t src_mtime_ns);
+
+/* Reads a cache written by cptc_bin_write; src_size / src_mtime_ns (may be
+ * NULL) receive the recorded stamp of the source text. Returns 0, -1 (cannot
+ * open), -3 (no memory) or -4 (not a cache, truncated, hash mismatch, or an
+ * index outside the recorded dims). */
+int cptc_bin_read(const char* path, cptc_coo* out, uint64_t* src_size,
+                  int64_t* src_mtime_ns);
+
+/* cptc_tns_read through a cache at cache_path (NULL or "": path +
+ * ".cptcbin"). The cache is used when its recorded stamp equals the .tns
+ * file's current size and modification time and its order is the one the
+ * text would be read with (order_hint, or the probed order when
+ * order_hint <= 0); otherwise the text is parsed and the cache
+ * rewritten — a cache that cannot be written leaves just the parse result.
+ * *from_cache (may be NULL) is 1 when the cache was used. Same results and
+ * return codes as cptc_tns_read. */
+int cptc_tns_read_cached(const char* path, int order_hint, const char* cache_path,
+                         cptc_coo* out, int* from_cache);
+
 /* Synthetic workloads of the benchmark (cfg 1..5: 128^3 planted rank 8;
  * 256^3 block-dense planted rank 32; 512^3 dense blocks + uniform residual;
  * 12092x9184x28818 Zipf(1.1) lognormal; 183x24x1140x1717 Zipf(1.2)

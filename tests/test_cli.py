@@ -41,6 +41,26 @@ def test_cli_binary_built():
     assert CLI.exists()
 
 
+def test_cli_binary_cache_switch(tmp_path):
+    # the load happens before the engine starts, so the cache lines show on
+    # a machine without a GPU too (the run then stops at cptc_create)
+    t = cp.gen_uniform((20, 30, 40), 500, seed=1)
+    p = tmp_path / "c.tns"
+    cp.write_tns(p, t)
+    env = dict(os.environ, CPTC_TNS_CACHE="1")
+    outs = [subprocess.run([str(CLI), str(p), "1", "8"], env=env, capture_output=True,
+                           text=True, timeout=300).stdout for _ in range(2)]
+    assert "[Main] binary cache: written from the text" in outs[0]
+    assert "[Main] binary cache: read" in outs[1]
+    assert "NNZ: 500" in outs[1]
+    u, hit = cp.read_tns_cached(p)
+    assert hit and np.array_equal(u.vals, t.vals)
+    named = tmp_path / "named.bin"
+    env["CPTC_TNS_CACHE"] = str(named)
+    subprocess.run([str(CLI), str(p), "1", "8"], env=env, capture_output=True, timeout=300)
+    assert named.exists()
+
+
 @pytest.mark.gpu
 def test_cli_order3_tf32_matches_reference(gpu, tmp_path):
     g = json.loads((GOLD / "cfg1_R32_auto.json").read_text())

@@ -101,3 +101,87 @@ def test_engine_loads_without_gpu_and_fails_loudly():
     else:
         assert rc == 0
         lib.cptc_destroy(h)
+
+
+def test_bin_cache_roundtrip_and_reuse(tmp_path):
+    t = cp.gen_uniform((30, 40, 7, 5), 3000, seed=9, values="lognormal")
+    p = tmp_path / "x.tns"
+    cp.write_tns(p, t)
+    u, hit = cp.read_tns_cached(p)
+    assert not hit and (tmp_path / "x.tns.cptcbin").exists()
+    v, hit = cp.read_tns_cached(p)
+    assert hit
+    ref = cp.read_tns(p)
+    for w in (u, v):
+        assert w.dims == ref.dims
+        for a, b in zip(w.idx, ref.idx):
+            assert np.array_equal(a, b)
+        assert np.array_equal(w.vals, ref.vals)
+    # the probed order as a hint uses the cache; another hint parses the
+    # text with that order (and caches that), after which the probed order
+    # parses again
+    assert cp.read_tns_cached(p, order=4)[1]
+    w, hit = cp.read_tns_cached(p, order=3)
+    assert not hit and w.order == 3
+    assert cp.read_tns_cached(p, order=3)[1]
+    w, hit = cp.read_tns_cached(p)
+    assert not hit and w.order == 4
+
+
+def test_bin_cache_is_stale_when_the_text_changes(tmp_path):
+    p = tmp_path / "y.tns"
+    p.write_text("1 2 3 1.5\n4 5 6 2.5\n")
+    t, hit = cp.read_tns_cached(p)
+    assert not hit and t.nnz == 2
+    st = p.stat()
+    p.write_text("1 2 3 1.5\n4 5 6 2.5\n7 1 1 3.0\n")
+    os.utime(p, ns=(st.st_atime_ns, st.st_mtime_ns + 10**9))
+    t, hit = cp.read_tns_cached(p)
+    assert not hit and t.nnz == 3 and t.dims == (7, 5, 6)
+    t, hit = cp.read_tns_cached(p)
+    assert hit and t.nnz == 3
+
+
+def test_bin_cache_rejects_corrupt_and_truncated_files(tmp_path):
+    t = cp.gen_uniform((50, 60, 70), 5000, seed=3)
+    b = tmp_path / "t.bin"
+    cp.write_bin(b, t, 123, 456)
+    u = cp.read_bin(b)
+    assert u.dims == t.dims and np.array_equal(u.vals, t.vals)
+    raw = bytearray(b.read_bytes())
+    bad = tmp_path / "bad.bin"
+    raw2 = bytearray(raw)
+    raw2[len(raw2) - 5] ^= 0x40  # a value byte
+    bad.write_bytes(bytes(raw2))
+    with pytest.raises(RuntimeError, match="hash"):
+        cp.read_bin(bad)
+    bad.write_bytes(bytes(raw[:-8]))
+    with pytest.raises(RuntimeError, match="truncated"):
+        cp.read_bin(bad)
+    bad.write_bytes(b"not a cache" * 20)
+    with pytest.raises(RuntimeError):
+        cp.read_bin(bad)
+    # a corrupt sidecar is replaced by a parse of the text
+    p = tmp_path / "z.tns"
+    cp.write_tns(p, t)
+    cp.read_tns_cached(p)
+    side = tmp_path / "z.tns.cptcbin"
+    raw = bytearray(side.read_bytes())
+    raw[200] ^= 1
+    side.write_bytes(bytes(raw))
+    os.utime(side, ns=(p.stat().st_atime_ns, p.stat().st_mtime_ns))
+    u, hit = cp.read_tns_cached(p)
+    assert not hit and np.array_equal(u.vals, cp.read_tns(p).vals)
+    assert cp.read_tns_cached(p)[1]
+
+
+def test_bin_cache_hash_independent_of_threads(tmp_path):
+    code = ("import cptc_b200 as cp, sys; t = cp.gen_config(4, scale=0.02); "
+            "cp.write_bin(sys.argv[1], t)")
+    outs = []
+    for th in ("1", "3"):
+        f = tmp_path / f"c{th}.bin"
+        env = dict(os.environ, CPTC_HOST_THREADS=th)
+        subprocess.run([sys.executable, "-c", code, str(f)], env=env, cwd=ROOT, check=True)
+        outs.append(f.read_bytes())
+    assert outs[0] == outs[1]
