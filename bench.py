@@ -49,6 +49,9 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--keep-tns", default="", help="reference arm: keep the .tns it writes here")
     p.add_argument("--ref-log", default="", help="reference arm: save cpTC's stdout here")
+    p.add_argument("--phases", type=int, default=0,
+                   help="after the timed steps, run this many iterations with per-phase "
+                        "timing events and report their mean phase times per rank")
     return p.parse_args()
 
 
@@ -286,9 +289,21 @@ def run_engine(a):
     e2e_s = (time.perf_counter() - te0) / a.steps
     d2h = sum(f.nbytes for f in host_F) + host_lam.nbytes + 16
 
+    # ---- per-phase times of each mode update (diagnostic, untimed) ---------
+    phase_ms = None
+    if a.phases > 0:
+        eng.set_phase_timing(True)
+        eng.als(1)  # the iteration graph is captured again with the events
+        ph = [r.phases for r in eng.als(a.phases)]
+        eng.set_phase_timing(False)
+        phase_ms = np.mean(ph, axis=0)
+
     # ---- roofline of the dominant kernel -----------------------------------
     prof = [eng.profile_mttkrp(n, reps=3) for n in range(t.order)]
     rank_mode_ms = None
+    rank_phase_ms = None
+    if phase_ms is not None:
+        rank_phase_ms = [np.round(phase_ms, 4).tolist()]
 
     if dist is not None:
         import torch
@@ -301,6 +316,11 @@ def run_engine(a):
         gathered = [torch.zeros_like(mm) for _ in range(world)]
         dist.all_gather(gathered, mm)
         rank_mode_ms = [[round(float(x), 4) for x in g] for g in gathered]
+        if phase_ms is not None:
+            pm = torch.tensor(phase_ms, dtype=torch.float64)
+            pg = [torch.zeros_like(pm) for _ in range(world)]
+            dist.all_gather(pg, pm)
+            rank_phase_ms = [np.round(g.numpy(), 4).tolist() for g in pg]
 
     if rank != 0:
         eng.close()
@@ -359,6 +379,8 @@ def run_engine(a):
             "build_s": build_s,
             "mttkrp_ms_per_mode": mode_ms,
             "mttkrp_ms_per_mode_by_rank": rank_mode_ms if world > 1 else None,
+            "phase_ms_by_rank": rank_phase_ms,
+            "phase_names": list(cp.Engine.PHASES) if rank_phase_ms is not None else None,
             "final_fit": fits[-1],
         },
         "e2e": {"value": e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,

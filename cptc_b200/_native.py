@@ -108,6 +108,8 @@ ENGINE_SYMBOLS = {
     "cptc_mttkrp_timed": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_double)]),
     "cptc_profile_mttkrp": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_double)]),
     "cptc_launch_count": (C.c_ulonglong, []),
+    "cptc_phase_timing": (C.c_int, [C.c_void_p, C.c_int]),
+    "cptc_phase_times": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.c_int]),
     "cptc_als": (C.c_int, [C.c_void_p, C.c_int, ITER_CB, C.c_void_p]),
     "cptc_get_stats": (C.c_int, [C.c_void_p, C.POINTER(Stats)]),
     "cptc_fit_terms": (C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),

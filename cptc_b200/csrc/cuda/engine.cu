@@ -90,6 +90,10 @@ Engine::~Engine() {
     if (e) cudaEventDestroy(e);
   for (auto& e : ev1)
     if (e) cudaEventDestroy(e);
+  for (auto& sl : evp)
+    for (auto& md : sl)
+      for (auto& e : md)
+        if (e) cudaEventDestroy(e);
   if (ev_fork) cudaEventDestroy(ev_fork);
   if (ev_join) cudaEventDestroy(ev_join);
   if (h_scal) cudaFreeHost(h_scal);
@@ -503,10 +507,14 @@ void Engine::update_mode(int n, bool last) {
   CPTC_CUDA(cudaStreamIsCapturing(stream, &cs));
   const unsigned rf = (cs == cudaStreamCaptureStatusActive) ? cudaEventRecordExternal
                                                             : cudaEventRecordDefault;
+  auto phase_end = [&](int k) {
+    if (phase_timing) CPTC_CUDA(cudaEventRecordWithFlags(evp[cur_slot][n][k], stream, rf));
+  };
   CPTC_CUDA(cudaEventRecordWithFlags(evc[2 * n], stream, rf));
   mttkrp(n);
   CPTC_CUDA(cudaEventRecordWithFlags(evc[2 * n + 1], stream, rf));
   comm_reduce_scatter_ftv(*this, n);
+  phase_end(0);
   CPTC_CUDA(cudaStreamWaitEvent(stream, ev_join, 0));
   const uint64_t lo = row_lo(n), rows = row_hi(n) - lo;
   const int nb = launch_apply_solve(FtV.p + lo * R, Ainv.p, lambda.p, generic ? 0 : 1, rows, R,
@@ -516,9 +524,11 @@ void Engine::update_mode(int n, bool last) {
   const int nd = last ? launch_col_dots(F[n].p + lo * R, FtV.p + lo * R, rows, R, dots.p,
                                         gpart_blocks, stream)
                       : 0;
+  phase_end(1);
   // One all-reduce (Gram partials, dot products) grouped with the all-gather
   // of the solved slab; every rank then normalises the whole factor.
   const double* gsum = comm_reduce_gram_gather(*this, n, nb, nd);
+  phase_end(2);
   launch_norm_finalize(gsum, 1, R, generic ? 1 : 0, lambda.p, G[n].p, colscale(), stream);
   launch_scale_cols(F[n].p, dims[n], R, colscale(), stream);
   if (last) {
@@ -526,6 +536,21 @@ void Engine::update_mode(int n, bool last) {
     for (int m = 0; m < N; ++m) gall[m] = G[m].p;
     launch_fit_final(gsum + (size_t)R * R, 1, colscale(), lambda.p, gall, N, R, scal.p, stream);
   }
+  phase_end(3);
+}
+
+void Engine::set_phase_timing(bool on) {
+  CPTC_CUDA(cudaSetDevice(device));
+  if (on && !evp[0][0][0])
+    for (auto& sl : evp)
+      for (auto& md : sl)
+        for (auto& e : md) CPTC_CUDA(cudaEventCreate(&e));
+  if (on != phase_timing) {
+    CPTC_CUDA(cudaStreamSynchronize(stream));
+    release_graph();  // the captured iteration has (or lacks) the events
+  }
+  phase_timing = on;
+  phase_valid = false;
 }
 
 double* Engine::colscale() { return cscale.p; }
@@ -543,6 +568,7 @@ void Engine::release_graph() {
 // solve status copied to readback slot `slot` of the pinned host buffer.
 void Engine::enqueue_iteration(int slot) {
   evc = slot ? ev1 : ev;
+  cur_slot = slot;
   for (int n = 0; n < N; ++n) update_mode(n, n == N - 1);
   double* hs = h_scal + 8 * slot;
   CPTC_CUDA(cudaMemcpyAsync(hs, scal.p, 2 * sizeof(double), cudaMemcpyDeviceToHost, stream));
@@ -616,6 +642,19 @@ void Engine::finish_iteration(int it, int slot, cptc_iter_cb cb, void* user) {
     float t = 0.f;
     cudaEventElapsedTime(&t, E[2 * n], E[2 * n + 1]);
     mode_ms[n] = t;
+  }
+  if (phase_timing) {
+    for (int n = 0; n < N; ++n) {
+      const cudaEvent_t b[5] = {E[2 * n + 1], evp[slot][n][0], evp[slot][n][1],
+                                evp[slot][n][2], evp[slot][n][3]};
+      phase_ms[n][0] = mode_ms[n];
+      for (int k = 0; k < 4; ++k) {
+        float t = 0.f;
+        CPTC_CUDA(cudaEventElapsedTime(&t, b[k], b[k + 1]));
+        phase_ms[n][k + 1] = t;
+      }
+    }
+    phase_valid = true;
   }
   last_iprod = iprod;
   last_model2 = model2;
@@ -825,6 +864,22 @@ int cptc_get_relabel(cptc_ctx* c, int mode, uint32_t* perm_out) {
     else
       std::memcpy(perm_out, e.perm[mode].data(), e.dims[mode] * sizeof(uint32_t));
   });
+}
+
+int cptc_phase_timing(cptc_ctx* c, int on) {
+  return guarded(c, [&](Engine& e) { e.set_phase_timing(on != 0); });
+}
+
+int cptc_phase_times(cptc_ctx* c, double* out, int cap) {
+  int written = 0;
+  const int rc = guarded(c, [&](Engine& e) {
+    CPTC_REQUIRE(out != nullptr || cap == 0, CPTC_E_ARG, "null output");
+    if (!e.phase_timing || !e.phase_valid) return;
+    for (int n = 0; n < e.N; ++n)
+      for (int p = 0; p < CPTC_NPHASES; ++p)
+        if (written < cap) out[written++] = e.phase_ms[n][p];
+  });
+  return rc != 0 ? rc : written;
 }
 
 int cptc_fit_terms(cptc_ctx* c, double* out3) {

@@ -95,6 +95,14 @@ struct Engine {
   cudaEvent_t ev1[2 * CPTC_MAX_ORDER + 2] = {};
   cudaEvent_t* evc = nullptr;  // events of the iteration being enqueued
   unsigned long long iter_kernels = 0;  // this library's kernels in the graph
+  // Phase timing (off by default; the events are extra graph nodes): per
+  // slot and mode, events after the reduce-scatter, the solve, the
+  // all-reduce + all-gather and the normalisation.
+  bool phase_timing = false;
+  int cur_slot = 0;
+  cudaEvent_t evp[2][CPTC_MAX_ORDER][4] = {};
+  double phase_ms[CPTC_MAX_ORDER][CPTC_NPHASES] = {};
+  bool phase_valid = false;
   std::string err;
 
   // Tensor (device COO, relabelled in place by the build).
@@ -156,6 +164,7 @@ struct Engine {
   void fetch_rows(const double* dev, int m, double* host);
   double* stage_rows();
   void release_graph();
+  void set_phase_timing(bool on);
   void enqueue_iteration(int slot);
   void launch_iteration(int slot);
   void finish_iteration(int it, int slot, cptc_iter_cb cb, void* user);

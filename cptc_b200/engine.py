@@ -44,6 +44,7 @@ class IterReport:
     ms: float
     fit: float
     mode_ms: list
+    phases: np.ndarray | None = None  # (order, 5) ms when phase timing is on
 
 
 def default_opts() -> N.Opts:
@@ -200,6 +201,22 @@ class Engine:
                     "profile_mttkrp")
         return {"tiles_ms": ms[0], "sparse_ms": ms[1], "total_ms": ms[2]}
 
+    PHASES = ("mttkrp", "reduce_scatter", "solve", "allreduce_gather", "normalise")
+
+    def set_phase_timing(self, on: bool = True) -> None:
+        """Time every phase of each mode update from the next als() on."""
+        self._check(self._lib.cptc_phase_timing(self._h, int(bool(on))), "phase_timing")
+
+    def phase_times(self) -> np.ndarray:
+        """(order, 5) device ms of the last finished iteration's phases, in
+        the order of PHASES; empty when phase timing is off."""
+        n = N.MAX_ORDER * len(self.PHASES)
+        buf = (C.c_double * n)()
+        got = self._lib.cptc_phase_times(self._h, buf, n)
+        if got < 0:
+            self._check(got, "phase_times")
+        return np.array(buf[:got], dtype=np.float64).reshape(-1, len(self.PHASES))
+
     def fit_terms(self) -> dict:
         out = (C.c_double * 3)()
         self._check(self._lib.cptc_fit_terms(self._h, out), "fit_terms")
@@ -219,7 +236,9 @@ class Engine:
         reports = []
 
         def _cb(it, ms, fit, mode_ms, nm, user):
-            r = IterReport(it, ms, fit, [mode_ms[i] for i in range(nm)])
+            ph = self.phase_times()
+            r = IterReport(it, ms, fit, [mode_ms[i] for i in range(nm)],
+                           ph if ph.size else None)
             reports.append(r)
             if callback is not None:
                 callback(r)

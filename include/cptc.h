@@ -160,6 +160,28 @@ int cptc_profile_mttkrp(cptc_ctx* ctx, int mode, int reps, double ms3[3]);
  * replayed CUDA graph of an ALS iteration counts the kernels it holds). */
 unsigned long long cptc_launch_count(void);
 
+/* Per-phase device times of each mode update (no counterpart in the
+ * reference, whose ALS_PROFILE reports the MTTKRP only: src/als.cu:535-604).
+ * cptc_phase_timing(ctx, 1) adds timing events after each phase of every
+ * mode update from the next cptc_als on (off by default: the events are
+ * extra nodes in the iteration's graph). cptc_phase_times then writes, for
+ * the last iteration that finished, out[n * CPTC_NPHASES + p] in ms for
+ * mode n < order and phase p:
+ *   0  MTTKRP (zero, residual kernel, dense tiles)
+ *   1  reduce-scatter of the MTTKRP into the row slabs (empty on one GPU)
+ *   2  wait for the R x R inverse, apply it, Gram partials (and the fit's
+ *      column dots on the last mode)
+ *   3  all-reduce of the Gram partials + all-gather of the slab (one GPU:
+ *      the partial sums)
+ *   4  normalisation (and the fit on the last mode)
+ * Writes at most `cap` values and returns how many (0 when phase timing is
+ * off or no iteration has run since it was turned on), or a negative
+ * status. On several GPUs each rank reports its own times: a phase that
+ * waits for the slowest rank shows that wait. */
+#define CPTC_NPHASES 5
+int cptc_phase_timing(cptc_ctx* ctx, int on);
+int cptc_phase_times(cptc_ctx* ctx, double* out, int cap);
+
 /* Runs `iters` CP-ALS iterations; cb (nullable) is called once per
  * iteration, in order, with that iteration's device time, fit and per-mode
  * MTTKRP times.  Iteration k+1 is already on the GPU when the callback of

@@ -293,3 +293,31 @@ def test_exact_residual(gpu, order):
     got = e.residual()
     assert abs(got["res_sq"] - want) <= 1e-10 * want
     assert abs(got["x_sq"] - float(t.vals @ t.vals)) <= 1e-12 * got["x_sq"]
+
+
+def test_phase_times(gpu):
+    # the phase events change no result; phase 0 is the MTTKRP time the
+    # iteration callback reports, and the phases fit inside the iteration
+    t = cp.gen_config(1)
+    runs = []
+    for on in (False, True):
+        e = engine_for(t, 16)
+        e.init_factors()
+        if on:
+            e.set_phase_timing(True)
+        runs.append(e.als(4))
+        if on:
+            ph = e.phase_times()
+            assert ph.shape == (3, len(cp.Engine.PHASES))
+            e.set_phase_timing(False)
+            assert e.als(1)[0].phases is None and e.phase_times().size == 0
+        e.close()
+    off, on = runs
+    # FP64 atomics order the MTTKRP sums differently from run to run (~1e-16)
+    # and the ALS iterations amplify that (measured: 2e-12 after 4 of them)
+    assert np.max(np.abs(np.subtract([r.fit for r in off], [r.fit for r in on]))) < 1e-9
+    for r in on:
+        assert r.phases.shape == (3, 5) and np.all(r.phases >= 0)
+        assert np.allclose(r.phases[:, 0], r.mode_ms)
+        assert r.phases.sum() <= r.ms + 1e-3
+    assert all(r.phases is None for r in off)
