@@ -49,6 +49,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--keep-tns", default="", help="reference arm: keep the .tns it writes here")
     p.add_argument("--ref-log", default="", help="reference arm: save cpTC's stdout here")
+    p.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
+                   help="how the ranks combine a mode update (several GPUs)")
     p.add_argument("--phases", type=int, default=0,
                    help="after the timed steps, run this many iterations with per-phase "
                         "timing events and report their mean phase times per rank")
@@ -247,7 +249,7 @@ def run_engine(a):
     # ---- end to end through the C ABI: host COO in, factors out ----------
     tb0 = time.perf_counter()
     eng.load(t)
-    eng.build(a.rank, threshold=a.threshold, path=a.path)
+    eng.build(a.rank, threshold=a.threshold, path=a.path, exchange=a.exchange)
     eng.init_factors()
     build_s = time.perf_counter() - tb0
     st = eng.stats()
@@ -375,6 +377,7 @@ def run_engine(a):
             "dense_nnz": st["dense_nnz"],
             "avg_fill": st["avg_fill"],
             "parallelism": f"row-slab x{world}" if world > 1 else "single GPU",
+            "exchange": a.exchange if world > 1 else None,
             "l2": "views (1.2 GB/mode) stream from HBM each MTTKRP; no flush needed",
             "build_s": build_s,
             "mttkrp_ms_per_mode": mode_ms,

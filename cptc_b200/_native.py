@@ -44,6 +44,7 @@ class Opts(C.Structure):
         ("dense_thr_generic", C.c_double),
         ("dense_inner", C.c_int * 3),
         ("verbose", C.c_int),
+        ("exchange", C.c_int),
     ]
 
 

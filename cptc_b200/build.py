@@ -32,6 +32,7 @@ CUDA_SRCS = [
     "cuda/units.cu",
     "cuda/als_kernels.cu",
     "cuda/comm.cu",
+    "cuda/peer.cu",
     "cuda/engine.cu",
     "cuda/noalloc.cu",
 ]

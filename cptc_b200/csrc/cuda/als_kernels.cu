@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(1024) k_pinv_jacobi(const double* __restrict__
     double s = 0.0;
     for (int k = 0; k < R; ++k) s = fma(W[k * R + a] * wgt[k], W[k * R + b], s);
     Ainv[o] = s;
-    if (!isfinite(s)) atomicExch(status, 1);
+    if (!isfinite(s)) atomicOr(status, 1);
   }
 }
 
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(NWARP * 32) k_sweep_inverse(GPtrs g, int ng, i
       if (i < R && k < R) {
         const double v = -M[m][c];
         Ainv[i * R + k] = v;
-        if (!isfinite(v)) atomicExch(status, 1);
+        if (!isfinite(v)) atomicOr(status, 1);
       }
     }
 }

@@ -35,6 +35,7 @@ void comm_init(Engine& E, const unsigned char idb[128], int rank, int nranks) {
   CPTC_REQUIRE(nranks >= 1 && rank >= 0 && rank < nranks, CPTC_E_ARG, "bad rank / nranks");
   CPTC_CUDA(cudaSetDevice(E.device));
   E.release_graph();  // it may hold NCCL calls on the old communicator
+  peer_unmap(E);      // collective over the old communicator
   comm_destroy(E);
   if (nranks == 1) {
     E.nranks = 1;

@@ -32,4 +32,13 @@ void comm_reduce_scatter_ftv(Engine& E, int n);
 // The full reduced FtV on every rank (reduce-scatter + all-gather).
 void comm_reduce_ftv(Engine& E, int n);
 
+// Peer-memory exchange (peer.cu).  peer_map / peer_unmap are collective:
+// map after the factor buffers are allocated, unmap before any of them is
+// freed.  The two others replace comm_reduce_scatter_ftv and
+// comm_reduce_gram_gather with the same results (sums in rank order).
+void peer_map(Engine& E);
+void peer_unmap(Engine& E);
+void peer_reduce_scatter_ftv(Engine& E, int n);
+const double* peer_reduce_gram_gather(Engine& E, int n, int nblk, int ndots);
+
 }  // namespace cptc

@@ -85,6 +85,10 @@ Engine::~Engine() {
   if (stream) cudaStreamSynchronize(stream);
   if (side) cudaStreamSynchronize(side);
   release_graph();  // before the communicator its NCCL nodes use
+  try {
+    peer_unmap(*this);  // collective when the peer exchange is mapped
+  } catch (...) {
+  }
   comm_destroy(*this);
   for (auto& e : ev)
     if (e) cudaEventDestroy(e);
@@ -225,6 +229,12 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
   R = R_;
   generic = (N != 3) || opts.generic;
   release_graph();
+  peer_unmap(*this);  // its mappings point at the buffers rebuilt below
+  CPTC_REQUIRE(opts.exchange == CPTC_EXCHANGE_NCCL || opts.exchange == CPTC_EXCHANGE_PEER,
+               CPTC_E_ARG, "unknown exchange");
+  CPTC_REQUIRE(opts.exchange == CPTC_EXCHANGE_NCCL || nranks == 1 ||
+                   (nranks <= kMaxPeers && nccl != nullptr),
+               CPTC_E_UNSUP, "the peer exchange needs 2 to 8 ranks");
   built = false;
   have_factors = false;
   views.clear();
@@ -303,6 +313,7 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
     v.t1 = v.ntasks * (uint64_t)(rank + 1) / (uint64_t)nranks;
   }
   CPTC_CUDA(cudaStreamSynchronize(stream));
+  if (nranks > 1 && opts.exchange == CPTC_EXCHANGE_PEER) peer_map(*this);
   build_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   built = true;
 }
@@ -513,7 +524,8 @@ void Engine::update_mode(int n, bool last) {
   CPTC_CUDA(cudaEventRecordWithFlags(evc[2 * n], stream, rf));
   mttkrp(n);
   CPTC_CUDA(cudaEventRecordWithFlags(evc[2 * n + 1], stream, rf));
-  comm_reduce_scatter_ftv(*this, n);
+  if (peer.on) peer_reduce_scatter_ftv(*this, n);
+  else comm_reduce_scatter_ftv(*this, n);
   phase_end(0);
   CPTC_CUDA(cudaStreamWaitEvent(stream, ev_join, 0));
   const uint64_t lo = row_lo(n), rows = row_hi(n) - lo;
@@ -527,7 +539,8 @@ void Engine::update_mode(int n, bool last) {
   phase_end(1);
   // One all-reduce (Gram partials, dot products) grouped with the all-gather
   // of the solved slab; every rank then normalises the whole factor.
-  const double* gsum = comm_reduce_gram_gather(*this, n, nb, nd);
+  const double* gsum = peer.on ? peer_reduce_gram_gather(*this, n, nb, nd)
+                               : comm_reduce_gram_gather(*this, n, nb, nd);
   phase_end(2);
   launch_norm_finalize(gsum, 1, R, generic ? 1 : 0, lambda.p, G[n].p, colscale(), stream);
   launch_scale_cols(F[n].p, dims[n], R, colscale(), stream);
@@ -629,6 +642,9 @@ void Engine::finish_iteration(int it, int slot, cptc_iter_cb cb, void* user) {
   std::memcpy(&h_status, hs + 4, sizeof(int));
   if (h_status != 0) {
     cudaStreamSynchronize(stream);  // the next iteration may be in flight
+    if (h_status & kStatusPeerTimeout)
+      throw CptcError(CPTC_E_COMM, "a peer barrier timed out (a rank is missing or stalled); "
+                                   "the exchange stays broken until the next cptc_build");
     throw CptcError(CPTC_E_NUMERIC, "non-finite values in the R x R solve");
   }
   const double xn = std::sqrt(x_norm_sq);
@@ -735,6 +751,7 @@ int cptc_opts_default(cptc_opts* o) {
   o->dense_inner[1] = 1;
   o->dense_inner[2] = 2;
   o->verbose = 0;
+  o->exchange = CPTC_EXCHANGE_NCCL;
   return CPTC_OK;
 }
 

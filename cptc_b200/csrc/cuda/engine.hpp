@@ -79,6 +79,23 @@ struct UnitPool {
 // Default fill-rate threshold of the dense-tile path on B200 for rank R.
 double b200_fill_min(int R);
 
+// Peer-memory exchange (cptc_opts.exchange = CPTC_EXCHANGE_PEER): every
+// rank's buffers mapped into this process with CUDA IPC.
+constexpr int kMaxPeers = 8;
+constexpr int kStatusPeerTimeout = 2;  // status bit: a peer barrier ran out of time
+struct PeerState {
+  bool on = false;
+  int G = 1;
+  int slot_stride = 0;                 // doubles per rank's slot: R*R + R
+  DArray<double> recv;                 // G regions of one slab: partial MTTKRP rows
+  DArray<unsigned char> arena;         // flags | epoch, broken | G slots
+  double* F_of[CPTC_MAX_ORDER][kMaxPeers] = {};
+  double* recv_of[kMaxPeers] = {};
+  unsigned char* arena_of[kMaxPeers] = {};
+  std::vector<void*> opened;           // imported mappings, closed at teardown
+  unsigned long long timeout_ns = 0;
+};
+
 struct Engine {
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -150,6 +167,7 @@ struct Engine {
   int nranks = 1, rank = 0;
   std::vector<uint64_t> slab[CPTC_MAX_ORDER];
   DArray<double> comm_buf;
+  PeerState peer;
 
   cudaEvent_t ev[2 * CPTC_MAX_ORDER + 2] = {};
 

@@ -30,6 +30,7 @@ from .tensor import CooTensor
 PATHS = {"auto": 0, "tf32": 1, "fp64": 2}
 REORDERS = {"default": -1, "none": 0, "cadr": 1, "hits": 2, "auto": 3}
 SOLVERS = {"default": 0, "chol": 1, "cholesky": 1, "pinv": 2, "svd": 2}
+EXCHANGES = {"nccl": 0, "peer": 1}
 
 
 class CptcError(RuntimeError):
@@ -116,8 +117,10 @@ class Engine:
               reorder: str = "default", reorder_rounds: int = 3,
               reorder_sample: int = 8_000_000, solver: str = "default", seed: int = 42,
               dense_generic: bool = True, dense_thr_generic: float = 0.03,
-              dense_inner: tuple = (0, 1, 2), fill_min: float = 0.0) -> None:
+              dense_inner: tuple = (0, 1, 2), fill_min: float = 0.0,
+              exchange: str = "nccl") -> None:
         o = default_opts()
+        o.exchange = EXCHANGES[exchange]
         o.path = PATHS[path]
         o.fill_min = float(fill_min)
         o.generic = int(bool(generic))

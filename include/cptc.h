@@ -59,6 +59,17 @@ enum { CPTC_REORDER_NONE = 0, CPTC_REORDER_CADR = 1, CPTC_REORDER_HITS = 2,
        CPTC_REORDER_AUTO = 3, CPTC_REORDER_DEFAULT = -1 };
 /* R x R solve (GEN_SOLVER of src/generic.cu:2114-2136). */
 enum { CPTC_SOLVER_DEFAULT = 0, CPTC_SOLVER_CHOL = 1, CPTC_SOLVER_PINV = 2 };
+/* How the ranks of a multi-GPU context combine a mode update (no
+ * counterpart in the reference, which runs on one GPU).
+ *   NCCL: reduce-scatter of the MTTKRP, then the Gram all-reduce grouped
+ *         with the slab all-gather (the default).
+ *   PEER: the same exchanges as stores into the other ranks' buffers over
+ *         NVLink (CUDA IPC mappings) with two bounded flag barriers per mode
+ *         update; sums in rank order.  2..8 ranks; cptc_build and
+ *         cptc_destroy become collective (they map and unmap the buffers);
+ *         a barrier that waits longer than CPTC_PEER_TIMEOUT_MS (default
+ *         5000) fails the iteration with CPTC_E_COMM. */
+enum { CPTC_EXCHANGE_NCCL = 0, CPTC_EXCHANGE_PEER = 1 };
 
 typedef struct cptc_opts {
   int path;                 /* CPTC_PATH_*                                   */
@@ -74,6 +85,8 @@ typedef struct cptc_opts {
   double dense_thr_generic; /* GEN_DENSE_THRESHOLD (0.03)                    */
   int dense_inner[3];       /* GEN_DENSE_INNER (0,1,2)                       */
   int verbose;              /* print the reference's progress lines          */
+  int exchange;             /* CPTC_EXCHANGE_*: how ranks combine a mode
+                               update (several GPUs only)                    */
 } cptc_opts;
 
 /* Per-iteration report: iteration number (1-based), device time of the

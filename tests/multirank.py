@@ -17,7 +17,9 @@ the host.
 from __future__ import annotations
 
 import datetime
+import hashlib
 import os
+import sys
 
 import numpy as np
 
@@ -176,10 +178,15 @@ def gpu_main(argv=None):
         F = e.factors()
         lam = e.lam()
         M0 = e.mttkrp(0)
+        # every rank's replica must hold the same bits
+        h = hashlib.sha1(b"".join(np.ascontiguousarray(f).tobytes() for f in F)).hexdigest()
+        hashes = [None] * world
+        dist.all_gather_object(hashes, h)
         dist.barrier()
         if rank == 0:
             np.savez(a.out, fits=np.array([r.fit for r in reps]), lam=lam, M0=M0,
-                     tf32=int(st["tf32_path"]), **{f"F{m}": f for m, f in enumerate(F)})
+                     tf32=int(st["tf32_path"]), replicas_equal=int(len(set(hashes)) == 1),
+                     **{f"F{m}": f for m, f in enumerate(F)})
         e.close()
     finally:
         dist.destroy_process_group()
@@ -191,6 +198,63 @@ GPU_CASES = {
     "hybrid_o3": dict(gen=("config", 4, 0.05, 0), R=32, iters=3, build=dict(path="tf32")),
     "generic_o4": dict(gen=("config", 5, 0.2, 0), R=16, iters=3, build=dict(generic=True)),
 }
+# the same cases with the peer-memory exchange (a 1-GPU run ignores it)
+for _k in list(GPU_CASES):
+    GPU_CASES[_k + "_peer"] = dict(GPU_CASES[_k], build=dict(GPU_CASES[_k]["build"],
+                                                             exchange="peer"))
+# R=17: odd slabs take the scalar copy kernels
+GPU_CASES["fp64_o3_r17_peer"] = dict(gen=("uniform", (301, 250, 199), 60_000, 4, "normal"), R=17,
+                                     iters=3, build=dict(path="fp64", exchange="peer"))
+
+
+def peer_timeout_main(out: str):
+    """Two torchrun ranks with the peer exchange and a 1 s barrier limit:
+    rank 0 runs one ALS iteration alone, so its first barrier waits for a
+    flag that nothing sets; the kernel gives up, the iteration fails with
+    CPTC_E_COMM, and after a collective rebuild both ranks run ALS again."""
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    import cptc_b200 as cp
+
+    os.environ["CPTC_PEER_TIMEOUT_MS"] = "1000"
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    try:
+        t = cp.gen_uniform((200, 150, 100), 20_000, seed=7, values="uniform")
+        e = cp.Engine(local)
+        obj = [cp.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        e.comm_init(obj[0], rank, world)
+        e.load(t)
+        e.build(8, path="fp64", exchange="peer")
+        e.init_factors()
+        e.als(1)
+        dist.barrier()
+        code, waited = 0, 0.0
+        if rank == 0:
+            t0 = time.perf_counter()
+            try:
+                e.als(1)
+            except cp.CptcError as x:
+                code = x.code
+            waited = time.perf_counter() - t0
+        dist.barrier()  # rank 1 waits here, off the GPU
+        e.build(8, path="fp64", exchange="peer")
+        e.init_factors()
+        fits = [r.fit for r in e.als(3)]
+        allf = [None] * world
+        dist.all_gather_object(allf, fits)
+        if rank == 0:
+            np.savez(out, code=code, waited=waited, fits=np.array(fits),
+                     ranks_agree=int(all(f == fits for f in allf)))
+        e.close()
+    finally:
+        dist.destroy_process_group()
 
 
 def make_case(spec):
@@ -203,4 +267,7 @@ def make_case(spec):
 
 
 if __name__ == "__main__":
-    gpu_main()
+    if len(sys.argv) > 2 and sys.argv[1] == "--peer-timeout":
+        peer_timeout_main(sys.argv[2])
+    else:
+        gpu_main()

@@ -185,3 +185,18 @@ def test_bin_cache_hash_independent_of_threads(tmp_path):
         subprocess.run([sys.executable, "-c", code, str(f)], env=env, cwd=ROOT, check=True)
         outs.append(f.read_bytes())
     assert outs[0] == outs[1]
+
+
+def test_ctypes_structs_match_the_c_headers(tmp_path):
+    # the Python mirrors of cptc_opts, cptc_stats and cptc_coo must have the
+    # C layout (a field added on one side only shifts every later field)
+    src = tmp_path / "sz.c"
+    src.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "cptc.h"\n'
+                   'int main(void) { printf("%zu %zu %zu %zu\\n", sizeof(cptc_opts), '
+                   'sizeof(cptc_stats), sizeof(cptc_coo), offsetof(cptc_opts, exchange)); '
+                   'return 0; }\n')
+    exe = tmp_path / "sz"
+    subprocess.run(["gcc", f"-I{ROOT / 'include'}", str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    assert got == [C.sizeof(N.Opts), C.sizeof(N.Stats), C.sizeof(N.Coo), N.Opts.exchange.offset]
