@@ -12,7 +12,10 @@ Per mode: partial MTTKRP of the rank's chunk -> reduce-scatter into the slabs
 are its diagonal; the last mode appends the fit's column dot products) beside
 the all-gather of the unnormalised slabs -> every rank normalises the whole
 factor.  Run with gloo it checks the order and payload of the collectives on
-the host.
+the host.  exchange="peer" restates the peer-memory exchange instead: every
+rank's partial slab rows reach the owner (region r of its receive buffer) and
+the owner adds the G partials in rank order 0..G-1; the Gram partials go to
+slot r of every rank, which adds the slots in rank order.
 """
 from __future__ import annotations
 
@@ -42,7 +45,7 @@ def truncated_pinv(A, R):
     return (V[:, keep] / w[keep]) @ V[:, keep].T
 
 
-def shard_als3(t, R, iters, rank, world, dist):
+def shard_als3(t, R, iters, rank, world, dist, exchange="nccl"):
     """The engine's distributed order-3 ALS on `world` CPU ranks (see module doc)."""
     import torch
 
@@ -68,11 +71,30 @@ def shard_als3(t, R, iters, rank, world, dist):
         dist.all_reduce(v)
         return v.numpy()
 
+    def gather(x):
+        parts = [torch.zeros(x.shape, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(x)))
+        return [p.numpy() for p in parts]
+
+    def rank_order_sum(parts):
+        acc = np.zeros_like(parts[0])
+        for p in parts:  # r = 0 .. world-1
+            acc = acc + p
+        return acc
+
     def reduce_scatter_rows(M, s):
         # padded to world * s rows; gloo has no reduce_scatter: all-reduce, keep own slab
         P = np.zeros((world * s, R))
         P[:M.shape[0]] = M
+        if exchange == "peer":
+            # region r of the owner's receive buffer holds rank r's rows of its slab
+            return rank_order_sum([g[rank * s:(rank + 1) * s] for g in gather(P)])
         return allreduce(P)[rank * s:(rank + 1) * s]
+
+    def reduce_slots(x):
+        if exchange == "peer":
+            return rank_order_sum(gather(x))
+        return allreduce(x)
 
     def allgather_rows(Fl, s, dim):
         parts = [torch.zeros((s, R), dtype=torch.float64) for _ in range(world)]
@@ -97,7 +119,7 @@ def shard_als3(t, R, iters, rank, world, dist):
             payload = [(Fl.T @ Fl).ravel()]
             if n == 2:
                 payload.append(np.einsum("kr,kr->r", Fl[:hi - lo], Ms[:hi - lo]))
-            red = allreduce(np.concatenate(payload))
+            red = reduce_slots(np.concatenate(payload))
             Gs = red[:R * R].reshape(R, R)
             Fn = allgather_rows(Fl, s, t.dims[n])
             nr = np.sqrt(np.diag(Gs))
@@ -136,7 +158,8 @@ def cpu_worker(rank, world, port, spec, q):
                             world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
         t = make_cpu_case(spec)
-        fits, F, lam, shares = shard_als3(t, spec["R"], spec["iters"], rank, world, dist)
+        fits, F, lam, shares = shard_als3(t, spec["R"], spec["iters"], rank, world, dist,
+                                          spec.get("exchange", "nccl"))
         q.put((rank, fits, F, lam, shares))
     except Exception as e:  # report instead of hanging the other ranks' test
         q.put((rank, repr(e), None, None, None))

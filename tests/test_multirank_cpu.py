@@ -2,9 +2,9 @@
 
 tests/multirank.py restates the engine's distributed ALS (nonzeros shared out
 by count, partial MTTKRP reduce-scattered into equal row slabs, Gram
-all-reduce, slab all-gather) over world-size 2 and 3 gloo groups; it must
-reproduce the single-process ALS, and every rank must end with the same
-factors.  The tensor has a Zipf-like head row so that one row is split
+all-reduce, slab all-gather; or the peer exchange's rank-order sums) over
+world-size 2 and 3 gloo groups; it must reproduce the single-process ALS, and
+every rank must end with the same factors.  The tensor has a Zipf-like head row so that one row is split
 between ranks.
 """
 import multiprocessing as mp
@@ -47,9 +47,10 @@ def _run(world, spec):
     return out
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_sharded_als_matches_single_process(world):
-    spec = dict(dims=(90, 70, 50), nnz=12_000, seed=21, values="lognormal", R=8, iters=4)
+@pytest.mark.parametrize("world,exchange", [(2, "nccl"), (3, "nccl"), (3, "peer")])
+def test_sharded_als_matches_single_process(world, exchange):
+    spec = dict(dims=(90, 70, 50), nnz=12_000, seed=21, values="lognormal", R=8, iters=4,
+                exchange=exchange)
     out = _run(world, spec)
     t = make_cpu_case(spec)
     ref = np_als3(t, spec["R"], spec["iters"])
@@ -64,6 +65,20 @@ def test_sharded_als_matches_single_process(world):
     for m in range(3):
         sizes = [out[r][3][m] for r in range(world)]
         assert sum(sizes) == spec["nnz"] and max(sizes) - min(sizes) <= 1
+
+
+def test_peer_exchange_sums_in_rank_order():
+    # the peer exchange adds the ranks' partials in rank order on every rank:
+    # the replicas agree bit for bit, and with the NCCL sums to rounding
+    spec = dict(dims=(60, 50, 40), nnz=9_000, seed=5, values="lognormal", R=8, iters=3,
+                heavy=0.45, exchange="peer")
+    out = _run(3, spec)
+    ref = _run(3, dict(spec, exchange="nccl"))
+    for r in (1, 2):
+        assert np.array_equal(out[r][0], out[0][0])
+        for a, b in zip(out[r][1], out[0][1]):
+            assert np.array_equal(a, b)
+    assert np.max(np.abs(out[0][0] - ref[0][0])) < 1e-12
 
 
 def test_sharded_als_with_a_split_head_row():
