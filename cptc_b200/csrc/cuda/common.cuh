@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <stdexcept>
@@ -32,12 +33,16 @@ struct CptcError : std::runtime_error {
     if (e_ != cudaSuccess) ::cptc::throw_cuda(e_, #call, __FILE__, __LINE__); \
   } while (0)
 
-extern unsigned long long g_launches;  // kernels launched by this library
+// Kernels launched by this library (all host threads), and by this host
+// thread (used to count the kernels a graph capture records).
+extern std::atomic<unsigned long long> g_launches;
+extern thread_local unsigned long long t_launches;
 
-#define CPTC_LAUNCH_CHECK()           \
-  do {                                \
-    CPTC_CUDA(cudaGetLastError());    \
-    ++::cptc::g_launches;             \
+#define CPTC_LAUNCH_CHECK()                                          \
+  do {                                                               \
+    CPTC_CUDA(cudaGetLastError());                                   \
+    ::cptc::g_launches.fetch_add(1, std::memory_order_relaxed);      \
+    ++::cptc::t_launches;                                            \
   } while (0)
 
 #define CPTC_REQUIRE(cond, code, msg)                 \

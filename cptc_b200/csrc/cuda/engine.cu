@@ -19,7 +19,8 @@
 
 namespace cptc {
 
-unsigned long long g_launches = 0;
+std::atomic<unsigned long long> g_launches{0};
+thread_local unsigned long long t_launches = 0;
 
 namespace {
 
@@ -609,7 +610,7 @@ void Engine::launch_iteration(int slot) {
   }
   if (!iter_exec[slot]) {
     // Kernels enqueued during capture are counted when the graph runs.
-    const unsigned long long l0 = g_launches;
+    const unsigned long long l0 = t_launches;
     CPTC_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
     try {
       enqueue_iteration(slot);
@@ -618,17 +619,19 @@ void Engine::launch_iteration(int slot) {
       cudaStreamEndCapture(stream, &g);
       if (g) cudaGraphDestroy(g);
       cudaGetLastError();
-      g_launches = l0;
+      g_launches.fetch_sub(t_launches - l0);
+      t_launches = l0;
       evc = ev;
       throw;
     }
-    iter_kernels = g_launches - l0;
-    g_launches = l0;
+    iter_kernels = t_launches - l0;
+    g_launches.fetch_sub(iter_kernels);  // counted when the graph runs
+    t_launches = l0;
     CPTC_CUDA(cudaStreamEndCapture(stream, &iter_graph[slot]));
     CPTC_CUDA(cudaGraphInstantiate(&iter_exec[slot], iter_graph[slot], 0));
   }
   CPTC_CUDA(cudaGraphLaunch(iter_exec[slot], stream));
-  g_launches += iter_kernels;
+  g_launches.fetch_add(iter_kernels);
   CPTC_CUDA(cudaEventRecord(E[2 * CPTC_MAX_ORDER + 1], stream));
 }
 
@@ -871,7 +874,7 @@ int cptc_profile_mttkrp(cptc_ctx* c, int mode, int reps, double* ms3) {
   });
 }
 
-unsigned long long cptc_launch_count(void) { return cptc::g_launches; }
+unsigned long long cptc_launch_count(void) { return cptc::g_launches.load(); }
 
 int cptc_get_relabel(cptc_ctx* c, int mode, uint32_t* perm_out) {
   return guarded(c, [&](Engine& e) {
