@@ -767,10 +767,15 @@ int cptc_create(cptc_ctx** out, int device, int flags) {
   try {
     c->e = new Engine(device);
   } catch (const CptcError& x) {
-    c->err = x.what();
     const int code = x.code;
     delete c;
     return code;
+  } catch (const std::bad_alloc&) {
+    delete c;
+    return CPTC_E_NOMEM;
+  } catch (...) {
+    delete c;
+    return CPTC_E_CUDA;
   }
   *out = c;
   return CPTC_OK;

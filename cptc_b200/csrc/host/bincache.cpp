@@ -147,166 +147,172 @@ using namespace cptc;
 extern "C" {
 
 int cptc_bin_write(const char* path, const cptc_coo* t, uint64_t src_size, int64_t src_mtime_ns) {
-  if (!path || !t || t->order < 1 || t->order > CPTC_MAX_ORDER) {
-    set_host_error("cptc_bin_write: bad tensor");
-    return -2;
-  }
-  Header h{};
-  std::memcpy(h.magic, kMagic, 8);
-  h.order = (uint32_t)t->order;
-  h.nnz = t->nnz;
-  h.src_size = src_size;
-  h.src_mtime_ns = src_mtime_ns;
-  for (int m = 0; m < t->order; ++m) h.dims[m] = t->dims[m];
-  const std::vector<Span> sp = spans_of(t);
-  const std::vector<Piece> pc = pieces_of(sp);
-  std::vector<uint64_t> ph(pc.size());
-  const int nt = std::max(1, std::min<int>(host_threads(), (int)pc.size()));
-#pragma omp parallel for num_threads(nt) schedule(static)
-  for (int64_t i = 0; i < (int64_t)pc.size(); ++i)
-    ph[i] = fnv_words(sp[pc[i].span].mem + pc[i].begin, pc[i].end - pc[i].begin);
-  h.hash = combine(ph);
-
-  // Written under a temporary name and renamed into place, so a reader (say
-  // another rank of the same job) sees the old file or the whole new one.
-  const std::string tmp = std::string(path) + ".tmp." + std::to_string((long)::getpid());
-  const int fd = ::open(tmp.c_str(), O_WRONLY | O_CREAT | O_TRUNC, 0644);
-  if (fd < 0) {
-    set_host_error("cptc_bin_write: cannot create the cache file");
-    return -1;
-  }
-  const uint64_t total = file_bytes(t->order, t->nnz);
-  bool ok = ::ftruncate(fd, (off_t)total) == 0 && write_all(fd, &h, sizeof(h), 0);
-  int bad = 0;
-  // Chunks written by all threads at their offsets (the padding between
-  // arrays stays the zeros of the ftruncate); on the 200 MB/s disk of the
-  // build machine this took 8.5 s for config 4, one sequential stream 22 s.
-#pragma omp parallel for num_threads(nt) schedule(static) reduction(| : bad)
-  for (int64_t i = 0; i < (int64_t)pc.size(); ++i) {
-    const Span& s = sp[pc[i].span];
-    if (!write_all(fd, s.mem + pc[i].begin, pc[i].end - pc[i].begin, s.off + pc[i].begin))
-      bad |= 1;
-  }
-  ok = ok && !bad;
-  ok = (::close(fd) == 0) && ok;
-  if (!ok || std::rename(tmp.c_str(), path) != 0) {
-    ::unlink(tmp.c_str());
-    set_host_error("cptc_bin_write: write failed");
-    return -1;
-  }
-  return 0;
+  return host_guard(nullptr, [&]() -> int {
+    if (!path || !t || t->order < 1 || t->order > CPTC_MAX_ORDER) {
+      set_host_error("cptc_bin_write: bad tensor");
+      return -2;
+    }
+    Header h{};
+    std::memcpy(h.magic, kMagic, 8);
+    h.order = (uint32_t)t->order;
+    h.nnz = t->nnz;
+    h.src_size = src_size;
+    h.src_mtime_ns = src_mtime_ns;
+    for (int m = 0; m < t->order; ++m) h.dims[m] = t->dims[m];
+    const std::vector<Span> sp = spans_of(t);
+    const std::vector<Piece> pc = pieces_of(sp);
+    std::vector<uint64_t> ph(pc.size());
+    const int nt = std::max(1, std::min<int>(host_threads(), (int)pc.size()));
+  #pragma omp parallel for num_threads(nt) schedule(static)
+    for (int64_t i = 0; i < (int64_t)pc.size(); ++i)
+      ph[i] = fnv_words(sp[pc[i].span].mem + pc[i].begin, pc[i].end - pc[i].begin);
+    h.hash = combine(ph);
+  
+    // Written under a temporary name and renamed into place, so a reader (say
+    // another rank of the same job) sees the old file or the whole new one.
+    const std::string tmp = std::string(path) + ".tmp." + std::to_string((long)::getpid());
+    const int fd = ::open(tmp.c_str(), O_WRONLY | O_CREAT | O_TRUNC, 0644);
+    if (fd < 0) {
+      set_host_error("cptc_bin_write: cannot create the cache file");
+      return -1;
+    }
+    const uint64_t total = file_bytes(t->order, t->nnz);
+    bool ok = ::ftruncate(fd, (off_t)total) == 0 && write_all(fd, &h, sizeof(h), 0);
+    int bad = 0;
+    // Chunks written by all threads at their offsets (the padding between
+    // arrays stays the zeros of the ftruncate); on the 200 MB/s disk of the
+    // build machine this took 8.5 s for config 4, one sequential stream 22 s.
+  #pragma omp parallel for num_threads(nt) schedule(static) reduction(| : bad)
+    for (int64_t i = 0; i < (int64_t)pc.size(); ++i) {
+      const Span& s = sp[pc[i].span];
+      if (!write_all(fd, s.mem + pc[i].begin, pc[i].end - pc[i].begin, s.off + pc[i].begin))
+        bad |= 1;
+    }
+    ok = ok && !bad;
+    ok = (::close(fd) == 0) && ok;
+    if (!ok || std::rename(tmp.c_str(), path) != 0) {
+      ::unlink(tmp.c_str());
+      set_host_error("cptc_bin_write: write failed");
+      return -1;
+    }
+    return 0;
+  });
 }
 
 int cptc_bin_read(const char* path, cptc_coo* out, uint64_t* src_size, int64_t* src_mtime_ns) {
-  if (!out) return -2;
-  std::memset(out, 0, sizeof(*out));
-  const int fd = ::open(path, O_RDONLY);
-  if (fd < 0) {
-    set_host_error("cptc_bin_read: cannot open the cache file");
-    return -1;
-  }
-  struct stat st;
-  if (::fstat(fd, &st) != 0 || (uint64_t)st.st_size < kHeader) {
+  return host_guard(out, [&]() -> int {
+    if (!out) return -2;
+    std::memset(out, 0, sizeof(*out));
+    const int fd = ::open(path, O_RDONLY);
+    if (fd < 0) {
+      set_host_error("cptc_bin_read: cannot open the cache file");
+      return -1;
+    }
+    struct stat st;
+    if (::fstat(fd, &st) != 0 || (uint64_t)st.st_size < kHeader) {
+      ::close(fd);
+      set_host_error("cptc_bin_read: not a tensor cache (too short)");
+      return -4;
+    }
+    const uint64_t fsz = (uint64_t)st.st_size;
+    void* mp = ::mmap(nullptr, (size_t)fsz, PROT_READ, MAP_PRIVATE, fd, 0);
     ::close(fd);
-    set_host_error("cptc_bin_read: not a tensor cache (too short)");
-    return -4;
-  }
-  const uint64_t fsz = (uint64_t)st.st_size;
-  void* mp = ::mmap(nullptr, (size_t)fsz, PROT_READ, MAP_PRIVATE, fd, 0);
-  ::close(fd);
-  if (mp == MAP_FAILED) {
-    set_host_error("cptc_bin_read: mmap failed");
-    return -1;
-  }
-  struct Unmap {
-    void* p;
-    size_t n;
-    ~Unmap() { ::munmap(p, n); }
-  } unmap{mp, (size_t)fsz};
-  const unsigned char* base = (const unsigned char*)mp;
-  Header h;
-  std::memcpy(&h, base, sizeof(h));
-  if (std::memcmp(h.magic, kMagic, 8) != 0 || h.order < 1 || h.order > CPTC_MAX_ORDER ||
-      h.nnz > (fsz / 12) || file_bytes((int)h.order, h.nnz) != fsz) {
-    set_host_error("cptc_bin_read: not a tensor cache, or truncated");
-    return -4;
-  }
-  if (!coo_alloc(out, (int)h.order, h.nnz)) {
-    cptc_coo_free(out);
-    set_host_error("cptc_bin_read: out of host memory");
-    return -3;
-  }
-  for (int m = 0; m < (int)h.order; ++m) out->dims[m] = h.dims[m];
-  ::madvise(mp, (size_t)fsz, MADV_SEQUENTIAL);
-  const std::vector<Span> sp = spans_of(out);
-  const std::vector<Piece> pc = pieces_of(sp);
-  std::vector<uint64_t> ph(pc.size());
-  const int nt = std::max(1, std::min<int>(host_threads(), (int)pc.size()));
-  // Copy and hash chunk by chunk (the destination pages are first touched by
-  // the thread that fills them).
-#pragma omp parallel for num_threads(nt) schedule(static)
-  for (int64_t i = 0; i < (int64_t)pc.size(); ++i) {
-    const Span& s = sp[pc[i].span];
-    const uint64_t n = pc[i].end - pc[i].begin;
-    std::memcpy(s.mem + pc[i].begin, base + s.off + pc[i].begin, (size_t)n);
-    ph[i] = fnv_words(s.mem + pc[i].begin, n);
-  }
-  if (combine(ph) != h.hash) {
-    cptc_coo_free(out);
-    std::memset(out, 0, sizeof(*out));
-    set_host_error("cptc_bin_read: payload hash mismatch (corrupt cache)");
-    return -4;
-  }
-  // Indices must lie inside the recorded dims (a consumer indexes factor
-  // rows with them).
-  uint64_t viol = 0;
-  for (int m = 0; m < (int)h.order; ++m) {
-    const uint32_t* ix = out->idx[m];
-    const uint64_t d = h.dims[m];
-#pragma omp parallel for num_threads(nt) schedule(static) reduction(+ : viol)
-    for (int64_t e = 0; e < (int64_t)h.nnz; ++e) viol += (uint64_t)(ix[e] >= d);
-  }
-  if (viol) {
-    cptc_coo_free(out);
-    std::memset(out, 0, sizeof(*out));
-    set_host_error("cptc_bin_read: index outside the recorded dims");
-    return -4;
-  }
-  if (src_size) *src_size = h.src_size;
-  if (src_mtime_ns) *src_mtime_ns = h.src_mtime_ns;
-  return 0;
+    if (mp == MAP_FAILED) {
+      set_host_error("cptc_bin_read: mmap failed");
+      return -1;
+    }
+    struct Unmap {
+      void* p;
+      size_t n;
+      ~Unmap() { ::munmap(p, n); }
+    } unmap{mp, (size_t)fsz};
+    const unsigned char* base = (const unsigned char*)mp;
+    Header h;
+    std::memcpy(&h, base, sizeof(h));
+    if (std::memcmp(h.magic, kMagic, 8) != 0 || h.order < 1 || h.order > CPTC_MAX_ORDER ||
+        h.nnz > (fsz / 12) || file_bytes((int)h.order, h.nnz) != fsz) {
+      set_host_error("cptc_bin_read: not a tensor cache, or truncated");
+      return -4;
+    }
+    if (!coo_alloc(out, (int)h.order, h.nnz)) {
+      cptc_coo_free(out);
+      set_host_error("cptc_bin_read: out of host memory");
+      return -3;
+    }
+    for (int m = 0; m < (int)h.order; ++m) out->dims[m] = h.dims[m];
+    ::madvise(mp, (size_t)fsz, MADV_SEQUENTIAL);
+    const std::vector<Span> sp = spans_of(out);
+    const std::vector<Piece> pc = pieces_of(sp);
+    std::vector<uint64_t> ph(pc.size());
+    const int nt = std::max(1, std::min<int>(host_threads(), (int)pc.size()));
+    // Copy and hash chunk by chunk (the destination pages are first touched by
+    // the thread that fills them).
+  #pragma omp parallel for num_threads(nt) schedule(static)
+    for (int64_t i = 0; i < (int64_t)pc.size(); ++i) {
+      const Span& s = sp[pc[i].span];
+      const uint64_t n = pc[i].end - pc[i].begin;
+      std::memcpy(s.mem + pc[i].begin, base + s.off + pc[i].begin, (size_t)n);
+      ph[i] = fnv_words(s.mem + pc[i].begin, n);
+    }
+    if (combine(ph) != h.hash) {
+      cptc_coo_free(out);
+      std::memset(out, 0, sizeof(*out));
+      set_host_error("cptc_bin_read: payload hash mismatch (corrupt cache)");
+      return -4;
+    }
+    // Indices must lie inside the recorded dims (a consumer indexes factor
+    // rows with them).
+    uint64_t viol = 0;
+    for (int m = 0; m < (int)h.order; ++m) {
+      const uint32_t* ix = out->idx[m];
+      const uint64_t d = h.dims[m];
+  #pragma omp parallel for num_threads(nt) schedule(static) reduction(+ : viol)
+      for (int64_t e = 0; e < (int64_t)h.nnz; ++e) viol += (uint64_t)(ix[e] >= d);
+    }
+    if (viol) {
+      cptc_coo_free(out);
+      std::memset(out, 0, sizeof(*out));
+      set_host_error("cptc_bin_read: index outside the recorded dims");
+      return -4;
+    }
+    if (src_size) *src_size = h.src_size;
+    if (src_mtime_ns) *src_mtime_ns = h.src_mtime_ns;
+    return 0;
+  });
 }
 
 int cptc_tns_read_cached(const char* path, int order_hint, const char* cache_path,
                          cptc_coo* out, int* from_cache) {
-  if (!path || !out) return -2;
-  if (from_cache) *from_cache = 0;
-  const std::string cp = cache_path && *cache_path ? std::string(cache_path)
-                                                   : std::string(path) + ".cptcbin";
-  uint64_t size = 0;
-  int64_t mtime = 0;
-  if (!file_stamp(path, &size, &mtime)) {
-    std::memset(out, 0, sizeof(*out));
-    set_host_error("cptc_tns_read_cached: cannot stat the .tns file");
-    return -1;
-  }
-  // The order the text would be parsed with (the cache may have been made
-  // with another hint).
-  const int order = order_hint > 0 ? order_hint : cptc_tns_probe_order(path);
-  uint64_t csize = 0;
-  int64_t cmtime = 0;
-  if (cptc_bin_read(cp.c_str(), out, &csize, &cmtime) == 0) {
-    if (csize == size && cmtime == mtime && out->order == order) {
-      if (from_cache) *from_cache = 1;
-      return 0;
+  return host_guard(out, [&]() -> int {
+    if (!path || !out) return -2;
+    if (from_cache) *from_cache = 0;
+    const std::string cp = cache_path && *cache_path ? std::string(cache_path)
+                                                     : std::string(path) + ".cptcbin";
+    uint64_t size = 0;
+    int64_t mtime = 0;
+    if (!file_stamp(path, &size, &mtime)) {
+      std::memset(out, 0, sizeof(*out));
+      set_host_error("cptc_tns_read_cached: cannot stat the .tns file");
+      return -1;
     }
-    cptc_coo_free(out);  // stale: made from another version of the text
-  }
-  const int rc = cptc_tns_read(path, order_hint, out);
-  if (rc != 0) return rc;
-  // Best effort: a cache that cannot be written leaves the parse result.
-  (void)cptc_bin_write(cp.c_str(), out, size, mtime);
-  return 0;
+    // The order the text would be parsed with (the cache may have been made
+    // with another hint).
+    const int order = order_hint > 0 ? order_hint : cptc_tns_probe_order(path);
+    uint64_t csize = 0;
+    int64_t cmtime = 0;
+    if (cptc_bin_read(cp.c_str(), out, &csize, &cmtime) == 0) {
+      if (csize == size && cmtime == mtime && out->order == order) {
+        if (from_cache) *from_cache = 1;
+        return 0;
+      }
+      cptc_coo_free(out);  // stale: made from another version of the text
+    }
+    const int rc = cptc_tns_read(path, order_hint, out);
+    if (rc != 0) return rc;
+    // Best effort: a cache that cannot be written leaves the parse result.
+    (void)cptc_bin_write(cp.c_str(), out, size, mtime);
+    return 0;
+  });
 }
 
 }  // extern "C"

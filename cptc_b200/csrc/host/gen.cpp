@@ -255,122 +255,126 @@ void cptc_coo_free(cptc_coo* t) {
 
 int cptc_gen_uniform(int order, const uint64_t* dims, uint64_t nnz, uint64_t seed,
                      int value_kind, cptc_coo* out) {
-  if (!out || !dims || order < 1 || order > CPTC_MAX_ORDER)
-    return host_fail(-2, "bad order");
-  std::memset(out, 0, sizeof(*out));
-  cptc_coo shape{};
-  shape.order = order;
-  for (int m = 0; m < order; ++m) {
-    if (dims[m] == 0 || dims[m] > UINT32_MAX) return host_fail(-2, "bad dims");
-    shape.dims[m] = dims[m];
-  }
-  const uint64_t space = key_space_of(&shape);
-  if (space == 0) return host_fail(-2, "key space exceeds 2^63");
-  if (nnz > space) return host_fail(-2, "nnz exceeds the number of cells");
-  auto keys = first_distinct(
-      nnz, [&](uint64_t d) { return rng_below(seed, 1, d, space); }, space);
-  if (keys.size() != nnz) return host_fail(-4, "generator did not converge");
-  int rc = finish(out, order, dims, keys);
-  if (rc) return rc;
-  kind_values(out, keys, value_kind, seed);
-  return 0;
-}
-
-int cptc_gen_config(int cfg, double nnz_scale, uint64_t seed, cptc_coo* out) {
-  if (!out) return host_fail(-2, "null output");
-  std::memset(out, 0, sizeof(*out));
-  if (!(nnz_scale > 0.0)) return host_fail(-2, "nnz_scale must be positive");
-  auto scaled = [&](double n) { return (uint64_t)std::llround(n * nnz_scale); };
-
-  if (cfg == 1 || cfg == 2) {
-    // Uniform distinct cells, planted low-rank values plus Gaussian noise.
-    const uint64_t n = (cfg == 1) ? 128 : 256;
-    const uint64_t dims[3] = {n, n, n};
-    const uint64_t nnz = scaled(cfg == 1 ? 200000.0 : 15100000.0);
-    const uint64_t space = n * n * n;
-    if (nnz > space) return host_fail(-2, "nnz exceeds cells");
+  return host_guard(out, [&]() -> int {
+    if (!out || !dims || order < 1 || order > CPTC_MAX_ORDER)
+      return host_fail(-2, "bad order");
+    std::memset(out, 0, sizeof(*out));
+    cptc_coo shape{};
+    shape.order = order;
+    for (int m = 0; m < order; ++m) {
+      if (dims[m] == 0 || dims[m] > UINT32_MAX) return host_fail(-2, "bad dims");
+      shape.dims[m] = dims[m];
+    }
+    const uint64_t space = key_space_of(&shape);
+    if (space == 0) return host_fail(-2, "key space exceeds 2^63");
+    if (nnz > space) return host_fail(-2, "nnz exceeds the number of cells");
     auto keys = first_distinct(
         nnz, [&](uint64_t d) { return rng_below(seed, 1, d, space); }, space);
     if (keys.size() != nnz) return host_fail(-4, "generator did not converge");
-    int rc = finish(out, 3, dims, keys);
+    int rc = finish(out, order, dims, keys);
     if (rc) return rc;
-    planted_values(out, keys, cfg == 1 ? 8 : 32, cfg == 1 ? 0.01 : 0.05, seed);
+    kind_values(out, keys, value_kind, seed);
     return 0;
-  }
+  });
+}
 
-  if (cfg == 3) {
-    // 40% of nonzeros inside random aligned 16^3 tiles with per-tile fill
-    // U[0.05, 0.6]; 60% uniform residual outside those cells; values U(0,1].
-    const uint64_t n = 512, nb = n / 16, space = n * n * n;
-    const uint64_t dims[3] = {n, n, n};
-    const uint64_t n_tile = scaled(8000000.0), n_res = scaled(12000000.0);
-    std::vector<uint64_t> tile_keys;
-    tile_keys.reserve(n_tile);
-    std::vector<char> used(nb * nb * nb, 0);
-    std::vector<uint16_t> pos(4096);
-    for (uint64_t t = 0; tile_keys.size() < n_tile && t < 100 * nb * nb * nb; ++t) {
-      const uint64_t tid = rng_below(seed, 20, t, nb * nb * nb);
-      if (used[tid]) continue;
-      used[tid] = 1;
-      const double f = 0.05 + 0.55 * rng_unit(seed, 21, t);
-      uint64_t cnt = (uint64_t)std::max<long long>(1, std::llround(f * 4096.0));
-      cnt = std::min<uint64_t>(cnt, n_tile - tile_keys.size());
-      for (int i = 0; i < 4096; ++i) pos[i] = (uint16_t)i;
-      const uint64_t bi = tid / (nb * nb), bj = (tid / nb) % nb, bk = tid % nb;
-      for (uint64_t i = 0; i < cnt; ++i) {  // partial Fisher-Yates
-        const uint64_t j = i + rng_below(seed, 22, t * 4096 + i, 4096 - i);
-        std::swap(pos[i], pos[j]);
-        const uint64_t li = pos[i] >> 8, lj = (pos[i] >> 4) & 15, lk = pos[i] & 15;
-        tile_keys.push_back(((bi * 16 + li) * n + (bj * 16 + lj)) * n + bk * 16 + lk);
-      }
+int cptc_gen_config(int cfg, double nnz_scale, uint64_t seed, cptc_coo* out) {
+  return host_guard(out, [&]() -> int {
+    if (!out) return host_fail(-2, "null output");
+    std::memset(out, 0, sizeof(*out));
+    if (!(nnz_scale > 0.0)) return host_fail(-2, "nnz_scale must be positive");
+    auto scaled = [&](double n) { return (uint64_t)std::llround(n * nnz_scale); };
+  
+    if (cfg == 1 || cfg == 2) {
+      // Uniform distinct cells, planted low-rank values plus Gaussian noise.
+      const uint64_t n = (cfg == 1) ? 128 : 256;
+      const uint64_t dims[3] = {n, n, n};
+      const uint64_t nnz = scaled(cfg == 1 ? 200000.0 : 15100000.0);
+      const uint64_t space = n * n * n;
+      if (nnz > space) return host_fail(-2, "nnz exceeds cells");
+      auto keys = first_distinct(
+          nnz, [&](uint64_t d) { return rng_below(seed, 1, d, space); }, space);
+      if (keys.size() != nnz) return host_fail(-4, "generator did not converge");
+      int rc = finish(out, 3, dims, keys);
+      if (rc) return rc;
+      planted_values(out, keys, cfg == 1 ? 8 : 32, cfg == 1 ? 0.01 : 0.05, seed);
+      return 0;
     }
-    __gnu_parallel::sort(tile_keys.begin(), tile_keys.end());
-    auto res = first_distinct(
-        n_res,
-        [&](uint64_t d) {
-          const uint64_t k = rng_below(seed, 23, d, space);
-          return std::binary_search(tile_keys.begin(), tile_keys.end(), k) ? UINT64_MAX
-                                                                            : k;
-        },
-        space);
-    if (res.size() != n_res) return host_fail(-4, "generator did not converge");
-    std::vector<uint64_t> keys(tile_keys.size() + res.size());
-    std::merge(tile_keys.begin(), tile_keys.end(), res.begin(), res.end(), keys.begin());
-    int rc = finish(out, 3, dims, keys);
-    if (rc) return rc;
-    kind_values(out, keys, 0, seed);
-    return 0;
-  }
-
-  if (cfg == 4 || cfg == 5) {
-    // Per-mode Zipf indices over a random permutation of each mode.
-    const int N = (cfg == 4) ? 3 : 4;
-    const uint64_t d4[3] = {12092, 9184, 28818};
-    const uint64_t d5[4] = {183, 24, 1140, 1717};
-    const uint64_t* dims = (cfg == 4) ? d4 : d5;
-    const double alpha = (cfg == 4) ? 1.1 : 1.2;
-    const uint64_t nnz = scaled(cfg == 4 ? 76900000.0 : 3300000.0);
-    std::vector<ZipfMode> z(N);
-    for (int m = 0; m < N; ++m) z[m].init(dims[m], alpha, seed, 100 + m);
-    cptc_coo shape{};
-    shape.order = N;
-    for (int m = 0; m < N; ++m) shape.dims[m] = dims[m];
-    const uint64_t space = key_space_of(&shape);
-    auto keys = first_distinct(
-        nnz,
-        [&](uint64_t d) {
-          uint64_t k = 0;
-          for (int m = 0; m < N; ++m) k = k * dims[m] + z[m].sample(rng_unit(seed, 10 + m, d));
-          return k;
-        },
-        space);
-    if (keys.size() != nnz) return host_fail(-4, "generator did not converge");
-    int rc = finish(out, N, dims, keys);
-    if (rc) return rc;
-    kind_values(out, keys, cfg == 4 ? 1 : 3, seed);
-    return 0;
-  }
-  return host_fail(-2, "unknown config (1..5)");
+  
+    if (cfg == 3) {
+      // 40% of nonzeros inside random aligned 16^3 tiles with per-tile fill
+      // U[0.05, 0.6]; 60% uniform residual outside those cells; values U(0,1].
+      const uint64_t n = 512, nb = n / 16, space = n * n * n;
+      const uint64_t dims[3] = {n, n, n};
+      const uint64_t n_tile = scaled(8000000.0), n_res = scaled(12000000.0);
+      std::vector<uint64_t> tile_keys;
+      tile_keys.reserve(n_tile);
+      std::vector<char> used(nb * nb * nb, 0);
+      std::vector<uint16_t> pos(4096);
+      for (uint64_t t = 0; tile_keys.size() < n_tile && t < 100 * nb * nb * nb; ++t) {
+        const uint64_t tid = rng_below(seed, 20, t, nb * nb * nb);
+        if (used[tid]) continue;
+        used[tid] = 1;
+        const double f = 0.05 + 0.55 * rng_unit(seed, 21, t);
+        uint64_t cnt = (uint64_t)std::max<long long>(1, std::llround(f * 4096.0));
+        cnt = std::min<uint64_t>(cnt, n_tile - tile_keys.size());
+        for (int i = 0; i < 4096; ++i) pos[i] = (uint16_t)i;
+        const uint64_t bi = tid / (nb * nb), bj = (tid / nb) % nb, bk = tid % nb;
+        for (uint64_t i = 0; i < cnt; ++i) {  // partial Fisher-Yates
+          const uint64_t j = i + rng_below(seed, 22, t * 4096 + i, 4096 - i);
+          std::swap(pos[i], pos[j]);
+          const uint64_t li = pos[i] >> 8, lj = (pos[i] >> 4) & 15, lk = pos[i] & 15;
+          tile_keys.push_back(((bi * 16 + li) * n + (bj * 16 + lj)) * n + bk * 16 + lk);
+        }
+      }
+      __gnu_parallel::sort(tile_keys.begin(), tile_keys.end());
+      auto res = first_distinct(
+          n_res,
+          [&](uint64_t d) {
+            const uint64_t k = rng_below(seed, 23, d, space);
+            return std::binary_search(tile_keys.begin(), tile_keys.end(), k) ? UINT64_MAX
+                                                                              : k;
+          },
+          space);
+      if (res.size() != n_res) return host_fail(-4, "generator did not converge");
+      std::vector<uint64_t> keys(tile_keys.size() + res.size());
+      std::merge(tile_keys.begin(), tile_keys.end(), res.begin(), res.end(), keys.begin());
+      int rc = finish(out, 3, dims, keys);
+      if (rc) return rc;
+      kind_values(out, keys, 0, seed);
+      return 0;
+    }
+  
+    if (cfg == 4 || cfg == 5) {
+      // Per-mode Zipf indices over a random permutation of each mode.
+      const int N = (cfg == 4) ? 3 : 4;
+      const uint64_t d4[3] = {12092, 9184, 28818};
+      const uint64_t d5[4] = {183, 24, 1140, 1717};
+      const uint64_t* dims = (cfg == 4) ? d4 : d5;
+      const double alpha = (cfg == 4) ? 1.1 : 1.2;
+      const uint64_t nnz = scaled(cfg == 4 ? 76900000.0 : 3300000.0);
+      std::vector<ZipfMode> z(N);
+      for (int m = 0; m < N; ++m) z[m].init(dims[m], alpha, seed, 100 + m);
+      cptc_coo shape{};
+      shape.order = N;
+      for (int m = 0; m < N; ++m) shape.dims[m] = dims[m];
+      const uint64_t space = key_space_of(&shape);
+      auto keys = first_distinct(
+          nnz,
+          [&](uint64_t d) {
+            uint64_t k = 0;
+            for (int m = 0; m < N; ++m) k = k * dims[m] + z[m].sample(rng_unit(seed, 10 + m, d));
+            return k;
+          },
+          space);
+      if (keys.size() != nnz) return host_fail(-4, "generator did not converge");
+      int rc = finish(out, N, dims, keys);
+      if (rc) return rc;
+      kind_values(out, keys, cfg == 4 ? 1 : 3, seed);
+      return 0;
+    }
+    return host_fail(-2, "unknown config (1..5)");
+  });
 }
 
 }  // extern "C"

@@ -108,126 +108,132 @@ using namespace cptc;
 extern "C" {
 
 int cptc_tns_probe_order(const char* path) {
-  FILE* f = std::fopen(path, "rb");
-  if (!f) return -1;
-  std::vector<char> buf(1 << 16);
-  const size_t got = std::fread(buf.data(), 1, buf.size(), f);
-  std::fclose(f);
-  return probe_order(buf.data(), buf.data() + got);
+  return host_guard(nullptr, [&]() -> int {
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return -1;
+    std::vector<char> buf(1 << 16);
+    const size_t got = std::fread(buf.data(), 1, buf.size(), f);
+    std::fclose(f);
+    return probe_order(buf.data(), buf.data() + got);
+  });
 }
 
 int cptc_tns_read(const char* path, int order_hint, cptc_coo* out) {
-  if (!out) return -2;
-  std::memset(out, 0, sizeof(*out));
-  const int fd = ::open(path, O_RDONLY);
-  if (fd < 0) return -1;
-  struct stat st;
-  if (::fstat(fd, &st) != 0) {
-    ::close(fd);
-    return -1;
-  }
-  const size_t fsz = (size_t)st.st_size;
-  const char* map = nullptr;
-  if (fsz > 0) {
-    void* mp = ::mmap(nullptr, fsz, PROT_READ, MAP_PRIVATE, fd, 0);
-    if (mp == MAP_FAILED) {
+  return host_guard(out, [&]() -> int {
+    if (!out) return -2;
+    std::memset(out, 0, sizeof(*out));
+    const int fd = ::open(path, O_RDONLY);
+    if (fd < 0) return -1;
+    struct stat st;
+    if (::fstat(fd, &st) != 0) {
       ::close(fd);
       return -1;
     }
-    map = (const char*)mp;
-    ::madvise(mp, fsz, MADV_SEQUENTIAL);
-  }
-  ::close(fd);
-  struct Unmap {
-    const char* p;
-    size_t n;
-    ~Unmap() {
-      if (p) ::munmap((void*)p, n);
+    const size_t fsz = (size_t)st.st_size;
+    const char* map = nullptr;
+    if (fsz > 0) {
+      void* mp = ::mmap(nullptr, fsz, PROT_READ, MAP_PRIVATE, fd, 0);
+      if (mp == MAP_FAILED) {
+        ::close(fd);
+        return -1;
+      }
+      map = (const char*)mp;
+      ::madvise(mp, fsz, MADV_SEQUENTIAL);
     }
-  } unmap{map, fsz};
-  // Everything up to the last newline is parsed in place; a final line
-  // without a newline goes through a copy that ends with one.
-  size_t body = fsz;
-  while (body > 0 && map[body - 1] != '\n') --body;
-  std::vector<char> tail(map + body, map + fsz);
-  tail.push_back('\n');
-  const char* b = map;
-  const char* e = map + body;
-  int N = order_hint;
-  if (N <= 0) {
-    N = probe_order(b, e);
-    if (N < 0) N = probe_order(tail.data(), tail.data() + tail.size());
-  }
-  if (N < 1 || N > CPTC_MAX_ORDER) return -2;
-
-  const int nt = std::max(1, std::min(host_threads(), (int)(body >> 20) + 1));
-  std::vector<const char*> cut(nt + 1);
-  cut[0] = b;
-  cut[nt] = e;
-  for (int t = 1; t < nt; ++t) {
-    const char* c = b + (body * (size_t)t) / (size_t)nt;
-    if (c < cut[t - 1]) c = cut[t - 1];
-    const char* nl = (const char*)std::memchr(c, '\n', (size_t)(e - c));
-    cut[t] = nl ? nl + 1 : e;
-  }
-  std::vector<Part> parts(nt + 1);
-#pragma omp parallel for num_threads(nt) schedule(static, 1)
-  for (int t = 0; t < nt; ++t) parse_range(cut[t], cut[t + 1], N, parts[t]);
-  parse_range(tail.data(), tail.data() + tail.size(), N, parts[nt]);
-
-  uint64_t nnz = 0;
-  std::vector<uint64_t> off(parts.size() + 1, 0);
-  for (size_t t = 0; t < parts.size(); ++t) off[t + 1] = off[t] + parts[t].val.size();
-  nnz = off[parts.size()];
-  if (!coo_alloc(out, N, nnz)) {
-    cptc_coo_free(out);
-    return -3;
-  }
-  // Parallel copy: the output pages are first touched by many threads.
-#pragma omp parallel for num_threads(nt) schedule(dynamic, 1)
-  for (int t = 0; t < (int)parts.size(); ++t) {
-    const Part& p = parts[t];
-    if (p.val.empty()) continue;
+    ::close(fd);
+    struct Unmap {
+      const char* p;
+      size_t n;
+      ~Unmap() {
+        if (p) ::munmap((void*)p, n);
+      }
+    } unmap{map, fsz};
+    // Everything up to the last newline is parsed in place; a final line
+    // without a newline goes through a copy that ends with one.
+    size_t body = fsz;
+    while (body > 0 && map[body - 1] != '\n') --body;
+    std::vector<char> tail(map + body, map + fsz);
+    tail.push_back('\n');
+    const char* b = map;
+    const char* e = map + body;
+    int N = order_hint;
+    if (N <= 0) {
+      N = probe_order(b, e);
+      if (N < 0) N = probe_order(tail.data(), tail.data() + tail.size());
+    }
+    if (N < 1 || N > CPTC_MAX_ORDER) return -2;
+  
+    const int nt = std::max(1, std::min(host_threads(), (int)(body >> 20) + 1));
+    std::vector<const char*> cut(nt + 1);
+    cut[0] = b;
+    cut[nt] = e;
+    for (int t = 1; t < nt; ++t) {
+      const char* c = b + (body * (size_t)t) / (size_t)nt;
+      if (c < cut[t - 1]) c = cut[t - 1];
+      const char* nl = (const char*)std::memchr(c, '\n', (size_t)(e - c));
+      cut[t] = nl ? nl + 1 : e;
+    }
+    std::vector<Part> parts(nt + 1);
+  #pragma omp parallel for num_threads(nt) schedule(static, 1)
+    for (int t = 0; t < nt; ++t) parse_range(cut[t], cut[t + 1], N, parts[t]);
+    parse_range(tail.data(), tail.data() + tail.size(), N, parts[nt]);
+  
+    uint64_t nnz = 0;
+    std::vector<uint64_t> off(parts.size() + 1, 0);
+    for (size_t t = 0; t < parts.size(); ++t) off[t + 1] = off[t] + parts[t].val.size();
+    nnz = off[parts.size()];
+    if (!coo_alloc(out, N, nnz)) {
+      cptc_coo_free(out);
+      return -3;
+    }
+    // Parallel copy: the output pages are first touched by many threads.
+  #pragma omp parallel for num_threads(nt) schedule(dynamic, 1)
+    for (int t = 0; t < (int)parts.size(); ++t) {
+      const Part& p = parts[t];
+      if (p.val.empty()) continue;
+      for (int m = 0; m < N; ++m)
+        std::memcpy(out->idx[m] + off[t], p.idx[m].data(), p.val.size() * sizeof(uint32_t));
+      std::memcpy(out->vals + off[t], p.val.data(), p.val.size() * sizeof(double));
+    }
+    for (const Part& p : parts)
+      for (int m = 0; m < N; ++m)
+        if (!p.val.empty()) out->dims[m] = std::max<uint64_t>(out->dims[m], p.mx[m] + 1);
     for (int m = 0; m < N; ++m)
-      std::memcpy(out->idx[m] + off[t], p.idx[m].data(), p.val.size() * sizeof(uint32_t));
-    std::memcpy(out->vals + off[t], p.val.data(), p.val.size() * sizeof(double));
-  }
-  for (const Part& p : parts)
-    for (int m = 0; m < N; ++m)
-      if (!p.val.empty()) out->dims[m] = std::max<uint64_t>(out->dims[m], p.mx[m] + 1);
-  for (int m = 0; m < N; ++m)
-    if (out->dims[m] == 0) out->dims[m] = 1;
-  return 0;
+      if (out->dims[m] == 0) out->dims[m] = 1;
+    return 0;
+  });
 }
 
 int cptc_tns_write(const char* path, const cptc_coo* t) {
-  if (!t || t->order < 1 || t->order > CPTC_MAX_ORDER) return -2;
-  FILE* f = std::fopen(path, "wb");
-  if (!f) return -1;
-  const int N = t->order;
-  const uint64_t nnz = t->nnz;
-  const uint64_t block = 1 << 20;
-  const int nt = host_threads();
-  std::vector<std::string> out((size_t)nt);
-  for (uint64_t s = 0; s < nnz; s += block * (uint64_t)nt) {
-#pragma omp parallel for num_threads(nt) schedule(static, 1)
-    for (int th = 0; th < nt; ++th) {
-      std::string& o = out[th];
-      o.clear();
-      const uint64_t a = s + (uint64_t)th * block;
-      const uint64_t z = std::min(nnz, a + block);
-      char line[256];
-      for (uint64_t e = a; e < z; ++e) {
-        int n = 0;
-        for (int m = 0; m < N; ++m)
-          n += std::snprintf(line + n, sizeof(line) - n, "%u ", t->idx[m][e] + 1u);
-        n += std::snprintf(line + n, sizeof(line) - n, "%.17g\n", t->vals[e]);
-        o.append(line, (size_t)n);
+  return host_guard(nullptr, [&]() -> int {
+    if (!t || t->order < 1 || t->order > CPTC_MAX_ORDER) return -2;
+    FILE* f = std::fopen(path, "wb");
+    if (!f) return -1;
+    const int N = t->order;
+    const uint64_t nnz = t->nnz;
+    const uint64_t block = 1 << 20;
+    const int nt = host_threads();
+    std::vector<std::string> out((size_t)nt);
+    for (uint64_t s = 0; s < nnz; s += block * (uint64_t)nt) {
+  #pragma omp parallel for num_threads(nt) schedule(static, 1)
+      for (int th = 0; th < nt; ++th) {
+        std::string& o = out[th];
+        o.clear();
+        const uint64_t a = s + (uint64_t)th * block;
+        const uint64_t z = std::min(nnz, a + block);
+        char line[256];
+        for (uint64_t e = a; e < z; ++e) {
+          int n = 0;
+          for (int m = 0; m < N; ++m)
+            n += std::snprintf(line + n, sizeof(line) - n, "%u ", t->idx[m][e] + 1u);
+          n += std::snprintf(line + n, sizeof(line) - n, "%.17g\n", t->vals[e]);
+          o.append(line, (size_t)n);
+        }
       }
+      for (int th = 0; th < nt; ++th) std::fwrite(out[th].data(), 1, out[th].size(), f);
     }
-    for (int th = 0; th < nt; ++th) std::fwrite(out[th].data(), 1, out[th].size(), f);
-  }
-  return std::fclose(f) == 0 ? 0 : -1;
+    return std::fclose(f) == 0 ? 0 : -1;
+  });
 }
 
 }  // extern "C"
