@@ -730,6 +730,9 @@ int guarded(cptc_ctx* c, F&& f) {
   } catch (const std::exception& x) {
     c->err = x.what();
     return CPTC_E_ARG;
+  } catch (...) {
+    c->err = "unknown error";
+    return CPTC_E_ARG;
   }
 }
 

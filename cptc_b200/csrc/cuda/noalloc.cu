@@ -97,5 +97,8 @@ extern "C" int cptc_residual_noalloc(int order, uint64_t nnz, const uint32_t* co
   } catch (const CptcError& x) {
     set_host_error(x.what());
     return x.code;
+  } catch (...) {  // std::mutex or the per-device cache
+    set_host_error("cptc_residual_noalloc: host error");
+    return CPTC_E_ARG;
   }
 }
