@@ -51,6 +51,9 @@ def parse_args():
     p.add_argument("--ref-log", default="", help="reference arm: save cpTC's stdout here")
     p.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
                    help="how the ranks combine a mode update (several GPUs)")
+    p.add_argument("--e2e-sharded", action="store_true",
+                   help="e2e on several GPUs: each rank uploads 1/G of every factor and the "
+                        "pieces are all-gathered on the GPUs (cptc_set_factors_sharded)")
     p.add_argument("--phases", type=int, default=0,
                    help="after the timed steps, run this many iterations with per-phase "
                         "timing events and report their mean phase times per rank")
@@ -278,9 +281,10 @@ def run_engine(a):
     h2d = sum(f.nbytes for f in host_F)
     barrier()
     te0 = time.perf_counter()
+    sharded = a.e2e_sharded and world > 1
     for _ in range(a.steps):
         for m in range(t.order):
-            eng.set_factor(m, host_F[m])
+            eng.set_factor(m, host_F[m], sharded=sharded)
         eng.als(1)
         # the factors are replicated on every rank after the all-gather: one
         # rank reads the step's result back (reads issue no collective)
@@ -289,6 +293,8 @@ def run_engine(a):
                 eng.factor(m, out=host_F[m])
             eng.lam(out=host_lam)
     e2e_s = (time.perf_counter() - te0) / a.steps
+    if not sharded:
+        h2d *= world  # every rank uploads its replica
     d2h = sum(f.nbytes for f in host_F) + host_lam.nbytes + 16
 
     # ---- per-phase times of each mode update (diagnostic, untimed) ---------
@@ -387,7 +393,9 @@ def run_engine(a):
             "final_fit": fits[-1],
         },
         "e2e": {"value": e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+                "d2h_bytes_per_step": d2h,
+                "upload": ("each rank 1/G, all-gathered on the GPUs" if sharded else
+                           "every rank its whole replica" if world > 1 else "whole factors")},
         "gpu_launches": int(l1 - l0),
         "clocks": clocks,
         "roofline": {

@@ -99,6 +99,13 @@ void comm_reduce_scatter_ftv(Engine& E, int n) {
                               comm_of(E), E.stream));
 }
 
+void comm_allgather_rows(Engine& E, int n, double* base) {
+  if (E.nranks == 1) return;
+  const uint64_t cnt = slab_rows(E, n) * (uint64_t)E.R;
+  CPTC_NCCL(ncclAllGather(base + (uint64_t)E.rank * cnt, base, cnt, ncclDouble, comm_of(E),
+                          E.stream));
+}
+
 static void allgather_slabs(Engine& E, int n, double* base) {
   if (E.nranks == 1) return;
   const uint64_t cnt = slab_rows(E, n) * (uint64_t)E.R;

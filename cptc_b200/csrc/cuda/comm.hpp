@@ -31,6 +31,9 @@ const double* comm_reduce_gram_gather(Engine& E, int n, int nblk, int ndots);
 void comm_reduce_scatter_ftv(Engine& E, int n);
 // The full reduced FtV on every rank (reduce-scatter + all-gather).
 void comm_reduce_ftv(Engine& E, int n);
+// In place: every rank's slab r of `base` (I_n rows padded to G slabs)
+// gathered into every rank's copy.
+void comm_allgather_rows(Engine& E, int n, double* base);
 
 // Peer-memory exchange (peer.cu).  peer_map / peer_unmap are collective:
 // map after the factor buffers are allocated, unmap before any of them is

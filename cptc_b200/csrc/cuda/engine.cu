@@ -365,7 +365,7 @@ void Engine::init_factors() {
 // copy at PCIe speed (DMA when the caller's buffer is pinned).
 double* Engine::stage_rows() {
   uint64_t maxd = 0;
-  for (int m = 0; m < N; ++m) maxd = std::max<uint64_t>(maxd, dims[m]);
+  for (int m = 0; m < N; ++m) maxd = std::max<uint64_t>(maxd, padded_rows(m));
   if (stage.n < maxd * (uint64_t)R) stage.alloc(maxd * (uint64_t)R);
   return stage.p;
 }
@@ -392,6 +392,32 @@ void Engine::set_factor(int m, const double* host) {
     CPTC_CUDA(cudaMemcpyAsync(lambda.p, one.data(), R * 8, cudaMemcpyHostToDevice, stream));
   }
   // The caller may reuse `host` once this returns.
+  CPTC_CUDA(cudaStreamSynchronize(stream));
+  have_factors = true;
+  grams_valid = false;
+}
+
+// Collective: rank r copies rows [r*s, (r+1)*s) of `host` (original index
+// space, s = ceil(I_m / G)) and the pieces are all-gathered on the device.
+void Engine::set_factor_sharded(int m, const double* host) {
+  CPTC_REQUIRE(built && m >= 0 && m < N && host, CPTC_E_ARG, "bad mode or call order");
+  if (nranks == 1) {
+    set_factor(m, host);
+    return;
+  }
+  const uint64_t s = slab_rows(*this, m);
+  const uint64_t lo = std::min<uint64_t>(s * (uint64_t)rank, dims[m]);
+  const uint64_t hi = std::min<uint64_t>(s * (uint64_t)(rank + 1), dims[m]);
+  double* dst = dperm[m].p ? stage_rows() : F[m].p;
+  if (hi > lo)
+    CPTC_CUDA(cudaMemcpyAsync(dst + lo * R, host + lo * R, (hi - lo) * (uint64_t)R * sizeof(double),
+                              cudaMemcpyHostToDevice, stream));
+  comm_allgather_rows(*this, m, dst);
+  if (dperm[m].p) permute_rows(dst, m, true, F[m].p);
+  if (!have_factors) {
+    std::vector<double> one(R, 1.0);
+    CPTC_CUDA(cudaMemcpyAsync(lambda.p, one.data(), R * 8, cudaMemcpyHostToDevice, stream));
+  }
   CPTC_CUDA(cudaStreamSynchronize(stream));
   have_factors = true;
   grams_valid = false;
@@ -814,6 +840,10 @@ int cptc_init_factors(cptc_ctx* c) {
 
 int cptc_set_factors(cptc_ctx* c, int mode, const double* host) {
   return guarded(c, [&](Engine& e) { e.set_factor(mode, host); });
+}
+
+int cptc_set_factors_sharded(cptc_ctx* c, int mode, const double* host) {
+  return guarded(c, [&](Engine& e) { e.set_factor_sharded(mode, host); });
 }
 
 int cptc_get_factors(cptc_ctx* c, int mode, double* host) {

@@ -151,11 +151,14 @@ class Engine:
     def _dims(self):
         return self._tensor.dims
 
-    def set_factor(self, mode: int, F: np.ndarray) -> None:
+    def set_factor(self, mode: int, F: np.ndarray, sharded: bool = False) -> None:
+        """Factor `mode` in the tensor's own labels.  sharded=True (collective
+        on several ranks): this rank copies only its 1/G of the rows and the
+        pieces are all-gathered on the GPUs."""
         F = np.ascontiguousarray(F, dtype=np.float64)
         assert F.shape == (self._dims()[mode], self.R)
-        self._check(self._lib.cptc_set_factors(self._h, int(mode),
-                                               F.ctypes.data_as(C.POINTER(C.c_double))),
+        fn = self._lib.cptc_set_factors_sharded if sharded else self._lib.cptc_set_factors
+        self._check(fn(self._h, int(mode), F.ctypes.data_as(C.POINTER(C.c_double))),
                     "set_factors")
 
     def factor(self, mode: int, out: np.ndarray = None) -> np.ndarray:

@@ -149,6 +149,13 @@ int cptc_init_factors(cptc_ctx* ctx);
  * pinned memory makes it a single DMA).  With several ranks every rank sets
  * the same factors (each holds a replica). */
 int cptc_set_factors(cptc_ctx* ctx, int mode, const double* host);
+/* The same result with the host-to-device copy shared out (no counterpart in
+ * the reference, which runs on one GPU). Collective: rank r of G copies only
+ * rows [r*s, min((r+1)*s, I)) of `host`, s = ceil(I / G), in the original
+ * index space (the other rows of `host` are not read), and the pieces are
+ * all-gathered over NVLink into every rank's replica. One rank: the same as
+ * cptc_set_factors. */
+int cptc_set_factors_sharded(cptc_ctx* ctx, int mode, const double* host);
 int cptc_get_factors(cptc_ctx* ctx, int mode, double* host);
 int cptc_get_lambda(cptc_ctx* ctx, double* host_R);
 

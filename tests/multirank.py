@@ -201,6 +201,18 @@ def gpu_main(argv=None):
         F = e.factors()
         lam = e.lam()
         M0 = e.mttkrp(0)
+        # sharded upload: each rank's host copy holds only its own rows (NaN
+        # elsewhere); every replica must end with all of them
+        s_ok = True
+        for m in range(t.order):
+            full = F[m] * 0.5 + 0.25
+            rows = -(-full.shape[0] // world)
+            part = np.full_like(full, np.nan)
+            part[rank * rows:(rank + 1) * rows] = full[rank * rows:(rank + 1) * rows]
+            e.set_factor(m, part, sharded=True)
+            s_ok &= bool(np.array_equal(e.factor(m), full))
+        for m in range(t.order):  # back to the ALS result
+            e.set_factor(m, F[m])
         # every rank's replica must hold the same bits
         h = hashlib.sha1(b"".join(np.ascontiguousarray(f).tobytes() for f in F)).hexdigest()
         hashes = [None] * world
@@ -209,6 +221,7 @@ def gpu_main(argv=None):
         if rank == 0:
             np.savez(a.out, fits=np.array([r.fit for r in reps]), lam=lam, M0=M0,
                      tf32=int(st["tf32_path"]), replicas_equal=int(len(set(hashes)) == 1),
+                     sharded_ok=int(s_ok),
                      **{f"F{m}": f for m, f in enumerate(F)})
         e.close()
     finally:

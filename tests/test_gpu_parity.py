@@ -321,3 +321,16 @@ def test_phase_times(gpu):
         assert np.allclose(r.phases[:, 0], r.mode_ms)
         assert r.phases.sum() <= r.ms + 1e-3
     assert all(r.phases is None for r in off)
+
+
+def test_sharded_factor_upload_on_one_gpu(gpu):
+    # one rank: the sharded upload is the plain upload (relabelled or not)
+    t = cp.gen_config(1, scale=0.2)
+    for reorder in ("default", "none"):
+        e = engine_for(t, 8, path="fp64", reorder=reorder)
+        F = rand_factors(t.dims, 8, signed=True)
+        for m in range(3):
+            e.set_factor(m, F[m], sharded=True)
+        for m in range(3):
+            assert np.array_equal(e.factor(m), F[m])
+        e.close()

@@ -73,6 +73,7 @@ def test_two_gpu_slab_als_matches_one_gpu(case, tmp_path):
 
     assert int(got["tf32"]) == int(st["tf32_path"])
     assert int(got["replicas_equal"]) == 1
+    assert int(got["sharded_ok"]) == 1
     tol = 1e-6 if st["tf32_path"] else 1e-9
     assert np.max(np.abs(got["fits"] - fits)) < tol * 10
     assert rel(got["lam"], lam) < tol
