@@ -286,16 +286,15 @@ def run_engine(a):
         for m in range(t.order):
             eng.set_factor(m, host_F[m], sharded=sharded)
         eng.als(1)
-        # the factors are replicated on every rank after the all-gather: one
-        # rank reads the step's result back (reads issue no collective)
-        if rank == 0:
-            for m in range(t.order):
-                eng.factor(m, out=host_F[m])
-            eng.lam(out=host_lam)
+        # every rank reads the step's result (its replica) back, so the next
+        # step starts every rank from the same host factors
+        for m in range(t.order):
+            eng.factor(m, out=host_F[m])
+        eng.lam(out=host_lam)
     e2e_s = (time.perf_counter() - te0) / a.steps
     if not sharded:
         h2d *= world  # every rank uploads its replica
-    d2h = sum(f.nbytes for f in host_F) + host_lam.nbytes + 16
+    d2h = (sum(f.nbytes for f in host_F) + host_lam.nbytes + 16) * world
 
     # ---- per-phase times of each mode update (diagnostic, untimed) ---------
     phase_ms = None
