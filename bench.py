@@ -205,7 +205,14 @@ def cpu_baseline(t, R: int) -> dict:
     for n in range(t.order):
         o.mttkrp(t, F, n, threads=threads)
     dt = time.perf_counter() - t0
-    return {"value": dt, "unit": UNIT, "cores": threads, "kind": "port",
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            model = next((ln.split(":", 1)[1].strip() for ln in f
+                          if ln.startswith("model name")), "")
+    except OSError:
+        pass
+    return {"value": dt, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": model,
             "sample": f"one ALS iteration's {t.order} FP64 MTTKRPs on the full tensor "
                       f"(oracle/cptc_oracle.cpp, OpenMP {threads} threads)"}
 
