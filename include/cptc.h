@@ -123,9 +123,11 @@ const char* cptc_last_error(const cptc_ctx* ctx);
 
 /* Multi-GPU (one process per GPU): rank 0 calls cptc_comm_unique_id and
  * shares the 128 bytes; every rank then calls cptc_comm_init before
- * cptc_build.  cptc_comm_init, cptc_als and cptc_mttkrp are collective:
- * every rank calls them, in the same order; the other functions are local
- * (for example one rank alone may read the replicated factors).  Each rank
+ * cptc_build.  cptc_comm_init, cptc_als, cptc_mttkrp and
+ * cptc_set_factors_sharded are collective (with CPTC_EXCHANGE_PEER also
+ * cptc_build and cptc_destroy): every rank calls them, in the same order; the
+ * other functions are local (for example one rank alone may read the
+ * replicated factors).  Each rank
  * computes an equal share of every mode's nonzeros; the partial MTTKRP is
  * reduce-scattered into equal row slabs, each rank solves its slab, and one
  * grouped call all-reduces the R x R Gram and all-gathers the slabs into
