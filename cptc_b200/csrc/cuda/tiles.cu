@@ -24,6 +24,7 @@
 //    consecutive tiles of the same 16 output rows in shared memory and
 //    issues the FP64 atomics once per row block instead of once per tile.
 #include <cfloat>
+#include <cstdlib>
 
 #include <cub/cub.cuh>
 
@@ -563,13 +564,26 @@ size_t tile_smem(int R) {
          (size_t)kStage * 8 + (size_t)(kStage / 2 + 2) * 4;
 }
 
-// Weight of a tile in the CTA balance: its nonzeros plus a fixed cost of
-// 512 for zeroing the tile and the 16 slab products.
+// Weight of a tile in the CTA (and rank) balance: its nonzeros plus a fixed
+// cost for zeroing the tile and the 16 slab products, in nonzero units.
 __global__ void k_tile_weights(const int4* __restrict__ tile, const uint32_t* __restrict__ order,
-                               uint64_t n, unsigned long long* __restrict__ w) {
+                               uint64_t n, unsigned long long fixed,
+                               unsigned long long* __restrict__ w) {
   for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < n;
        k += (uint64_t)gridDim.x * blockDim.x)
-    w[k] = (unsigned long long)tile[order[k]].w + 512ull;
+    w[k] = (unsigned long long)tile[order[k]].w + fixed;
+}
+
+// 512 by default.  The per-tile and per-nonzero costs fitted on configs 2-4
+// (a + b*nnz: R=16 4.1 + 0.0053, R=32 6 + 0.005, R=128 20 + 0.012 ns) put
+// a/b at 770-1670; CPTC_TILE_FIXED_COST overrides the constant for that
+// comparison.
+unsigned long long tile_fixed_cost() {
+  if (const char* e = std::getenv("CPTC_TILE_FIXED_COST")) {
+    const long long v = std::atoll(e);
+    if (v >= 0) return (unsigned long long)v;
+  }
+  return 512ull;
 }
 
 // cut[c] = first k whose inclusive prefix exceeds c * total / blocks.
@@ -635,7 +649,7 @@ void tile_cuts(Engine& E, int slot) {
   }
   DArray<unsigned long long> w(n), pre(n);
   k_tile_weights<<<grid_for(n, 256, 148 * 16), 256, 0, E.stream>>>(U.unit.p, U.order[slot].p, n,
-                                                                   w.p);
+                                                                   tile_fixed_cost(), w.p);
   CPTC_LAUNCH_CHECK();
   size_t tb = 0;
   CPTC_CUDA(cub::DeviceScan::InclusiveSum(nullptr, tb, w.p, pre.p, (int64_t)n, E.stream));
