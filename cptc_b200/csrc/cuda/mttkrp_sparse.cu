@@ -668,6 +668,16 @@ int rec3_r32_variant() {
   return v;
 }
 
+// At R=128, CPTC_REC3_R128=u2 keeps two nonzeros' rows in flight per warp
+// (at most 128 registers, 2 CTAs per SM) instead of one.
+int rec3_r128_variant() {
+  static const int v = [] {
+    const char* e = std::getenv("CPTC_REC3_R128");
+    return (e && std::strcmp(e, "u2") == 0) ? 1 : 0;
+  }();
+  return v;
+}
+
 }  // namespace
 
 void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
@@ -695,7 +705,10 @@ void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
         else launch_rec3s<16, 2, 2, 4>(a, s);
         return;
       case 64: launch_rec3s<16, 4, 2, 1, true>(a, s); return;
-      case 128: launch_rec3s<32, 4, 1, 1, true>(a, s); return;
+      case 128:
+        if (rec3_r128_variant() == 1) launch_rec3s<32, 4, 2, 2, true>(a, s);
+        else launch_rec3s<32, 4, 1, 1, true>(a, s);
+        return;
       default: break;
     }
     if (a.R <= 32) launch_rec3<32, 1, false, 4>(a, s);
