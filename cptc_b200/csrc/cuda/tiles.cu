@@ -25,6 +25,7 @@
 //    issues the FP64 atomics once per row block instead of once per tile.
 #include <cfloat>
 #include <cstdlib>
+#include <cstring>
 
 #include <cub/cub.cuh>
 
@@ -607,6 +608,22 @@ __global__ void k_tile_cuts(const unsigned long long* __restrict__ pre, uint64_t
 
 }  // namespace
 
+namespace {
+
+// CPTC_TILES_SHAPE=nw2 (for measurement): at most 2 n-tiles per warp and 5
+// resident CTAs per SM (96 registers, no spills) instead of 4 n-tiles and 4
+// CTAs (128 registers): more warps to hide latency, each slab's A fragments
+// read by two warps instead of one at R=32.
+bool tiles_nw2() {
+  static const bool v = [] {
+    const char* e = std::getenv("CPTC_TILES_SHAPE");
+    return e && std::strcmp(e, "nw2") == 0;
+  }();
+  return v;
+}
+
+}  // namespace
+
 uint32_t tile_blocks_for(int R, int device, uint64_t ntiles) {
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
@@ -620,10 +637,11 @@ uint32_t tile_blocks_for(int R, int device, uint64_t ntiles) {
   const size_t smem = tile_smem(R);
   const int NT = R / 8;
   const int ntm = NT < 4 ? NT : 4;
-  auto kern = ntm == 1 ? k_tiles<0, 1, 2, 1, 4>
-              : ntm == 2 ? k_tiles<0, 1, 2, 2, 4>
-              : ntm == 3 ? k_tiles<0, 1, 2, 3, 4>
-                         : k_tiles<0, 1, 2, 4, 4>;
+  auto kern = tiles_nw2() ? (ntm == 1 ? k_tiles<0, 1, 2, 1, 5> : k_tiles<0, 1, 2, 2, 5>)
+              : ntm == 1  ? k_tiles<0, 1, 2, 1, 4>
+              : ntm == 2  ? k_tiles<0, 1, 2, 2, 4>
+              : ntm == 3  ? k_tiles<0, 1, 2, 3, 4>
+                          : k_tiles<0, 1, 2, 4, 4>;
   CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
   int per_sm = 0;
@@ -675,21 +693,24 @@ void launch_mttkrp_tiles3(const TileArgs& a_in, const uint32_t* order, const uin
   const int roles = a.tslot * 100 + a.cslot * 10 + a.sslot;
   // 4 resident CTAs per SM (<= 128 registers): measured against 5 (96
   // registers, spills at 4 n-tiles per warp) on config 4, 4 is faster.
-#define CPTC_TILES(TS_, CS_, SS_, NTM)                                                     \
+#define CPTC_TILES(TS_, CS_, SS_, NTM, MINB_)                                              \
   do {                                                                                     \
-    auto kern = k_tiles<TS_, CS_, SS_, NTM, 4>;                                            \
+    auto kern = k_tiles<TS_, CS_, SS_, NTM, MINB_>;                                        \
     CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                                    (int)smem));                                            \
     CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,   \
                                    100));                                                  \
     kern<<<blocks, 128, smem, s>>>(a, order, cut);                                         \
   } while (0)
-#define CPTC_TILES_R(TS_, CS_, SS_)          \
-  do {                                       \
-    if (ntm == 1) CPTC_TILES(TS_, CS_, SS_, 1); \
-    else if (ntm == 2) CPTC_TILES(TS_, CS_, SS_, 2); \
-    else if (ntm == 3) CPTC_TILES(TS_, CS_, SS_, 3); \
-    else CPTC_TILES(TS_, CS_, SS_, 4);       \
+#define CPTC_TILES_R(TS_, CS_, SS_)                          \
+  do {                                                       \
+    if (tiles_nw2()) {                                       \
+      if (ntm == 1) CPTC_TILES(TS_, CS_, SS_, 1, 5);         \
+      else CPTC_TILES(TS_, CS_, SS_, 2, 5);                  \
+    } else if (ntm == 1) CPTC_TILES(TS_, CS_, SS_, 1, 4);    \
+    else if (ntm == 2) CPTC_TILES(TS_, CS_, SS_, 2, 4);      \
+    else if (ntm == 3) CPTC_TILES(TS_, CS_, SS_, 3, 4);      \
+    else CPTC_TILES(TS_, CS_, SS_, 4, 4);                    \
   } while (0)
   switch (roles) {
     case 12: CPTC_TILES_R(0, 1, 2); break;   // order-3 mode 0; N-order slot 0
