@@ -316,8 +316,11 @@ def run_engine(a):
     prof = [eng.profile_mttkrp(n, reps=3) for n in range(t.order)]
     rank_mode_ms = None
     rank_phase_ms = None
+    rank_kernel_ms = None
+    kern_ms = np.array([[p["sparse_ms"], p["tiles_ms"]] for p in prof])  # (modes, 2)
     if phase_ms is not None:
         rank_phase_ms = [np.round(phase_ms, 4).tolist()]
+        rank_kernel_ms = [np.round(kern_ms, 4).tolist()]
 
     if dist is not None:
         import torch
@@ -335,6 +338,11 @@ def run_engine(a):
             pg = [torch.zeros_like(pm) for _ in range(world)]
             dist.all_gather(pg, pm)
             rank_phase_ms = [np.round(g.numpy(), 4).tolist() for g in pg]
+            # this rank's share of the residual and tile kernels, per mode
+            km = torch.tensor(kern_ms, dtype=torch.float64)
+            kg = [torch.zeros_like(km) for _ in range(world)]
+            dist.all_gather(kg, km)
+            rank_kernel_ms = [np.round(g.numpy(), 4).tolist() for g in kg]
 
     if rank != 0:
         eng.close()
@@ -396,6 +404,7 @@ def run_engine(a):
             "mttkrp_ms_per_mode_by_rank": rank_mode_ms if world > 1 else None,
             "phase_ms_by_rank": rank_phase_ms,
             "phase_names": list(cp.Engine.PHASES) if rank_phase_ms is not None else None,
+            "residual_tile_ms_by_rank": rank_kernel_ms,
             "final_fit": fits[-1],
         },
         "e2e": {"value": e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
