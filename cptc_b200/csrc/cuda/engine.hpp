@@ -94,6 +94,9 @@ struct PeerState {
   unsigned char* arena_of[kMaxPeers] = {};
   std::vector<void*> opened;           // imported mappings, closed at teardown
   unsigned long long timeout_ns = 0;
+  // Rows [lo, hi) of each mode that rank q's share of the MTTKRP can write.
+  uint64_t rows_lo[CPTC_MAX_ORDER][kMaxPeers] = {};
+  uint64_t rows_hi[CPTC_MAX_ORDER][kMaxPeers] = {};
 };
 
 struct Engine {

@@ -122,40 +122,62 @@ struct PushArgs {
   const double* src;          // own partial MTTKRP (all padded rows)
   double* recv[kMaxPeers];    // every rank's receive buffer
   uint64_t per;               // elements of one slab (slab rows x R)
+  uint64_t lo, hi;            // elements this rank's share can write: [lo, hi)
   int rank;
 };
 
-// blockIdx.y = owner o; owner o's slab of src goes to region `rank` of o's
-// receive buffer.  The owner's own slab is not copied (it is summed in place).
+// blockIdx.y = owner o; the part of owner o's slab that this rank's share can
+// have written (its touched rows) goes to region `rank` of o's receive
+// buffer, at the same offsets.  The owner's own slab is summed in place.
 template <bool VEC>
 __global__ void __launch_bounds__(256) k_peer_push(PushArgs a) {
   const int o = blockIdx.y;
   if (o == a.rank) return;
-  const double* s = a.src + (uint64_t)o * a.per;
-  double* d = pick(a.recv, o) + (uint64_t)a.rank * a.per;
-  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  if (VEC) {
-    const uint64_t n2 = a.per >> 1;
-    const double2* s2 = reinterpret_cast<const double2*>(s);
-    double2* d2 = reinterpret_cast<double2*>(d);
-    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n2; i += stride)
-      d2[i] = s2[i];
-  } else {
-    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < a.per; i += stride)
-      d[i] = s[i];
+  const uint64_t s0 = (uint64_t)o * a.per;
+  const uint64_t b = a.lo > s0 ? a.lo : s0;
+  const uint64_t e = a.hi < s0 + a.per ? a.hi : s0 + a.per;
+  if (b < e) {
+    const double* s = a.src + b;
+    double* d = pick(a.recv, o) + (uint64_t)a.rank * a.per + (b - s0);
+    const uint64_t n = e - b;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    if (VEC) {  // b and n even: 16-byte aligned on both sides
+      const double2* s2 = reinterpret_cast<const double2*>(s);
+      double2* d2 = reinterpret_cast<double2*>(d);
+      for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n / 2; i += stride)
+        d2[i] = s2[i];
+    } else {
+      for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+        d[i] = s[i];
+    }
   }
   __threadfence_system();  // the stores reach the peer before the barrier's signal
 }
 
-// own[i] = sum over r = 0..G-1 (rank order) of rank r's partial of this slab.
-__global__ void __launch_bounds__(256) k_peer_slab_sum(double* __restrict__ own,
-                                                       const double* __restrict__ recv,
-                                                       uint64_t per, int rank, int G) {
+struct SlabSumArgs {
+  double* own;                 // own slab of FtV
+  const double* recv;          // own receive buffer
+  uint64_t per;
+  uint64_t lo[kMaxPeers];      // rank r's region holds data in [lo[r], hi[r]) (slab offsets)
+  uint64_t hi[kMaxPeers];
+  int rank, G;
+};
+
+// own[i] = sum over r = 0..G-1 (rank order) of rank r's partial of this slab;
+// outside rank r's touched rows its partial is zero and is not read.
+__global__ void __launch_bounds__(256) k_peer_slab_sum(SlabSumArgs a) {
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < per; i += stride) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < a.per; i += stride) {
     double s = 0.0;
-    for (int r = 0; r < G; ++r) s += (r == rank) ? own[i] : recv[(uint64_t)r * per + i];
-    own[i] = s;
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r) {
+      if (r < a.G) {
+        if (r == a.rank) s += a.own[i];
+        else if (i >= a.lo[r] && i < a.hi[r]) s += a.recv[(uint64_t)r * a.per + i];
+        else s += 0.0;  // the zero a full-slab copy would have added
+      }
+    }
+    a.own[i] = s;
   }
 }
 
@@ -239,6 +261,47 @@ unsigned copy_grid(uint64_t n) {
 
 }  // namespace
 
+// Rows [lo, hi) of mode n that this rank's share of the MTTKRP can write:
+// the rows of its residual tasks and the target blocks of its dense tiles
+// (both visited in row order), as one hull.
+static void touched_rows(Engine& E, int n, uint64_t& lo, uint64_t& hi) {
+  lo = UINT64_MAX;
+  hi = 0;
+  auto get32 = [&](const uint32_t* p, uint64_t i) {
+    uint32_t v = 0;
+    CPTC_CUDA(cudaMemcpy(&v, p + i, sizeof(v), cudaMemcpyDeviceToHost));
+    return v;
+  };
+  const View& v = E.views[n];
+  if (v.nnz > 0 && v.t1 > v.t0) {
+    const uint32_t first = get32(v.rows.p, get32(v.task_row.p, v.t0));
+    // the row holding task t1's first element bounds task t1 - 1's last row
+    const uint32_t last = v.t1 < v.ntasks ? get32(v.rows.p, get32(v.task_row.p, v.t1))
+                                          : get32(v.rows.p, v.nrows - 1);
+    lo = first;
+    hi = (uint64_t)last + 1;
+  }
+  if (E.dense_active) {
+    const UnitPool& U = E.units;
+    for (int ts = 0; ts < 3; ++ts) {
+      if (U.inner[ts] != n || U.cnt[ts] == 0) continue;
+      const uint32_t k0 = get32(U.cut[ts].p, (uint64_t)E.rank * U.blocks);
+      const uint32_t k1 = get32(U.cut[ts].p, (uint64_t)(E.rank + 1) * U.blocks);
+      if (k1 <= k0) continue;
+      int4 u0, u1;
+      CPTC_CUDA(cudaMemcpy(&u0, U.unit.p + get32(U.order[ts].p, k0), sizeof(int4),
+                           cudaMemcpyDeviceToHost));
+      CPTC_CUDA(cudaMemcpy(&u1, U.unit.p + get32(U.order[ts].p, k1 - 1), sizeof(int4),
+                           cudaMemcpyDeviceToHost));
+      const int b0 = ts == 0 ? u0.x : ts == 1 ? u0.y : u0.z;
+      const int b1 = ts == 0 ? u1.x : ts == 1 ? u1.y : u1.z;
+      lo = std::min<uint64_t>(lo, (uint64_t)b0 * 16);
+      hi = std::max<uint64_t>(hi, std::min<uint64_t>((uint64_t)b1 * 16 + 16, E.dims[n]));
+    }
+  }
+  if (lo >= hi) lo = hi = 0;
+}
+
 void peer_map(Engine& E) {
   PeerState& P = E.peer;
   CPTC_REQUIRE(!P.on, CPTC_E_ARG, "peer buffers are already mapped");
@@ -276,6 +339,25 @@ void peer_map(Engine& E) {
   CPTC_CUDA(cudaMemcpyAsync(all.data(), dex.p, (uint64_t)G * sizeof(Ex), cudaMemcpyDeviceToHost,
                             E.stream));
   CPTC_CUDA(cudaStreamSynchronize(E.stream));
+
+  // Every rank's touched rows per mode, so owners read only what was pushed.
+  CPTC_CUDA(cudaStreamSynchronize(E.stream));
+  std::vector<uint64_t> hl(2 * CPTC_MAX_ORDER, 0);
+  for (int m = 0; m < E.N; ++m) touched_rows(E, m, hl[2 * m], hl[2 * m + 1]);
+  DArray<uint64_t> dh((uint64_t)G * 2 * CPTC_MAX_ORDER);
+  CPTC_CUDA(cudaMemcpyAsync(dh.p + (uint64_t)E.rank * 2 * CPTC_MAX_ORDER, hl.data(),
+                            hl.size() * sizeof(uint64_t), cudaMemcpyHostToDevice, E.stream));
+  CPTC_NCCL_P(ncclAllGather(dh.p + (uint64_t)E.rank * 2 * CPTC_MAX_ORDER, dh.p,
+                            2 * CPTC_MAX_ORDER, ncclUint64, comm_of(E), E.stream));
+  std::vector<uint64_t> allh((uint64_t)G * 2 * CPTC_MAX_ORDER);
+  CPTC_CUDA(cudaMemcpyAsync(allh.data(), dh.p, allh.size() * sizeof(uint64_t),
+                            cudaMemcpyDeviceToHost, E.stream));
+  CPTC_CUDA(cudaStreamSynchronize(E.stream));
+  for (int q = 0; q < G; ++q)
+    for (int m = 0; m < E.N; ++m) {
+      P.rows_lo[m][q] = allh[(uint64_t)q * 2 * CPTC_MAX_ORDER + 2 * m];
+      P.rows_hi[m][q] = allh[(uint64_t)q * 2 * CPTC_MAX_ORDER + 2 * m + 1];
+    }
 
   auto open = [&](const cudaIpcMemHandle_t& h) {
     void* p = nullptr;
@@ -328,20 +410,36 @@ void peer_unmap(Engine& E) {
 
 void peer_reduce_scatter_ftv(Engine& E, int n) {
   PeerState& P = E.peer;
-  const uint64_t per = slab_rows(E, n) * (uint64_t)E.R;
+  const uint64_t R = (uint64_t)E.R;
+  const uint64_t per = slab_rows(E, n) * R;
   PushArgs a{};
   a.src = E.FtV.p;
   for (int q = 0; q < P.G; ++q) a.recv[q] = P.recv_of[q];
   a.per = per;
+  a.lo = P.rows_lo[n][E.rank] * R;
+  a.hi = P.rows_hi[n][E.rank] * R;
   a.rank = E.rank;
-  const bool vec = (per % 2) == 0;  // every slab then starts on 16 bytes
-  const dim3 grid(copy_grid(vec ? per / 2 : per), (unsigned)P.G);
+  // even R: every slab, every row and so every copied range start on 16 bytes
+  const bool vec = (R % 2) == 0;
+  const uint64_t span = a.hi > a.lo ? a.hi - a.lo : 1;
+  const dim3 grid(copy_grid(vec ? span / 2 : span), (unsigned)P.G);
   if (vec) k_peer_push<true><<<grid, 256, 0, E.stream>>>(a);
   else k_peer_push<false><<<grid, 256, 0, E.stream>>>(a);
   CPTC_LAUNCH_CHECK();
   launch_barrier(E);
-  k_peer_slab_sum<<<copy_grid(per), 256, 0, E.stream>>>(E.FtV.p + (uint64_t)E.rank * per,
-                                                        P.recv.p, per, E.rank, P.G);
+  SlabSumArgs b{};
+  b.own = E.FtV.p + (uint64_t)E.rank * per;
+  b.recv = P.recv.p;
+  b.per = per;
+  const uint64_t s0 = (uint64_t)E.rank * per;
+  for (int q = 0; q < P.G; ++q) {  // rank q's touched elements inside this slab
+    const uint64_t lo = P.rows_lo[n][q] * R, hi = P.rows_hi[n][q] * R;
+    b.lo[q] = lo > s0 ? std::min(lo - s0, per) : 0;
+    b.hi[q] = hi > s0 ? std::min(hi - s0, per) : 0;
+  }
+  b.rank = E.rank;
+  b.G = P.G;
+  k_peer_slab_sum<<<copy_grid(per), 256, 0, E.stream>>>(b);
   CPTC_LAUNCH_CHECK();
 }
 

@@ -82,13 +82,27 @@ def shard_als3(t, R, iters, rank, world, dist, exchange="nccl"):
             acc = acc + p
         return acc
 
-    def reduce_scatter_rows(M, s):
+    def reduce_scatter_rows(M, s, n):
         # padded to world * s rows; gloo has no reduce_scatter: all-reduce, keep own slab
         P = np.zeros((world * s, R))
         P[:M.shape[0]] = M
         if exchange == "peer":
-            # region r of the owner's receive buffer holds rank r's rows of its slab
-            return rank_order_sum([g[rank * s:(rank + 1) * s] for g in gather(P)])
+            # region r of the owner's receive buffer holds rank r's rows of its
+            # slab, pushed only inside rank r's touched rows [lo_r, hi_r)
+            rows = idx[n][chunk[n]]
+            hull = np.array([rows.min(), rows.max() + 1] if rows.size else [0, 0])
+            hulls = gather(hull.astype(np.float64))
+            parts = []
+            for r, g in enumerate(gather(P)):
+                reg = np.zeros((s, R))
+                lo, hi = int(hulls[r][0]), int(hulls[r][1])
+                a, b = max(lo, rank * s), min(hi, (rank + 1) * s)
+                if r == rank:
+                    reg = g[rank * s:(rank + 1) * s]
+                elif a < b:
+                    reg[a - rank * s:b - rank * s] = g[a:b]
+                parts.append(reg)
+            return rank_order_sum(parts)
         return allreduce(P)[rank * s:(rank + 1) * s]
 
     def reduce_slots(x):
@@ -109,7 +123,7 @@ def shard_als3(t, R, iters, rank, world, dist, exchange="nccl"):
             M = np_mttkrp([i[mine] for i in idx], t.vals[mine], t.dims, F, n)
             s = srows[n]
             lo, hi = min(rank * s, t.dims[n]), min((rank + 1) * s, t.dims[n])
-            Ms = reduce_scatter_rows(M, s)          # own slab, padded to s rows
+            Ms = reduce_scatter_rows(M, s, n)       # own slab, padded to s rows
             A = truncated_pinv(FtF, R)
             Fl = np.zeros((s, R))
             Fl[:hi - lo] = Ms[:hi - lo] @ A.T / lam
