@@ -312,11 +312,42 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
     View& v = views[n];
     v.t0 = v.ntasks * (uint64_t)rank / (uint64_t)nranks;
     v.t1 = v.ntasks * (uint64_t)(rank + 1) / (uint64_t)nranks;
+    if (nranks > 1) split_tasks_by_cost(v);
   }
   CPTC_CUDA(cudaStreamSynchronize(stream));
   if (nranks > 1 && opts.exchange == CPTC_EXCHANGE_PEER) peer_map(*this);
   build_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   built = true;
+}
+
+// With CPTC_TASK_ROW_COST = c > 0 (for measurement; default 0 keeps equal
+// task counts) the ranks' task ranges are cut at equal cost, a task costing
+// its nonzeros plus c per target row it touches (each row end is a flush of
+// R sums).  Every rank computes the same cut points from the same view.
+void Engine::split_tasks_by_cost(View& v) {
+  static const double row_cost = [] {
+    const char* e = std::getenv("CPTC_TASK_ROW_COST");
+    return e ? std::atof(e) : 0.0;
+  }();
+  if (!(row_cost > 0.0) || v.ntasks < (uint64_t)nranks) return;
+  std::vector<uint32_t> tr(v.ntasks);
+  CPTC_CUDA(cudaMemcpyAsync(tr.data(), v.task_row.p, v.ntasks * sizeof(uint32_t),
+                            cudaMemcpyDeviceToHost, stream));
+  CPTC_CUDA(cudaStreamSynchronize(stream));
+  std::vector<double> pre(v.ntasks + 1, 0.0);
+  for (uint64_t t = 0; t < v.ntasks; ++t) {
+    const uint64_t first = t * (uint64_t)v.task;
+    const uint64_t n_t = std::min<uint64_t>(v.task, v.nnz - first);
+    const uint64_t next = (t + 1 < v.ntasks) ? tr[t + 1] : v.nrows - 1;
+    const double rows_t = (double)(next - tr[t] + 1);
+    pre[t + 1] = pre[t] + (double)n_t + row_cost * rows_t;
+  }
+  auto cut = [&](int r) -> uint64_t {  // first task whose prefix reaches r/G of the cost
+    const double target = pre[v.ntasks] * (double)r / (double)nranks;
+    return (uint64_t)(std::lower_bound(pre.begin(), pre.end(), target) - pre.begin());
+  };
+  v.t0 = rank == 0 ? 0 : std::min<uint64_t>(cut(rank), v.ntasks);
+  v.t1 = rank == nranks - 1 ? v.ntasks : std::min<uint64_t>(cut(rank + 1), v.ntasks);
 }
 
 double* Engine::scal_tmp() {

@@ -206,6 +206,7 @@ struct Engine {
   void reorder();
   void alloc_workspace();
   void update_mode(int n, bool last);
+  void split_tasks_by_cost(View& v);
   void gram_of(int m);
 };
 
