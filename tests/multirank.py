@@ -252,6 +252,11 @@ GPU_CASES = {
 for _k in list(GPU_CASES):
     GPU_CASES[_k + "_peer"] = dict(GPU_CASES[_k], build=dict(GPU_CASES[_k]["build"],
                                                              exchange="peer"))
+# other rank cut points (the split changes only which rank sums which part)
+GPU_CASES["fp64_o3_rowcost"] = dict(GPU_CASES["fp64_o3"], env={"CPTC_TASK_ROW_COST": "4"})
+GPU_CASES["hybrid_o3_tilecost_peer"] = dict(GPU_CASES["hybrid_o3_peer"],
+                                            env={"CPTC_TILE_FIXED_COST": "1200",
+                                                 "CPTC_TASK_ROW_COST": "4"})
 # R=17: odd slabs take the scalar copy kernels
 GPU_CASES["fp64_o3_r17_peer"] = dict(gen=("uniform", (301, 250, 199), 60_000, 4, "normal"), R=17,
                                      iters=3, build=dict(path="fp64", exchange="peer"))

@@ -42,14 +42,16 @@ def rel(a, b):
 
 
 @pytest.mark.parametrize("case", ["fp64_o3", "hybrid_o3", "generic_o4", "fp64_o3_peer",
-                                  "hybrid_o3_peer", "generic_o4_peer", "fp64_o3_r17_peer"])
+                                  "hybrid_o3_peer", "generic_o4_peer", "fp64_o3_r17_peer",
+                                  "fp64_o3_rowcost", "hybrid_o3_tilecost_peer"])
 def test_two_gpu_slab_als_matches_one_gpu(case, tmp_path):
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs")
     from multirank import GPU_CASES, make_case
 
     out = tmp_path / f"{case}.npz"
-    env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(HERE.parent), str(HERE)]))
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(HERE.parent), str(HERE)]),
+               **GPU_CASES[case].get("env", {}))
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
            f"--master-port={_free_port()}", str(HERE / "multirank.py"), "--out", str(out),
