@@ -293,15 +293,17 @@ def run_engine(a):
         for m in range(t.order):
             eng.set_factor(m, host_F[m], sharded=sharded)
         eng.als(1)
-        # every rank reads the step's result (its replica) back, so the next
-        # step starts every rank from the same host factors
+        # every rank reads the step's result back (its replica; sharded: its
+        # 1/G of the rows, the ones it uploads next), so every rank starts
+        # the next step from the same factors
         for m in range(t.order):
-            eng.factor(m, out=host_F[m])
+            eng.factor(m, out=host_F[m], sharded=sharded)
         eng.lam(out=host_lam)
     e2e_s = (time.perf_counter() - te0) / a.steps
+    fbytes = sum(f.nbytes for f in host_F)
     if not sharded:
         h2d *= world  # every rank uploads its replica
-    d2h = (sum(f.nbytes for f in host_F) + host_lam.nbytes + 16) * world
+    d2h = (fbytes if sharded else fbytes * world) + (host_lam.nbytes + 16) * world
 
     # ---- per-phase times of each mode update (diagnostic, untimed) ---------
     phase_ms = None

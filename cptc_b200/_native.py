@@ -104,6 +104,7 @@ ENGINE_SYMBOLS = {
     "cptc_init_factors": (C.c_int, [C.c_void_p]),
     "cptc_set_factors": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double)]),
     "cptc_set_factors_sharded": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double)]),
+    "cptc_get_factors_sharded": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double)]),
     "cptc_get_factors": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double)]),
     "cptc_get_lambda": (C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
     "cptc_mttkrp": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double)]),

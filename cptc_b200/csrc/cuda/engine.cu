@@ -460,6 +460,30 @@ void Engine::get_factor(int m, double* host) {
   fetch_rows(F[m].p, m, host);
 }
 
+// Local: rows [r*s, (r+1)*s) of the factor (original index space) into the
+// same rows of `host`; the other rows of `host` are not written.
+void Engine::get_factor_sharded(int m, double* host) {
+  CPTC_REQUIRE(built && have_factors && m >= 0 && m < N && host, CPTC_E_ARG,
+               "bad mode or call order");
+  if (nranks == 1) {
+    fetch_rows(F[m].p, m, host);
+    return;
+  }
+  const uint64_t s = slab_rows(*this, m);
+  const uint64_t lo = std::min<uint64_t>(s * (uint64_t)rank, dims[m]);
+  const uint64_t hi = std::min<uint64_t>(s * (uint64_t)(rank + 1), dims[m]);
+  const double* src = F[m].p;
+  if (dperm[m].p) {
+    double* st = stage_rows();
+    permute_rows(F[m].p, m, false, st);
+    src = st;
+  }
+  if (hi > lo)
+    CPTC_CUDA(cudaMemcpyAsync(host + lo * R, src + lo * R, (hi - lo) * (uint64_t)R * sizeof(double),
+                              cudaMemcpyDeviceToHost, stream));
+  CPTC_CUDA(cudaStreamSynchronize(stream));
+}
+
 void Engine::fetch_rows(const double* dev, int m, double* host) {
   const uint64_t bytes = dims[m] * (uint64_t)R * sizeof(double);
   const double* src = dev;
@@ -875,6 +899,10 @@ int cptc_set_factors(cptc_ctx* c, int mode, const double* host) {
 
 int cptc_set_factors_sharded(cptc_ctx* c, int mode, const double* host) {
   return guarded(c, [&](Engine& e) { e.set_factor_sharded(mode, host); });
+}
+
+int cptc_get_factors_sharded(cptc_ctx* c, int mode, double* host) {
+  return guarded(c, [&](Engine& e) { e.get_factor_sharded(mode, host); });
 }
 
 int cptc_get_factors(cptc_ctx* c, int mode, double* host) {

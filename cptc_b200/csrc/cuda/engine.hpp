@@ -182,6 +182,7 @@ struct Engine {
   void init_factors();
   void set_factor(int m, const double* host);
   void set_factor_sharded(int m, const double* host);
+  void get_factor_sharded(int m, double* host);
   void get_factor(int m, double* host);
   void fetch_rows(const double* dev, int m, double* host);
   double* stage_rows();

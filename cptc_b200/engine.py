@@ -161,16 +161,18 @@ class Engine:
         self._check(fn(self._h, int(mode), F.ctypes.data_as(C.POINTER(C.c_double))),
                     "set_factors")
 
-    def factor(self, mode: int, out: np.ndarray = None) -> np.ndarray:
+    def factor(self, mode: int, out: np.ndarray = None, sharded: bool = False) -> np.ndarray:
         """Factor `mode` in the tensor's own labels.  `out`, when given, is a
-        C-contiguous float64 (I_mode, R) array to fill (e.g. pinned memory)."""
+        C-contiguous float64 (I_mode, R) array to fill (e.g. pinned memory).
+        sharded=True fills only this rank's 1/G of the rows (the others are
+        left as they are)."""
         shape = (self._dims()[mode], self.R)
         if out is None:
-            out = np.empty(shape, dtype=np.float64)
+            out = np.zeros(shape, dtype=np.float64) if sharded else np.empty(shape, np.float64)
         elif out.shape != shape or out.dtype != np.float64 or not out.flags.c_contiguous:
             raise ValueError(f"out must be a C-contiguous float64 array of shape {shape}")
-        self._check(self._lib.cptc_get_factors(self._h, int(mode),
-                                               out.ctypes.data_as(C.POINTER(C.c_double))),
+        fn = self._lib.cptc_get_factors_sharded if sharded else self._lib.cptc_get_factors
+        self._check(fn(self._h, int(mode), out.ctypes.data_as(C.POINTER(C.c_double))),
                     "get_factors")
         return out
 

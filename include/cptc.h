@@ -158,6 +158,10 @@ int cptc_set_factors(cptc_ctx* ctx, int mode, const double* host);
  * all-gathered over NVLink into every rank's replica. One rank: the same as
  * cptc_set_factors. */
 int cptc_set_factors_sharded(cptc_ctx* ctx, int mode, const double* host);
+/* Local counterpart for reading: rank r copies only rows [r*s, (r+1)*s) of
+ * the factor (original index space) into the same rows of `host`; the other
+ * rows are not written. One rank: the same as cptc_get_factors. */
+int cptc_get_factors_sharded(cptc_ctx* ctx, int mode, double* host);
 int cptc_get_factors(cptc_ctx* ctx, int mode, double* host);
 int cptc_get_lambda(cptc_ctx* ctx, double* host_R);
 

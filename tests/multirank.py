@@ -225,6 +225,9 @@ def gpu_main(argv=None):
             part[rank * rows:(rank + 1) * rows] = full[rank * rows:(rank + 1) * rows]
             e.set_factor(m, part, sharded=True)
             s_ok &= bool(np.array_equal(e.factor(m), full))
+            back = np.full_like(full, np.nan)
+            e.factor(m, out=back, sharded=True)  # only this rank's rows written
+            s_ok &= bool(np.array_equal(back, part, equal_nan=True))
         for m in range(t.order):  # back to the ALS result
             e.set_factor(m, F[m])
         # every rank's replica must hold the same bits

@@ -333,4 +333,5 @@ def test_sharded_factor_upload_on_one_gpu(gpu):
             e.set_factor(m, F[m], sharded=True)
         for m in range(3):
             assert np.array_equal(e.factor(m), F[m])
+            assert np.array_equal(e.factor(m, sharded=True), F[m])
         e.close()
