@@ -11,15 +11,22 @@
 //   GEN_DENSE, GEN_DENSE_THRESHOLD, GEN_DENSE_INNER, GEN_REORDER,
 //   GEN_REORDER_T, GEN_REORDER_SAMPLE, GEN_SOLVER, GEN_SEED, GEN_DUMP,
 //   GEN_PROFILE, CPTC_DEVICE, CPTC_TNS_CACHE (binary copy of the parsed
-//   tensor beside the .tns, used while the text is unchanged).
+//   tensor beside the .tns, used while the text is unchanged), CPTC_NGPU
+//   (one process per GPU on devices CPTC_DEVICE.., NCCL between them).
 // Output lines keep the reference's formats ("[ALS] iter i/N time=<ms> ms
 // fit=<f>", "[GEN] iter ... fit=", "[ALS] Lambda:", export files).
+#include <signal.h>
+#include <sys/prctl.h>
+#include <sys/wait.h>
+#include <unistd.h>
+
 #include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "cptc.h"
@@ -27,6 +34,90 @@
 namespace {
 
 const char* env(const char* k) { return std::getenv(k); }
+
+// Several GPUs from the command line (CPTC_NGPU=G > 1; the reference runs on
+// one GPU): one process per GPU, forked at the start of main, before any
+// OpenMP thread pool or CUDA context exists (neither survives a fork).
+// Rank 0 makes the NCCL id and writes it into a pipe per child; every rank
+// runs the same calls (the ALS is collective), rank 0 alone prints and
+// exports.  A rank that fails ends the job: rank 0 watches its children and
+// stops the others, and children die with rank 0.
+std::vector<pid_t> g_kids;  // rank 0 only
+std::thread g_watch;
+int g_watch_rc = 0;
+
+void stop_kids() {
+  for (pid_t k : g_kids) kill(k, SIGTERM);
+}
+
+// Reaps every child; the first one that fails stops the rest and ends rank 0.
+void watch_kids() {
+  size_t left = g_kids.size();
+  while (left > 0) {
+    int st = 0;
+    const pid_t p = waitpid(-1, &st, 0);
+    if (p < 0) break;
+    --left;
+    if (!WIFEXITED(st) || WEXITSTATUS(st) != 0) {
+      std::fprintf(stderr, "[cptc] a rank (pid %d) failed; stopping the job\n", (int)p);
+      stop_kids();
+      std::fflush(stdout);
+      _exit(1);
+    }
+  }
+}
+
+bool write_all(int fd, const void* p, size_t n) {
+  const char* c = (const char*)p;
+  while (n > 0) {
+    const ssize_t w = write(fd, c, n);
+    if (w <= 0) return false;
+    c += w;
+    n -= (size_t)w;
+  }
+  return true;
+}
+
+bool read_all(int fd, void* p, size_t n) {
+  char* c = (char*)p;
+  while (n > 0) {
+    const ssize_t r = read(fd, c, n);
+    if (r <= 0) return false;
+    c += r;
+    n -= (size_t)r;
+  }
+  return true;
+}
+
+// Forks ranks 1..G-1; returns this process's rank (-1 on failure) and, in the
+// children, the read end of their id pipe; in rank 0 the write ends.
+int fork_ranks(int G, std::vector<int>& id_out, int& id_in) {
+  std::fflush(stdout);
+  std::fflush(stderr);
+  const pid_t parent = getpid();
+  for (int r = 1; r < G; ++r) {
+    int fd[2];
+    if (pipe(fd) != 0) return -1;
+    const pid_t pid = fork();
+    if (pid < 0) return -1;
+    if (pid == 0) {
+      prctl(PR_SET_PDEATHSIG, SIGKILL);
+      if (getppid() != parent) _exit(1);
+      close(fd[1]);
+      for (int w : id_out) close(w);
+      id_out.clear();
+      g_kids.clear();
+      id_in = fd[0];
+      if (!std::freopen("/dev/null", "w", stdout)) _exit(1);
+      return r;
+    }
+    close(fd[0]);
+    id_out.push_back(fd[1]);
+    g_kids.push_back(pid);
+  }
+  g_watch = std::thread(watch_kids);
+  return 0;
+}
 
 struct IterLog {
   bool generic = false;
@@ -60,6 +151,11 @@ void on_iter(int it, double ms, double fit, const double* mode_ms, int nm, void*
 
 int fail(cptc_ctx* c, const char* what, int rc) {
   std::fprintf(stderr, "[cptc] %s failed (%d): %s\n", what, rc, c ? cptc_last_error(c) : "");
+  std::fflush(stdout);
+  if (!g_kids.empty()) {  // rank 0: the other ranks cannot finish without it
+    stop_kids();
+    _exit(1);
+  }
   return 1;
 }
 
@@ -86,10 +182,24 @@ int main(int argc, char** argv) {
   if (iters <= 0) iters = 1;
   if (R <= 0) R = 1;
 
+  // The ranks are forked before anything else runs (no OpenMP pool, no CUDA
+  // context exists yet); each parses the tensor itself.
+  const int ngpu = env("CPTC_NGPU") ? std::max(1, std::atoi(env("CPTC_NGPU"))) : 1;
+  int rank = 0;
+  std::vector<int> id_out;
+  int id_in = -1;
+  if (ngpu > 1) {
+    rank = fork_ranks(ngpu, id_out, id_in);
+    if (rank < 0) {
+      std::fprintf(stderr, "[cptc] cannot start %d ranks\n", ngpu);
+      return fail(nullptr, "fork", -1);
+    }
+  }
+
   const int order = cptc_tns_probe_order(filename.c_str());
   if (order < 0) {
     std::fprintf(stderr, "[Main] cannot determine tensor order of: %s\n", filename.c_str());
-    return 1;
+    return fail(nullptr, "probe", -1);
   }
   const bool generic = (order != 3) || env("ALS_GENERIC_FORCE");
 
@@ -106,7 +216,7 @@ int main(int argc, char** argv) {
                             : cptc_tns_read(filename.c_str(), order, &t);
   if (lrc != 0) {
     std::fprintf(stderr, "[Error] Cannot open file: %s\n", filename.c_str());
-    return 1;
+    return fail(nullptr, "read", lrc);
   }
   const double load_ms =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
@@ -150,10 +260,26 @@ int main(int argc, char** argv) {
     }
   }
 
-  int dev = env("CPTC_DEVICE") ? std::atoi(env("CPTC_DEVICE")) : 0;
+  unsigned char id[128];
+  if (ngpu > 1) {
+    if (rank == 0) {
+      const int irc = cptc_comm_unique_id(id);
+      for (int w : id_out) {
+        if (irc == 0) write_all(w, id, sizeof(id));
+        close(w);  // a child that reads nothing gives up
+      }
+      if (irc) return fail(nullptr, "cptc_comm_unique_id", irc);
+    } else {
+      const bool ok = read_all(id_in, id, sizeof(id));
+      close(id_in);
+      if (!ok) return 1;
+    }
+  }
+  int dev = (env("CPTC_DEVICE") ? std::atoi(env("CPTC_DEVICE")) : 0) + rank;
   cptc_ctx* c = nullptr;
   int rc = cptc_create(&c, dev, 0);
   if (rc) return fail(c, "cptc_create", rc);
+  if (ngpu > 1 && (rc = cptc_comm_init(c, id, rank, ngpu))) return fail(c, "comm_init", rc);
   if ((rc = cptc_load_coo(c, &t))) return fail(c, "load", rc);
   if ((rc = cptc_build(c, R, threshold, &o))) return fail(c, "build", rc);
   cptc_stats st;
@@ -185,6 +311,11 @@ int main(int argc, char** argv) {
   const double als_ms =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - ta).count();
 
+  if (rank != 0) {  // the replicated results are reported and exported by rank 0
+    cptc_destroy(c);
+    cptc_coo_free(&t);
+    return 0;
+  }
   std::vector<double> lam(R);
   cptc_get_lambda(c, lam.data());
   double res[2] = {0, 0};
@@ -256,7 +387,9 @@ int main(int argc, char** argv) {
       std::printf("[GEN] factors dumped to %s\n", path.c_str());
     }
   }
+  std::fflush(stdout);
   cptc_destroy(c);
   cptc_coo_free(&t);
+  if (g_watch.joinable()) g_watch.join();  // every other rank has finished
   return 0;
 }

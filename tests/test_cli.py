@@ -90,3 +90,44 @@ def test_cli_generic_matches_reference(gpu, tmp_path):
     assert np.max(np.abs(fits - np.array(g["fits"]))) < 1e-5
     assert "[GEN] exact:" in out
     assert (tmp_path / "d.factors.txt").read_text().startswith("# cpTC factor dump")
+
+
+def _gpu_count() -> int:
+    try:
+        import torch
+
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def test_cli_ranks_end_together_when_one_fails(tmp_path):
+    # CPTC_NGPU=3 on a machine without GPUs: every rank fails at cptc_create;
+    # the job must end (no rank left waiting for the others) with a failure
+    # status, and only rank 0 prints
+    if _gpu_count() > 0:
+        pytest.skip("checks the failure path; needs a machine without GPUs")
+    t = cp.gen_uniform((20, 30, 40), 500, seed=1)
+    p = tmp_path / "t.tns"
+    cp.write_tns(p, t)
+    r = subprocess.run([str(CLI), str(p), "1", "8"], env=dict(os.environ, CPTC_NGPU="3"),
+                       capture_output=True, text=True, timeout=120)
+    assert r.returncode != 0
+    assert r.stdout.count("[Main] Load time") == 1
+
+
+@pytest.mark.gpu
+def test_cli_two_gpus_match_one(gpu, tmp_path):
+    # one process per GPU from the command line: the same fits as one GPU
+    if _gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    g = json.loads((GOLD / "cfg1_R32_auto.json").read_text())
+    tns = tmp_path / "t.tns"
+    golden_tensor(g, tns)
+    one = fits_of(run([tns, g["iters"], g["R"], g["threshold"]], {"ALS_FORCE_CUDA": "1"}), "ALS")
+    two_out = run([tns, g["iters"], g["R"], g["threshold"]],
+                  {"ALS_FORCE_CUDA": "1", "CPTC_NGPU": "2"})
+    two = fits_of(two_out, "ALS")
+    assert len(two) == len(one) == g["iters"]
+    assert np.max(np.abs(two - one)) < 1e-9
+    assert two_out.count("[ALS] Final RMSE=") == 1
