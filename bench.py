@@ -259,13 +259,17 @@ def run_engine(a):
     # ---- end to end through the C ABI: host COO in, factors out ----------
     tb0 = time.perf_counter()
     eng.load(t)
+    tb1 = time.perf_counter()
     eng.build(a.rank, threshold=a.threshold, path=a.path, exchange=a.exchange)
     eng.init_factors()
     build_s = time.perf_counter() - tb0
+    load_s = tb1 - tb0
     st = eng.stats()
 
-    # warm-up iterations (also the e2e steps' starting point)
-    eng.als(a.warmup)
+    # warm-up iterations (also the e2e steps' starting point); the first one
+    # (graph capture included) is reported apart
+    warm = eng.als(a.warmup)
+    first_iter_ms = warm[0].ms if warm else None
 
     # ---- device-timed steps (inputs resident) ------------------------------
     barrier()
@@ -402,6 +406,9 @@ def run_engine(a):
             "exchange": a.exchange if world > 1 else None,
             "l2": "views (1.2 GB/mode) stream from HBM each MTTKRP; no flush needed",
             "build_s": build_s,
+            "load_s": load_s,
+            "device_build_ms": st["build_ms"],
+            "first_iter_ms": first_iter_ms,
             "mttkrp_ms_per_mode": mode_ms,
             "mttkrp_ms_per_mode_by_rank": rank_mode_ms if world > 1 else None,
             "phase_ms_by_rank": rank_phase_ms,
