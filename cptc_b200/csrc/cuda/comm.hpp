@@ -16,6 +16,9 @@ namespace cptc {
 // Row slabs of every mode (single rank: whole modes).
 void comm_prepare(Engine& E);
 void comm_destroy(Engine& E);
+// Aborts the communicator (its unfinished collectives return) and drops it:
+// cptc_comm_init has to run again before the next collective.
+void comm_abort(Engine& E);
 void comm_init(Engine& E, const unsigned char id[128], int rank, int nranks);
 int comm_unique_id(unsigned char out[128]);
 // Rows per slab of mode m (slab r = rows [r * s, min((r + 1) * s, I_m))).

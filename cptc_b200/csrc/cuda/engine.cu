@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstring>
 #include <random>
+#include <thread>
 
 #include "../host/coo.hpp"
 #include "../host/reorder.hpp"
@@ -716,12 +717,47 @@ void Engine::launch_iteration(int slot) {
   CPTC_CUDA(cudaEventRecord(E[2 * CPTC_MAX_ORDER + 1], stream));
 }
 
+// Waits for the end of an iteration.  With several ranks and
+// CPTC_COMM_TIMEOUT_MS set, the wait is bounded: an iteration that has not
+// finished by then is taken to be stuck in a collective waiting for a rank
+// that is not there, the communicator is aborted (its kernels return) and
+// the call fails with CPTC_E_COMM.  Without it the wait is unbounded, as a
+// plain stream synchronisation.
+void Engine::wait_iteration(cudaEvent_t done) {
+  static const long long limit_ms = [] {
+    const char* e = std::getenv("CPTC_COMM_TIMEOUT_MS");
+    return e ? std::atoll(e) : 0ll;
+  }();
+  if (nranks == 1 || limit_ms <= 0) {
+    CPTC_CUDA(cudaEventSynchronize(done));
+    return;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(done);
+    if (q == cudaSuccess) return;
+    if (q != cudaErrorNotReady) CPTC_CUDA(q);
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                        std::chrono::steady_clock::now() - t0).count();
+    if (ms > limit_ms) {
+      comm_abort(*this);
+      cudaStreamSynchronize(stream);
+      cudaStreamSynchronize(side);
+      release_graph();
+      throw CptcError(CPTC_E_COMM, "an iteration did not finish within CPTC_COMM_TIMEOUT_MS (a "
+                                   "rank is missing or stalled); the communicator was aborted, "
+                                   "call cptc_comm_init again");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
 // Waits for iteration `it` (readback slot `slot`), checks the solve status,
 // computes the fit and reports it.
 void Engine::finish_iteration(int it, int slot, cptc_iter_cb cb, void* user) {
   cudaEvent_t* E = slot ? ev1 : ev;
   const double* hs = h_scal + 8 * slot;
-  CPTC_CUDA(cudaEventSynchronize(E[2 * CPTC_MAX_ORDER + 1]));
+  wait_iteration(E[2 * CPTC_MAX_ORDER + 1]);
   int h_status = 0;
   std::memcpy(&h_status, hs + 4, sizeof(int));
   if (h_status != 0) {

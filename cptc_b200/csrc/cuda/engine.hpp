@@ -191,6 +191,7 @@ struct Engine {
   void enqueue_iteration(int slot);
   void launch_iteration(int slot);
   void finish_iteration(int it, int slot, cptc_iter_cb cb, void* user);
+  void wait_iteration(cudaEvent_t done);
   uint64_t padded_rows(int m) const;
   void permute_rows(const double* in, int m, bool to_relabelled, double* out);
   void mttkrp(int mode);  // into FtV (relabelled rows), stream-ordered
