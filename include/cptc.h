@@ -131,7 +131,11 @@ const char* cptc_last_error(const cptc_ctx* ctx);
  * computes an equal share of every mode's nonzeros; the partial MTTKRP is
  * reduce-scattered into equal row slabs, each rank solves its slab, and one
  * grouped call all-reduces the R x R Gram and all-gathers the slabs into
- * every rank's factor replica.  The reference runs on one GPU. */
+ * every rank's factor replica.  The reference runs on one GPU.
+ * CPTC_COMM_TIMEOUT_MS (environment, unset = no limit) bounds how long
+ * cptc_als waits for an iteration on several GPUs: past it the communicator
+ * is aborted and the call returns CPTC_E_COMM (cptc_comm_init again before
+ * the next collective call). */
 int cptc_comm_unique_id(unsigned char out_id[128]);
 int cptc_comm_init(cptc_ctx* ctx, const unsigned char id[128], int rank, int nranks);
 
