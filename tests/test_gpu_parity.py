@@ -40,6 +40,7 @@ CASES = [
     ((3000, 20, 50), 60000, 64, "uniform"),  # mode-1 rows of ~3000 nnz span tasks
     ((500, 400, 300), 30000, 128, "normal"),
     ((200, 1, 300), 4000, 24, "uniform"),    # a mode of length 1
+    ((60, 50, 40), 8000, 1, "normal"),        # rank 1
 ]
 
 
