@@ -61,6 +61,16 @@ __global__ void k_permute_rows(const double* __restrict__ in, const uint32_t* __
 
 }  // namespace
 
+// CPTC_OVERLAP_TILES=1: the tile and residual kernels of a mode run side by
+// side (Engine::mttkrp).
+static bool overlap_tiles() {
+  static const bool v = [] {
+    const char* e = std::getenv("CPTC_OVERLAP_TILES");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
 double b200_fill_min(int R) {
   if (R <= 32) return 0.07;
   if (R >= 128) return 0.04;
@@ -79,6 +89,9 @@ Engine::Engine(int dev) : device(dev) {
   evc = ev;
   CPTC_CUDA(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming));
   CPTC_CUDA(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming));
+  CPTC_CUDA(cudaStreamCreateWithFlags(&tstream, cudaStreamNonBlocking));
+  CPTC_CUDA(cudaEventCreateWithFlags(&ev_tfork, cudaEventDisableTiming));
+  CPTC_CUDA(cudaEventCreateWithFlags(&ev_tjoin, cudaEventDisableTiming));
   CPTC_CUDA(cudaMallocHost((void**)&h_scal, 16 * sizeof(double)));
 }
 
@@ -102,6 +115,12 @@ Engine::~Engine() {
         if (e) cudaEventDestroy(e);
   if (ev_fork) cudaEventDestroy(ev_fork);
   if (ev_join) cudaEventDestroy(ev_join);
+  if (ev_tfork) cudaEventDestroy(ev_tfork);
+  if (ev_tjoin) cudaEventDestroy(ev_tjoin);
+  if (tstream) {
+    cudaStreamSynchronize(tstream);
+    cudaStreamDestroy(tstream);
+  }
   if (h_scal) cudaFreeHost(h_scal);
   if (side) cudaStreamDestroy(side);
   if (stream) cudaStreamDestroy(stream);
@@ -116,7 +135,8 @@ uint64_t Engine::device_bytes() const {
   b += units.unit.bytes() + units.start.bytes() + units.lid.bytes() + units.val.bytes() +
        units.outer_idx.bytes();
   for (int m = 0; m < 3; ++m) b += units.order[m].bytes();
-  b += FtV.bytes() + FtF.bytes() + Ainv.bytes() + gpart.bytes() + dots.bytes() + lambda.bytes();
+  b += FtV.bytes() + FtV2.bytes() + FtF.bytes() + Ainv.bytes() + gpart.bytes() + dots.bytes() +
+       lambda.bytes();
   return b;
 }
 
@@ -204,6 +224,8 @@ void Engine::alloc_workspace() {
   uint64_t maxd = 0;
   for (int m = 0; m < N; ++m) maxd = std::max<uint64_t>(maxd, padded_rows(m));
   FtV.alloc(maxd * (uint64_t)R);
+  if (overlap_tiles()) FtV2.alloc(maxd * (uint64_t)R);
+  else FtV2.release();
   FtF.alloc((uint64_t)R * R);
   Ainv.alloc(2 * (uint64_t)R * R + 1);
   gpart_blocks = 148;
@@ -497,9 +519,33 @@ void Engine::fetch_rows(const double* dev, int m, double* host) {
   CPTC_CUDA(cudaStreamSynchronize(stream));
 }
 
+bool Engine::tiles_target(int mode) const {
+  if (!dense_active) return false;
+  for (int q = 0; q < 3; ++q)
+    if (units.inner[q] == mode && units.cnt[q] > 0) return true;
+  return false;
+}
+
 // FtV = MTTKRP of `mode` (relabelled rows): zero, dense tiles, residual.
 void Engine::mttkrp(int mode) {
-  CPTC_CUDA(cudaMemsetAsync(FtV.p, 0, padded_rows(mode) * (uint64_t)R * sizeof(double), stream));
+  const uint64_t n = padded_rows(mode) * (uint64_t)R;
+  CPTC_CUDA(cudaMemsetAsync(FtV.p, 0, n * sizeof(double), stream));
+  if (overlap_tiles() && FtV2.p && tiles_target(mode)) {
+    // The two kernels side by side: the residual kernel waits on its row
+    // gathers and the tile kernel on its own latency, so each can fill the
+    // other's idle issue slots.  The residual kernel writes rows it owns
+    // with plain read-modify-writes, so the tiles go to a buffer of their
+    // own, added afterwards.
+    CPTC_CUDA(cudaMemsetAsync(FtV2.p, 0, n * sizeof(double), stream));
+    CPTC_CUDA(cudaEventRecord(ev_tfork, stream));
+    CPTC_CUDA(cudaStreamWaitEvent(tstream, ev_tfork, 0));
+    mttkrp_tiles(mode, FtV2.p, tstream);
+    CPTC_CUDA(cudaEventRecord(ev_tjoin, tstream));
+    mttkrp_sparse(mode);
+    CPTC_CUDA(cudaStreamWaitEvent(stream, ev_tjoin, 0));
+    launch_add_into(FtV.p, FtV2.p, n, stream);
+    return;
+  }
   // The residual kernel first: its many short CTAs rebalance around an SM
   // that the side stream's inverse may hold; the persistent tile grid is
   // launched once that SM is free again.
@@ -507,7 +553,7 @@ void Engine::mttkrp(int mode) {
   mttkrp_tiles(mode);
 }
 
-void Engine::mttkrp_tiles(int mode) {
+void Engine::mttkrp_tiles(int mode, double* out, cudaStream_t s) {
   if (!dense_active) return;
   int ts = -1;
   for (int q = 0; q < 3; ++q)
@@ -539,9 +585,9 @@ void Engine::mttkrp_tiles(int mode) {
   ta.outer_idx = units.outer_idx.p;
   for (int q = 0; q < units.nouter; ++q) ta.Fout[q] = F[units.outer[q]].p;
   ta.store_dups = units.store_dups ? 1 : 0;
-  ta.out = FtV.p;
+  ta.out = out ? out : FtV.p;
   launch_mttkrp_tiles3(ta, units.order[ts].p, units.cut[ts].p + (uint64_t)rank * units.blocks,
-                       units.blocks, stream);
+                       units.blocks, s ? s : stream);
 }
 
 void Engine::mttkrp_sparse(int mode) {

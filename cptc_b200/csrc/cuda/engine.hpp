@@ -106,6 +106,11 @@ struct Engine {
   // other modes' Grams and so runs beside that mode's MTTKRP.
   cudaStream_t side = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  // CPTC_OVERLAP_TILES=1 (for measurement): the dense-tile kernel runs on
+  // its own stream into FtV2 beside the residual kernel, then FtV += FtV2.
+  cudaStream_t tstream = nullptr;
+  cudaEvent_t ev_tfork = nullptr, ev_tjoin = nullptr;
+  DArray<double> FtV2;
   // One ALS iteration captured as a CUDA graph (rebuilt after load, build
   // and communicator changes).
   // Two of them, for two iterations in flight (slot = iteration parity),
@@ -195,7 +200,10 @@ struct Engine {
   uint64_t padded_rows(int m) const;
   void permute_rows(const double* in, int m, bool to_relabelled, double* out);
   void mttkrp(int mode);  // into FtV (relabelled rows), stream-ordered
-  void mttkrp_tiles(int mode);   // dense-tile TF32 part only (accumulates)
+  void mttkrp_tiles(int mode, double* out = nullptr, cudaStream_t s = nullptr);
+                                 // dense-tile TF32 part only (accumulates into out, FtV
+                                 // by default, on s, the engine stream by default)
+  bool tiles_target(int mode) const;  // the dense tiles contribute to this mode
   void mttkrp_sparse(int mode);  // FP64 view part only (accumulates)
   void als(int iters, cptc_iter_cb cb, void* user);
   uint64_t device_bytes() const;

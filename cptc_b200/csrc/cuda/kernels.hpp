@@ -100,6 +100,8 @@ int launch_apply_solve(const double* FtV, const double* Ainv, const double* lamb
 void launch_norm_finalize(const double* part, int nblk, int R, int generic_norm,
                           double* lambda, double* G, double* scale, cudaStream_t s);
 void launch_scale_cols(double* F, uint64_t rows, int R, const double* scale, cudaStream_t s);
+// y += x over n doubles.
+void launch_add_into(double* y, const double* x, uint64_t n, cudaStream_t s);
 // dots[r] partials of sum_i F[i,r] * FtV[i,r]; returns nblk.
 int launch_col_dots(const double* F, const double* FtV, uint64_t rows, int R, double* part,
                     int max_blocks, cudaStream_t s);

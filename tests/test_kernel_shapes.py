@@ -1,5 +1,6 @@
-"""The kernel shapes selectable for measurement (CPTC_REC3_R32=8x4,
-CPTC_REC3_R128=u2, CPTC_TILES_SHAPE=nw2) compute what the default shapes do.
+"""The kernel shapes and launch orders selectable for measurement
+(CPTC_REC3_R32=8x4, CPTC_REC3_R128=u2, CPTC_TILES_SHAPE=nw2,
+CPTC_OVERLAP_TILES=1) compute what the defaults do.
 
 The library reads these switches once per process, so each shape runs in a
 child process (this file's __main__) that writes its MTTKRPs to a .npz; the
@@ -26,6 +27,8 @@ def case_tensor(kind):
     if kind == "zipf":  # config 4's index distribution, 0.5% of its nonzeros
         t = cp.gen_config(4, scale=0.005)
         return cp.CooTensor(tuple(int(i.max()) + 1 for i in t.idx), t.idx, t.vals)
+    if kind == "mixed":  # config 3 at 2%: dense tiles and a residual
+        return cp.gen_config(3, scale=0.02)
     return cp.gen_uniform((64, 64, 64), 120_000, seed=8, values="lognormal")
 
 
@@ -78,6 +81,19 @@ def test_tile_shape_nw2(gpu, oracle, R, tmp_path):
     got = run_shape({"CPTC_TILES_SHAPE": "nw2"}, "dense", R, "tf32", tmp_path)
     assert int(got["tf32"]) == 1
     t = case_tensor("dense")
+    F = factors(t.dims, R)
+    for n in range(3):
+        hyb, _ = oracle.mttkrp_hybrid3(t, F, n, thr=0.03, threads=8)
+        assert rel(got[f"M{n}"], hyb) < 1e-5, n
+
+
+@pytest.mark.parametrize("R", [32, 128])
+def test_tiles_beside_residual(gpu, oracle, R, tmp_path):
+    # CPTC_OVERLAP_TILES=1: the tile kernel on its own stream into a second
+    # buffer, added after both kernels
+    got = run_shape({"CPTC_OVERLAP_TILES": "1"}, "mixed", R, "tf32", tmp_path)
+    assert int(got["tf32"]) == 1
+    t = case_tensor("mixed")
     F = factors(t.dims, R)
     for n in range(3):
         hyb, _ = oracle.mttkrp_hybrid3(t, F, n, thr=0.03, threads=8)
