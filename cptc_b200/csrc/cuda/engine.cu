@@ -321,7 +321,7 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
   alloc_workspace();
   for (int t = 0; t < 3; ++t) units.cnt[t] = units.nunits;
   if (dense_active) {
-    units.blocks = tile_blocks_for(R, device, units.nunits / (uint64_t)nranks);
+    units.blocks = tile_blocks_for(R, device, units.nunits / (uint64_t)nranks, overlap_tiles());
     for (int t = 0; t < 3; ++t) tile_cuts(*this, t);
   }
   for (int n = 0; n < N; ++n) {

@@ -57,7 +57,9 @@ struct TileArgs {
 void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, const uint32_t* cut,
                           uint32_t blocks, cudaStream_t s);
 // CTAs the tile kernel runs for rank R (shared-memory occupancy x SMs).
-uint32_t tile_blocks_for(int R, int device, uint64_t ntiles);
+// share_sms: one wave using at most half of the CTAs an SM holds, leaving
+// room for the residual kernel running beside it.
+uint32_t tile_blocks_for(int R, int device, uint64_t ntiles, bool share_sms = false);
 // Balanced CTA ranges over E.units.order[slot] (fills E.units.cut[slot]).
 void tile_cuts(Engine& E, int slot);
 // Partition of Engine::tiles + residual selection (tiles.cu).

@@ -624,7 +624,7 @@ bool tiles_nw2() {
 
 }  // namespace
 
-uint32_t tile_blocks_for(int R, int device, uint64_t ntiles) {
+uint32_t tile_blocks_for(int R, int device, uint64_t ntiles, bool share_sms) {
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   // A whole number of waves of the CTAs the SMs hold at once (registers
@@ -647,6 +647,7 @@ uint32_t tile_blocks_for(int R, int device, uint64_t ntiles) {
   int per_sm = 0;
   CPTC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem));
   if (per_sm < 1) per_sm = 1;
+  if (share_sms) return (uint32_t)sms * (uint32_t)((per_sm + 1) / 2);
   const uint64_t wave = (uint64_t)sms * per_sm;
   uint64_t waves = ntiles / (wave * 16);
   if (waves < 1) waves = 1;
