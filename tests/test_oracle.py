@@ -22,7 +22,9 @@ def rand_factors(dims, R, seed=1):
 
 
 @pytest.mark.parametrize("dims,nnz,R", [((30, 20, 40), 3000, 8), ((17, 33, 9, 12), 2500, 5),
-                                        ((5, 7, 6, 4, 3), 400, 16), ((64, 1), 50, 3)])
+                                        ((5, 7, 6, 4, 3), 400, 16), ((64, 1), 50, 3),
+                                        ((5, 4, 3, 6, 4, 3), 600, 4),
+                                        ((3, 2, 3, 2, 3, 2, 3, 2), 300, 2)])
 def test_mttkrp_matches_numpy(oracle, dims, nnz, R):
     t = cp.gen_uniform(dims, nnz, seed=3, values="normal")
     F = rand_factors(t.dims, R)
