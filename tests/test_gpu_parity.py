@@ -102,7 +102,9 @@ def test_mttkrp_fp64_nway_records(gpu, oracle, order, R):
 
 @pytest.mark.parametrize("dims,nnz,R", [((30, 20, 25, 40), 20000, 16),
                                         ((12, 9, 15, 8, 11), 8000, 32),
-                                        ((300, 200), 5000, 8)])
+                                        ((300, 200), 5000, 8),
+                                        ((9, 7, 8, 6, 7, 5, 6), 9000, 16),      # order 7
+                                        ((6, 5, 7, 4, 6, 5, 4, 6), 9000, 8)])  # order 8
 def test_mttkrp_fp64_generic(gpu, oracle, dims, nnz, R):
     t = cp.gen_uniform(dims, nnz, seed=5, values="normal")
     e = engine_for(t, R, dense_generic=False)
