@@ -1,18 +1,21 @@
 #!/usr/bin/env python
-"""CP-ALS benchmark: seconds per ALS iteration on BASELINE config 4.
+"""CP-ALS benchmark: seconds per ALS iteration on the 76.9M-nonzero order-3
+power-law tensor (config 4).
 
 Workload: order-3 synthetic tensor 12092 x 9184 x 28818 with 76.9M nonzeros,
 Zipf(1.1) indices per mode over a random permutation, lognormal values
-(cptc_gen_config(4)); CP rank R=32 (R=128 with --rank 128); one step = one
-CP-ALS iteration (3 mode updates + Gram fit).  The tensor views are streamed
-from HBM every MTTKRP (1.2 GB per mode, larger than the 126 MB L2), so no
-explicit L2 flush is needed between steps.
+(cptc_gen_config(4)); CP rank R=32 (R=128 with --rank 128, and an R=128
+sub-record in every default run); one step = one CP-ALS iteration (3 mode
+updates + Gram fit).  The tensor views are streamed from HBM every MTTKRP
+(1.2 GB per mode, larger than the 126 MB L2), so no explicit L2 flush is
+needed between steps.
 
   python bench.py [--gpus N --steps K --warmup W --rank R]
   python bench.py --impl reference ...   # cpTC's own build (oracle/_ref)
 
 One JSON line on rank 0: metric, value, unit, e2e, roofline, cpu_baseline,
-clocks, gpu_launches and the workload config.
+clocks, gpu_launches, the workload config (identical keys in both arms) and
+the engine's own measurements under `detail`.
 """
 from __future__ import annotations
 
@@ -54,6 +57,8 @@ def parse_args():
     p.add_argument("--e2e-sharded", action="store_true",
                    help="e2e on several GPUs: each rank uploads 1/G of every factor and the "
                         "pieces are all-gathered on the GPUs (cptc_set_factors_sharded)")
+    p.add_argument("--no-r128", action="store_true",
+                   help="skip the R=128 sub-record of an R=32 run")
     p.add_argument("--phases", type=int, default=0,
                    help="after the timed steps, run this many iterations with per-phase "
                         "timing events and report their mean phase times per rank")
@@ -67,6 +72,21 @@ def workload_name(a) -> str:
     if a.scale != 1.0:
         s += f" (nnz x{a.scale})"
     return f"{s}, CP-ALS R={a.rank}"
+
+
+L2_NOTE = "views (1.2 GB/mode) stream from HBM each MTTKRP; no flush needed"
+
+
+def shared_config(a, nnz: int, dims) -> dict:
+    """The workload as both arms state it (same keys, same values): which
+    tensor, rank and cutoff; measurements go elsewhere in the line."""
+    return {"workload": workload_name(a), "rank": a.rank, "nnz": int(nnz),
+            "dims": [int(d) for d in dims], "threshold": a.threshold, "seed": 0,
+            "l2": L2_NOTE}
+
+
+def want_r128(a) -> bool:
+    return a.rank == 32 and not a.no_r128
 
 
 # ---------------------------------------------------------------------------
@@ -328,12 +348,33 @@ def run_engine(a):
         rank_phase_ms = [np.round(phase_ms, 4).tolist()]
         rank_kernel_ms = [np.round(kern_ms, 4).tolist()]
 
+    # ---- R=128 sub-record: the metric's second rank, same tensor ----------
+    r128 = None
+    if want_r128(a):
+        eng.build(128, threshold=a.threshold, path=a.path, exchange=a.exchange)
+        eng.init_factors()
+        eng.als(a.warmup)
+        barrier()
+        reps128 = eng.als(min(a.steps, 10))
+        prof128 = [eng.profile_mttkrp(n, reps=2) for n in range(t.order)]
+        st128 = eng.stats()
+        r128 = {"ms_per_iter": float(np.mean([r.ms for r in reps128])),
+                "iters": len(reps128),
+                "mttkrp_ms_per_mode": np.mean([r.mode_ms for r in reps128], axis=0).tolist(),
+                "sparse_kernel_ms_per_mode": [p["sparse_ms"] for p in prof128],
+                "tile_kernel_ms_per_mode": [p["tiles_ms"] for p in prof128],
+                "final_fit": reps128[-1].fit,
+                "tf32_path": bool(st128["tf32_path"])}
+
     if dist is not None:
         import torch
 
-        v = torch.tensor([dev_s, e2e_s], dtype=torch.float64)
+        v = torch.tensor([dev_s, e2e_s, r128["ms_per_iter"] if r128 else 0.0],
+                         dtype=torch.float64)
         dist.all_reduce(v, op=dist.ReduceOp.MAX)
         dev_s, e2e_s = float(v[0]), float(v[1])
+        if r128:
+            r128["ms_per_iter"] = float(v[2])  # max over ranks
         # per-rank MTTKRP times (the iteration waits for the slowest rank)
         mm = torch.tensor(mode_ms, dtype=torch.float64)
         gathered = [torch.zeros_like(mm) for _ in range(world)]
@@ -357,28 +398,6 @@ def run_engine(a):
             dist.destroy_process_group()
         return
 
-    sp = [p["sparse_ms"] for p in prof]
-    tl = [p["tiles_ms"] for p in prof]
-    dominant = "k_mttkrp_rec3s" if t.order == 3 else "k_mttkrp_view"
-    nnz_view = st["sparse_nnz"]
-    # Per launch (one mode): the benchmark's algorithmic bytes (every factor-row
-    # gather) and the compulsory bytes (each stored byte once).
-    algo = [algorithmic_bytes(nnz_view, t.order, a.rank, t.dims[n]) for n in range(t.order)]
-    comp = 16 * nnz_view + 8 * a.rank * sum(t.dims)
-    algo_launch = float(np.mean(algo))
-    ktime = float(np.mean(sp)) / 1000.0
-    peaks = measured_peaks()
-    achieved = algo_launch / ktime / 1e9 if ktime > 0 else None
-    traffic = None
-    prof_file = ROOT / "profiles" / "traffic.json"
-    if prof_file.exists():
-        try:
-            traffic = json.loads(prof_file.read_text()).get(f"cfg{a.config}_R{a.rank}")
-        except Exception:
-            traffic = None
-        if traffic is not None and a.scale != 1.0:
-            traffic = None  # recorded for the full-size workload only
-
     value = dev_s / a.steps
     line = {
         "metric": METRIC,
@@ -393,18 +412,15 @@ def run_engine(a):
         "vs_baseline": None,
         "dtype": "f64+tf32" if st["tf32_path"] else "f64",
         "data": "synthetic (seeded generator, cptc_gen_config)",
-        "config": {
-            "workload": workload_name(a),
-            "rank": a.rank,
-            "nnz": t.nnz,
-            "dims": list(t.dims),
+        "config": shared_config(a, t.nnz, t.dims),
+        "detail": {
             "path": "tf32 dense tiles + fp64 residual" if st["tf32_path"] else "fp64",
             "dense_tiles": st["dense_tiles"],
             "dense_nnz": st["dense_nnz"],
+            "sparse_nnz": st["sparse_nnz"],
             "avg_fill": st["avg_fill"],
             "parallelism": f"row-slab x{world}" if world > 1 else "single GPU",
             "exchange": a.exchange if world > 1 else None,
-            "l2": "views (1.2 GB/mode) stream from HBM each MTTKRP; no flush needed",
             "build_s": build_s,
             "load_s": load_s,
             "device_build_ms": st["build_ms"],
@@ -416,34 +432,14 @@ def run_engine(a):
             "residual_tile_ms_by_rank": rank_kernel_ms,
             "final_fit": fits[-1],
         },
+        "r128": r128,
         "e2e": {"value": e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "upload": ("each rank 1/G, all-gathered on the GPUs" if sharded else
                            "every rank its whole replica" if world > 1 else "whole factors")},
         "gpu_launches": int(l1 - l0),
         "clocks": clocks,
-        "roofline": {
-            "bound": "hbm",
-            "kernel": dominant,
-            "achieved": achieved,
-            "peak": peaks["hbm_gbs"],
-            "unit": "GB/s",
-            "frac": (achieved / peaks["hbm_gbs"]) if achieved else None,
-            "peak_src": peaks["src"],
-            "traffic": traffic,
-            "algorithmic_bytes_per_launch": algo_launch,
-            "bytes_note": "algorithmic bytes count every factor-row gather; "
-                          "most gathers hit L1/L2, so frac can exceed 1; compulsory_frac "
-                          "counts each stored byte once",
-            "compulsory_bytes_per_launch": comp,
-            "compulsory_frac": (comp / ktime / 1e9 / peaks["hbm_gbs"]) if ktime > 0 else None,
-            "sparse_kernel_ms_per_mode": sp,
-            "tile_kernel_ms_per_mode": tl,
-            "tile_tflops": tile_tflops(st, a.rank, tl),
-            # no measured TF32 peak exists for this pool: nominal dense TF32
-            "tile_tf32_frac_of_nominal": (tile_tflops(st, a.rank, tl) / TF32_NOMINAL_TFLOPS
-                                          if tile_tflops(st, a.rank, tl) else None),
-        },
+        "roofline": roofline_record(a, t, st, prof),
     }
     if not a.no_cpu_baseline and world == 1:  # measured at N=1 only
         line["cpu_baseline"] = cpu_baseline(t, a.rank)
@@ -454,70 +450,169 @@ def run_engine(a):
         dist.destroy_process_group()
 
 
+def recorded_traffic(a):
+    """ncu DRAM bytes per launch of the dominant kernel for this workload
+    (profiles/traffic.json), or None."""
+    prof_file = ROOT / "profiles" / "traffic.json"
+    if not prof_file.exists() or a.scale != 1.0:
+        return None  # recorded for the full-size workload only
+    try:
+        return json.loads(prof_file.read_text()).get(f"cfg{a.config}_R{a.rank}")
+    except Exception:
+        return None
+
+
+def roofline_record(a, t, st, prof) -> dict:
+    """Roofline of the dominant kernel (the FP64 residual MTTKRP).
+
+    `achieved` counts the bytes the kernel must move from HBM at least (its
+    record stream once, each factor matrix it reads once, each output row
+    once) per launch, over the kernel's mean CUDA-event duration; `frac` is
+    that rate over the measured HBM copy bandwidth.  The bytes the kernel's
+    factor-row gathers move through L1/L2 (a row per use) are reported apart,
+    as `gather_bytes_per_launch` and `gather_rate_gbs`."""
+    sp = [p["sparse_ms"] for p in prof]
+    tl = [p["tiles_ms"] for p in prof]
+    dominant = "k_mttkrp_rec3s" if t.order == 3 else "k_mttkrp_view"
+    nnz_view = st["sparse_nnz"]
+    rec_bytes = 16 if t.order == 3 else 32
+    comp = [rec_bytes * nnz_view + 8 * a.rank * (sum(t.dims) - t.dims[n]) + 8 * a.rank * t.dims[n]
+            for n in range(t.order)]
+    gath = [algorithmic_bytes(nnz_view, t.order, a.rank, t.dims[n]) for n in range(t.order)]
+    comp_launch = float(np.mean(comp))
+    gath_launch = float(np.mean(gath))
+    ktime = float(np.mean(sp)) / 1000.0
+    peaks = measured_peaks()
+    achieved = comp_launch / ktime / 1e9 if ktime > 0 else None
+    tf = tile_tflops(st, a.rank, tl)
+    return {
+        "bound": "hbm",
+        "kernel": dominant,
+        "achieved": achieved,
+        "peak": peaks["hbm_gbs"],
+        "unit": "GB/s",
+        "frac": (achieved / peaks["hbm_gbs"]) if achieved else None,
+        "peak_src": peaks["src"],
+        "traffic": recorded_traffic(a),
+        "algorithmic_bytes_per_launch": comp_launch,
+        "bytes_note": "algorithmic = compulsory HBM bytes per launch (record stream once, "
+                      "factor matrices once, output rows once); the survey's gather-counted "
+                      "bytes are gather_bytes_per_launch, moved through L1/L2",
+        "gather_bytes_per_launch": gath_launch,
+        "gather_rate_gbs": gath_launch / ktime / 1e9 if ktime > 0 else None,
+        "sparse_kernel_ms_per_mode": sp,
+        "tile_kernel_ms_per_mode": tl,
+        "tile_tflops": tf,
+        # no measured TF32 peak exists for this pool: nominal dense TF32
+        "tile_tf32_frac_of_nominal": (tf / TF32_NOMINAL_TFLOPS) if tf else None,
+    }
+
+
 # ---------------------------------------------------------------------------
 # reference arm: cpTC's own sources rebuilt for sm_100a (oracle/_ref)
 # ---------------------------------------------------------------------------
-def run_reference(a):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    import cptc_b200 as cp
-
-    binary = ROOT / "oracle" / "_ref" / "cptc_opt"
-    t = load_or_generate(a)
-    if not binary.exists():
-        # Oracle port on the host cores instead.
-        from oracle import oracle as o
-
-        threads = os.cpu_count() or 1
-        t0 = time.perf_counter()
-        fits, _, _ = o.cp_als3(t, a.rank, 1, thr=a.threshold, path="fp64", threads=threads)
-        v = time.perf_counter() - t0
-        line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
-                "higher_is_better": False, "n_gpus": 0, "steps": 1, "warmup": 0,
-                "config": {"workload": workload_name(a)},
-                "cpu_baseline": {"kind": "port", "cores": threads, "value": v, "unit": UNIT,
-                                 "sample": "one full CP-ALS iteration incl. CADR and init"},
-                "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
-        return
-    with tempfile.TemporaryDirectory() as d:
-        tns = Path(a.keep_tns) if a.keep_tns else Path(d) / "bench.tns"
-        cp.write_tns(tns, t)
-        iters = a.warmup + a.steps
-        env = dict(os.environ)
-        if t.order != 3:
-            # config 5's switches: HITS relabelling (3 rounds), dense units
-            # at cutoff 0.03
-            env.update({"GEN_REORDER": "hits", "GEN_REORDER_T": "3",
-                        "GEN_DENSE_THRESHOLD": str(a.threshold)})
-        r = subprocess.run([str(binary), str(tns), str(iters), str(a.rank), str(a.threshold)],
-                           capture_output=True, text=True, env=env, timeout=1800)
-        out = r.stdout
-    if a.ref_log:
-        Path(a.ref_log).write_text(out + "\n--- stderr ---\n" + r.stderr)
-    if r.returncode != 0:
-        print(json.dumps({"impl": "reference", "unavailable":
-                          f"cpTC exited {r.returncode}: {r.stderr.strip()[-200:]}"}))
-        return
+def parse_ref_log(out: str):
     times, fits = [], []
     for ln in out.splitlines():
         if ln.startswith("[ALS] iter ") or ln.startswith("[GEN] iter "):
             parts = dict(kv.split("=") for kv in ln.split() if "=" in kv)
             times.append(float(parts["time"]))
             fits.append(float(parts["fit"]))
-    timed = times[a.warmup:]
+    return times, fits
+
+
+def run_ref_binary(a, binary: Path, tns: Path, R: int, order: int):
+    """cpTC on `tns` for warmup + steps iterations; (timed ms list, fits,
+    selector line, stdout) or raises RuntimeError with its exit status."""
+    env = dict(os.environ)
+    if order != 3:
+        # config 5's switches: HITS relabelling (3 rounds), dense units at
+        # the cutoff of the run
+        env.update({"GEN_REORDER": "hits", "GEN_REORDER_T": "3",
+                    "GEN_DENSE_THRESHOLD": str(a.threshold)})
+    iters = a.warmup + a.steps
+    r = subprocess.run([str(binary), str(tns), str(iters), str(R), str(a.threshold)],
+                       capture_output=True, text=True, env=env, timeout=1800)
+    if a.ref_log:
+        with open(a.ref_log, "a") as f:
+            f.write(f"=== R={R}\n" + r.stdout + "\n--- stderr ---\n" + r.stderr)
+    if r.returncode != 0:
+        raise RuntimeError(f"cpTC exited {r.returncode}: {r.stderr.strip()[-200:]}")
+    times, fits = parse_ref_log(r.stdout)
+    selector = next((ln for ln in r.stdout.splitlines() if "avg_fill=" in ln), "")
+    return times[a.warmup:], fits, selector
+
+
+def run_reference_port(a):
+    """Without cpTC's own build: the oracle's restatement of its order-3
+    CP-ALS on all host cores, one iteration (CADR and init included) of the
+    same tensor."""
+    import cptc_b200 as cp
+    from oracle import oracle as o
+
+    t = cp.gen_config(a.config, a.scale)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    o.cp_als3(t, a.rank, 1, thr=a.threshold, path="fp64", threads=threads)
+    v = time.perf_counter() - t0
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
+                      "higher_is_better": False, "n_gpus": 0, "steps": 1, "warmup": 0,
+                      "config": shared_config(a, t.nnz, t.dims),
+                      "cpu_baseline": {"kind": "port", "cores": threads, "value": v,
+                                       "unit": UNIT,
+                                       "sample": "one full CP-ALS iteration incl. CADR and init"},
+                      "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def run_reference(a):
+    """The reference arm runs programs only: this repository's standalone
+    generator (cptc_gen) writes the seeded tensor as .tns, then cpTC's own
+    driver, rebuilt from its unmodified sources, reads and decomposes it.
+    No library of this repository is loaded into this process."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    binary = ROOT / "oracle" / "_ref" / "cptc_opt"
+    gen = ROOT / "cptc_b200" / "_lib" / "cptc_gen"
+    if not binary.exists() or not gen.exists():
+        run_reference_port(a)
+        return
+    with tempfile.TemporaryDirectory() as d:
+        tns = Path(a.keep_tns) if a.keep_tns else Path(d) / "bench.tns"
+        g = subprocess.run([str(gen), str(a.config), repr(a.scale), str(tns)],
+                           capture_output=True, text=True, timeout=1800)
+        if g.returncode != 0:
+            print(json.dumps({"impl": "reference",
+                              "unavailable": f"cptc_gen exited {g.returncode}: "
+                                             f"{g.stderr.strip()[-200:]}"}))
+            return
+        info = json.loads(g.stdout.strip().splitlines()[-1])
+        order, nnz, dims = info["order"], info["nnz"], info["nominal_dims"]
+        try:
+            timed, fits, selector = run_ref_binary(a, binary, tns, a.rank, order)
+            r128 = None
+            if want_r128(a):
+                t128, f128, _ = run_ref_binary(a, binary, tns, 128, order)
+                r128 = {"ms_per_iter": float(np.mean(t128)) if t128 else None,
+                        "median_ms_per_iter": float(np.median(t128)) if t128 else None,
+                        "iters": len(t128), "final_fit": f128[-1] if f128 else None}
+        except RuntimeError as e:
+            print(json.dumps({"impl": "reference", "unavailable": str(e)}))
+            return
     v = float(np.mean(timed)) / 1000.0
-    med = float(np.median(timed)) if timed else None
-    selector = next((ln for ln in out.splitlines() if "avg_fill=" in ln), "")
+    med = float(np.median(timed)) / 1000.0 if timed else None
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
             "higher_is_better": False, "n_gpus": 1, "steps": len(timed), "warmup": a.warmup,
-            "ms_per_step": v * 1000.0, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f64+tf32", "data": "synthetic (same generator and seed)",
-            "config": {"workload": workload_name(a), "rank": a.rank, "nnz": t.nnz,
-                       "selector_line": selector[:300], "final_fit": fits[-1] if fits else None,
-                       "median_ms_per_step": med, "max_ms_per_step": max(timed) if timed else None},
+            "ms_per_step": v * 1000.0, "median": med, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f64+tf32",
+            "data": "synthetic (same generator and seed, written as .tns by cptc_gen)",
+            "config": shared_config(a, nnz, dims),
+            "detail": {"selector_line": selector[:300], "final_fit": fits[-1] if fits else None,
+                       "median_ms_per_step": med * 1000.0 if med else None,
+                       "max_ms_per_step": max(timed) if timed else None,
+                       "dims_read": info["dims"]},
+            "r128": r128,
             "cpu_baseline": {"kind": "reference", "cores": 1, "value": v, "unit": UNIT,
                              "sample": "zhixianzhu/cpTC sources rebuilt for sm_100a "
                                        "(oracle/build_ref.sh), one host thread driving one "

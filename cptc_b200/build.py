@@ -120,10 +120,24 @@ def build_cli(verbose: bool = False) -> Path:
     return out
 
 
+def build_gen(verbose: bool = False) -> Path:
+    """cptc_gen: the .tns generator as a self-contained executable (the
+    generator and writer sources compiled in, no library of this project
+    loaded at run time)."""
+    LIB.mkdir(exist_ok=True)
+    out = LIB / "cptc_gen"
+    srcs = [CSRC / "cli" / "cptc_gen.cpp", CSRC / "host" / "gen.cpp", CSRC / "host" / "tns.cpp"]
+    if _stale(out, srcs + _headers()):
+        _run(["g++", "-O3", "-std=c++17", "-fopenmp", f"-I{ROOT / 'include'}"]
+             + [str(s) for s in srcs] + ["-o", str(out)], verbose)
+    return out
+
+
 def build_all(verbose: bool = False) -> None:
     build_host(verbose)
     build_cuda(verbose)
     build_cli(verbose)
+    build_gen(verbose)
 
 
 if __name__ == "__main__":

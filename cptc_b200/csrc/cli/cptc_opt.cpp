@@ -10,9 +10,11 @@
 //   ALS_EXPORT_FACTORS, ALS_PROFILE,
 //   GEN_DENSE, GEN_DENSE_THRESHOLD, GEN_DENSE_INNER, GEN_REORDER,
 //   GEN_REORDER_T, GEN_REORDER_SAMPLE, GEN_SOLVER, GEN_SEED, GEN_DUMP,
-//   GEN_PROFILE, CPTC_DEVICE, CPTC_TNS_CACHE (binary copy of the parsed
-//   tensor beside the .tns, used while the text is unchanged), CPTC_NGPU
-//   (one process per GPU on devices CPTC_DEVICE.., NCCL between them).
+//   GEN_PROFILE, GEN_SELFTEST (the N-order dense-path known-answer test,
+//   src/generic.cu:1389-1637, then exit), CPTC_DEVICE, CPTC_TNS_CACHE
+//   (binary copy of the parsed tensor beside the .tns, used while the text
+//   is unchanged), CPTC_NGPU (one process per GPU on devices CPTC_DEVICE..,
+//   NCCL between them).
 // Output lines keep the reference's formats ("[ALS] iter i/N time=<ms> ms
 // fit=<f>", "[GEN] iter ... fit=", "[ALS] Lambda:", export files).
 #include <signal.h>
@@ -22,6 +24,7 @@
 
 #include <chrono>
 #include <cmath>
+#include <random>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -169,6 +172,128 @@ int reorder_of(const char* s) {
   return CPTC_REORDER_CADR;
 }
 
+// GEN_SELFTEST: the reference's known-answer test of the N-order dense path
+// (src/generic.cu:1389-1637).  The same order-4 tensor (40 x 24 x 36 x 3,
+// drawn from mt19937(1234) in the reference's order: two ~50%-full tiles per
+// outer slice, the partial corner tile at ~60%, 4000 scattered nonzeros),
+// the same factors, R = 8; for each inner-mode set and each pass (every
+// nonzero in dense units, then units at cutoff 0.01 plus the FP64 residual)
+// the engine's MTTKRP of every inner mode is compared with an exact host
+// MTTKRP by relative L2 error, bound 2e-3.  Returns the exit status.
+int run_selftest(int dev) {
+  const int N = 4, R = 8;
+  const int dims[4] = {40, 24, 36, 3};
+  std::vector<uint32_t> co[4];
+  std::vector<double> vals;
+  std::mt19937 gen(1234);
+  std::uniform_real_distribution<double> uv(0.0, 1.0);
+  auto add = [&](int i, int j, int k, int l, double v) {
+    co[0].push_back((uint32_t)i);
+    co[1].push_back((uint32_t)j);
+    co[2].push_back((uint32_t)k);
+    co[3].push_back((uint32_t)l);
+    vals.push_back(v);
+  };
+  const int tb[2][3] = {{0, 0, 0}, {1, 0, 1}};
+  for (int l = 0; l < dims[3]; ++l)
+    for (int t = 0; t < 2; ++t)
+      for (int a = 0; a < 16; ++a)
+        for (int b = 0; b < 16; ++b)
+          for (int c = 0; c < 16; ++c)
+            if (uv(gen) < 0.5) add(tb[t][0] * 16 + a, tb[t][1] * 16 + b, tb[t][2] * 16 + c, l, 1.0 + uv(gen));
+  for (int l = 0; l < dims[3]; ++l)
+    for (int a = 32; a < dims[0]; ++a)
+      for (int b = 16; b < dims[1]; ++b)
+        for (int c = 32; c < dims[2]; ++c)
+          if (uv(gen) < 0.6) add(a, b, c, l, 1.0 + uv(gen));
+  // The reference draws these five numbers as the arguments of one call,
+  // which its host compiler (g++) evaluates last argument first: the value,
+  // then the indices from the last mode to the first.
+  for (int e = 0; e < 4000; ++e) {
+    const double v = 1.0 + uv(gen);
+    const int l = (int)(uv(gen) * dims[3]) % dims[3];
+    const int k = (int)(uv(gen) * dims[2]) % dims[2];
+    const int j = (int)(uv(gen) * dims[1]) % dims[1];
+    const int i = (int)(uv(gen) * dims[0]) % dims[0];
+    add(i, j, k, l, v);
+  }
+  const size_t nnz = vals.size();
+  std::printf("[SELFTEST] N=%d dims=%d,%d,%d,%d nnz=%zu R=%d\n", N, dims[0], dims[1], dims[2],
+              dims[3], nnz, R);
+  std::vector<double> F[4];
+  for (int m = 0; m < N; ++m) {
+    F[m].resize((size_t)dims[m] * R);
+    for (double& x : F[m]) x = uv(gen);
+  }
+  std::vector<double> exact[4];
+  for (int n = 0; n < N; ++n) {
+    exact[n].assign((size_t)dims[n] * R, 0.0);
+    for (size_t e = 0; e < nnz; ++e)
+      for (int r = 0; r < R; ++r) {
+        double q = vals[e];
+        for (int m = 0; m < N; ++m)
+          if (m != n) q *= F[m][(size_t)co[m][e] * R + r];
+        exact[n][(size_t)co[n][e] * R + r] += q;
+      }
+  }
+  cptc_coo t{};
+  t.order = N;
+  t.nnz = nnz;
+  for (int m = 0; m < N; ++m) {
+    t.dims[m] = (uint64_t)dims[m];
+    t.idx[m] = co[m].data();
+  }
+  t.vals = vals.data();
+  cptc_ctx* c = nullptr;
+  int rc = cptc_create(&c, dev, 0);
+  if (rc) return fail(c, "cptc_create", rc);
+  if ((rc = cptc_load_coo(c, &t))) return fail(c, "load", rc);
+  int fails = 0;
+  const int sets[4][3] = {{0, 1, 2}, {1, 2, 3}, {0, 1, 3}, {0, 2, 3}};
+  for (int si = 0; si < 4; ++si)
+    for (int pass = 0; pass < 2; ++pass) {
+      const int* in = sets[si];
+      std::printf("[SELFTEST] --- inner=(%d,%d,%d) pass %d (%s) ---\n", in[0], in[1], in[2], pass,
+                  pass == 0 ? "dense-only" : "mixed dense+FP64");
+      cptc_opts o;
+      cptc_opts_default(&o);
+      o.generic = 1;
+      o.reorder = CPTC_REORDER_NONE;
+      o.dense_generic = 1;
+      // cutoff int(4096 * thr): 0 puts every unit on the dense path
+      o.dense_thr_generic = pass == 0 ? 1e-12 : 0.01;
+      for (int q = 0; q < 3; ++q) o.dense_inner[q] = in[q];
+      if ((rc = cptc_build(c, R, 0.03, &o))) return fail(c, "build", rc);
+      for (int m = 0; m < N; ++m)
+        if ((rc = cptc_set_factors(c, m, F[m].data()))) return fail(c, "set_factors", rc);
+      cptc_stats st;
+      cptc_get_stats(c, &st);
+      std::printf("[SELFTEST]   units=%llu dense_nnz=%llu (%.1f%%)\n",
+                  (unsigned long long)st.dense_tiles, (unsigned long long)st.dense_nnz,
+                  100.0 * (double)st.dense_nnz / (double)nnz);
+      for (int q = 0; q < 3; ++q) {
+        const int n = in[q];
+        std::vector<double> got((size_t)dims[n] * R);
+        if ((rc = cptc_mttkrp(c, n, got.data()))) return fail(c, "mttkrp", rc);
+        double num = 0.0, den = 0.0;
+        for (size_t i = 0; i < got.size(); ++i) {
+          const double d = got[i] - exact[n][i];
+          num += d * d;
+          den += exact[n][i] * exact[n][i];
+        }
+        const double rel = den > 0.0 ? std::sqrt(num / den) : 0.0;
+        const bool ok = rel < 2e-3;
+        std::printf("[SELFTEST]   mode %d: relative L2 error = %.3e  %s\n", n, rel,
+                    ok ? "OK" : "FAIL");
+        if (!ok) ++fails;
+      }
+    }
+  std::printf("[SELFTEST] %s (%d failures)\n", fails ? "FAILED" : "PASSED", fails);
+  std::fflush(stdout);
+  cptc_destroy(c);
+  return fails ? 1 : 0;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -181,6 +306,8 @@ int main(int argc, char** argv) {
   if (argc > 4) threshold = std::atof(argv[4]);
   if (iters <= 0) iters = 1;
   if (R <= 0) R = 1;
+  if (env("GEN_SELFTEST"))  // src/main.cu:89-91: the known-answer test, then exit
+    return run_selftest(env("CPTC_DEVICE") ? std::atoi(env("CPTC_DEVICE")) : 0);
 
   // The ranks are forked before anything else runs (no OpenMP pool, no CUDA
   // context exists yet); each parses the tensor itself.
@@ -286,11 +413,20 @@ int main(int argc, char** argv) {
   cptc_get_stats(c, &st);
   std::printf("[Main] build (reorder + partition + views) = %g ms\n", st.build_ms);
   if (!generic) {
-    std::printf("[Main] density check: dense_nnz=%llu sparse_nnz=%llu tiles=%llu avg_fill=%g "
-                "(threshold %g) -> %s\n",
+    // The reference's selector line (src/main.cu:408-416), same labels and
+    // texts: dense/sparse nonzeros, tiles, mean tile fill, dense nonzeros
+    // weighted by the fill, the dense share, the threshold, the chosen path
+    // (TF32 tiles + FP64 residual, or FP64 only).
+    const double eff_dense = (double)st.dense_nnz * st.avg_fill;
+    const double dense_ratio =
+        st.nnz > 0 ? (double)st.dense_nnz / (double)(st.dense_nnz + st.sparse_nnz) : 0.0;
+    std::printf("[Main] 稠密度检测: dense_nnz=%llu sparse_nnz=%llu "
+                "tiles=%llu avg_fill=%g eff_dense=%g dense_ratio=%g (阈值 %g) -> %s\n",
                 (unsigned long long)st.dense_nnz, (unsigned long long)st.sparse_nnz,
-                (unsigned long long)st.dense_tiles, st.avg_fill, st.fill_min,
-                st.tf32_path ? "TF32 dense tiles + FP64 residual" : "FP64 only");
+                (unsigned long long)st.dense_tiles, st.avg_fill, eff_dense, dense_ratio,
+                st.fill_min,
+                st.tf32_path ? "双流串行(WMMA+FP64)"
+                             : "纯 CUDA core(全 FP64)");
     std::printf("[ALS] Starting CP-ALS: rank=%d, max_iters=%d\n", R, iters);
   } else {
     std::printf("[GEN] N-order CP-ALS: order=%d R=%d iters=%d nnz=%llu\n", order, R, iters,

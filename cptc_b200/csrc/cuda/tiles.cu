@@ -624,6 +624,18 @@ bool tiles_nw2() {
 
 }  // namespace
 
+// The 2-n-tile shape covers R/8 n-tiles with at most 4 warp groups only up
+// to R = 64; larger ranks keep the 4-n-tile shape.
+static bool use_nw2(int R) { return tiles_nw2() && R / 8 <= 8; }
+
+// k_tiles splits the R/8 n-tiles into ceil(NT/NW) groups over its 4 warps;
+// more than 4 groups would leave every warp without a slab group.
+static void require_tile_shape(int R, int NW) {
+  const int NT = R / 8;
+  CPTC_REQUIRE(NW >= 1 && (NT + NW - 1) / NW <= 4, CPTC_E_UNSUP,
+               "tile kernel shape: more n-tile groups than warps");
+}
+
 uint32_t tile_blocks_for(int R, int device, uint64_t ntiles, bool share_sms) {
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
@@ -637,7 +649,7 @@ uint32_t tile_blocks_for(int R, int device, uint64_t ntiles, bool share_sms) {
   const size_t smem = tile_smem(R);
   const int NT = R / 8;
   const int ntm = NT < 4 ? NT : 4;
-  auto kern = tiles_nw2() ? (ntm == 1 ? k_tiles<0, 1, 2, 1, 5> : k_tiles<0, 1, 2, 2, 5>)
+  auto kern = use_nw2(R) ? (ntm == 1 ? k_tiles<0, 1, 2, 1, 5> : k_tiles<0, 1, 2, 2, 5>)
               : ntm == 1  ? k_tiles<0, 1, 2, 1, 4>
               : ntm == 2  ? k_tiles<0, 1, 2, 2, 4>
               : ntm == 3  ? k_tiles<0, 1, 2, 3, 4>
@@ -696,6 +708,7 @@ void launch_mttkrp_tiles3(const TileArgs& a_in, const uint32_t* order, const uin
   // registers, spills at 4 n-tiles per warp) on config 4, 4 is faster.
 #define CPTC_TILES(TS_, CS_, SS_, NTM, MINB_)                                              \
   do {                                                                                     \
+    require_tile_shape(R, NTM);                                                            \
     auto kern = k_tiles<TS_, CS_, SS_, NTM, MINB_>;                                        \
     CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                                    (int)smem));                                            \
@@ -705,7 +718,7 @@ void launch_mttkrp_tiles3(const TileArgs& a_in, const uint32_t* order, const uin
   } while (0)
 #define CPTC_TILES_R(TS_, CS_, SS_)                          \
   do {                                                       \
-    if (tiles_nw2()) {                                       \
+    if (use_nw2(R)) {                                        \
       if (ntm == 1) CPTC_TILES(TS_, CS_, SS_, 1, 5);         \
       else CPTC_TILES(TS_, CS_, SS_, 2, 5);                  \
     } else if (ntm == 1) CPTC_TILES(TS_, CS_, SS_, 1, 4);    \

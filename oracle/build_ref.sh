@@ -1,13 +1,13 @@
 #!/bin/bash
 # Builds the reference CP-ALS program (zhixianzhu/cpTC) from its own sources,
 # unmodified, for sm_100a, into oracle/_ref/cptc_opt.  Test and baseline
-# infrastructure only.  Needs the reference tree (REF_DIR); machines without
-# it use the prebuilt binary.
+# infrastructure only.  The caller names the reference tree in REF_DIR;
+# machines without it use the prebuilt binary.
 #   - MAGMA is replaced by oracle/refstub/magma_v2.h (only dead code uses it)
 #   - oracle/refstub/preinclude.h adds <cstdint> for include/generic.hpp
 set -euo pipefail
 HERE="$(cd "$(dirname "$0")" && pwd)"
-REF_DIR="${REF_DIR:-/root/reference}"
+: "${REF_DIR:?set REF_DIR to the reference source tree}"
 OUT="$HERE/_ref"
 if [ ! -d "$REF_DIR/src" ]; then
   echo "reference sources not found at $REF_DIR" >&2

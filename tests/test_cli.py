@@ -73,6 +73,11 @@ def test_cli_order3_tf32_matches_reference(gpu, tmp_path):
     assert len(fits) == g["iters"]
     assert np.max(np.abs(fits - np.array(g["fits"]))) < 1e-5
     assert "[ALS] Lambda:" in out and "[ALS] Final RMSE=" in out
+    # the selector line up to the threshold is the reference's, character for
+    # character (the threshold itself is this build's B200 rule)
+    ref_sel = next(ln for ln in g["notes"] if "avg_fill=" in ln)
+    sel = next(ln for ln in out.splitlines() if "avg_fill=" in ln)
+    assert sel.split(" (")[0] == ref_sel.split(" (")[0]
     head = (tmp_path / "exp.0.out").read_text().split("\n")[:3]
     assert head == ["matrix", "2", f"{t.dims[0]} {g['R']}"]
     lam = (tmp_path / "exp.lambda.out").read_text().split()
@@ -131,3 +136,63 @@ def test_cli_two_gpus_match_one(gpu, tmp_path):
     assert len(two) == len(one) == g["iters"]
     assert np.max(np.abs(two - one)) < 1e-8
     assert two_out.count("[ALS] Final RMSE=") == 1
+
+
+def _selftest_counts(txt):
+    """(inner set, pass) -> (units, dense_nnz) from GEN_SELFTEST output."""
+    out, key = {}, None
+    for ln in txt.splitlines():
+        m = re.search(r"inner=\((\d),(\d),(\d)\) pass (\d)", ln)
+        if m:
+            key = (m.group(1) + m.group(2) + m.group(3), int(m.group(4)))
+        m = re.search(r"units=(\d+) dense_nnz=(\d+)", ln)
+        if m and key is not None:
+            out[key] = (int(m.group(1)), int(m.group(2)))
+    return out
+
+
+@pytest.mark.gpu
+def test_cli_selftest_known_answers(gpu):
+    # GEN_SELFTEST=1: the reference's own known-answer test of the N-order
+    # dense path on the same tensor (mt19937(1234); nnz 16827 as the
+    # reference prints it).  Every inner-mode set passes here, including the
+    # three the reference's kernel fails, with the reference's unit counts.
+    r = subprocess.run([str(CLI)], env=dict(os.environ, GEN_SELFTEST="1"),
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+    assert "[SELFTEST] N=4 dims=40,24,36,3 nnz=16827 R=8" in r.stdout
+    assert "[SELFTEST] PASSED (0 failures)" in r.stdout
+    assert r.stdout.count("OK") == 24
+    ref = _selftest_counts((GOLD / "selftest.txt").read_text())
+    got = _selftest_counts(r.stdout)
+    assert set(got) == set(ref)
+    assert got == ref
+
+
+def test_cli_density_line_text():
+    # the selector line keeps the reference's labels (src/main.cu:408-416),
+    # which scripts grep for
+    src = (ROOT / "cptc_b200" / "csrc" / "cli" / "cptc_opt.cpp").read_text()
+    assert "[Main] 稠密度检测: dense_nnz=" in src
+    assert "(阈值 %g) -> %s" in src
+    assert "双流串行(WMMA+FP64)" in src and "纯 CUDA core(全 FP64)" in src
+    for label in ("sparse_nnz=", "tiles=", "avg_fill=", "eff_dense=", "dense_ratio="):
+        assert label in src
+
+
+def test_generator_executable_matches_library(tmp_path):
+    # cptc_gen writes the tensor cptc_gen_config makes (the reference arm of
+    # bench.py feeds it to the reference's driver)
+    gen = ROOT / "cptc_b200" / "_lib" / "cptc_gen"
+    p = tmp_path / "g.tns"
+    r = subprocess.run([str(gen), "3", "0.002", str(p)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr
+    info = json.loads(r.stdout.strip().splitlines()[-1])
+    t = cp.gen_config(3, 0.002)
+    u = cp.read_tns(p)
+    assert info["nnz"] == t.nnz == u.nnz and info["nominal_dims"] == list(t.dims)
+    assert info["dims"] == list(u.dims)
+    for m in range(3):
+        assert np.array_equal(u.idx[m], t.idx[m])
+    assert np.array_equal(u.vals, t.vals)

@@ -5,6 +5,8 @@ Tolerances are the reference's own bounds: FP64 paths 1e-12 relative
 and final fit 1e-4 absolute.  Norm-wise relative error is used for the FP64
 MTTKRP: || got - ref || / || ref ||.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -338,3 +340,115 @@ def test_sharded_factor_upload_on_one_gpu(gpu):
             assert np.array_equal(e.factor(m), F[m])
             assert np.array_equal(e.factor(m, sharded=True), F[m])
         e.close()
+
+
+def _block(rng, lo, ext, fill):
+    """Distinct cells of the box [lo, lo + ext) at the given fill."""
+    cells = np.array(np.meshgrid(*[np.arange(l, l + e) for l, e in zip(lo, ext)],
+                                 indexing="ij")).reshape(len(lo), -1).T
+    return cells[rng.random(len(cells)) < fill]
+
+
+def _distinct(dims, parts, rng, values="lognormal"):
+    c = np.unique(np.concatenate(parts).astype(np.uint64) @ np.array(
+        [np.prod(dims[m + 1:], dtype=np.uint64) for m in range(len(dims))], dtype=np.uint64))
+    idx, rest = [], c
+    for m in range(len(dims) - 1, -1, -1):
+        idx.append((rest % np.uint64(dims[m])).astype(np.uint32))
+        rest = rest // np.uint64(dims[m])
+    idx = idx[::-1]
+    v = rng.lognormal(0.0, 1.0, len(c)) if values == "lognormal" else rng.standard_normal(len(c))
+    return cp.CooTensor(tuple(dims), idx, v)
+
+
+@pytest.mark.parametrize("path", ["fp64", "tf32"])
+def test_mttkrp_modes_beyond_32768(gpu, oracle, path):
+    # Mode lengths 70000 and 40000 (the reference packs coordinates into 15-bit
+    # fields and drops the residual beyond 32767, src/partition.cu:1896-1906):
+    # a uniform residual plus dense blocks at coordinates >= 32768, one of
+    # them the partial last block of mode 1 (300 = 18*16 + 12)
+    rng = np.random.default_rng(31)
+    dims = (70000, 300, 40000)
+    parts = [np.stack([rng.integers(0, d, 150_000) for d in dims], axis=1),
+             _block(rng, (69984, 288, 39984), (16, 12, 16), 0.6),
+             _block(rng, (32768, 0, 32768), (16, 16, 16), 0.5),
+             _block(rng, (40000, 100, 16), (32, 16, 16), 0.4)]
+    t = _distinct(dims, parts, rng)
+    R = 32
+    e = engine_for(t, R, path=path, threshold=0.03, reorder="none")
+    F = rand_factors(t.dims, R)
+    for m in range(3):
+        e.set_factor(m, F[m])
+    if path == "tf32":
+        st = e.stats()
+        ps = oracle.partition_stats3(t, thr=0.03)
+        assert st["tf32_path"] == 1 and st["dense_tiles"] == ps["tiles"] == 6
+        assert st["dense_nnz"] == ps["dense_nnz"]
+    for n in range(3):
+        got = e.mttkrp(n)
+        exact = oracle.mttkrp(t, F, n, threads=8)
+        if path == "fp64":
+            assert rel(got, exact) < FP64_TOL, n
+        else:
+            hyb, _ = oracle.mttkrp_hybrid3(t, F, n, thr=0.03, threads=8)
+            assert rel(got, hyb) < 1e-5, n
+            nz = exact != 0.0
+            assert np.max(np.abs(got - exact)[nz] / np.abs(exact)[nz]) < 2e-3, n
+
+
+@pytest.mark.parametrize("dense", [False, True])
+def test_mttkrp_order4_mode_beyond_32768(gpu, oracle, dense):
+    # order 4 with a 40000-row mode, FP64 records, and dense units over the
+    # inner modes (0, 1, 2) with a block at rows >= 32768
+    rng = np.random.default_rng(32)
+    dims = (40000, 30, 20, 25)
+    parts = [np.stack([rng.integers(0, d, 80_000) for d in dims], axis=1)]
+    for l in range(3):
+        b = _block(rng, (36000, 0, 0), (16, 16, 16), 0.5)
+        parts.append(np.concatenate([b, np.full((len(b), 1), l)], axis=1))
+    t = _distinct(dims, parts, rng)
+    R = 16
+    e = engine_for(t, R, dense_generic=dense, reorder="none")
+    assert e.stats()["tf32_path"] == (1 if dense else 0)
+    F = rand_factors(t.dims, R)
+    for m in range(4):
+        e.set_factor(m, F[m])
+    for n in range(4):
+        got = e.mttkrp(n)
+        exact = oracle.mttkrp(t, F, n, threads=8)
+        if not dense:
+            assert rel(got, exact) < FP64_TOL, n
+        else:
+            nz = exact != 0.0
+            assert np.max(np.abs(got - exact)[nz] / np.abs(exact)[nz]) < 2e-3, n
+
+
+def test_mttkrp_full_size_config4_entrywise(gpu, oracle):
+    # Config 4 at full size (76.9M nonzeros), R=32, hybrid path, mode 2: every
+    # entry against the oracle's TF32 emulation (1e-5 norm-wise) and against
+    # the exact FP64 MTTKRP (2e-3 per entry).  The tensor is relabelled with
+    # the oracle's restatement of the reference's CADR, so the partition is
+    # the reference's (81,886 tiles, 37,821,322 residual nonzeros).
+    t = cp.gen_config(4)
+    dims = tuple(int(i.max()) + 1 for i in t.idx)
+    idx = []
+    for m in range(3):
+        perm = oracle.cadr_perm(dims[m], t.idx[m]).astype(np.uint32)
+        idx.append(perm[t.idx[m]])
+    u = cp.CooTensor(dims, idx, t.vals)
+    R = 32
+    e = engine_for(u, R, path="tf32", threshold=0.03, reorder="none")
+    st = e.stats()
+    assert st["dense_tiles"] == 81886 and st["sparse_nnz"] == 37821322
+    F = rand_factors(u.dims, R, seed=9)
+    for m in range(3):
+        e.set_factor(m, F[m])
+    got = e.mttkrp(2)
+    e.close()
+    threads = os.cpu_count() or 8
+    hyb, _ = oracle.mttkrp_hybrid3(u, F, 2, thr=0.03, threads=threads)
+    assert rel(got, hyb) < 1e-5
+    exact = oracle.mttkrp(u, F, 2, threads=threads)
+    nz = exact != 0.0
+    assert np.max(np.abs(got - exact)[nz] / np.abs(exact)[nz]) < 2e-3
+    assert np.all(got[~nz] == 0.0)
