@@ -29,6 +29,7 @@ CUDA_SRCS = [
     "cuda/views.cu",
     "cuda/mttkrp_sparse.cu",
     "cuda/tiles.cu",
+    "cuda/tiles_pool.cu",
     "cuda/units.cu",
     "cuda/als_kernels.cu",
     "cuda/comm.cu",

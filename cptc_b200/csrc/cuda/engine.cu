@@ -61,16 +61,6 @@ __global__ void k_permute_rows(const double* __restrict__ in, const uint32_t* __
 
 }  // namespace
 
-// CPTC_OVERLAP_TILES=1: the tile and residual kernels of a mode run side by
-// side (Engine::mttkrp).
-static bool overlap_tiles() {
-  static const bool v = [] {
-    const char* e = std::getenv("CPTC_OVERLAP_TILES");
-    return e && e[0] == '1';
-  }();
-  return v;
-}
-
 double b200_fill_min(int R) {
   if (R <= 32) return 0.07;
   if (R >= 128) return 0.04;
@@ -89,9 +79,6 @@ Engine::Engine(int dev) : device(dev) {
   evc = ev;
   CPTC_CUDA(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming));
   CPTC_CUDA(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming));
-  CPTC_CUDA(cudaStreamCreateWithFlags(&tstream, cudaStreamNonBlocking));
-  CPTC_CUDA(cudaEventCreateWithFlags(&ev_tfork, cudaEventDisableTiming));
-  CPTC_CUDA(cudaEventCreateWithFlags(&ev_tjoin, cudaEventDisableTiming));
   CPTC_CUDA(cudaMallocHost((void**)&h_scal, 16 * sizeof(double)));
 }
 
@@ -115,12 +102,6 @@ Engine::~Engine() {
         if (e) cudaEventDestroy(e);
   if (ev_fork) cudaEventDestroy(ev_fork);
   if (ev_join) cudaEventDestroy(ev_join);
-  if (ev_tfork) cudaEventDestroy(ev_tfork);
-  if (ev_tjoin) cudaEventDestroy(ev_tjoin);
-  if (tstream) {
-    cudaStreamSynchronize(tstream);
-    cudaStreamDestroy(tstream);
-  }
   if (h_scal) cudaFreeHost(h_scal);
   if (side) cudaStreamDestroy(side);
   if (stream) cudaStreamDestroy(stream);
@@ -133,9 +114,11 @@ uint64_t Engine::device_bytes() const {
     b += v.gw.bytes() + v.oidx.bytes() + v.val.bytes() + v.rec.bytes() + v.rows.bytes() +
          v.task_row.bytes();
   b += units.unit.bytes() + units.start.bytes() + units.lid.bytes() + units.val.bytes() +
-       units.outer_idx.bytes();
-  for (int m = 0; m < 3; ++m) b += units.order[m].bytes();
-  b += FtV.bytes() + FtV2.bytes() + FtF.bytes() + Ainv.bytes() + gpart.bytes() + dots.bytes() +
+       units.outer_idx.bytes() + units.words.bytes() + units.pstart.bytes();
+  for (int m = 0; m < 3; ++m)
+    b += units.order[m].bytes() + units.vtile[m].bytes() + units.vstart[m].bytes();
+  b += Ftf.bytes();
+  b += FtV.bytes() + FtF.bytes() + Ainv.bytes() + gpart.bytes() + dots.bytes() +
        lambda.bytes();
   return b;
 }
@@ -224,8 +207,6 @@ void Engine::alloc_workspace() {
   uint64_t maxd = 0;
   for (int m = 0; m < N; ++m) maxd = std::max<uint64_t>(maxd, padded_rows(m));
   FtV.alloc(maxd * (uint64_t)R);
-  if (overlap_tiles()) FtV2.alloc(maxd * (uint64_t)R);
-  else FtV2.release();
   FtF.alloc((uint64_t)R * R);
   Ainv.alloc(2 * (uint64_t)R * R + 1);
   gpart_blocks = 148;
@@ -236,6 +217,8 @@ void Engine::alloc_workspace() {
   scal.alloc(8);
   status.alloc(1);
   lambda.alloc(R);
+  if (dense_active && !generic) Ftf.alloc(maxd * (uint64_t)R);
+  else Ftf.release();
   for (int m = 0; m < N; ++m) {
     F[m].alloc(padded_rows(m) * (uint64_t)R);
     CPTC_CUDA(cudaMemsetAsync(F[m].p, 0, padded_rows(m) * (uint64_t)R * sizeof(double), stream));
@@ -320,9 +303,18 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
   comm_prepare(*this);
   alloc_workspace();
   for (int t = 0; t < 3; ++t) units.cnt[t] = units.nunits;
-  if (dense_active) {
-    units.blocks = tile_blocks_for(R, device, units.nunits / (uint64_t)nranks, overlap_tiles());
-    for (int t = 0; t < 3; ++t) tile_cuts(*this, t);
+  if (dense_active && !generic) {
+    // order 3: the packed word pool (tiles_pool.cu)
+    units.blocks = tile3w_blocks_for(R, device, units.nunits / (uint64_t)nranks);
+    for (int t = 0; t < 3; ++t) {
+      tile_cuts(*this, t, tile3w_fixed_cost(R));
+      tile_visit_lists(*this, t);
+    }
+  } else if (dense_active) {
+    // N-order units: a tile weighs its nonzeros plus 512 (zeroing the tile
+    // and the 16 slab products, in nonzero units)
+    units.blocks = tile_blocks_for(R, device, units.nunits / (uint64_t)nranks);
+    for (int t = 0; t < 3; ++t) tile_cuts(*this, t, 512ull);
   }
   for (int n = 0; n < N; ++n) {
     // Residual-only views for modes the dense tiles cover as a target.
@@ -530,22 +522,6 @@ bool Engine::tiles_target(int mode) const {
 void Engine::mttkrp(int mode) {
   const uint64_t n = padded_rows(mode) * (uint64_t)R;
   CPTC_CUDA(cudaMemsetAsync(FtV.p, 0, n * sizeof(double), stream));
-  if (overlap_tiles() && FtV2.p && tiles_target(mode)) {
-    // The two kernels side by side: the residual kernel waits on its row
-    // gathers and the tile kernel on its own latency, so each can fill the
-    // other's idle issue slots.  The residual kernel writes rows it owns
-    // with plain read-modify-writes, so the tiles go to a buffer of their
-    // own, added afterwards.
-    CPTC_CUDA(cudaMemsetAsync(FtV2.p, 0, n * sizeof(double), stream));
-    CPTC_CUDA(cudaEventRecord(ev_tfork, stream));
-    CPTC_CUDA(cudaStreamWaitEvent(tstream, ev_tfork, 0));
-    mttkrp_tiles(mode, FtV2.p, tstream);
-    CPTC_CUDA(cudaEventRecord(ev_tjoin, tstream));
-    mttkrp_sparse(mode);
-    CPTC_CUDA(cudaStreamWaitEvent(stream, ev_tjoin, 0));
-    launch_add_into(FtV.p, FtV2.p, n, stream);
-    return;
-  }
   // The residual kernel first: its many short CTAs rebalance around an SM
   // that the side stream's inverse may hold; the persistent tile grid is
   // launched once that SM is free again.
@@ -559,6 +535,30 @@ void Engine::mttkrp_tiles(int mode, double* out, cudaStream_t s) {
   for (int q = 0; q < 3; ++q)
     if (units.inner[q] == mode) ts = q;
   if (ts < 0 || units.cnt[ts] == 0) return;
+  cudaStream_t st = s ? s : stream;
+  double* dst = out ? out : FtV.p;
+  const uint32_t* cut = units.cut[ts].p + (uint64_t)rank * units.blocks;
+  if (!generic) {
+    // Order-3 roles (src/dense.cu:339-1075): mode 0 contracts j in TF32
+    // and weights k-slabs; mode 1 contracts i, weights k; mode 2 contracts
+    // i, weights j.
+    Tile3Args ta{};
+    ta.vtile = units.vtile[ts].p;
+    ta.vstart = units.vstart[ts].p;
+    ta.words = units.words.p;
+    ta.ntiles = units.cnt[ts];
+    ta.R = R;
+    ta.tslot = ts;
+    ta.cslot = (ts == 0) ? 1 : 0;
+    ta.sslot = (ts == 2) ? 1 : 2;
+    for (int q = 0; q < 3; ++q) ta.dims[q] = dims[q];
+    launch_to_tf32(F[ta.cslot].p, dims[ta.cslot] * (uint64_t)R, Ftf.p, st);
+    ta.Fct = Ftf.p;
+    ta.Fs = F[ta.sslot].p;
+    ta.out = dst;
+    launch_tiles3w(ta, cut, units.blocks, st);
+    return;
+  }
   TileArgs ta{};
   ta.tile = units.unit.p;
   ta.start = units.start.p;
@@ -567,17 +567,9 @@ void Engine::mttkrp_tiles(int mode, double* out, cudaStream_t s) {
   ta.ntiles = units.cnt[ts];
   ta.R = R;
   ta.tslot = ts;
-  if (!generic) {
-    // Order-3 roles (src/dense.cu:339-1075): mode 0 contracts j in TF32
-    // and weights k-slabs; mode 1 contracts i, weights k; mode 2 contracts
-    // i, weights j.
-    ta.cslot = (ts == 0) ? 1 : 0;
-    ta.sslot = (ts == 2) ? 1 : 2;
-  } else {
-    // N-order roles (src/generic.cu:486-487): fold slot t+1, weight t+2.
-    ta.cslot = (ts + 1) % 3;
-    ta.sslot = (ts + 2) % 3;
-  }
+  // N-order roles (src/generic.cu:486-487): fold slot t+1, weight t+2.
+  ta.cslot = (ts + 1) % 3;
+  ta.sslot = (ts + 2) % 3;
   for (int q = 0; q < 3; ++q) ta.dims[q] = dims[units.inner[q]];
   ta.Fc = F[units.inner[ta.cslot]].p;
   ta.Fs = F[units.inner[ta.sslot]].p;
@@ -585,9 +577,8 @@ void Engine::mttkrp_tiles(int mode, double* out, cudaStream_t s) {
   ta.outer_idx = units.outer_idx.p;
   for (int q = 0; q < units.nouter; ++q) ta.Fout[q] = F[units.outer[q]].p;
   ta.store_dups = units.store_dups ? 1 : 0;
-  ta.out = out ? out : FtV.p;
-  launch_mttkrp_tiles3(ta, units.order[ts].p, units.cut[ts].p + (uint64_t)rank * units.blocks,
-                       units.blocks, s ? s : stream);
+  ta.out = dst;
+  launch_mttkrp_tiles3(ta, units.order[ts].p, cut, units.blocks, st);
 }
 
 void Engine::mttkrp_sparse(int mode) {

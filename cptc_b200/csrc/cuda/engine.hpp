@@ -65,8 +65,18 @@ struct UnitPool {
   DArray<int4> unit;           // x,y,z tile block coords of the inner modes, w = count
   DArray<uint64_t> start;      // first element of each tile in the pool
   DArray<uint32_t> outer_idx;  // nunits x nouter (unit-major)
-  DArray<uint16_t> lid;        // (l0 << 8) | (l1 << 4) | l2
-  DArray<double> val;
+  DArray<uint16_t> lid;        // N-order units: (l0 << 8) | (l1 << 4) | l2
+  DArray<double> val;          // N-order units: values
+  // Order-3 tiles: one word per nonzero, the value as TF32 bits (sign,
+  // exponent, top 10 mantissa bits) with the 12-bit local id in the low bits
+  // the TF32 truncation clears; each tile's words start on a 16-byte
+  // boundary (pstart, in words; the gap words are zero and never read as
+  // nonzeros).
+  DArray<uint32_t> words;
+  DArray<uint32_t> pstart;
+  // Per target slot, the tiles and their word starts in visiting order.
+  DArray<int4> vtile[3];
+  DArray<uint32_t> vstart[3];
   DArray<uint32_t> order[3];   // visiting order per inner target slot
   uint64_t cnt[3] = {0, 0, 0}; // tiles per inner target slot
   // CTA ranges over each visiting order with balanced nonzero counts:
@@ -106,11 +116,6 @@ struct Engine {
   // other modes' Grams and so runs beside that mode's MTTKRP.
   cudaStream_t side = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
-  // CPTC_OVERLAP_TILES=1 (for measurement): the dense-tile kernel runs on
-  // its own stream into FtV2 beside the residual kernel, then FtV += FtV2.
-  cudaStream_t tstream = nullptr;
-  cudaEvent_t ev_tfork = nullptr, ev_tjoin = nullptr;
-  DArray<double> FtV2;
   // One ALS iteration captured as a CUDA graph (rebuilt after load, build
   // and communicator changes).
   // Two of them, for two iterations in flight (slot = iteration parity),
@@ -165,6 +170,9 @@ struct Engine {
   DArray<double> G[CPTC_MAX_ORDER];
   DArray<double> lambda;
   DArray<double> FtV, FtF, Ainv, gpart, dots, scal, cscale;
+  // The contracted factor of an order-3 tile launch as TF32 bit patterns
+  // (float, max_m I_m x R), written just before the launch.
+  DArray<float> Ftf;
   DArray<int> status;
   double* h_scal = nullptr;  // pinned, 16 doubles: two readback slots of 8
   int gpart_blocks = 0;

@@ -54,14 +54,41 @@ struct TileArgs {
 };
 // order: tile visiting order for this mode (sorted by target block);
 // cut: blocks+1 CTA range starts over `order` (balanced by nonzeros).
+// N-order units (outer weights, duplicates summed).
 void launch_mttkrp_tiles3(const TileArgs& a, const uint32_t* order, const uint32_t* cut,
                           uint32_t blocks, cudaStream_t s);
-// CTAs the tile kernel runs for rank R (shared-memory occupancy x SMs).
-// share_sms: one wave using at most half of the CTAs an SM holds, leaving
-// room for the residual kernel running beside it.
-uint32_t tile_blocks_for(int R, int device, uint64_t ntiles, bool share_sms = false);
-// Balanced CTA ranges over E.units.order[slot] (fills E.units.cut[slot]).
-void tile_cuts(Engine& E, int slot);
+
+// Order-3 dense tiles from the packed word pool (UnitPool::words): the
+// tiles of target slot `tslot` in visiting order (vtile, vstart), CTA
+// ranges `cut` over that order.  Fct is the contracted factor as TF32 bit
+// patterns, Fs the FP64 weighting factor.
+struct Tile3Args {
+  const int4* vtile;       // x,y,z = block coords of modes 0,1,2, w = count
+  const uint32_t* vstart;  // first word of each tile (a multiple of 4)
+  const uint32_t* words;   // TF32 value bits | (l0 << 8) | (l1 << 4) | l2
+  uint64_t ntiles;
+  int R;
+  int tslot, cslot, sslot;
+  uint64_t dims[3];
+  const float* Fct;
+  const double* Fs;
+  double* out;
+};
+void launch_tiles3w(const Tile3Args& a, const uint32_t* cut, uint32_t blocks, cudaStream_t s);
+// CTAs of one launch of launch_tiles3w (waves of what the SMs hold at once).
+uint32_t tile3w_blocks_for(int R, int device, uint64_t ntiles);
+// out[i] = F[i] as a TF32 bit pattern (float, low 13 mantissa bits cleared).
+void launch_to_tf32(const double* F, uint64_t n, float* out, cudaStream_t s);
+// Per-tile cost of launch_tiles3w in nonzero units (CTA range balancing).
+unsigned long long tile3w_fixed_cost(int R);
+// Order-3 pool packing (after partition_tiles3) and visit lists per slot.
+void pack_tile_words(Engine& E);
+void tile_visit_lists(Engine& E, int slot);
+// CTAs the N-order unit kernel runs for rank R (occupancy x SMs, waves).
+uint32_t tile_blocks_for(int R, int device, uint64_t ntiles);
+// Balanced CTA ranges over E.units.order[slot] (fills E.units.cut[slot]),
+// a tile weighing its nonzeros plus `fixed`.
+void tile_cuts(Engine& E, int slot, unsigned long long fixed);
 // Partition of Engine::tiles + residual selection (tiles.cu).
 void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64_t& nsel);
 // Views (views.cu).

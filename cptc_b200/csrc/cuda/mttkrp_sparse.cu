@@ -656,28 +656,6 @@ void launch(const MttkrpArgs& a, cudaStream_t s) {
   CPTC_LAUNCH_CHECK();
 }
 
-// Alternative lane shape at R=32 for measurement: CPTC_REC3_R32=8x4 runs
-// 8-lane groups of 4 ranks (four nonzeros per warp instruction instead of
-// two, so the record decode and row addressing are shared by more work, at
-// more registers per thread).  Default: 16-lane groups of 2 ranks.
-int rec3_r32_variant() {
-  static const int v = [] {
-    const char* e = std::getenv("CPTC_REC3_R32");
-    return (e && std::strcmp(e, "8x4") == 0) ? 1 : 0;
-  }();
-  return v;
-}
-
-// At R=128, CPTC_REC3_R128=u2 keeps two nonzeros' rows in flight per warp
-// (at most 128 registers, 2 CTAs per SM) instead of one.
-int rec3_r128_variant() {
-  static const int v = [] {
-    const char* e = std::getenv("CPTC_REC3_R128");
-    return (e && std::strcmp(e, "u2") == 0) ? 1 : 0;
-  }();
-  return v;
-}
-
 }  // namespace
 
 void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
@@ -700,15 +678,9 @@ void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
     switch (a.R) {
       case 8: launch_rec3s<8, 1, 4, 1>(a, s); return;
       case 16: launch_rec3s<8, 2, 2, 4>(a, s); return;
-      case 32:
-        if (rec3_r32_variant() == 1) launch_rec3s<8, 4, 2, 3>(a, s);
-        else launch_rec3s<16, 2, 2, 4>(a, s);
-        return;
+      case 32: launch_rec3s<16, 2, 2, 4>(a, s); return;
       case 64: launch_rec3s<16, 4, 2, 1, true>(a, s); return;
-      case 128:
-        if (rec3_r128_variant() == 1) launch_rec3s<32, 4, 2, 2, true>(a, s);
-        else launch_rec3s<32, 4, 1, 1, true>(a, s);
-        return;
+      case 128: launch_rec3s<32, 4, 1, 1, true>(a, s); return;
       default: break;
     }
     if (a.R <= 32) launch_rec3<32, 1, false, 4>(a, s);

@@ -540,7 +540,8 @@ void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64
     CPTC_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, xb, c64.p, P.start.p, (int64_t)ntiles, s));
     if (xb > temp.bytes()) temp.alloc(xb);
     CPTC_CUDA(cub::DeviceScan::ExclusiveSum(temp.p, xb, c64.p, P.start.p, (int64_t)ntiles, s));
-    // Per-mode visiting order: by target block (stable).
+    // Per-mode visiting order: by target block (stable).  (The order-3 pool
+    // is packed into words after this, pack_tile_words.)
     for (int m = 0; m < 3; ++m) {
       DArray<uint32_t> ka(ntiles), kb(ntiles), ia(ntiles);
       P.order[m].alloc(ntiles);
@@ -556,6 +557,7 @@ void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64
     }
   }
   CPTC_CUDA(cudaStreamSynchronize(s));
+  pack_tile_words(E);
 }
 
 namespace {
@@ -573,18 +575,6 @@ __global__ void k_tile_weights(const int4* __restrict__ tile, const uint32_t* __
   for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < n;
        k += (uint64_t)gridDim.x * blockDim.x)
     w[k] = (unsigned long long)tile[order[k]].w + fixed;
-}
-
-// 512 by default.  The per-tile and per-nonzero costs fitted on configs 2-4
-// (a + b*nnz: R=16 4.1 + 0.0053, R=32 6 + 0.005, R=128 20 + 0.012 ns) put
-// a/b at 770-1670; CPTC_TILE_FIXED_COST overrides the constant for that
-// comparison.
-unsigned long long tile_fixed_cost() {
-  if (const char* e = std::getenv("CPTC_TILE_FIXED_COST")) {
-    const long long v = std::atoll(e);
-    if (v >= 0) return (unsigned long long)v;
-  }
-  return 512ull;
 }
 
 // cut[c] = first k whose inclusive prefix exceeds c * total / blocks.
@@ -608,26 +598,6 @@ __global__ void k_tile_cuts(const unsigned long long* __restrict__ pre, uint64_t
 
 }  // namespace
 
-namespace {
-
-// CPTC_TILES_SHAPE=nw2 (for measurement): at most 2 n-tiles per warp and 5
-// resident CTAs per SM (96 registers, no spills) instead of 4 n-tiles and 4
-// CTAs (128 registers): more warps to hide latency, each slab's A fragments
-// read by two warps instead of one at R=32.
-bool tiles_nw2() {
-  static const bool v = [] {
-    const char* e = std::getenv("CPTC_TILES_SHAPE");
-    return e && std::strcmp(e, "nw2") == 0;
-  }();
-  return v;
-}
-
-}  // namespace
-
-// The 2-n-tile shape covers R/8 n-tiles with at most 4 warp groups only up
-// to R = 64; larger ranks keep the 4-n-tile shape.
-static bool use_nw2(int R) { return tiles_nw2() && R / 8 <= 8; }
-
 // k_tiles splits the R/8 n-tiles into ceil(NT/NW) groups over its 4 warps;
 // more than 4 groups would leave every warp without a slab group.
 static void require_tile_shape(int R, int NW) {
@@ -636,7 +606,7 @@ static void require_tile_shape(int R, int NW) {
                "tile kernel shape: more n-tile groups than warps");
 }
 
-uint32_t tile_blocks_for(int R, int device, uint64_t ntiles, bool share_sms) {
+uint32_t tile_blocks_for(int R, int device, uint64_t ntiles) {
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   // A whole number of waves of the CTAs the SMs hold at once (registers
@@ -649,8 +619,7 @@ uint32_t tile_blocks_for(int R, int device, uint64_t ntiles, bool share_sms) {
   const size_t smem = tile_smem(R);
   const int NT = R / 8;
   const int ntm = NT < 4 ? NT : 4;
-  auto kern = use_nw2(R) ? (ntm == 1 ? k_tiles<0, 1, 2, 1, 5> : k_tiles<0, 1, 2, 2, 5>)
-              : ntm == 1  ? k_tiles<0, 1, 2, 1, 4>
+  auto kern = ntm == 1  ? k_tiles<0, 1, 2, 1, 4>
               : ntm == 2  ? k_tiles<0, 1, 2, 2, 4>
               : ntm == 3  ? k_tiles<0, 1, 2, 3, 4>
                           : k_tiles<0, 1, 2, 4, 4>;
@@ -659,7 +628,6 @@ uint32_t tile_blocks_for(int R, int device, uint64_t ntiles, bool share_sms) {
   int per_sm = 0;
   CPTC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem));
   if (per_sm < 1) per_sm = 1;
-  if (share_sms) return (uint32_t)sms * (uint32_t)((per_sm + 1) / 2);
   const uint64_t wave = (uint64_t)sms * per_sm;
   uint64_t waves = ntiles / (wave * 16);
   if (waves < 1) waves = 1;
@@ -667,7 +635,7 @@ uint32_t tile_blocks_for(int R, int device, uint64_t ntiles, bool share_sms) {
   return (uint32_t)(wave * waves);
 }
 
-void tile_cuts(Engine& E, int slot) {
+void tile_cuts(Engine& E, int slot, unsigned long long fixed) {
   UnitPool& U = E.units;
   const uint64_t n = U.cnt[slot];
   // One set of `blocks` CTA ranges per rank, cut over the whole visiting
@@ -680,7 +648,7 @@ void tile_cuts(Engine& E, int slot) {
   }
   DArray<unsigned long long> w(n), pre(n);
   k_tile_weights<<<grid_for(n, 256, 148 * 16), 256, 0, E.stream>>>(U.unit.p, U.order[slot].p, n,
-                                                                   tile_fixed_cost(), w.p);
+                                                                   fixed, w.p);
   CPTC_LAUNCH_CHECK();
   size_t tb = 0;
   CPTC_CUDA(cub::DeviceScan::InclusiveSum(nullptr, tb, w.p, pre.p, (int64_t)n, E.stream));
@@ -718,10 +686,7 @@ void launch_mttkrp_tiles3(const TileArgs& a_in, const uint32_t* order, const uin
   } while (0)
 #define CPTC_TILES_R(TS_, CS_, SS_)                          \
   do {                                                       \
-    if (use_nw2(R)) {                                        \
-      if (ntm == 1) CPTC_TILES(TS_, CS_, SS_, 1, 5);         \
-      else CPTC_TILES(TS_, CS_, SS_, 2, 5);                  \
-    } else if (ntm == 1) CPTC_TILES(TS_, CS_, SS_, 1, 4);    \
+    if (ntm == 1) CPTC_TILES(TS_, CS_, SS_, 1, 4);           \
     else if (ntm == 2) CPTC_TILES(TS_, CS_, SS_, 2, 4);      \
     else if (ntm == 3) CPTC_TILES(TS_, CS_, SS_, 3, 4);      \
     else CPTC_TILES(TS_, CS_, SS_, 4, 4);                    \
