@@ -69,6 +69,7 @@ class Stats(C.Structure):
         ("fiber_mode", C.c_int * MAX_ORDER),
         ("nranks", C.c_int),
         ("rank_id", C.c_int),
+        ("reorder_ms", C.c_double),
     ]
 
 

@@ -33,7 +33,8 @@ CUDA_SRCS = [
     "cuda/units.cu",
     "cuda/als_kernels.cu",
     "cuda/comm.cu",
-    "cuda/peer.cu",
+    "cuda/shard.cu",
+    "cuda/reorder_gpu.cu",
     "cuda/engine.cu",
     "cuda/noalloc.cu",
 ]

@@ -82,8 +82,9 @@ __global__ void __launch_bounds__(256) k_gram_partial(const double* __restrict__
 // the block adds partials w, w + 8, w + 16, ... for 32 consecutive entries
 // (coalesced), then the 8 warp sums are added in warp order.  One block per
 // 32 entries, so an R x R Gram (R = 128: 512 blocks) is reduced across the GPU.
+// out[i] = (add ? out[i] : 0) + sum over the nblk partials, in a fixed order.
 __global__ void __launch_bounds__(256) k_partial_sum(const double* __restrict__ part, int nblk,
-                                                     int len, double* __restrict__ out) {
+                                                     int len, double* __restrict__ out, int add) {
   __shared__ double sh[8][32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int i = blockIdx.x * 32 + lane;
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(256) k_partial_sum(const double* __restrict__ 
     double t = 0.0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) t += sh[k][lane];
-    out[i] = t;
+    out[i] = add ? out[i] + t : t;
   }
 }
 
@@ -552,7 +553,12 @@ int launch_gram_partial(const double* F, uint64_t rows, int R, double* part, int
 }
 
 void launch_partial_sum(const double* part, int nblk, int len, double* out, cudaStream_t s) {
-  k_partial_sum<<<(unsigned)((len + 31) / 32), 256, 0, s>>>(part, nblk, len, out);
+  k_partial_sum<<<(unsigned)((len + 31) / 32), 256, 0, s>>>(part, nblk, len, out, 0);
+  CPTC_LAUNCH_CHECK();
+}
+
+void launch_partial_sum_add(const double* part, int nblk, int len, double* out, cudaStream_t s) {
+  k_partial_sum<<<(unsigned)((len + 31) / 32), 256, 0, s>>>(part, nblk, len, out, 1);
   CPTC_LAUNCH_CHECK();
 }
 

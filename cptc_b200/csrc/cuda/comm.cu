@@ -35,7 +35,6 @@ void comm_init(Engine& E, const unsigned char idb[128], int rank, int nranks) {
   CPTC_REQUIRE(nranks >= 1 && rank >= 0 && rank < nranks, CPTC_E_ARG, "bad rank / nranks");
   CPTC_CUDA(cudaSetDevice(E.device));
   E.release_graph();  // it may hold NCCL calls on the old communicator
-  peer_unmap(E);      // collective over the old communicator
   comm_destroy(E);
   if (nranks == 1) {
     E.nranks = 1;
@@ -71,39 +70,59 @@ uint64_t slab_rows(const Engine& E, int m) {
 }
 
 void comm_prepare(Engine& E) {
-  for (int m = 0; m < E.N; ++m) E.slab[m].clear();
-  if (E.nranks == 1) return;
   for (int m = 0; m < E.N; ++m) {
-    const uint64_t s = slab_rows(E, m);
-    std::vector<uint64_t> cuts(E.nranks + 1);
-    for (int r = 0; r <= E.nranks; ++r) cuts[r] = std::min<uint64_t>((uint64_t)r * s, E.dims[m]);
-    E.slab[m] = cuts;
+    E.slab[m].clear();
+    E.slab_blocks[m].clear();
+    E.heavy_rows[m] = 0;
   }
 }
 
-const double* comm_reduce_gram_gather(Engine& E, int n, int nblk, int ndots) {
+namespace {
+
+// In-place broadcast of every rank's published rows [row_lo(q), row_hi(q))
+// of `base` from rank q (inside an NCCL group): together an all-gather of
+// slabs of unequal length.
+void broadcast_slabs(Engine& E, int n, double* base) {
+  const int H = (int)E.heavy_rows[n];
+  for (int q = 0; q < E.nranks; ++q) {
+    const uint64_t lo = std::max<uint64_t>(E.slab[n][q], (uint64_t)H);
+    const uint64_t hi = std::max<uint64_t>(E.slab[n][q + 1], (uint64_t)H);
+    if (hi <= lo) continue;
+    double* p = base + lo * (uint64_t)E.R;
+    CPTC_NCCL(ncclBroadcast(p, p, (hi - lo) * (uint64_t)E.R, ncclDouble, q, comm_of(E), E.stream));
+  }
+}
+
+}  // namespace
+
+double* comm_exchange_mode(Engine& E, int n, int nblk, int ndots) {
   const int RR = E.R * E.R;
   double* out = E.comm_buf.p;
   launch_partial_sum(E.gpart.p, nblk, RR, out, E.stream);
-  if (ndots > 0) launch_partial_sum(E.dots.p, ndots, E.R, out + RR, E.stream);
+  if (ndots >= 0) launch_partial_sum(E.dots.p, ndots, E.R, out + RR, E.stream);
   if (E.nranks > 1) {
-    const uint64_t cnt = slab_rows(E, n) * (uint64_t)E.R;
-    double* F = E.F[n].p;
+    const uint64_t H = E.heavy_rows[n];
     CPTC_NCCL(ncclGroupStart());
-    CPTC_NCCL(ncclAllReduce(out, out, RR + (ndots > 0 ? E.R : 0), ncclDouble, ncclSum, comm_of(E),
+    CPTC_NCCL(ncclAllReduce(out, out, RR + (ndots >= 0 ? E.R : 0), ncclDouble, ncclSum, comm_of(E),
                             E.stream));
-    CPTC_NCCL(ncclAllGather(F + (uint64_t)E.rank * cnt, F, cnt, ncclDouble, comm_of(E), E.stream));
+    if (H > 0)
+      CPTC_NCCL(ncclAllReduce(E.FtV.p, E.FtV.p, H * (uint64_t)E.R, ncclDouble, ncclSum, comm_of(E),
+                              E.stream));
+    broadcast_slabs(E, n, E.F[n].p);
     CPTC_NCCL(ncclGroupEnd());
   }
   return out;
 }
 
-void comm_reduce_scatter_ftv(Engine& E, int n) {
+void comm_reduce_ftv(Engine& E, int n) {
   if (E.nranks == 1) return;
-  const uint64_t cnt = slab_rows(E, n) * (uint64_t)E.R;
-  // In place: rank r's slab of the summed result lands at FtV + r * cnt.
-  CPTC_NCCL(ncclReduceScatter(E.FtV.p, E.FtV.p + (uint64_t)E.rank * cnt, cnt, ncclDouble, ncclSum,
-                              comm_of(E), E.stream));
+  const uint64_t H = E.heavy_rows[n];
+  CPTC_NCCL(ncclGroupStart());
+  if (H > 0)
+    CPTC_NCCL(ncclAllReduce(E.FtV.p, E.FtV.p, H * (uint64_t)E.R, ncclDouble, ncclSum, comm_of(E),
+                            E.stream));
+  broadcast_slabs(E, n, E.FtV.p);
+  CPTC_NCCL(ncclGroupEnd());
 }
 
 void comm_allgather_rows(Engine& E, int n, double* base) {
@@ -111,18 +130,6 @@ void comm_allgather_rows(Engine& E, int n, double* base) {
   const uint64_t cnt = slab_rows(E, n) * (uint64_t)E.R;
   CPTC_NCCL(ncclAllGather(base + (uint64_t)E.rank * cnt, base, cnt, ncclDouble, comm_of(E),
                           E.stream));
-}
-
-static void allgather_slabs(Engine& E, int n, double* base) {
-  if (E.nranks == 1) return;
-  const uint64_t cnt = slab_rows(E, n) * (uint64_t)E.R;
-  CPTC_NCCL(ncclAllGather(base + (uint64_t)E.rank * cnt, base, cnt, ncclDouble, comm_of(E),
-                          E.stream));
-}
-
-void comm_reduce_ftv(Engine& E, int n) {
-  comm_reduce_scatter_ftv(E, n);
-  allgather_slabs(E, n, E.FtV.p);
 }
 
 }  // namespace cptc

@@ -87,10 +87,6 @@ Engine::~Engine() {
   if (stream) cudaStreamSynchronize(stream);
   if (side) cudaStreamSynchronize(side);
   release_graph();  // before the communicator its NCCL nodes use
-  try {
-    peer_unmap(*this);  // collective when the peer exchange is mapped
-  } catch (...) {
-  }
   comm_destroy(*this);
   for (auto& e : ev)
     if (e) cudaEventDestroy(e);
@@ -163,22 +159,22 @@ void Engine::load(const cptc_coo* t) {
 }
 
 void Engine::reorder() {
+  const auto t0 = std::chrono::steady_clock::now();
   perm.assign(N, {});
   int kind = opts.reorder;
-  if (!generic) {
-    // Order-3 hybrid pipeline: CADR unless explicitly disabled.
-    if (kind == CPTC_REORDER_DEFAULT) kind = CPTC_REORDER_CADR;
-    if (kind == CPTC_REORDER_CADR) {
-      for (int m = 0; m < N; ++m) cadr_perm_ref(dims[m], nnz, host_idx[m].data(), perm[m]);
-    } else if (kind != CPTC_REORDER_NONE) {
-      std::vector<const uint32_t*> ip(N);
-      for (int m = 0; m < N; ++m) ip[m] = host_idx[m].data();
-      reorder_generic(N, dims, nnz, ip.data(), kind, opts.reorder_rounds, opts.reorder_sample,
-                      perm, &reorder_note);
-      perm.resize(N);
-    }
-  } else {
-    if (kind == CPTC_REORDER_DEFAULT) kind = (N >= 4) ? CPTC_REORDER_HITS : CPTC_REORDER_CADR;
+  if (!generic && kind == CPTC_REORDER_DEFAULT) kind = CPTC_REORDER_CADR;
+  if (generic && kind == CPTC_REORDER_DEFAULT)
+    kind = (N >= 4) ? CPTC_REORDER_HITS : CPTC_REORDER_CADR;
+  if (!generic && kind == CPTC_REORDER_CADR) {
+    // Order-3 CADR: the reference's unstable std::sort decides the order of
+    // equal degrees, so the permutation is made by the same call on the host.
+    for (int m = 0; m < N; ++m) cadr_perm_ref(dims[m], nnz, host_idx[m].data(), perm[m]);
+  } else if (kind == CPTC_REORDER_HITS) {
+    gpu_hits(*this, opts.reorder_rounds, opts.reorder_sample, perm);
+  } else if (kind == CPTC_REORDER_CADR) {
+    gpu_degree_rank(*this, perm);  // N-order CADR: ties by index
+  } else if (kind == CPTC_REORDER_AUTO) {
+    // probe of the tile fill before and after HITS (host, sampled)
     std::vector<const uint32_t*> ip(N);
     for (int m = 0; m < N; ++m) ip[m] = host_idx[m].data();
     reorder_generic(N, dims, nnz, ip.data(), kind, opts.reorder_rounds, opts.reorder_sample,
@@ -195,6 +191,7 @@ void Engine::reorder() {
     CPTC_LAUNCH_CHECK();
     CPTC_CUDA(cudaStreamSynchronize(stream));
   }
+  reorder_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
 }
 
 // Factor-shaped buffers hold nranks equal slabs (padding rows past I_m are
@@ -236,12 +233,10 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
   R = R_;
   generic = (N != 3) || opts.generic;
   release_graph();
-  peer_unmap(*this);  // its mappings point at the buffers rebuilt below
   CPTC_REQUIRE(opts.exchange == CPTC_EXCHANGE_NCCL || opts.exchange == CPTC_EXCHANGE_PEER,
                CPTC_E_ARG, "unknown exchange");
-  CPTC_REQUIRE(opts.exchange == CPTC_EXCHANGE_NCCL || nranks == 1 ||
-                   (nranks <= kMaxPeers && nccl != nullptr),
-               CPTC_E_UNSUP, "the peer exchange needs 2 to 8 ranks");
+  CPTC_REQUIRE(opts.exchange == CPTC_EXCHANGE_NCCL || nranks == 1, CPTC_E_UNSUP,
+               "the ranks exchange through NCCL (one grouped call per mode update)");
   built = false;
   have_factors = false;
   views.clear();
@@ -300,20 +295,37 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
   }
   dense_active = tf32;
   views.resize(N);
-  comm_prepare(*this);
+  comm_prepare(*this);  // transfer slabs; one rank: the whole modes
+  // Several ranks: rows of every mode in slabs, each rank keeping only the
+  // nonzeros and tiles of its rows and its share of the heavy prefix.
+  if (nranks > 1) shard_plan(*this, sel.p, nsel);
   alloc_workspace();
   for (int t = 0; t < 3; ++t) units.cnt[t] = units.nunits;
+  if (dense_active && nranks > 1) {
+    for (int t = 0; t < 3; ++t) {
+      DArray<uint32_t> mine;
+      units.cnt[t] = shard_tiles(*this, t, mine);
+      units.order[t] = std::move(mine);
+    }
+  }
+  uint64_t most = 0;
+  for (int t = 0; t < 3; ++t) most = std::max<uint64_t>(most, units.cnt[t]);
   if (dense_active && !generic) {
     // order 3: the packed word pool (tiles_pool.cu)
-    units.blocks = tile3w_blocks_for(R, device, units.nunits / (uint64_t)nranks);
+    units.blocks = tile3w_blocks_for(R, device, most);
     for (int t = 0; t < 3; ++t) {
       tile_cuts(*this, t, tile3w_fixed_cost(R));
       tile_visit_lists(*this, t);
+      if (nranks > 1) compact_slot_pool(*this, t);
+    }
+    if (nranks > 1) {
+      units.words.release();
+      units.pstart.release();
     }
   } else if (dense_active) {
     // N-order units: a tile weighs its nonzeros plus 512 (zeroing the tile
     // and the 16 slab products, in nonzero units)
-    units.blocks = tile_blocks_for(R, device, units.nunits / (uint64_t)nranks);
+    units.blocks = tile_blocks_for(R, device, most);
     for (int t = 0; t < 3; ++t) tile_cuts(*this, t, 512ull);
   }
   for (int n = 0; n < N; ++n) {
@@ -322,47 +334,19 @@ void Engine::build(int R_, double threshold, const cptc_opts* o) {
                          (n == units.inner[0] || n == units.inner[1] || n == units.inner[2]);
     const uint32_t* base = covered ? sel.p : nullptr;
     const uint64_t nbase = covered ? nsel : nnz;
-    build_view(*this, views[n], n, base, nbase);
-    // This rank's share: an equal range of the nonzero-balanced tasks.
-    View& v = views[n];
-    v.t0 = v.ntasks * (uint64_t)rank / (uint64_t)nranks;
-    v.t1 = v.ntasks * (uint64_t)(rank + 1) / (uint64_t)nranks;
-    if (nranks > 1) split_tasks_by_cost(v);
+    if (nranks > 1) {
+      DArray<uint32_t> mine;
+      const uint64_t nm = shard_select(*this, n, base, nbase, mine);
+      build_view(*this, views[n], n, mine.p, nm);
+    } else {
+      build_view(*this, views[n], n, base, nbase);
+    }
+    views[n].t0 = 0;
+    views[n].t1 = views[n].ntasks;
   }
   CPTC_CUDA(cudaStreamSynchronize(stream));
-  if (nranks > 1 && opts.exchange == CPTC_EXCHANGE_PEER) peer_map(*this);
   build_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   built = true;
-}
-
-// With CPTC_TASK_ROW_COST = c > 0 (for measurement; default 0 keeps equal
-// task counts) the ranks' task ranges are cut at equal cost, a task costing
-// its nonzeros plus c per target row it touches (each row end is a flush of
-// R sums).  Every rank computes the same cut points from the same view.
-void Engine::split_tasks_by_cost(View& v) {
-  static const double row_cost = [] {
-    const char* e = std::getenv("CPTC_TASK_ROW_COST");
-    return e ? std::atof(e) : 0.0;
-  }();
-  if (!(row_cost > 0.0) || v.ntasks < (uint64_t)nranks) return;
-  std::vector<uint32_t> tr(v.ntasks);
-  CPTC_CUDA(cudaMemcpyAsync(tr.data(), v.task_row.p, v.ntasks * sizeof(uint32_t),
-                            cudaMemcpyDeviceToHost, stream));
-  CPTC_CUDA(cudaStreamSynchronize(stream));
-  std::vector<double> pre(v.ntasks + 1, 0.0);
-  for (uint64_t t = 0; t < v.ntasks; ++t) {
-    const uint64_t first = t * (uint64_t)v.task;
-    const uint64_t n_t = std::min<uint64_t>(v.task, v.nnz - first);
-    const uint64_t next = (t + 1 < v.ntasks) ? tr[t + 1] : v.nrows - 1;
-    const double rows_t = (double)(next - tr[t] + 1);
-    pre[t + 1] = pre[t] + (double)n_t + row_cost * rows_t;
-  }
-  auto cut = [&](int r) -> uint64_t {  // first task whose prefix reaches r/G of the cost
-    const double target = pre[v.ntasks] * (double)r / (double)nranks;
-    return (uint64_t)(std::lower_bound(pre.begin(), pre.end(), target) - pre.begin());
-  };
-  v.t0 = rank == 0 ? 0 : std::min<uint64_t>(cut(rank), v.ntasks);
-  v.t1 = rank == nranks - 1 ? v.ntasks : std::min<uint64_t>(cut(rank + 1), v.ntasks);
 }
 
 double* Engine::scal_tmp() {
@@ -520,8 +504,16 @@ bool Engine::tiles_target(int mode) const {
 
 // FtV = MTTKRP of `mode` (relabelled rows): zero, dense tiles, residual.
 void Engine::mttkrp(int mode) {
-  const uint64_t n = padded_rows(mode) * (uint64_t)R;
-  CPTC_CUDA(cudaMemsetAsync(FtV.p, 0, n * sizeof(double), stream));
+  if (nranks == 1) {
+    CPTC_CUDA(cudaMemsetAsync(FtV.p, 0, dims[mode] * (uint64_t)R * sizeof(double), stream));
+  } else {
+    // the rows this rank's nonzeros can reach: the heavy prefix and its slab
+    const uint64_t H = heavy_rows[mode], lo = row_lo(mode), hi = row_hi(mode);
+    if (H > 0) CPTC_CUDA(cudaMemsetAsync(FtV.p, 0, H * (uint64_t)R * sizeof(double), stream));
+    if (hi > lo)
+      CPTC_CUDA(cudaMemsetAsync(FtV.p + lo * (uint64_t)R, 0,
+                                (hi - lo) * (uint64_t)R * sizeof(double), stream));
+  }
   // The residual kernel first: its many short CTAs rebalance around an SM
   // that the side stream's inverse may hold; the persistent tile grid is
   // launched once that SM is free again.
@@ -537,7 +529,7 @@ void Engine::mttkrp_tiles(int mode, double* out, cudaStream_t s) {
   if (ts < 0 || units.cnt[ts] == 0) return;
   cudaStream_t st = s ? s : stream;
   double* dst = out ? out : FtV.p;
-  const uint32_t* cut = units.cut[ts].p + (uint64_t)rank * units.blocks;
+  const uint32_t* cut = units.cut[ts].p;
   if (!generic) {
     // Order-3 roles (src/dense.cu:339-1075): mode 0 contracts j in TF32
     // and weights k-slabs; mode 1 contracts i, weights k; mode 2 contracts
@@ -545,7 +537,7 @@ void Engine::mttkrp_tiles(int mode, double* out, cudaStream_t s) {
     Tile3Args ta{};
     ta.vtile = units.vtile[ts].p;
     ta.vstart = units.vstart[ts].p;
-    ta.words = units.words.p;
+    ta.words = units.swords[ts].p ? units.swords[ts].p : units.words.p;
     ta.ntiles = units.cnt[ts];
     ta.R = R;
     ta.tslot = ts;
@@ -644,12 +636,11 @@ void Engine::update_mode(int n, bool last) {
   CPTC_CUDA(cudaEventRecordWithFlags(evc[2 * n], stream, rf));
   mttkrp(n);
   CPTC_CUDA(cudaEventRecordWithFlags(evc[2 * n + 1], stream, rf));
-  if (peer.on) peer_reduce_scatter_ftv(*this, n);
-  else comm_reduce_scatter_ftv(*this, n);
-  phase_end(0);
   CPTC_CUDA(cudaStreamWaitEvent(stream, ev_join, 0));
+  phase_end(0);
+  const int div = generic ? 0 : 1;
   const uint64_t lo = row_lo(n), rows = row_hi(n) - lo;
-  const int nb = launch_apply_solve(FtV.p + lo * R, Ainv.p, lambda.p, generic ? 0 : 1, rows, R,
+  const int nb = launch_apply_solve(FtV.p + lo * R, Ainv.p, lambda.p, div, rows, R,
                                     F[n].p + lo * R, gpart.p, gpart_blocks, stream);
   // The last mode also yields the fit's column dot products, taken on the
   // solved (not yet normalised) rows and scaled with the column scales.
@@ -657,10 +648,22 @@ void Engine::update_mode(int n, bool last) {
                                         gpart_blocks, stream)
                       : 0;
   phase_end(1);
-  // One all-reduce (Gram partials, dot products) grouped with the all-gather
-  // of the solved slab; every rank then normalises the whole factor.
-  const double* gsum = peer.on ? peer_reduce_gram_gather(*this, n, nb, nd)
-                               : comm_reduce_gram_gather(*this, n, nb, nd);
+  // The Gram partial (and fit dots) summed over blocks and ranks; with
+  // several ranks grouped with the all-reduce of the heavy prefix's partial
+  // MTTKRP and the broadcast of every rank's solved slab.
+  double* gsum = comm_exchange_mode(*this, n, nb, last ? nd : -1);
+  const uint64_t H = heavy_rows[n];
+  if (H > 0) {
+    // The heavy prefix, now summed over the ranks, is solved by every rank
+    // (the same bits everywhere) and its Gram and dots added once.
+    const int nbh = launch_apply_solve(FtV.p, Ainv.p, lambda.p, div, H, R, F[n].p, gpart.p,
+                                       gpart_blocks, stream);
+    launch_partial_sum_add(gpart.p, nbh, R * R, gsum, stream);
+    if (last) {
+      const int ndh = launch_col_dots(F[n].p, FtV.p, H, R, dots.p, gpart_blocks, stream);
+      launch_partial_sum_add(dots.p, ndh, R, gsum + (size_t)R * R, stream);
+    }
+  }
   phase_end(2);
   launch_norm_finalize(gsum, 1, R, generic ? 1 : 0, lambda.p, G[n].p, colscale(), stream);
   launch_scale_cols(F[n].p, dims[n], R, colscale(), stream);
@@ -799,9 +802,6 @@ void Engine::finish_iteration(int it, int slot, cptc_iter_cb cb, void* user) {
   std::memcpy(&h_status, hs + 4, sizeof(int));
   if (h_status != 0) {
     cudaStreamSynchronize(stream);  // the next iteration may be in flight
-    if (h_status & kStatusPeerTimeout)
-      throw CptcError(CPTC_E_COMM, "a peer barrier timed out (a rank is missing or stalled); "
-                                   "the exchange stays broken until the next cptc_build");
     throw CptcError(CPTC_E_NUMERIC, "non-finite values in the R x R solve");
   }
   const double xn = std::sqrt(x_norm_sq);
@@ -1129,6 +1129,7 @@ int cptc_get_stats(cptc_ctx* c, cptc_stats* s) {
       s->fiber_mode[m] = e.views[m].nout > 0 ? e.views[m].omode[0] : -1;
     s->nranks = e.nranks;
     s->rank_id = e.rank;
+    s->reorder_ms = e.reorder_ms;
   });
 }
 

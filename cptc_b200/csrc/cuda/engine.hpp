@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -77,37 +78,19 @@ struct UnitPool {
   // Per target slot, the tiles and their word starts in visiting order.
   DArray<int4> vtile[3];
   DArray<uint32_t> vstart[3];
+  // Several ranks: each slot's own tiles copied into a pool of their own
+  // (vstart[slot] then indexes swords[slot]); one rank: the shared pool.
+  DArray<uint32_t> swords[3];
   DArray<uint32_t> order[3];   // visiting order per inner target slot
   uint64_t cnt[3] = {0, 0, 0}; // tiles per inner target slot
-  // CTA ranges over each visiting order with balanced nonzero counts:
-  // nranks * blocks + 1 cut points; rank r launches `blocks` CTAs on
-  // cut[r * blocks .. (r + 1) * blocks].
+  // CTA ranges over each visiting order with balanced estimated costs:
+  // blocks + 1 cut points.
   DArray<uint32_t> cut[3];
   uint32_t blocks = 0;
 };
 
 // Default fill-rate threshold of the dense-tile path on B200 for rank R.
 double b200_fill_min(int R);
-
-// Peer-memory exchange (cptc_opts.exchange = CPTC_EXCHANGE_PEER): every
-// rank's buffers mapped into this process with CUDA IPC.
-constexpr int kMaxPeers = 8;
-constexpr int kStatusPeerTimeout = 2;  // status bit: a peer barrier ran out of time
-struct PeerState {
-  bool on = false;
-  int G = 1;
-  int slot_stride = 0;                 // doubles per rank's slot: R*R + R
-  DArray<double> recv;                 // G regions of one slab: partial MTTKRP rows
-  DArray<unsigned char> arena;         // flags | epoch, broken | G slots
-  double* F_of[CPTC_MAX_ORDER][kMaxPeers] = {};
-  double* recv_of[kMaxPeers] = {};
-  unsigned char* arena_of[kMaxPeers] = {};
-  std::vector<void*> opened;           // imported mappings, closed at teardown
-  unsigned long long timeout_ns = 0;
-  // Rows [lo, hi) of each mode that rank q's share of the MTTKRP can write.
-  uint64_t rows_lo[CPTC_MAX_ORDER][kMaxPeers] = {};
-  uint64_t rows_hi[CPTC_MAX_ORDER][kMaxPeers] = {};
-};
 
 struct Engine {
   int device = 0;
@@ -162,6 +145,7 @@ struct Engine {
   double avg_fill = 0.0, fill_min = 0.0;
   int cutoff = 0;
   double build_ms = 0.0;
+  double reorder_ms = 0.0;
 
   // Factors (relabelled space) and ALS workspace.
   bool have_factors = false;
@@ -178,12 +162,16 @@ struct Engine {
   int gpart_blocks = 0;
   double last_iprod = 0.0, last_model2 = 0.0, last_fit = 0.0;
 
-  // Multi-GPU: mode-n rows [slab[n][r], slab[n][r+1]) belong to rank r.
+  // Multi-GPU (shard.cu, comm.cu): mode-n rows [slab[n][r], slab[n][r+1])
+  // belong to rank r, in 16-row blocks [slab_blocks[n][r], ..[r+1]); the
+  // first heavy_rows[n] rows (inside rank 0's slab) are a heavy prefix
+  // whose nonzeros every rank shares and whose rows every rank solves.
   void* nccl = nullptr;  // ncclComm_t
   int nranks = 1, rank = 0;
   std::vector<uint64_t> slab[CPTC_MAX_ORDER];
+  std::vector<uint64_t> slab_blocks[CPTC_MAX_ORDER];
+  uint64_t heavy_rows[CPTC_MAX_ORDER] = {0};
   DArray<double> comm_buf;
-  PeerState peer;
 
   cudaEvent_t ev[2 * CPTC_MAX_ORDER + 2] = {};
 
@@ -215,8 +203,13 @@ struct Engine {
   void mttkrp_sparse(int mode);  // FP64 view part only (accumulates)
   void als(int iters, cptc_iter_cb cb, void* user);
   uint64_t device_bytes() const;
-  uint64_t row_lo(int m) const { return slab[m].empty() ? 0 : slab[m][rank]; }
-  uint64_t row_hi(int m) const { return slab[m].empty() ? dims[m] : slab[m][rank + 1]; }
+  // Rows this rank solves and publishes: its slab without the heavy prefix.
+  uint64_t row_lo(int m) const {
+    return slab[m].empty() ? 0 : std::max<uint64_t>(slab[m][rank], heavy_rows[m]);
+  }
+  uint64_t row_hi(int m) const {
+    return slab[m].empty() ? dims[m] : std::max<uint64_t>(slab[m][rank + 1], heavy_rows[m]);
+  }
   double* scal_tmp();
   double* colscale();
 
@@ -224,7 +217,6 @@ struct Engine {
   void reorder();
   void alloc_workspace();
   void update_mode(int n, bool last);
-  void split_tasks_by_cost(View& v);
   void gram_of(int m);
 };
 

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <vector>
 
 #include "engine.hpp"
 
@@ -84,6 +85,8 @@ unsigned long long tile3w_fixed_cost(int R);
 // Order-3 pool packing (after partition_tiles3) and visit lists per slot.
 void pack_tile_words(Engine& E);
 void tile_visit_lists(Engine& E, int slot);
+// Visit lists of `slot` from a visiting order of n tile indices.
+void tile_visit_lists_from(Engine& E, int slot, const uint32_t* order, uint64_t n);
 // CTAs the N-order unit kernel runs for rank R (occupancy x SMs, waves).
 uint32_t tile_blocks_for(int R, int device, uint64_t ntiles);
 // Balanced CTA ranges over E.units.order[slot] (fills E.units.cut[slot]),
@@ -91,6 +94,20 @@ uint32_t tile_blocks_for(int R, int device, uint64_t ntiles);
 void tile_cuts(Engine& E, int slot, unsigned long long fixed);
 // Partition of Engine::tiles + residual selection (tiles.cu).
 void partition_tiles3(Engine& E, double threshold, DArray<uint32_t>& sel, uint64_t& nsel);
+// Device relabelling (reorder_gpu.cu): HITS scores with the reference's
+// summation order, and degree order with ties by index; rank[m][old] = new.
+void gpu_hits(Engine& E, int rounds, uint64_t budget, std::vector<std::vector<uint32_t>>& rank);
+void gpu_degree_rank(Engine& E, std::vector<std::vector<uint32_t>>& rank);
+// Row-slab sharding (shard.cu): the plan (E.slab, E.slab_blocks,
+// E.heavy_rows) from the residual selection and the dense tiles; this rank's
+// residual elements of target mode n (out; the selection or every nonzero
+// when sel is null); this rank's tiles of a target slot in visiting order.
+void shard_plan(Engine& E, const uint32_t* sel, uint64_t nsel);
+uint64_t shard_select(Engine& E, int n, const uint32_t* sel, uint64_t nsel, DArray<uint32_t>& out);
+uint64_t shard_tiles(Engine& E, int slot, DArray<uint32_t>& local_order);
+// Copies the tiles listed in E.units.vtile/vstart[slot] into swords[slot]
+// and points vstart[slot] into it.
+void compact_slot_pool(Engine& E, int slot);
 // Views (views.cu).
 void build_view(Engine& E, View& v, int n, const uint32_t* d_sel, uint64_t nsel);
 
@@ -104,6 +121,8 @@ int launch_gram_partial(const double* F, uint64_t rows, int R, double* part, int
                         cudaStream_t s);
 // out[i] = sum_b part[b*len + i], i < len (fixed order).
 void launch_partial_sum(const double* part, int nblk, int len, double* out, cudaStream_t s);
+// out[i] += sum_b part[b*len + i], i < len (fixed order).
+void launch_partial_sum_add(const double* part, int nblk, int len, double* out, cudaStream_t s);
 // G = sum of nblk partials (fixed order).
 void launch_gram_reduce(const double* part, int nblk, int R, double* G, cudaStream_t s);
 // FtF = prod of the ng Grams Gs (elementwise, written out) and Ainv = its

@@ -37,6 +37,11 @@ struct FoPtrs {
   const double* p[4];
 };
 
+// Ranks held by lane `glane` of a GW-lane group.  Vector paths: 1 or 2
+// consecutive ranks, or with 4 ranks two pairs, one in each half of the row
+// (ranks 2g, 2g+1 and 2GW+2g, 2GW+2g+1), so that each 16-byte load
+// instruction of the group reads one contiguous half row: every sector it
+// touches is used whole.  Scalar paths: ranks glane + k*GW.
 template <int GW, int RPL, bool VEC>
 struct Lanes {
   int r[RPL];
@@ -44,7 +49,8 @@ struct Lanes {
   __device__ Lanes(int glane, int R) {
 #pragma unroll
     for (int k = 0; k < RPL; ++k) {
-      r[k] = VEC ? glane * RPL + k : glane + k * GW;
+      if (VEC && RPL == 4) r[k] = (k < 2) ? 2 * glane + k : 2 * GW + 2 * glane + (k - 2);
+      else r[k] = VEC ? glane * RPL + k : glane + k * GW;
       ok[k] = r[k] < R;
     }
   }
@@ -61,8 +67,8 @@ __device__ __forceinline__ void load_row(const double* __restrict__ F, uint64_t 
     x[0] = a.x;
     x[1] = a.y;
   } else if constexpr (VEC && RPL == 4) {
-    const double2 a = __ldg(reinterpret_cast<const double2*>(base) + 2 * glane);
-    const double2 b = __ldg(reinterpret_cast<const double2*>(base) + 2 * glane + 1);
+    const double2 a = __ldg(reinterpret_cast<const double2*>(base) + glane);
+    const double2 b = __ldg(reinterpret_cast<const double2*>(base) + GW + glane);
     x[0] = a.x;
     x[1] = a.y;
     x[2] = b.x;

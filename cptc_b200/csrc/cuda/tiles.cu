@@ -638,9 +638,9 @@ uint32_t tile_blocks_for(int R, int device, uint64_t ntiles) {
 void tile_cuts(Engine& E, int slot, unsigned long long fixed) {
   UnitPool& U = E.units;
   const uint64_t n = U.cnt[slot];
-  // One set of `blocks` CTA ranges per rank, cut over the whole visiting
-  // order: rank r takes the r-th equal-weight share of the tiles.
-  const uint32_t total = U.blocks * (uint32_t)E.nranks;
+  // `blocks` CTA ranges over this rank's visiting order (with several ranks
+  // it lists only the rank's own tiles).
+  const uint32_t total = U.blocks;
   U.cut[slot].alloc((uint64_t)total + 1);
   if (n == 0) {
     CPTC_CUDA(cudaMemsetAsync(U.cut[slot].p, 0, ((uint64_t)total + 1) * 4, E.stream));

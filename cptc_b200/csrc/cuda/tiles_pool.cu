@@ -87,6 +87,20 @@ __global__ void k_visit(const uint32_t* __restrict__ order, const int4* __restri
   }
 }
 
+// Words of the listed tiles (visiting order) copied to consecutive padded
+// offsets: dst[nst[k] + j] = src[vs[k] + j], j < padded count.
+__global__ void k_copy_tile_words(const int4* __restrict__ vt, const uint32_t* __restrict__ vs,
+                                  const uint64_t* __restrict__ nst, uint64_t n,
+                                  const uint32_t* __restrict__ src, uint32_t* __restrict__ dst,
+                                  uint32_t* __restrict__ vs_new) {
+  for (uint64_t k = blockIdx.x; k < n; k += gridDim.x) {
+    const int cnt = (vt[k].w + 3) & ~3;
+    const uint64_t s0 = vs[k], d0 = nst[k];
+    for (int j = threadIdx.x; j < cnt; j += blockDim.x) dst[d0 + j] = src[s0 + j];
+    if (threadIdx.x == 0) vs_new[k] = (uint32_t)d0;
+  }
+}
+
 __global__ void k_to_tf32(const double* __restrict__ F, uint64_t n, float* __restrict__ out) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
        i += (uint64_t)gridDim.x * blockDim.x)
@@ -238,6 +252,10 @@ __global__ void __launch_bounds__(128, MINB) k_tiles3w(Tile3Args a, const uint32
     w2 = a.vstart[k0 + 1];
   }
   issue(0, T1, w1);
+  // Shared memory starts undefined: the tile (and the flush buffer it
+  // holds) is cleared once here, and after that by each tile's own cells.
+  for (int i = tid; i < kTileFloats / 4; i += NTH)
+    reinterpret_cast<float4*>(X)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   int cur_tb = -1;
 #pragma unroll 1
   for (uint64_t k = k0; k < k1; ++k) {
@@ -400,17 +418,51 @@ void pack_tile_words(Engine& E) {
   P.val.release();
 }
 
-// Tiles and word starts of target slot `slot` in its visiting order.
-void tile_visit_lists(Engine& E, int slot) {
+// Tiles and word starts of target slot `slot` in a visiting order of n
+// tile indices.
+void tile_visit_lists_from(Engine& E, int slot, const uint32_t* order, uint64_t n) {
   UnitPool& P = E.units;
-  const uint64_t n = P.cnt[slot];
   P.vtile[slot].alloc(n);
   P.vstart[slot].alloc(n);
   if (n == 0) return;
-  k_visit<<<grid_for(n, 256, 148 * 16), 256, 0, E.stream>>>(P.order[slot].p, P.unit.p,
-                                                            P.pstart.p, n, P.vtile[slot].p,
-                                                            P.vstart[slot].p);
+  k_visit<<<grid_for(n, 256, 148 * 16), 256, 0, E.stream>>>(order, P.unit.p, P.pstart.p, n,
+                                                            P.vtile[slot].p, P.vstart[slot].p);
   CPTC_LAUNCH_CHECK();
+}
+
+void tile_visit_lists(Engine& E, int slot) {
+  tile_visit_lists_from(E, slot, E.units.order[slot].p, E.units.cnt[slot]);
+}
+
+void compact_slot_pool(Engine& E, int slot) {
+  UnitPool& P = E.units;
+  cudaStream_t s = E.stream;
+  const uint64_t n = P.cnt[slot];
+  if (n == 0) {
+    P.swords[slot].alloc(4);
+    return;
+  }
+  DArray<uint64_t> pc(n), nst(n);
+  k_pad_counts<<<grid_for(n, 256, 148 * 16), 256, 0, s>>>(P.vtile[slot].p, n, pc.p);
+  CPTC_LAUNCH_CHECK();
+  size_t tb = 0;
+  CPTC_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tb, pc.p, nst.p, (int64_t)n, s));
+  DArray<unsigned char> temp(tb);
+  CPTC_CUDA(cub::DeviceScan::ExclusiveSum(temp.p, tb, pc.p, nst.p, (int64_t)n, s));
+  uint64_t last[2] = {0, 0};
+  CPTC_CUDA(cudaMemcpyAsync(&last[0], nst.p + n - 1, 8, cudaMemcpyDeviceToHost, s));
+  CPTC_CUDA(cudaMemcpyAsync(&last[1], pc.p + n - 1, 8, cudaMemcpyDeviceToHost, s));
+  CPTC_CUDA(cudaStreamSynchronize(s));
+  const uint64_t total = last[0] + last[1];
+  P.swords[slot].alloc(total + 4);
+  CPTC_CUDA(cudaMemsetAsync(P.swords[slot].p, 0, (total + 4) * sizeof(uint32_t), s));
+  DArray<uint32_t> vs_new(n);
+  k_copy_tile_words<<<grid_for(n, 1, 148 * 32), 128, 0, s>>>(P.vtile[slot].p, P.vstart[slot].p,
+                                                             nst.p, n, P.words.p,
+                                                             P.swords[slot].p, vs_new.p);
+  CPTC_LAUNCH_CHECK();
+  CPTC_CUDA(cudaStreamSynchronize(s));
+  P.vstart[slot] = std::move(vs_new);
 }
 
 // Per-tile cost of k_tiles3w in nonzero units, for balancing CTA ranges:

@@ -139,6 +139,14 @@ class Engine:
     def init_factors(self) -> None:
         self._check(self._lib.cptc_init_factors(self._h), "init_factors")
 
+    def relabel(self, mode: int) -> np.ndarray:
+        """The build's relabelling of `mode`: out[old index] = new index."""
+        out = np.empty(int(self._tensor.dims[mode]), dtype=np.uint32)
+        self._check(self._lib.cptc_get_relabel(self._h, int(mode),
+                                               out.ctypes.data_as(C.POINTER(C.c_uint32))),
+                    "relabel")
+        return out
+
     def stats(self) -> dict:
         s = N.Stats()
         self._check(self._lib.cptc_get_stats(self._h, C.byref(s)), "stats")

@@ -112,6 +112,8 @@ typedef struct cptc_stats {
   int fiber_mode[CPTC_MAX_ORDER]; /* per target mode: mode whose rows are
                                      reused along a sorted run               */
   int nranks, rank_id;
+  double reorder_ms;        /* relabelling share of build_ms (HITS, degree
+                               order: on the device; order-3 CADR: host)     */
 } cptc_stats;
 
 int cptc_opts_default(cptc_opts* o);

@@ -1,21 +1,20 @@
 """Worker code for the multi-rank tests (imported by spawned processes).
 
 `shard_als3` restates, with numpy on CPU ranks, what the engine does on G GPUs
-for the order-3 ALS.  Work and ownership are split separately:
-  * work: the nonzeros of each mode, sorted by target row, are cut into G
-    equal-count chunks (the engine gives each rank an equal range of its
-    nonzero-balanced tasks and an equal-weight range of the dense tiles), so
-    a heavy row is shared by several ranks;
-  * ownership: rows in G equal slabs (ceil(I/G) rows each).
-Per mode: partial MTTKRP of the rank's chunk -> reduce-scatter into the slabs
--> solve of the own slab -> one all-reduce of the partial Gram (column norms
-are its diagonal; the last mode appends the fit's column dot products) beside
-the all-gather of the unnormalised slabs -> every rank normalises the whole
-factor.  Run with gloo it checks the order and payload of the collectives on
-the host.  exchange="peer" restates the peer-memory exchange instead: every
-rank's partial slab rows reach the owner (region r of its receive buffer) and
-the owner adds the G partials in rank order 0..G-1; the Gram partials go to
-slot r of every rank, which adds the slots in rank order.
+for the order-3 ALS (cptc_b200/csrc/cuda/shard.cu, comm.cu):
+  * rows of each mode are cut into 16-row blocks; a block's weight is its
+    nonzero count; the heavy prefix ends with the last block above an eighth
+    of a rank's share, and the remaining blocks are cut into G contiguous
+    slabs of equal weight (each cut at the nearest block boundary);
+  * each rank keeps the nonzeros of its slab and, of the heavy prefix's
+    nonzeros (in the tensor's order), every G-th one starting at its rank;
+  * per mode: local MTTKRP -> solve of the own slab rows -> one exchange:
+    all-reduce of [Gram partial | fit dots], all-reduce of the heavy rows'
+    partial MTTKRP, every rank's solved slab broadcast to all -> every rank
+    solves the heavy rows itself and adds their Gram and dots -> every rank
+    normalises the whole factor.
+Run with gloo it checks the partition and the payload of the collectives on
+the host.
 """
 from __future__ import annotations
 
@@ -45,7 +44,42 @@ def truncated_pinv(A, R):
     return (V[:, keep] / w[keep]) @ V[:, keep].T
 
 
-def shard_als3(t, R, iters, rank, world, dist, exchange="nccl"):
+MAX_HEAVY_ROWS = 4096
+
+
+def shard_plan(rows_idx, dim, world):
+    """(heavy rows, row cut points, block cut points) of one mode from the
+    target indices of its nonzeros (every nonzero weighs 1)."""
+    nb = -(-dim // 16)
+    w = np.bincount(rows_idx // 16, minlength=nb).astype(np.float64)
+    W = w.sum()
+    heavy = np.nonzero(w > W / (8.0 * world))[0]
+    h = int(heavy[-1]) + 1 if heavy.size else 0
+    h = min(h, MAX_HEAVY_ROWS // 16)
+    Wn = w[h:].sum()
+    cb = [h] + [nb] * world
+    acc, b = 0.0, h
+    for r in range(1, world):
+        target = Wn * r / world
+        while b < nb and acc + 0.5 * w[b] <= target:
+            acc += w[b]
+            b += 1
+        cb[r] = b
+    slab = [0] + [min(c * 16, dim) for c in cb[1:world]] + [dim]
+    return min(h * 16, dim), slab, cb
+
+
+def shard_select(rows_idx, H, cb, rank, world):
+    """Positions of this rank's nonzeros for one target mode."""
+    blk = rows_idx // 16
+    hb = -(-H // 16)
+    heavy = blk < hb
+    hord = np.cumsum(heavy) - heavy  # ordinal among the heavy nonzeros
+    mine = np.where(heavy, hord % world == rank, (blk >= cb[rank]) & (blk < cb[rank + 1]))
+    return np.nonzero(mine)[0]
+
+
+def shard_als3(t, R, iters, rank, world, dist):
     """The engine's distributed order-3 ALS on `world` CPU ranks (see module doc)."""
     import torch
 
@@ -58,84 +92,46 @@ def shard_als3(t, R, iters, rank, world, dist, exchange="nccl"):
     G = [f.T @ f for f in F]
     X2 = float(t.vals @ t.vals)
     fits = []
-    srows = [-(-d // world) for d in t.dims]
-    # this rank's nonzeros per target mode: an equal share of the row-sorted order
-    chunk = []
-    for n in range(3):
-        order = np.argsort(idx[n], kind="stable")
-        a, b = t.nnz * rank // world, t.nnz * (rank + 1) // world
-        chunk.append(order[a:b])
+    plan = [shard_plan(idx[n], t.dims[n], world) for n in range(3)]
+    mine = [shard_select(idx[n], plan[n][0], plan[n][2], rank, world) for n in range(3)]
 
     def allreduce(x):
         v = torch.from_numpy(np.ascontiguousarray(x))
         dist.all_reduce(v)
         return v.numpy()
 
-    def gather(x):
-        parts = [torch.zeros(x.shape, dtype=torch.float64) for _ in range(world)]
-        dist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(x)))
-        return [p.numpy() for p in parts]
-
-    def rank_order_sum(parts):
-        acc = np.zeros_like(parts[0])
-        for p in parts:  # r = 0 .. world-1
-            acc = acc + p
-        return acc
-
-    def reduce_scatter_rows(M, s, n):
-        # padded to world * s rows; gloo has no reduce_scatter: all-reduce, keep own slab
-        P = np.zeros((world * s, R))
-        P[:M.shape[0]] = M
-        if exchange == "peer":
-            # region r of the owner's receive buffer holds rank r's rows of its
-            # slab, pushed only inside rank r's touched rows [lo_r, hi_r)
-            rows = idx[n][chunk[n]]
-            hull = np.array([rows.min(), rows.max() + 1] if rows.size else [0, 0])
-            hulls = gather(hull.astype(np.float64))
-            parts = []
-            for r, g in enumerate(gather(P)):
-                reg = np.zeros((s, R))
-                lo, hi = int(hulls[r][0]), int(hulls[r][1])
-                a, b = max(lo, rank * s), min(hi, (rank + 1) * s)
-                if r == rank:
-                    reg = g[rank * s:(rank + 1) * s]
-                elif a < b:
-                    reg[a - rank * s:b - rank * s] = g[a:b]
-                parts.append(reg)
-            return rank_order_sum(parts)
-        return allreduce(P)[rank * s:(rank + 1) * s]
-
-    def reduce_slots(x):
-        if exchange == "peer":
-            return rank_order_sum(gather(x))
-        return allreduce(x)
-
-    def allgather_rows(Fl, s, dim):
-        parts = [torch.zeros((s, R), dtype=torch.float64) for _ in range(world)]
-        dist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(Fl)))
-        return np.concatenate([p.numpy() for p in parts])[:dim]
+    def broadcast_slabs(Fn, n):
+        H, slab, _ = plan[n]
+        for q in range(world):
+            lo, hi = max(slab[q], H), max(slab[q + 1], H)
+            if hi > lo:
+                v = torch.from_numpy(np.ascontiguousarray(Fn[lo:hi]))
+                dist.broadcast(v, src=q)
+                Fn[lo:hi] = v.numpy()
 
     for _ in range(iters):
         for n in range(3):
             p, q = [m for m in range(3) if m != n]
-            FtF = G[p] * G[q]
-            mine = chunk[n]
-            M = np_mttkrp([i[mine] for i in idx], t.vals[mine], t.dims, F, n)
-            s = srows[n]
-            lo, hi = min(rank * s, t.dims[n]), min((rank + 1) * s, t.dims[n])
-            Ms = reduce_scatter_rows(M, s, n)       # own slab, padded to s rows
-            A = truncated_pinv(FtF, R)
-            Fl = np.zeros((s, R))
-            Fl[:hi - lo] = Ms[:hi - lo] @ A.T / lam
-            # one all-reduce (Gram partials, and for the last mode the fit's
-            # column dots of the unnormalised rows) beside the all-gather of
-            # the unnormalised slab; every rank then normalises the factor
-            payload = [(Fl.T @ Fl).ravel()]
+            A = truncated_pinv(G[p] * G[q], R)
+            H, slab, _ = plan[n]
+            lo, hi = max(slab[rank], H), max(slab[rank + 1], H)
+            sel = mine[n]
+            M = np_mttkrp([i[sel] for i in idx], t.vals[sel], t.dims, F, n)
+            Fn = np.zeros((t.dims[n], R))
+            Fn[lo:hi] = M[lo:hi] @ A.T / lam
+            payload = [(Fn[lo:hi].T @ Fn[lo:hi]).ravel()]
             if n == 2:
-                payload.append(np.einsum("kr,kr->r", Fl[:hi - lo], Ms[:hi - lo]))
-            red = reduce_slots(np.concatenate(payload))
+                payload.append(np.einsum("kr,kr->r", Fn[lo:hi], M[lo:hi]))
+            red = allreduce(np.concatenate(payload))
+            if H > 0:
+                M[:H] = allreduce(M[:H])
+            broadcast_slabs(Fn, n)
+            if H > 0:  # the heavy rows, solved by every rank, added once
+                Fn[:H] = M[:H] @ A.T / lam
+                red[:R * R] += (Fn[:H].T @ Fn[:H]).ravel()
+                if n == 2:
+                    red[R * R:] += np.einsum("kr,kr->r", Fn[:H], M[:H])
             Gs = red[:R * R].reshape(R, R)
-            Fn = allgather_rows(Fl, s, t.dims[n])
             nr = np.sqrt(np.diag(Gs))
             zero = nr < 1e-14
             scale = np.where(zero, 0.0, 1.0 / np.where(zero, 1.0, nr))
@@ -146,7 +142,7 @@ def shard_als3(t, R, iters, rank, world, dist, exchange="nccl"):
         iprod = float(lam @ dots)
         model2 = float(lam @ (G[0] * G[1] * G[2]) @ lam)
         fits.append(1 - np.sqrt(max(X2 - 2 * iprod + model2, 0.0)) / np.sqrt(X2))
-    return np.array(fits), F, lam, [c.size for c in chunk]
+    return np.array(fits), F, lam, [int(m.size) for m in mine], [pl[0] for pl in plan]
 
 
 def make_cpu_case(spec):
@@ -172,11 +168,10 @@ def cpu_worker(rank, world, port, spec, q):
                             world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
         t = make_cpu_case(spec)
-        fits, F, lam, shares = shard_als3(t, spec["R"], spec["iters"], rank, world, dist,
-                                          spec.get("exchange", "nccl"))
-        q.put((rank, fits, F, lam, shares))
+        fits, F, lam, shares, heavy = shard_als3(t, spec["R"], spec["iters"], rank, world, dist)
+        q.put((rank, fits, F, lam, shares, heavy))
     except Exception as e:  # report instead of hanging the other ranks' test
-        q.put((rank, repr(e), None, None, None))
+        q.put((rank, repr(e), None, None, None, None))
         raise
     finally:
         dist.destroy_process_group()
@@ -249,75 +244,17 @@ GPU_CASES = {
     "fp64_o3": dict(gen=("uniform", (600, 500, 400), 400_000, 3, "lognormal"), R=16, iters=4,
                     build=dict(path="fp64")),
     "hybrid_o3": dict(gen=("config", 4, 0.05, 0), R=32, iters=3, build=dict(path="tf32")),
+    "hybrid_o3_r128": dict(gen=("config", 4, 0.02, 0), R=128, iters=2, build=dict(path="tf32")),
     "generic_o4": dict(gen=("config", 5, 0.2, 0), R=16, iters=3, build=dict(generic=True)),
+    # R=17: odd rank on the FP64 path
+    "fp64_o3_r17": dict(gen=("uniform", (301, 250, 199), 60_000, 4, "normal"), R=17, iters=3,
+                        build=dict(path="fp64")),
 }
-# the same cases with the peer-memory exchange (a 1-GPU run ignores it)
-for _k in list(GPU_CASES):
-    GPU_CASES[_k + "_peer"] = dict(GPU_CASES[_k], build=dict(GPU_CASES[_k]["build"],
-                                                             exchange="peer"))
-# other rank cut points (the split changes only which rank sums which part)
-GPU_CASES["fp64_o3_rowcost"] = dict(GPU_CASES["fp64_o3"], env={"CPTC_TASK_ROW_COST": "4"})
-GPU_CASES["hybrid_o3_tilecost_peer"] = dict(GPU_CASES["hybrid_o3_peer"],
-                                            env={"CPTC_TILE_FIXED_COST": "1200",
-                                                 "CPTC_TASK_ROW_COST": "4"})
-# R=17: odd slabs take the scalar copy kernels
-GPU_CASES["fp64_o3_r17_peer"] = dict(gen=("uniform", (301, 250, 199), 60_000, 4, "normal"), R=17,
-                                     iters=3, build=dict(path="fp64", exchange="peer"))
-
-
-def peer_timeout_main(out: str):
-    """Two torchrun ranks with the peer exchange and a 1 s barrier limit:
-    rank 0 runs one ALS iteration alone, so its first barrier waits for a
-    flag that nothing sets; the kernel gives up, the iteration fails with
-    CPTC_E_COMM, and after a collective rebuild both ranks run ALS again."""
-    import time
-
-    import torch
-    import torch.distributed as dist
-
-    import cptc_b200 as cp
-
-    os.environ["CPTC_PEER_TIMEOUT_MS"] = "1000"
-    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
-    local = int(os.environ.get("LOCAL_RANK", rank))
-    torch.cuda.set_device(local)
-    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
-    try:
-        t = cp.gen_uniform((200, 150, 100), 20_000, seed=7, values="uniform")
-        e = cp.Engine(local)
-        obj = [cp.comm_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        e.comm_init(obj[0], rank, world)
-        e.load(t)
-        e.build(8, path="fp64", exchange="peer")
-        e.init_factors()
-        e.als(1)
-        dist.barrier()
-        code, waited = 0, 0.0
-        if rank == 0:
-            t0 = time.perf_counter()
-            try:
-                e.als(1)
-            except cp.CptcError as x:
-                code = x.code
-            waited = time.perf_counter() - t0
-        dist.barrier()  # rank 1 waits here, off the GPU
-        e.build(8, path="fp64", exchange="peer")
-        e.init_factors()
-        fits = [r.fit for r in e.als(3)]
-        allf = [None] * world
-        dist.all_gather_object(allf, fits)
-        if rank == 0:
-            np.savez(out, code=code, waited=waited, fits=np.array(fits),
-                     ranks_agree=int(all(f == fits for f in allf)))
-        e.close()
-    finally:
-        dist.destroy_process_group()
 
 
 def comm_timeout_main(out: str):
     """Two torchrun ranks on the NCCL exchange with CPTC_COMM_TIMEOUT_MS=2000:
-    rank 0 runs one ALS iteration alone, so its reduce-scatter waits for a
+    rank 0 runs one ALS iteration alone, so its first exchange waits for a
     rank that never joins; the host wait gives up, aborts the communicator
     and reports CPTC_E_COMM.  Both ranks then leave without touching the
     aborted communicator again."""
@@ -370,9 +307,7 @@ def make_case(spec):
 
 
 if __name__ == "__main__":
-    if len(sys.argv) > 2 and sys.argv[1] == "--peer-timeout":
-        peer_timeout_main(sys.argv[2])
-    elif len(sys.argv) > 2 and sys.argv[1] == "--comm-timeout":
+    if len(sys.argv) > 2 and sys.argv[1] == "--comm-timeout":
         comm_timeout_main(sys.argv[2])
     else:
         gpu_main()

@@ -1,10 +1,11 @@
-"""The engine's NCCL row-slab ALS on 2 GPUs against the same engine on 1 GPU.
+"""The engine's sharded row-slab ALS on 2 GPUs against the same engine on 1 GPU.
 
 Each case runs tests/multirank.py under torchrun (one process per GPU; gloo
 only to pass the NCCL unique id) and compares rank 0's fits, lambda, factors
 and a final MTTKRP with a single-GPU run of the same build.  Sums are the same
 terms in another order, so FP64 agrees to rounding; the TF32 tiles compute
-each tile identically on either layout.
+each tile identically on either layout.  Every rank's replica must hold the
+same bits.
 """
 import os
 import socket
@@ -41,9 +42,8 @@ def rel(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
 
 
-@pytest.mark.parametrize("case", ["fp64_o3", "hybrid_o3", "generic_o4", "fp64_o3_peer",
-                                  "hybrid_o3_peer", "generic_o4_peer", "fp64_o3_r17_peer",
-                                  "fp64_o3_rowcost", "hybrid_o3_tilecost_peer"])
+@pytest.mark.parametrize("case", ["fp64_o3", "hybrid_o3", "hybrid_o3_r128", "generic_o4",
+                                  "fp64_o3_r17"])
 def test_two_gpu_slab_als_matches_one_gpu(case, tmp_path):
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs")
@@ -82,26 +82,6 @@ def test_two_gpu_slab_als_matches_one_gpu(case, tmp_path):
     for m, f in enumerate(F):
         assert rel(got[f"F{m}"], f) < tol, m
     assert rel(got["M0"], M0) < tol
-
-
-def test_peer_barrier_timeout_is_reported(tmp_path):
-    # rank 0 runs an iteration alone: its first barrier gives up after 1 s,
-    # the iteration reports CPTC_E_COMM, and a rebuild makes the pair usable
-    if _gpus() < 2:
-        pytest.skip("needs 2 GPUs")
-    out = tmp_path / "timeout.npz"
-    env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(HERE.parent), str(HERE)]),
-               NCCL_NVLS_ENABLE="0")
-    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
-           "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
-           f"--master-port={_free_port()}", str(HERE / "multirank.py"), "--peer-timeout",
-           str(out)]
-    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
-    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    got = np.load(out)
-    assert int(got["code"]) == -5  # CPTC_E_COMM
-    assert 0.9 < float(got["waited"]) < 30.0
-    assert int(got["ranks_agree"]) == 1 and np.all(np.isfinite(got["fits"]))
 
 
 def test_collective_timeout_is_reported(tmp_path):
