@@ -52,8 +52,9 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--keep-tns", default="", help="reference arm: keep the .tns it writes here")
     p.add_argument("--ref-log", default="", help="reference arm: save cpTC's stdout here")
-    p.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
-                   help="how the ranks combine a mode update (several GPUs)")
+    p.add_argument("--exchange", default="nccl", choices=["nccl"],
+                   help="how the ranks combine a mode update (several GPUs): one grouped "
+                        "NCCL call per mode update")
     p.add_argument("--e2e-sharded", action="store_true",
                    help="e2e on several GPUs: each rank uploads 1/G of every factor and the "
                         "pieces are all-gathered on the GPUs (cptc_set_factors_sharded)")

@@ -217,7 +217,7 @@ class Engine:
                     "profile_mttkrp")
         return {"tiles_ms": ms[0], "sparse_ms": ms[1], "total_ms": ms[2]}
 
-    PHASES = ("mttkrp", "reduce_scatter", "solve", "allreduce_gather", "normalise")
+    PHASES = ("mttkrp", "inverse_wait", "solve", "exchange", "normalise")
 
     def set_phase_timing(self, on: bool = True) -> None:
         """Time every phase of each mode update from the next als() on."""

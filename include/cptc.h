@@ -61,14 +61,11 @@ enum { CPTC_REORDER_NONE = 0, CPTC_REORDER_CADR = 1, CPTC_REORDER_HITS = 2,
 enum { CPTC_SOLVER_DEFAULT = 0, CPTC_SOLVER_CHOL = 1, CPTC_SOLVER_PINV = 2 };
 /* How the ranks of a multi-GPU context combine a mode update (no
  * counterpart in the reference, which runs on one GPU).
- *   NCCL: reduce-scatter of the MTTKRP, then the Gram all-reduce grouped
- *         with the slab all-gather (the default).
- *   PEER: the same exchanges as stores into the other ranks' buffers over
- *         NVLink (CUDA IPC mappings) with two bounded flag barriers per mode
- *         update; sums in rank order.  2..8 ranks; cptc_build and
- *         cptc_destroy become collective (they map and unmap the buffers);
- *         a barrier that waits longer than CPTC_PEER_TIMEOUT_MS (default
- *         5000) fails the iteration with CPTC_E_COMM. */
+ *   NCCL: one grouped NCCL call per mode update: all-reduce of the Gram
+ *         partials (and fit dots), all-reduce of the heavy prefix's partial
+ *         MTTKRP rows, broadcast of every rank's solved slab (the default).
+ *   PEER: reserved (a peer-memory exchange); cptc_build returns
+ *         CPTC_E_UNSUP for it on several ranks. */
 enum { CPTC_EXCHANGE_NCCL = 0, CPTC_EXCHANGE_PEER = 1 };
 
 typedef struct cptc_opts {
@@ -125,19 +122,19 @@ const char* cptc_last_error(const cptc_ctx* ctx);
 
 /* Multi-GPU (one process per GPU): rank 0 calls cptc_comm_unique_id and
  * shares the 128 bytes; every rank then calls cptc_comm_init before
- * cptc_build.  cptc_comm_init, cptc_als, cptc_mttkrp and
- * cptc_set_factors_sharded are collective (with CPTC_EXCHANGE_PEER also
- * cptc_build and cptc_destroy): every rank calls them, in the same order; the
- * other functions are local (for example one rank alone may read the
- * replicated factors).  Each rank
- * computes an equal share of every mode's nonzeros; the partial MTTKRP is
- * reduce-scattered into equal row slabs, each rank solves its slab, and one
- * grouped call all-reduces the R x R Gram and all-gathers the slabs into
- * every rank's factor replica.  The reference runs on one GPU.
- * CPTC_COMM_TIMEOUT_MS (environment, unset = no limit) bounds how long
- * cptc_als waits for an iteration on several GPUs: past it the communicator
- * is aborted and the call returns CPTC_E_COMM (cptc_comm_init again before
- * the next collective call). */
+ * cptc_build.  cptc_comm_init, cptc_build, cptc_als, cptc_mttkrp and
+ * cptc_set_factors_sharded are collective: every rank calls them, in the
+ * same order; the other functions are local (for example one rank alone may
+ * read the replicated factors).  The rows of every mode are owned in slabs
+ * of equal estimated MTTKRP cost and each rank keeps only the nonzeros (FP64
+ * residual and dense tiles) of its rows; a heavy prefix of rows (a Zipf
+ * head) has its nonzeros dealt to all ranks and its partial rows
+ * all-reduced.  Each mode update is one grouped NCCL call (see
+ * CPTC_EXCHANGE_NCCL) and every rank ends with the whole factor.  The
+ * reference runs on one GPU.  CPTC_COMM_TIMEOUT_MS (environment, unset = no
+ * limit) bounds how long cptc_als waits for an iteration on several GPUs:
+ * past it the communicator is aborted and the call returns CPTC_E_COMM
+ * (cptc_comm_init again before the next collective call). */
 int cptc_comm_unique_id(unsigned char out_id[128]);
 int cptc_comm_init(cptc_ctx* ctx, const unsigned char id[128], int rank, int nranks);
 
@@ -200,11 +197,13 @@ unsigned long long cptc_launch_count(void);
  * the last iteration that finished, out[n * CPTC_NPHASES + p] in ms for
  * mode n < order and phase p:
  *   0  MTTKRP (zero, residual kernel, dense tiles)
- *   1  reduce-scatter of the MTTKRP into the row slabs (empty on one GPU)
- *   2  wait for the R x R inverse, apply it, Gram partials (and the fit's
+ *   1  wait for the R x R inverse (computed beside the MTTKRP)
+ *   2  apply the inverse to this rank's rows, Gram partials (and the fit's
  *      column dots on the last mode)
- *   3  all-reduce of the Gram partials + all-gather of the slab (one GPU:
- *      the partial sums)
+ *   3  the exchange: partial sums, and on several GPUs one NCCL group
+ *      (all-reduce of Gram and dots, all-reduce of the heavy prefix's
+ *      MTTKRP, broadcast of every rank's solved rows), then the solve of
+ *      the heavy prefix
  *   4  normalisation (and the fit on the last mode)
  * Writes at most `cap` values and returns how many (0 when phase timing is
  * off or no iteration has run since it was turned on), or a negative
@@ -259,7 +258,10 @@ int cptc_residual(cptc_ctx* ctx, double out2[2]);
  * (16 KiB) on every GPU that loads it, held until the process exits.  The
  * first call on each device sets up that device's address of the array
  * (cudaGetSymbolAddress, with the device current): make that first call
- * before any stream capture.  All calls share the array, which keeps the
+ * before any stream capture.  The address is kept for the life of the
+ * process, so a cudaDeviceReset of a device after its first call is not
+ * supported (the library's module, and the array, are gone with the
+ * context).  All calls share the array, which keeps the
  * last call's contents; each call writes every slot it later reads, so no
  * clearing is needed.  Calls that overlap on the GPU (concurrent streams,
  * or host threads sharing a device) race on the array: serialise them. */
