@@ -50,13 +50,6 @@ void comm_init(Engine& E, const unsigned char idb[128], int rank, int nranks) {
   E.rank = rank;
 }
 
-void comm_abort(Engine& E) {
-  if (E.nccl) {
-    ncclCommAbort(comm_of(E));  // unfinished collectives return
-    E.nccl = nullptr;
-  }
-}
-
 void comm_destroy(Engine& E) {
   if (E.nccl) {
     ncclCommDestroy(comm_of(E));

@@ -14,9 +14,6 @@ namespace cptc {
 // Clears the MTTKRP partition (one rank: whole modes; shard_plan fills it).
 void comm_prepare(Engine& E);
 void comm_destroy(Engine& E);
-// Aborts the communicator (its unfinished collectives return) and drops it:
-// cptc_comm_init has to run again before the next collective.
-void comm_abort(Engine& E);
 void comm_init(Engine& E, const unsigned char id[128], int rank, int nranks);
 int comm_unique_id(unsigned char out[128]);
 // Rows per transfer slab of mode m for the sharded factor upload and

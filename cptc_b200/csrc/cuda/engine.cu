@@ -214,7 +214,7 @@ void Engine::alloc_workspace() {
   scal.alloc(8);
   status.alloc(1);
   lambda.alloc(R);
-  if (dense_active && !generic) Ftf.alloc(maxd * (uint64_t)R);
+  if (dense_active && !generic) Ftf.alloc(((maxd + 15) / 16) * 16 * (uint64_t)R);
   else Ftf.release();
   for (int m = 0; m < N; ++m) {
     F[m].alloc(padded_rows(m) * (uint64_t)R);
@@ -544,7 +544,7 @@ void Engine::mttkrp_tiles(int mode, double* out, cudaStream_t s) {
     ta.cslot = (ts == 0) ? 1 : 0;
     ta.sslot = (ts == 2) ? 1 : 2;
     for (int q = 0; q < 3; ++q) ta.dims[q] = dims[q];
-    launch_to_tf32(F[ta.cslot].p, dims[ta.cslot] * (uint64_t)R, Ftf.p, st);
+    launch_to_tf32_blocks(F[ta.cslot].p, dims[ta.cslot], R, Ftf.p, st);
     ta.Fct = Ftf.p;
     ta.Fs = F[ta.sslot].p;
     ta.out = dst;
@@ -757,47 +757,12 @@ void Engine::launch_iteration(int slot) {
   CPTC_CUDA(cudaEventRecord(E[2 * CPTC_MAX_ORDER + 1], stream));
 }
 
-// Waits for the end of an iteration.  With several ranks and
-// CPTC_COMM_TIMEOUT_MS set, the wait is bounded: an iteration that has not
-// finished by then is taken to be stuck in a collective waiting for a rank
-// that is not there, the communicator is aborted (its kernels return) and
-// the call fails with CPTC_E_COMM.  Without it the wait is unbounded, as a
-// plain stream synchronisation.
-void Engine::wait_iteration(cudaEvent_t done) {
-  static const long long limit_ms = [] {
-    const char* e = std::getenv("CPTC_COMM_TIMEOUT_MS");
-    return e ? std::atoll(e) : 0ll;
-  }();
-  if (nranks == 1 || limit_ms <= 0) {
-    CPTC_CUDA(cudaEventSynchronize(done));
-    return;
-  }
-  const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {
-    const cudaError_t q = cudaEventQuery(done);
-    if (q == cudaSuccess) return;
-    if (q != cudaErrorNotReady) CPTC_CUDA(q);
-    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
-                        std::chrono::steady_clock::now() - t0).count();
-    if (ms > limit_ms) {
-      comm_abort(*this);
-      cudaStreamSynchronize(stream);
-      cudaStreamSynchronize(side);
-      release_graph();
-      throw CptcError(CPTC_E_COMM, "an iteration did not finish within CPTC_COMM_TIMEOUT_MS (a "
-                                   "rank is missing or stalled); the communicator was aborted, "
-                                   "call cptc_comm_init again");
-    }
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
-  }
-}
-
 // Waits for iteration `it` (readback slot `slot`), checks the solve status,
 // computes the fit and reports it.
 void Engine::finish_iteration(int it, int slot, cptc_iter_cb cb, void* user) {
   cudaEvent_t* E = slot ? ev1 : ev;
   const double* hs = h_scal + 8 * slot;
-  wait_iteration(E[2 * CPTC_MAX_ORDER + 1]);
+  CPTC_CUDA(cudaEventSynchronize(E[2 * CPTC_MAX_ORDER + 1]));
   int h_status = 0;
   std::memcpy(&h_status, hs + 4, sizeof(int));
   if (h_status != 0) {

@@ -154,8 +154,8 @@ struct Engine {
   DArray<double> G[CPTC_MAX_ORDER];
   DArray<double> lambda;
   DArray<double> FtV, FtF, Ainv, gpart, dots, scal, cscale;
-  // The contracted factor of an order-3 tile launch as TF32 bit patterns
-  // (float, max_m I_m x R), written just before the launch.
+  // The contracted factor of an order-3 tile launch as TF32 bit patterns in
+  // 16-row blocks (launch_to_tf32_blocks), written just before the launch.
   DArray<float> Ftf;
   DArray<int> status;
   double* h_scal = nullptr;  // pinned, 16 doubles: two readback slots of 8
@@ -192,7 +192,6 @@ struct Engine {
   void enqueue_iteration(int slot);
   void launch_iteration(int slot);
   void finish_iteration(int it, int slot, cptc_iter_cb cb, void* user);
-  void wait_iteration(cudaEvent_t done);
   uint64_t padded_rows(int m) const;
   void permute_rows(const double* in, int m, bool to_relabelled, double* out);
   void mttkrp(int mode);  // into FtV (relabelled rows), stream-ordered

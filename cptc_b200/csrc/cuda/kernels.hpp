@@ -71,15 +71,17 @@ struct Tile3Args {
   int R;
   int tslot, cslot, sslot;
   uint64_t dims[3];
-  const float* Fct;
+  const float* Fct;        // contracted factor in 16-row TF32 blocks (launch_to_tf32_blocks)
   const double* Fs;
   double* out;
 };
 void launch_tiles3w(const Tile3Args& a, const uint32_t* cut, uint32_t blocks, cudaStream_t s);
 // CTAs of one launch of launch_tiles3w (waves of what the SMs hold at once).
 uint32_t tile3w_blocks_for(int R, int device, uint64_t ntiles);
-// out[i] = F[i] as a TF32 bit pattern (float, low 13 mantissa bits cleared).
-void launch_to_tf32(const double* F, uint64_t n, float* out, cudaStream_t s);
+// The first `dim` rows of F (R columns) as TF32 bit patterns in 16-row
+// blocks, each block rank-major with the tile kernel's column order; rows up
+// to the next multiple of 16 are zero.  out holds ceil(dim/16)*16*R floats.
+void launch_to_tf32_blocks(const double* F, uint64_t dim, int R, float* out, cudaStream_t s);
 // Per-tile cost of launch_tiles3w in nonzero units (CTA range balancing).
 unsigned long long tile3w_fixed_cost(int R);
 // Order-3 pool packing (after partition_tiles3) and visit lists per slot.

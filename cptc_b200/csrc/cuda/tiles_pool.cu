@@ -24,10 +24,16 @@
 //    converted once per launch by k_to_tf32) and its 16 weighting-factor
 //    rows (FP64); rows past the end of a mode are zero-filled by the copy;
 //  * the tile is scattered into a zero tile in shared memory laid out per
-//    mode as (s, t, c) with a 20-float row stride (the A-fragment loads of
-//    mma.sync m16n8k8 are then bank-conflict free); after the products it
-//    is zeroed again by writing zero to the cells it set (or by clearing
-//    the whole tile when it holds more nonzeros than the stage);
+//    mode as (s, t, c), a 16-float row per (s, t) with the columns in the
+//    order c = 0,4,8,12, 1,5,9,13, ...: the four A-fragment values a lane
+//    needs from a row (columns t4, t4+4, t4+8, t4+12 of both k-steps) are
+//    one 16-byte load, bank-conflict free; after the products the tile is
+//    zeroed again by writing zero to the cells it set (or by clearing the
+//    whole tile when it holds more nonzeros than the stage);
+//  * the contracted factor is converted once per launch (k_to_tf32_blocks)
+//    into 16-row blocks stored rank-major with the same column order, so a
+//    lane's B-fragment values of one n-tile are one 16-byte load, and a
+//    block is one contiguous copy (rows past the mode's end are zeros);
 //  * warps are (n-tile group, slab group) pairs, an A fragment is loaded
 //    once per warp and used for all of its n-tiles; FP64 results stay in
 //    registers across the consecutive tiles of one target block and are
@@ -45,9 +51,13 @@ namespace cptc {
 
 namespace {
 
-constexpr int kSt = 20;                // t stride (floats) of the slab layout
+constexpr int kSt = 16;                // t stride (floats) of the slab layout
 constexpr int kSs = 16 * kSt;          // s stride
-constexpr int kTileFloats = 16 * kSs;  // 5120 floats = 20 KB
+constexpr int kTileFloats = 16 * kSs;  // 4096 floats = 16 KB
+
+// Position of column c in a 16-float row: columns c, c+4, c+8, c+12 are
+// adjacent, so the fragment values of lane t4 are one 16-byte chunk.
+__host__ __device__ constexpr int cpos(int c) { return (c & 3) * 4 + (c >> 2); }
 constexpr uint32_t kValMask = 0xFFFFE000u;
 
 __device__ __forceinline__ uint32_t tf32_of(double v) {
@@ -101,10 +111,21 @@ __global__ void k_copy_tile_words(const int4* __restrict__ vt, const uint32_t* _
   }
 }
 
-__global__ void k_to_tf32(const double* __restrict__ F, uint64_t n, float* __restrict__ out) {
+// The contracted factor as TF32 bit patterns in 16-row blocks: block b holds
+// rows 16b..16b+15 rank-major, out[b*16R + r*16 + cpos(c)] = F[16b + c, r],
+// zero for rows past `dim`.  n = ceil(dim/16)*16*R entries.
+__global__ void k_to_tf32_blocks(const double* __restrict__ F, uint64_t dim, int R, uint64_t n,
+                                 float* __restrict__ out) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
-       i += (uint64_t)gridDim.x * blockDim.x)
-    out[i] = __uint_as_float(__float_as_uint((float)F[i]) & kValMask);
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t row = i / (uint64_t)R;
+    const int r = (int)(i - row * R);
+    const uint64_t b = row >> 4;
+    const int c = (int)(row & 15);
+    const float v = row < dim ? (float)F[i] : 0.0f;
+    out[b * 16 * (uint64_t)R + (uint64_t)r * 16 + cpos(c)] =
+        __uint_as_float(__float_as_uint(v) & kValMask);
+  }
 }
 
 __device__ __forceinline__ void cp16(void* sdst, const void* gsrc, bool ok) {
@@ -130,10 +151,10 @@ __device__ __forceinline__ int blk(const int4& T) {
   return SLOT == 0 ? T.x : SLOT == 1 ? T.y : T.z;
 }
 
-// Bytes of one stage: words, contracted-factor rows (row stride R + 8
-// floats: bank-conflict-free B-fragment loads), weighting-factor rows.
+// Bytes of one stage: words, the contracted-factor block (16 x R floats),
+// the weighting-factor rows (16 x R doubles).
 __host__ __device__ constexpr size_t stage_bytes(int capw, int R) {
-  return (size_t)capw * 4 + (size_t)16 * (R + 8) * 4 + (size_t)16 * R * 8;
+  return (size_t)capw * 4 + (size_t)16 * R * 4 + (size_t)16 * R * 8;
 }
 
 // TS/CS/SS: target, contracted and weighting slots; NW: n-tiles (8 ranks
@@ -143,7 +164,7 @@ template <int TS, int CS, int SS, int NW, int CAPW, int MINB>
 __global__ void __launch_bounds__(128, MINB) k_tiles3w(Tile3Args a, const uint32_t* __restrict__ cut) {
   constexpr int NTH = 128, WARPS = 4;
   extern __shared__ __align__(16) unsigned char smraw[];
-  const int R = a.R, Rs = R + 8;
+  const int R = a.R;
   float* X = reinterpret_cast<float*>(smraw);
   double* accS = reinterpret_cast<double*>(smraw);  // 16 x R, only while X is all zero
   unsigned char* stg = smraw + (size_t)kTileFloats * 4;
@@ -151,7 +172,7 @@ __global__ void __launch_bounds__(128, MINB) k_tiles3w(Tile3Args a, const uint32
   auto s_words = [&](int b) { return reinterpret_cast<uint32_t*>(stg + b * sb); };
   auto s_fc = [&](int b) { return reinterpret_cast<float*>(stg + b * sb + CAPW * 4); };
   auto s_fs = [&](int b) {
-    return reinterpret_cast<double*>(stg + b * sb + CAPW * 4 + (size_t)16 * Rs * 4);
+    return reinterpret_cast<double*>(stg + b * sb + CAPW * 4 + (size_t)16 * R * 4);
   };
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
@@ -162,10 +183,10 @@ __global__ void __launch_bounds__(128, MINB) k_tiles3w(Tile3Args a, const uint32
   const int ntg = warp % ng, my_sg = warp / ng;
   const int nt_base = ntg * NW;
   const uint64_t dimT = a.dims[TS], dimC = a.dims[CS], dimS = a.dims[SS];
-  // 16-byte chunks per contracted row (R/4) and per weighting row (R/2);
-  // row = chunk / per-row by a float reciprocal, exact for these sizes.
-  const int cpr = R >> 2, cps = R >> 1;
-  const float icpr = 1.0f / (float)cpr, icps = 1.0f / (float)cps;
+  // 16-byte chunks per weighting row (R/2); row = chunk / per-row by a
+  // float reciprocal, exact for these sizes.
+  const int cps = R >> 1;
+  const float icps = 1.0f / (float)cps;
 
   const uint64_t k0 = cut[blockIdx.x], k1 = cut[blockIdx.x + 1];
   if (k0 >= k1) return;
@@ -184,12 +205,8 @@ __global__ void __launch_bounds__(128, MINB) k_tiles3w(Tile3Args a, const uint32
       cp16(dw + 4 * q, a.words + (uint64_t)ws + 4 * q, true);
     const uint64_t cb = (uint64_t)blk<CS>(T) * 16, sbk = (uint64_t)blk<SS>(T) * 16;
     float* dfc = s_fc(b);
-    for (int q = tid; q < 16 * cpr; q += NTH) {
-      const int row = (int)(((float)q + 0.5f) * icpr), ch = q - row * cpr;
-      const uint64_t gr = cb + row;
-      const bool ok = gr < dimC;
-      cp16(dfc + row * Rs + 4 * ch, a.Fct + (ok ? gr : 0) * (uint64_t)R + 4 * ch, ok);
-    }
+    const float* sfc = a.Fct + cb * (uint64_t)R;  // block cb/16, padded with zero rows
+    for (int q = tid; q < 4 * R; q += NTH) cp16(dfc + 4 * q, sfc + 4 * q, true);
     double* dfs = s_fs(b);
     for (int q = tid; q < 16 * cps; q += NTH) {
       const int row = (int)(((float)q + 0.5f) * icps), ch = q - row * cps;
@@ -239,7 +256,7 @@ __global__ void __launch_bounds__(128, MINB) k_tiles3w(Tile3Args a, const uint32
     const int lt = TS == 0 ? l0 : TS == 1 ? l1 : l2;
     const int lc = CS == 0 ? l0 : CS == 1 ? l1 : l2;
     const int ls = SS == 0 ? l0 : SS == 1 ? l1 : l2;
-    return ls * kSs + lt * kSt + lc;
+    return ls * kSs + lt * kSt + cpos(lc);
   };
 
   // Tile metadata two tiles ahead: T1 is the next tile, T2 the one after.
@@ -292,26 +309,23 @@ __global__ void __launch_bounds__(128, MINB) k_tiles3w(Tile3Args a, const uint32
 #pragma unroll
       for (int q = 0; q < NW; ++q) {
         const int nt = nt_base + q;
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          bf[q][ks][0] = bf[q][ks][1] = 0u;
-          if (nt < NT) {
-            bf[q][ks][0] = __float_as_uint(fc[(ks * 8 + t4) * Rs + nt * 8 + g]);
-            bf[q][ks][1] = __float_as_uint(fc[(ks * 8 + t4 + 4) * Rs + nt * 8 + g]);
-          }
+        bf[q][0][0] = bf[q][0][1] = bf[q][1][0] = bf[q][1][1] = 0u;
+        if (nt < NT) {
+          // rows t4, t4+4 (k-step 0) and t4+8, t4+12 (k-step 1) of column
+          // nt*8 + g of the contracted block
+          const uint4 v = *reinterpret_cast<const uint4*>(fc + (nt * 8 + g) * 16 + 4 * t4);
+          bf[q][0][0] = v.x;
+          bf[q][0][1] = v.y;
+          bf[q][1][0] = v.z;
+          bf[q][1][1] = v.w;
         }
       }
 #pragma unroll 2
       for (int s = my_sg; s < 16; s += SG) {
-        uint32_t af[2][4];
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          const float* base = X + s * kSs + ks * 8;
-          af[ks][0] = __float_as_uint(base[g * kSt + t4]);
-          af[ks][1] = __float_as_uint(base[(g + 8) * kSt + t4]);
-          af[ks][2] = __float_as_uint(base[g * kSt + t4 + 4]);
-          af[ks][3] = __float_as_uint(base[(g + 8) * kSt + t4 + 4]);
-        }
+        // rows g and g+8 of slab s, columns t4, t4+4, t4+8, t4+12
+        const uint4 lo = *reinterpret_cast<const uint4*>(X + s * kSs + g * kSt + 4 * t4);
+        const uint4 hi = *reinterpret_cast<const uint4*>(X + s * kSs + (g + 8) * kSt + 4 * t4);
+        const uint32_t af[2][4] = {{lo.x, hi.x, lo.y, hi.y}, {lo.z, hi.z, lo.w, hi.w}};
 #pragma unroll
         for (int q = 0; q < NW; ++q) {
           const int nt = nt_base + q;
@@ -474,8 +488,9 @@ unsigned long long tile3w_fixed_cost(int R) {
   return (unsigned long long)(44 * R + 256 * ng);
 }
 
-void launch_to_tf32(const double* F, uint64_t n, float* out, cudaStream_t s) {
-  k_to_tf32<<<grid_for(n, 256, 148 * 8), 256, 0, s>>>(F, n, out);
+void launch_to_tf32_blocks(const double* F, uint64_t dim, int R, float* out, cudaStream_t s) {
+  const uint64_t n = ((dim + 15) / 16) * 16 * (uint64_t)R;
+  k_to_tf32_blocks<<<grid_for(n, 256, 148 * 8), 256, 0, s>>>(F, dim, R, n, out);
   CPTC_LAUNCH_CHECK();
 }
 

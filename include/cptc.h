@@ -131,10 +131,10 @@ const char* cptc_last_error(const cptc_ctx* ctx);
  * head) has its nonzeros dealt to all ranks and its partial rows
  * all-reduced.  Each mode update is one grouped NCCL call (see
  * CPTC_EXCHANGE_NCCL) and every rank ends with the whole factor.  The
- * reference runs on one GPU.  CPTC_COMM_TIMEOUT_MS (environment, unset = no
- * limit) bounds how long cptc_als waits for an iteration on several GPUs:
- * past it the communicator is aborted and the call returns CPTC_E_COMM
- * (cptc_comm_init again before the next collective call). */
+ * reference runs on one GPU.  A rank that stops calling leaves the others'
+ * next collective waiting on the GPU: callers detect a lost rank on the host
+ * (their own heartbeat or store) before the next collective call and end
+ * the job, as the CLI does (CPTC_NGPU). */
 int cptc_comm_unique_id(unsigned char out_id[128]);
 int cptc_comm_init(cptc_ctx* ctx, const unsigned char id[128], int rank, int nranks);
 

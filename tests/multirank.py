@@ -252,51 +252,6 @@ GPU_CASES = {
 }
 
 
-def comm_timeout_main(out: str):
-    """Two torchrun ranks on the NCCL exchange with CPTC_COMM_TIMEOUT_MS=2000:
-    rank 0 runs one ALS iteration alone, so its first exchange waits for a
-    rank that never joins; the host wait gives up, aborts the communicator
-    and reports CPTC_E_COMM.  Both ranks then leave without touching the
-    aborted communicator again."""
-    import time
-
-    import torch
-    import torch.distributed as dist
-
-    import cptc_b200 as cp
-
-    os.environ["CPTC_COMM_TIMEOUT_MS"] = "2000"
-    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
-    local = int(os.environ.get("LOCAL_RANK", rank))
-    torch.cuda.set_device(local)
-    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
-    t = cp.gen_uniform((200, 150, 100), 20_000, seed=7, values="uniform")
-    e = cp.Engine(local)
-    obj = [cp.comm_unique_id() if rank == 0 else None]
-    dist.broadcast_object_list(obj, src=0)
-    e.comm_init(obj[0], rank, world)
-    e.load(t)
-    e.build(8, path="fp64")
-    e.init_factors()
-    ok_fits = [r.fit for r in e.als(2)]
-    dist.barrier()
-    code, waited = 0, 0.0
-    if rank == 0:
-        t0 = time.perf_counter()
-        try:
-            e.als(1)
-        except cp.CptcError as x:
-            code = x.code
-        waited = time.perf_counter() - t0
-        np.savez(out, code=code, waited=waited, fits=np.array(ok_fits))
-    dist.barrier()  # rank 1 waits here, off the GPU
-    dist.destroy_process_group()
-    # the peer of an aborted communicator may not be able to destroy its own
-    # cleanly: leave without running the destructors
-    sys.stdout.flush()
-    os._exit(0)
-
-
 def make_case(spec):
     import cptc_b200 as cp
 
@@ -307,7 +262,4 @@ def make_case(spec):
 
 
 if __name__ == "__main__":
-    if len(sys.argv) > 2 and sys.argv[1] == "--comm-timeout":
-        comm_timeout_main(sys.argv[2])
-    else:
-        gpu_main()
+    gpu_main()

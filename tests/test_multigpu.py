@@ -82,23 +82,3 @@ def test_two_gpu_slab_als_matches_one_gpu(case, tmp_path):
     for m, f in enumerate(F):
         assert rel(got[f"F{m}"], f) < tol, m
     assert rel(got["M0"], M0) < tol
-
-
-def test_collective_timeout_is_reported(tmp_path):
-    # NCCL exchange: rank 0 iterates alone; with CPTC_COMM_TIMEOUT_MS=2000 its
-    # host wait gives up, aborts the communicator and reports CPTC_E_COMM
-    if _gpus() < 2:
-        pytest.skip("needs 2 GPUs")
-    out = tmp_path / "ctimeout.npz"
-    env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(HERE.parent), str(HERE)]),
-               NCCL_NVLS_ENABLE="0")
-    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
-           "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
-           f"--master-port={_free_port()}", str(HERE / "multirank.py"), "--comm-timeout",
-           str(out)]
-    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
-    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    got = np.load(out)
-    assert int(got["code"]) == -5  # CPTC_E_COMM
-    assert 1.9 < float(got["waited"]) < 60.0
-    assert np.all(np.isfinite(got["fits"]))
