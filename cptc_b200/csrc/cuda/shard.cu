@@ -122,9 +122,12 @@ void exclusive_scan_u32(const uint32_t* in, uint32_t* out, uint64_t n, cudaStrea
 
 }  // namespace
 
-// Cost of a tile in residual-nonzero units: the tile kernel's cost per
-// nonzero relative to the residual kernel's, and its fixed per-tile part.
-static double tile_cost_ratio() { return 0.5; }
+// Cost of one tile-kernel unit (a dense nonzero, or 1/tile3w_fixed_cost of
+// a tile's fixed part) in residual-nonzero units.  Measured on config 4 (one
+// B200, ms per mode): R=32 tiles 0.45 ms for 39.1M nonzeros in 81,886 tiles
+// against the residual's 0.95 ms for 37.8M nonzeros gives 0.10; R=128
+// (1.42 against 3.16 ms) 0.029; about 3.2 / R.
+static double tile_cost_ratio(int R) { return std::min(0.5, 3.2 / (double)R); }
 
 void shard_plan(Engine& E, const uint32_t* sel, uint64_t nsel) {
   const int G = E.nranks;
@@ -159,7 +162,7 @@ void shard_plan(Engine& E, const uint32_t* sel, uint64_t nsel) {
     CPTC_CUDA(cudaMemcpyAsync(hdz.data(), dz.p, nb * 8, cudaMemcpyDeviceToHost, s));
     CPTC_CUDA(cudaMemcpyAsync(hdt.data(), dt.p, nb * 8, cudaMemcpyDeviceToHost, s));
     CPTC_CUDA(cudaStreamSynchronize(s));
-    const double rho = tile_cost_ratio();
+    const double rho = tile_cost_ratio(E.R);
     const double fixed = E.generic ? 512.0 : (double)tile3w_fixed_cost(E.R);
     std::vector<double> w(nb);
     double W = 0.0;

@@ -11,10 +11,14 @@
 //
 // B200 layout and schedule:
 //  * the pool holds one 32-bit word per nonzero: the TF32 bit pattern of
-//    its value, whose low 13 bits are zero, carries the 12-bit local id
-//    (l0 << 8 | l1 << 4 | l2) in those bits, so a nonzero is 4 bytes (the
-//    reference's pool: 12) and the kernel never converts a value; each
-//    tile's words start on a 16-byte boundary;
+//    its value, whose low 13 bits are zero, carries the 12-bit local id in
+//    those bits, so a nonzero is 4 bytes (the reference's pool: 12) and the
+//    kernel never converts a value; each tile's words start on a 16-byte
+//    boundary.  The local coordinates are stored permuted, p = cpos(l) (the
+//    order 0,4,8,12, 1,5,9,13, ...; cpos is its own inverse), which is the
+//    order the shared-memory tile uses, and a tile's words are stored in a
+//    strided order (element j at (a*j) mod count) so that the 32 nonzeros
+//    a warp scatters at once are spread over the banks;
 //  * per target mode the tiles are listed in visiting order (sorted by
 //    target block) with their word offsets, so a CTA reads its tile list
 //    as a contiguous stream;
@@ -24,12 +28,14 @@
 //    converted once per launch by k_to_tf32) and its 16 weighting-factor
 //    rows (FP64); rows past the end of a mode are zero-filled by the copy;
 //  * the tile is scattered into a zero tile in shared memory laid out per
-//    mode as (s, t, c), a 16-float row per (s, t) with the columns in the
-//    order c = 0,4,8,12, 1,5,9,13, ...: the four A-fragment values a lane
-//    needs from a row (columns t4, t4+4, t4+8, t4+12 of both k-steps) are
-//    one 16-byte load, bank-conflict free; after the products the tile is
-//    zeroed again by writing zero to the cells it set (or by clearing the
-//    whole tile when it holds more nonzeros than the stage);
+//    mode as (s, t, c) in the permuted coordinates: a 16-float row per
+//    (s, t), slabs 260 floats apart; the four A-fragment values a lane needs
+//    from a row (columns t4, t4+4, t4+8, t4+12 of both k-steps) are then
+//    one 16-byte load, bank-conflict free; the weighting rows are staged in
+//    the permuted slab order and the 16 output rows are put back in order
+//    when a target block is flushed; after the products the tile is zeroed
+//    again by writing zero to the cells it set (or by clearing the whole
+//    tile when it holds more nonzeros than the stage);
 //  * the contracted factor is converted once per launch (k_to_tf32_blocks)
 //    into 16-row blocks stored rank-major with the same column order, so a
 //    lane's B-fragment values of one n-tile are one 16-byte load, and a
@@ -52,8 +58,8 @@ namespace cptc {
 namespace {
 
 constexpr int kSt = 16;                // t stride (floats) of the slab layout
-constexpr int kSs = 16 * kSt;          // s stride
-constexpr int kTileFloats = 16 * kSs;  // 4096 floats = 16 KB
+constexpr int kSs = 16 * kSt + 4;      // s stride: slabs 4 banks apart
+constexpr int kTileFloats = 16 * kSs;  // 4160 floats = 16.25 KB
 
 // Position of column c in a 16-float row: columns c, c+4, c+8, c+12 are
 // adjacent, so the fragment values of lane t4 are one 16-byte chunk.
@@ -72,7 +78,9 @@ __global__ void k_pad_counts(const int4* __restrict__ tile, uint64_t n, uint64_t
 }
 
 // One CTA per tile (grid-stride over tiles): the packed words of the tile's
-// nonzeros at its padded offset.
+// nonzeros at its padded offset, coordinates permuted (cpos), element j at
+// position (a*j) mod cnt with a = 101 (103 when 101 divides cnt): a
+// bijection, so every nonzero is stored once.
 __global__ void k_pack_words(const int4* __restrict__ tile, const uint64_t* __restrict__ start,
                              const uint64_t* __restrict__ pst, const uint16_t* __restrict__ lid,
                              const double* __restrict__ val, uint64_t ntiles,
@@ -80,8 +88,13 @@ __global__ void k_pack_words(const int4* __restrict__ tile, const uint64_t* __re
   for (uint64_t k = blockIdx.x; k < ntiles; k += gridDim.x) {
     const int cnt = tile[k].w;
     const uint64_t s0 = start[k], d0 = pst[k];
-    for (int j = threadIdx.x; j < cnt; j += blockDim.x)
-      words[d0 + j] = tf32_of(val[s0 + j]) | (uint32_t)lid[s0 + j];
+    const uint32_t a = (cnt % 101 == 0) ? 103u : 101u;
+    for (int j = threadIdx.x; j < cnt; j += blockDim.x) {
+      const uint32_t l = lid[s0 + j];
+      const uint32_t pl = ((uint32_t)cpos((int)(l >> 8) & 15) << 8) |
+                          ((uint32_t)cpos((int)(l >> 4) & 15) << 4) | (uint32_t)cpos((int)l & 15);
+      words[d0 + (uint64_t)((a * (uint32_t)j) % (uint32_t)cnt)] = tf32_of(val[s0 + j]) | pl;
+    }
     if (threadIdx.x == 0) pst32[k] = (uint32_t)d0;
   }
 }
@@ -212,7 +225,8 @@ __global__ void __launch_bounds__(128, MINB) k_tiles3w(Tile3Args a, const uint32
       const int row = (int)(((float)q + 0.5f) * icps), ch = q - row * cps;
       const uint64_t gr = sbk + row;
       const bool ok = gr < dimS;
-      cp16(dfs + row * R + 2 * ch, a.Fs + (ok ? gr : 0) * (uint64_t)R + 2 * ch, ok);
+      // stored at the tile's (permuted) slab position of this row
+      cp16(dfs + cpos(row) * R + 2 * ch, a.Fs + (ok ? gr : 0) * (uint64_t)R + 2 * ch, ok);
     }
     cp_commit();
   };
@@ -241,7 +255,7 @@ __global__ void __launch_bounds__(128, MINB) k_tiles3w(Tile3Args a, const uint32
 #pragma unroll
       for (int x = 0; x < 4; ++x) acc[q][x] = 0.0;
     for (int t = warp; t < 16; t += WARPS) {
-      const uint64_t row = (uint64_t)tb * 16 + t;
+      const uint64_t row = (uint64_t)tb * 16 + cpos(t);  // stored row t holds row cpos(t)
       for (int r = lane; r < R; r += 32) {
         const double v = accS[t * R + r];
         if (row < dimT && v != 0.0) atomicAdd(a.out + row * (uint64_t)R + r, v);
@@ -256,7 +270,7 @@ __global__ void __launch_bounds__(128, MINB) k_tiles3w(Tile3Args a, const uint32
     const int lt = TS == 0 ? l0 : TS == 1 ? l1 : l2;
     const int lc = CS == 0 ? l0 : CS == 1 ? l1 : l2;
     const int ls = SS == 0 ? l0 : SS == 1 ? l1 : l2;
-    return ls * kSs + lt * kSt + cpos(lc);
+    return ls * kSs + lt * kSt + lc;  // the word's coordinates are already permuted
   };
 
   // Tile metadata two tiles ahead: T1 is the next tile, T2 the one after.
