@@ -345,6 +345,7 @@ def run_engine(a):
     rank_phase_ms = None
     rank_kernel_ms = None
     kern_ms = np.array([[p["sparse_ms"], p["tiles_ms"]] for p in prof])  # (modes, 2)
+    gceil = gather_ceiling(eng, local, t, st["sparse_nnz"], a.rank, [p["sparse_ms"] for p in prof])
     if phase_ms is not None:
         rank_phase_ms = [np.round(phase_ms, 4).tolist()]
         rank_kernel_ms = [np.round(kern_ms, 4).tolist()]
@@ -366,6 +367,8 @@ def run_engine(a):
                 "tile_kernel_ms_per_mode": [p["tiles_ms"] for p in prof128],
                 "final_fit": reps128[-1].fit,
                 "tf32_path": bool(st128["tf32_path"])}
+        r128["gather_ceiling"] = gather_ceiling(eng, local, t, st128["sparse_nnz"], 128,
+                                                r128["sparse_kernel_ms_per_mode"])
 
     if dist is not None:
         import torch
@@ -442,6 +445,7 @@ def run_engine(a):
         "clocks": clocks,
         "roofline": roofline_record(a, t, st, prof),
     }
+    line["roofline"]["gather_ceiling"] = gceil
     if not a.no_cpu_baseline and world == 1:  # measured at N=1 only
         line["cpu_baseline"] = cpu_baseline(t, a.rank)
     print(json.dumps(line), flush=True)
@@ -461,6 +465,36 @@ def recorded_traffic(a):
         return json.loads(prof_file.read_text()).get(f"cfg{a.config}_R{a.rank}")
     except Exception:
         return None
+
+
+def gather_ceiling(eng, device, t, nnz_view, R, sparse_ms) -> dict:
+    """The residual kernel against the floor set by its own memory accesses.
+
+    `replay_ms_per_mode`: a gather-only replay of each mode's residual
+    MTTKRP (the same tasks, records and factor rows with the same lane layout,
+    no arithmetic; cptc_profile_gather), beside the kernel's own time;
+    `frac` = replay time / kernel time.  `uniform_probe_gbs`: uniformly random
+    R-wide rows of an L2-resident matrix of the longest mode's size
+    (cptc_gather_peak), the rate such gathers reach without the tensor's
+    locality; `kernel_row_gbs` counts one row per nonzero at the kernel's
+    rate (the outer rows, reused along fibers, are mostly L1 hits)."""
+    import cptc_b200 as cp
+
+    out = {"unit": "ms"}
+    if t.order == 3:
+        g = [eng.profile_gather(n, reps=3) for n in range(t.order)]
+        rep = [x["replay_ms"] for x in g]
+        ker = [x["kernel_ms"] for x in g]
+        out.update({"replay_ms_per_mode": rep, "kernel_ms_per_mode": ker,
+                    "frac": float(np.sum(rep) / np.sum(ker)) if np.sum(ker) > 0 else None})
+    rows = int(max(t.dims))
+    peak = cp.gather_peak(device, rows, R, max(int(nnz_view), 1 << 20), reps=3)
+    ktime = float(np.mean(sparse_ms)) / 1000.0
+    out.update({"uniform_probe_gbs": peak,
+                "kernel_row_gbs": nnz_view * 8.0 * R / ktime / 1e9 if ktime > 0 else None,
+                "uniform_probe": f"uniformly random rows of an L2-resident {rows}x{R} FP64 "
+                                 "matrix, the kernel's row layout (cptc_gather_peak)"})
+    return out
 
 
 def roofline_record(a, t, st, prof) -> dict:

@@ -7,7 +7,7 @@ cptc_b200.build``.
 """
 from .tensor import (CooTensor, gen_config, gen_uniform, probe_order, read_bin, read_tns,
                      read_tns_cached, write_bin, write_tns)
-from .engine import CptcError, Engine, IterReport, comm_unique_id
+from .engine import CptcError, Engine, IterReport, comm_unique_id, gather_peak
 
 __all__ = [
     "CooTensor",
@@ -16,6 +16,7 @@ __all__ = [
     "IterReport",
     "comm_unique_id",
     "gen_config",
+    "gather_peak",
     "gen_uniform",
     "probe_order",
     "read_bin",

@@ -111,7 +111,10 @@ ENGINE_SYMBOLS = {
     "cptc_mttkrp": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double)]),
     "cptc_mttkrp_timed": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_double)]),
     "cptc_profile_mttkrp": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_double)]),
+    "cptc_profile_gather": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_double)]),
     "cptc_launch_count": (C.c_ulonglong, []),
+    "cptc_gather_peak": (C.c_int, [C.c_int, C.c_uint64, C.c_int, C.c_uint64, C.c_int,
+                                   C.POINTER(C.c_double)]),
     "cptc_phase_timing": (C.c_int, [C.c_void_p, C.c_int]),
     "cptc_phase_times": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.c_int]),
     "cptc_als": (C.c_int, [C.c_void_p, C.c_int, ITER_CB, C.c_void_p]),

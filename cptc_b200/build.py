@@ -37,6 +37,7 @@ CUDA_SRCS = [
     "cuda/reorder_gpu.cu",
     "cuda/engine.cu",
     "cuda/noalloc.cu",
+    "cuda/probe.cu",
 ]
 
 

@@ -983,6 +983,26 @@ int cptc_mttkrp_timed(cptc_ctx* c, int mode, int reps, double* ms) {
   });
 }
 
+int cptc_profile_gather(cptc_ctx* c, int mode, int reps, double* ms2) {
+  return guarded(c, [&](Engine& e) {
+    CPTC_REQUIRE(e.built && e.have_factors && mode >= 0 && mode < e.N && reps > 0 && ms2,
+                 CPTC_E_ARG, "bad mode or call order");
+    CPTC_CUDA(cudaSetDevice(e.device));
+    const cptc::View& v = e.views[mode];
+    ms2[0] = cptc::time_gather_replay(v, e.R, e.F[v.gmode].p, e.F[v.omode[0]].p, reps, e.stream);
+    CPTC_CUDA(cudaMemsetAsync(e.FtV.p, 0, e.dims[mode] * (uint64_t)e.R * sizeof(double),
+                              e.stream));
+    e.mttkrp_sparse(mode);  // warm-up
+    CPTC_CUDA(cudaEventRecord(e.ev[0], e.stream));
+    for (int r = 0; r < reps; ++r) e.mttkrp_sparse(mode);
+    CPTC_CUDA(cudaEventRecord(e.ev[1], e.stream));
+    CPTC_CUDA(cudaEventSynchronize(e.ev[1]));
+    float b = 0.f;
+    CPTC_CUDA(cudaEventElapsedTime(&b, e.ev[0], e.ev[1]));
+    ms2[1] = b / reps;
+  });
+}
+
 int cptc_profile_mttkrp(cptc_ctx* c, int mode, int reps, double* ms3) {
   return guarded(c, [&](Engine& e) {
     CPTC_REQUIRE(e.built && e.have_factors && mode >= 0 && mode < e.N && reps > 0 && ms3,

@@ -29,6 +29,10 @@ struct MttkrpArgs {
 };
 
 void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s);
+// ms per launch of a gather-only replay of view v's order-3 residual MTTKRP
+// accesses (probe.cu): the same records and factor rows, no arithmetic.
+double time_gather_replay(const View& v, int R, const double* Fg, const double* Fo, int reps,
+                          cudaStream_t s);
 
 // Dense 16^3 tiles on the tensor cores: TF32 slabs with FP64 weighting.
 // Slots 0,1,2 are the tile's three modes (order 3: modes 0,1,2; N-order

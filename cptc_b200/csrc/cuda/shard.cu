@@ -7,8 +7,8 @@
 // rank's share would unbalance it (a Zipf head row holds ~15% of a mode,
 // config 4's first block ~45%); the relabelling puts them first, so the
 // prefix of blocks that ends with the last such block is "heavy": its
-// residual nonzeros are dealt to the ranks in turn (by their position in the
-// residual), its tiles likewise, and its rows' partial MTTKRPs are summed by
+// residual nonzeros are dealt to the ranks by a hash of their fiber, its
+// tiles in turn, and its rows' partial MTTKRPs are summed by
 // an all-reduce of the heavy prefix (at most kMaxHeavyRows rows), which every
 // rank then solves itself.
 //
@@ -52,27 +52,41 @@ __global__ void k_tile_hist(const int4* __restrict__ tile, uint64_t n, int slot,
   }
 }
 
-// 1 where the element's target block is in the heavy prefix.
-__global__ void k_heavy_flag(const uint32_t* __restrict__ idx, const uint32_t* __restrict__ sel,
-                             uint64_t n, uint32_t hblocks, uint32_t* __restrict__ hf) {
-  for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < n;
-       k += (uint64_t)gridDim.x * blockDim.x) {
-    const uint32_t e = sel ? sel[k] : (uint32_t)k;
-    hf[k] = (idx[e] >> 4) < hblocks ? 1u : 0u;
-  }
+// Index arrays of the modes that, with the target, key a fiber of the
+// target's view (the modes other than the gathered one).
+struct FiberModes {
+  const uint32_t* p[CPTC_MAX_ORDER];
+  int n;
+};
+
+__device__ __forceinline__ uint32_t mix32(uint32_t h) {
+  h ^= h >> 16;
+  h *= 0x7feb352du;
+  h ^= h >> 15;
+  h *= 0x846ca68bu;
+  h ^= h >> 16;
+  return h;
 }
 
-// Elements of this rank: heavy ones by ordinal (hord = exclusive scan of the
-// heavy flags) modulo G, the others by owned block range [blo, bhi).
+// Elements of this rank: heavy ones by a hash of their fiber (target index
+// and the view's outer indices) modulo G, so that a fiber's nonzeros, which
+// share the outer factor rows, stay on one rank; the others by owned block
+// range [blo, bhi).
 __global__ void k_mine_flag(const uint32_t* __restrict__ idx, const uint32_t* __restrict__ sel,
-                            uint64_t n, const uint32_t* __restrict__ hord, uint32_t hblocks,
-                            uint32_t blo, uint32_t bhi, int G, int rank, uint8_t* __restrict__ mine) {
+                            uint64_t n, FiberModes fm, uint32_t hblocks, uint32_t blo,
+                            uint32_t bhi, int G, int rank, uint8_t* __restrict__ mine) {
   for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < n;
        k += (uint64_t)gridDim.x * blockDim.x) {
     const uint32_t e = sel ? sel[k] : (uint32_t)k;
-    const uint32_t b = idx[e] >> 4;
-    mine[k] = b < hblocks ? ((int)(hord[k] % (uint32_t)G) == rank ? 1 : 0)
-                          : (b >= blo && b < bhi ? 1 : 0);
+    const uint32_t t = idx[e];
+    const uint32_t b = t >> 4;
+    if (b < hblocks) {
+      uint32_t h = mix32(t + 0x9e3779b9u);
+      for (int q = 0; q < fm.n; ++q) h = mix32(h ^ (fm.p[q][e] + 0x9e3779b9u));
+      mine[k] = (int)(h % (uint32_t)G) == rank ? 1 : 0;
+    } else {
+      mine[k] = (b >= blo && b < bhi) ? 1 : 0;
+    }
   }
 }
 
@@ -202,14 +216,22 @@ uint64_t shard_select(Engine& E, int n, const uint32_t* sel, uint64_t nsel, DArr
   out.alloc(mn);
   if (mn == 0) return 0;
   const uint32_t hb = (uint32_t)(E.heavy_rows[n] + 15) / 16;
-  DArray<uint32_t> hf(mn), hord(mn);
+  // Fibers are keyed by the target and every other mode but the longest:
+  // the view's gathered mode for order > 3, and for order 3 usually (that
+  // view keeps whichever order has fewer fibers, in practice the one with
+  // the shorter outer mode; otherwise fibers are split, which costs only
+  // locality).
+  std::vector<int> others;
+  for (int m = 0; m < E.N; ++m)
+    if (m != n) others.push_back(m);
+  std::stable_sort(others.begin(), others.end(),
+                   [&](int x, int y) { return E.dims[x] < E.dims[y]; });
+  FiberModes fm{};
+  fm.n = (int)others.size() - 1;
+  for (int q = 0; q < fm.n; ++q) fm.p[q] = E.idx[others[q]].p;
   DArray<uint8_t> mine(mn);
   const unsigned gb = grid_for(mn, 256, 148 * 16);
-  k_heavy_flag<<<gb, 256, 0, s>>>(E.idx[n].p, sel, mn, hb, hf.p);
-  CPTC_LAUNCH_CHECK();
-  exclusive_scan_u32(hf.p, hord.p, mn, s);
-  k_mine_flag<<<gb, 256, 0, s>>>(E.idx[n].p, sel, mn, hord.p, hb,
-                                 (uint32_t)E.slab_blocks[n][E.rank],
+  k_mine_flag<<<gb, 256, 0, s>>>(E.idx[n].p, sel, mn, fm, hb, (uint32_t)E.slab_blocks[n][E.rank],
                                  (uint32_t)E.slab_blocks[n][E.rank + 1], E.nranks, E.rank, mine.p);
   CPTC_LAUNCH_CHECK();
   if (sel) return select_flagged(sel, mine.p, mn, out.p, s);

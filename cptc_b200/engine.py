@@ -59,6 +59,18 @@ def launch_count() -> int:
     return int(N.engine_lib().cptc_launch_count())
 
 
+def gather_peak(device: int, rows: int, R: int, n: int, reps: int = 3) -> float:
+    """GB/s of uniformly random R-wide FP64 row gathers from an L2-resident
+    rows x R matrix with the residual kernel's row layout (cptc_gather_peak):
+    the ceiling of the sparse MTTKRP's factor-row gathers on this GPU."""
+    out = C.c_double(0.0)
+    rc = N.engine_lib().cptc_gather_peak(int(device), int(rows), int(R), int(n), int(reps),
+                                         C.byref(out))
+    if rc != 0:
+        raise CptcError(rc, "cptc_gather_peak failed")
+    return float(out.value)
+
+
 def comm_unique_id() -> bytes:
     buf = (C.c_ubyte * 128)()
     rc = N.engine_lib().cptc_comm_unique_id(buf)
@@ -216,6 +228,14 @@ class Engine:
         self._check(self._lib.cptc_profile_mttkrp(self._h, int(mode), int(reps), ms),
                     "profile_mttkrp")
         return {"tiles_ms": ms[0], "sparse_ms": ms[1], "total_ms": ms[2]}
+
+    def profile_gather(self, mode: int, reps: int = 3) -> dict:
+        """Device ms per launch of a gather-only replay of the order-3 residual
+        MTTKRP's memory accesses and of the kernel itself (cptc_profile_gather)."""
+        ms = (C.c_double * 2)()
+        self._check(self._lib.cptc_profile_gather(self._h, int(mode), int(reps), ms),
+                    "profile_gather")
+        return {"replay_ms": ms[0], "kernel_ms": ms[1]}
 
     PHASES = ("mttkrp", "inverse_wait", "solve", "exchange", "normalise")
 

@@ -189,6 +189,23 @@ int cptc_profile_mttkrp(cptc_ctx* ctx, int mode, int reps, double ms3[3]);
  * replayed CUDA graph of an ALS iteration counts the kernels it holds). */
 unsigned long long cptc_launch_count(void);
 
+/* The order-3 FP64 residual MTTKRP of `mode` against the floor set by its own
+ * memory accesses (no counterpart in the reference; measurement only):
+ * ms2[0] = ms per launch of a gather-only replay (the same tasks, records and
+ * factor rows with the same lane layout, the fastest of three depths of
+ * records in flight, no arithmetic), ms2[1] = ms per launch of the kernel
+ * itself. Order-3 record views, R in {16, 32, 64, 128}; else CPTC_E_UNSUP. */
+int cptc_profile_gather(cptc_ctx* ctx, int mode, int reps, double ms2[2]);
+
+/* Measured ceiling of the FP64 MTTKRP's factor-row gathers on `device` (no
+ * counterpart in the reference; measurement only): gathers n uniformly
+ * random rows of an L2-resident rows x R FP64 matrix with the residual
+ * kernel's row layout (R/2 lanes up to a warp per row, 16-byte loads) and
+ * nothing else, and writes the rate in GB/s (n * 8R bytes per launch over
+ * its CUDA-event time, mean of `reps` launches). R in {16, 32, 64, 128}.
+ * Allocates and frees its own buffers. */
+int cptc_gather_peak(int device, uint64_t rows, int R, uint64_t n, int reps, double* gbs);
+
 /* Per-phase device times of each mode update (no counterpart in the
  * reference, whose ALS_PROFILE reports the MTTKRP only: src/als.cu:535-604).
  * cptc_phase_timing(ctx, 1) adds timing events after each phase of every
