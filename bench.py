@@ -342,6 +342,7 @@ def run_engine(a):
     # ---- roofline of the dominant kernel -----------------------------------
     prof = [eng.profile_mttkrp(n, reps=3) for n in range(t.order)]
     rank_mode_ms = None
+    shards = None
     rank_phase_ms = None
     rank_kernel_ms = None
     kern_ms = np.array([[p["sparse_ms"], p["tiles_ms"]] for p in prof])  # (modes, 2)
@@ -394,6 +395,12 @@ def run_engine(a):
             kg = [torch.zeros_like(km) for _ in range(world)]
             dist.all_gather(kg, km)
             rank_kernel_ms = [np.round(g.numpy(), 4).tolist() for g in kg]
+        # each rank's share of every mode's MTTKRP (residual nonzeros, rows,
+        # tiles, tile words)
+        mine = {k: list(st[k]) for k in ("local_sparse_nnz", "local_rows", "local_tiles",
+                                         "local_tile_words")}
+        shards = [None] * world
+        dist.all_gather_object(shards, mine)
 
     if rank != 0:
         eng.close()
@@ -434,6 +441,7 @@ def run_engine(a):
             "phase_ms_by_rank": rank_phase_ms,
             "phase_names": list(cp.Engine.PHASES) if rank_phase_ms is not None else None,
             "residual_tile_ms_by_rank": rank_kernel_ms,
+            "shard_by_rank": shards,
             "final_fit": fits[-1],
         },
         "r128": r128,

@@ -70,6 +70,10 @@ class Stats(C.Structure):
         ("nranks", C.c_int),
         ("rank_id", C.c_int),
         ("reorder_ms", C.c_double),
+        ("local_sparse_nnz", C.c_uint64 * MAX_ORDER),
+        ("local_rows", C.c_uint64 * MAX_ORDER),
+        ("local_tiles", C.c_uint64 * MAX_ORDER),
+        ("local_tile_words", C.c_uint64 * MAX_ORDER),
     ]
 
 

@@ -125,6 +125,20 @@ void comm_allgather_rows(Engine& E, int n, double* base) {
                           E.stream));
 }
 
+void comm_allgather_host(Engine& E, const double* in, int count, double* out) {
+  const int G = E.nranks;
+  if (G == 1) {
+    std::memcpy(out, in, sizeof(double) * count);
+    return;
+  }
+  DArray<double> d(((size_t)G + 1) * count);
+  CPTC_CUDA(cudaMemcpyAsync(d.p, in, sizeof(double) * count, cudaMemcpyHostToDevice, E.stream));
+  CPTC_NCCL(ncclAllGather(d.p, d.p + count, count, ncclDouble, comm_of(E), E.stream));
+  CPTC_CUDA(cudaMemcpyAsync(out, d.p + count, sizeof(double) * G * count, cudaMemcpyDeviceToHost,
+                            E.stream));
+  CPTC_CUDA(cudaStreamSynchronize(E.stream));
+}
+
 }  // namespace cptc
 
 extern "C" {

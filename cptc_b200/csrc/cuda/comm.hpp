@@ -33,5 +33,8 @@ void comm_reduce_ftv(Engine& E, int n);
 // In place: every rank's transfer slab r of `base` (I_n rows padded to G
 // slabs) gathered into every rank's copy.
 void comm_allgather_rows(Engine& E, int n, double* base);
+// Host values: out[r * count + i] = rank r's in[i], for every rank
+// (synchronous; every rank calls it at the same point).
+void comm_allgather_host(Engine& E, const double* in, int count, double* out);
 
 }  // namespace cptc

@@ -223,7 +223,25 @@ void Engine::alloc_workspace() {
   }
 }
 
+// With several ranks the slabs are cut twice: the first pass cuts them at
+// equal estimated cost, each rank then times its own MTTKRP of every mode,
+// and the second pass cuts again with each rank's measured time per unit of
+// estimated cost applied to the blocks it held (shard_calibrate).
 void Engine::build(int R_, double threshold, const cptc_opts* o) {
+  for (int m = 0; m < CPTC_MAX_ORDER; ++m) {
+    shard_speed[m].clear();
+    prev_blocks[m].clear();
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  build_pass(R_, threshold, o);
+  if (nranks > 1 && nnz > 0) {
+    shard_calibrate(*this);
+    build_pass(R_, threshold, o);
+  }
+  build_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
+
+void Engine::build_pass(int R_, double threshold, const cptc_opts* o) {
   CPTC_REQUIRE(N >= 2, CPTC_E_ARG, "load a tensor first");
   CPTC_REQUIRE(R_ >= 1 && R_ <= 128, CPTC_E_UNSUP, "rank must be in [1, 128]");
   CPTC_CUDA(cudaSetDevice(device));
@@ -1115,6 +1133,15 @@ int cptc_get_stats(cptc_ctx* c, cptc_stats* s) {
     s->nranks = e.nranks;
     s->rank_id = e.rank;
     s->reorder_ms = e.reorder_ms;
+    for (int m = 0; m < e.N && m < (int)e.views.size(); ++m) {
+      s->local_sparse_nnz[m] = e.views[m].nnz;
+      s->local_rows[m] = e.views[m].nrows;
+      for (int t = 0; t < 3; ++t)
+        if (e.dense_active && e.units.inner[t] == m) {
+          s->local_tiles[m] = e.units.cnt[t];
+          s->local_tile_words[m] = e.generic ? 0 : e.units.wcnt[t];
+        }
+    }
   });
 }
 

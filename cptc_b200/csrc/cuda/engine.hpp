@@ -83,6 +83,7 @@ struct UnitPool {
   DArray<uint32_t> swords[3];
   DArray<uint32_t> order[3];   // visiting order per inner target slot
   uint64_t cnt[3] = {0, 0, 0}; // tiles per inner target slot
+  uint64_t wcnt[3] = {0, 0, 0};  // words of those tiles (order 3, padded to 4 per tile)
   // CTA ranges over each visiting order with balanced estimated costs:
   // blocks + 1 cut points.
   DArray<uint32_t> cut[3];
@@ -171,6 +172,12 @@ struct Engine {
   std::vector<uint64_t> slab[CPTC_MAX_ORDER];
   std::vector<uint64_t> slab_blocks[CPTC_MAX_ORDER];
   uint64_t heavy_rows[CPTC_MAX_ORDER] = {0};
+  // Estimated MTTKRP cost of every rank's share of mode n (the heavy
+  // prefix's share plus its slab), and the measured speed correction per
+  // rank that the second build pass applies to the first pass's slabs.
+  std::vector<double> slab_cost[CPTC_MAX_ORDER];
+  std::vector<double> shard_speed[CPTC_MAX_ORDER];
+  std::vector<uint64_t> prev_blocks[CPTC_MAX_ORDER];
   DArray<double> comm_buf;
 
   cudaEvent_t ev[2 * CPTC_MAX_ORDER + 2] = {};
@@ -215,6 +222,7 @@ struct Engine {
  private:
   void reorder();
   void alloc_workspace();
+  void build_pass(int R, double threshold, const cptc_opts* o);
   void update_mode(int n, bool last);
   void gram_of(int m);
 };

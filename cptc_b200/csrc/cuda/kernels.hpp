@@ -109,6 +109,10 @@ void gpu_degree_rank(Engine& E, std::vector<std::vector<uint32_t>>& rank);
 // residual elements of target mode n (out; the selection or every nonzero
 // when sel is null); this rank's tiles of a target slot in visiting order.
 void shard_plan(Engine& E, const uint32_t* sel, uint64_t nsel);
+// Times this rank's MTTKRP of every mode, gathers the times of all ranks and
+// sets E.shard_speed / E.prev_blocks for the next shard_plan (every rank
+// must call it at the same point).
+void shard_calibrate(Engine& E);
 uint64_t shard_select(Engine& E, int n, const uint32_t* sel, uint64_t nsel, DArray<uint32_t>& out);
 uint64_t shard_tiles(Engine& E, int slot, DArray<uint32_t>& local_order);
 // Copies the tiles listed in E.units.vtile/vstart[slot] into swords[slot]

@@ -10,7 +10,13 @@
 // residual nonzeros are dealt to the ranks by a hash of their fiber, its
 // tiles in turn, and its rows' partial MTTKRPs are summed by
 // an all-reduce of the heavy prefix (at most kMaxHeavyRows rows), which every
-// rank then solves itself.
+// rank then solves itself.  The estimate (residual nonzeros and rows, tile
+// nonzeros and tiles, with fixed relative costs) misses how locality varies
+// along a mode: the residual nonzeros of the light tail rows, whose fibers
+// are short, cost more each than those of the head rows.  So the engine
+// builds twice: each rank times its own MTTKRP of every mode after the first
+// pass (shard_calibrate), and the second pass weighs every block by the time
+// per unit of estimated cost measured on the rank that held it.
 //
 // Reference: cpTC runs on one GPU (src/common.cu:43-46); this is the
 // partition the north star asks for (row slabs, nonzeros sharded to match,
@@ -39,6 +45,24 @@ __global__ void k_block_hist(const uint32_t* __restrict__ idx, const uint32_t* _
     const uint32_t e = sel ? sel[k] : (uint32_t)k;
     atomicAdd(cnt + (idx[e] >> 4), 1ull);
   }
+}
+
+// Nonzeros per target row (residual elements).
+__global__ void k_row_hist(const uint32_t* __restrict__ idx, const uint32_t* __restrict__ sel,
+                           uint64_t n, uint32_t* __restrict__ cnt) {
+  for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < n;
+       k += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t e = sel ? sel[k] : (uint32_t)k;
+    atomicAdd(cnt + idx[e], 1u);
+  }
+}
+
+// Non-empty rows per 16-row block.
+__global__ void k_block_rows(const uint32_t* __restrict__ cnt, uint64_t dim,
+                             unsigned long long* __restrict__ rows) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < dim;
+       i += (uint64_t)gridDim.x * blockDim.x)
+    if (cnt[i]) atomicAdd(rows + (i >> 4), 1ull);
 }
 
 __global__ void k_tile_hist(const int4* __restrict__ tile, uint64_t n, int slot,
@@ -143,6 +167,10 @@ void exclusive_scan_u32(const uint32_t* in, uint32_t* out, uint64_t n, cudaStrea
 // (1.42 against 3.16 ms) 0.029; about 3.2 / R.
 static double tile_cost_ratio(int R) { return std::min(0.5, 3.2 / (double)R); }
 
+// Cost of one non-empty target row of the residual view (the row's write,
+// its row-index load and the task boundary work) in residual-nonzero units.
+static double row_cost(int R) { return 0.0 * R; }
+
 void shard_plan(Engine& E, const uint32_t* sel, uint64_t nsel) {
   const int G = E.nranks;
   cudaStream_t s = E.stream;
@@ -158,12 +186,19 @@ void shard_plan(Engine& E, const uint32_t* sel, uint64_t nsel) {
         if (E.units.inner[q] == n && E.units.nunits > 0) ts = q;
     const uint32_t* msel = ts >= 0 ? sel : nullptr;
     const uint64_t mn = ts >= 0 ? nsel : E.nnz;
-    DArray<unsigned long long> rc(nb), dz(nb), dt(nb);
+    DArray<unsigned long long> rc(nb), dz(nb), dt(nb), rr(nb);
+    DArray<uint32_t> rowc(E.dims[n]);
     CPTC_CUDA(cudaMemsetAsync(rc.p, 0, nb * 8, s));
     CPTC_CUDA(cudaMemsetAsync(dz.p, 0, nb * 8, s));
     CPTC_CUDA(cudaMemsetAsync(dt.p, 0, nb * 8, s));
+    CPTC_CUDA(cudaMemsetAsync(rr.p, 0, nb * 8, s));
+    CPTC_CUDA(cudaMemsetAsync(rowc.p, 0, E.dims[n] * 4, s));
     if (mn) {
       k_block_hist<<<grid_for(mn, 256, 148 * 16), 256, 0, s>>>(E.idx[n].p, msel, mn, rc.p);
+      CPTC_LAUNCH_CHECK();
+      k_row_hist<<<grid_for(mn, 256, 148 * 16), 256, 0, s>>>(E.idx[n].p, msel, mn, rowc.p);
+      CPTC_LAUNCH_CHECK();
+      k_block_rows<<<grid_for(E.dims[n], 256, 148 * 8), 256, 0, s>>>(rowc.p, E.dims[n], rr.p);
       CPTC_LAUNCH_CHECK();
     }
     if (ts >= 0) {
@@ -171,17 +206,20 @@ void shard_plan(Engine& E, const uint32_t* sel, uint64_t nsel) {
           E.units.unit.p, E.units.nunits, ts, dz.p, dt.p);
       CPTC_LAUNCH_CHECK();
     }
-    std::vector<unsigned long long> hrc(nb), hdz(nb), hdt(nb);
+    std::vector<unsigned long long> hrc(nb), hdz(nb), hdt(nb), hrr(nb);
     CPTC_CUDA(cudaMemcpyAsync(hrc.data(), rc.p, nb * 8, cudaMemcpyDeviceToHost, s));
+    CPTC_CUDA(cudaMemcpyAsync(hrr.data(), rr.p, nb * 8, cudaMemcpyDeviceToHost, s));
     CPTC_CUDA(cudaMemcpyAsync(hdz.data(), dz.p, nb * 8, cudaMemcpyDeviceToHost, s));
     CPTC_CUDA(cudaMemcpyAsync(hdt.data(), dt.p, nb * 8, cudaMemcpyDeviceToHost, s));
     CPTC_CUDA(cudaStreamSynchronize(s));
     const double rho = tile_cost_ratio(E.R);
     const double fixed = E.generic ? 512.0 : (double)tile3w_fixed_cost(E.R);
+    const double crow = row_cost(E.R);
     std::vector<double> w(nb);
     double W = 0.0;
     for (uint64_t b = 0; b < nb; ++b) {
-      w[b] = (double)hrc[b] + rho * ((double)hdz[b] + fixed * (double)hdt[b]);
+      w[b] = (double)hrc[b] + crow * (double)hrr[b] +
+             rho * ((double)hdz[b] + fixed * (double)hdt[b]);
       W += w[b];
     }
     // Heavy prefix: up to the last block above an eighth of a rank's share.
@@ -189,6 +227,18 @@ void shard_plan(Engine& E, const uint32_t* sel, uint64_t nsel) {
     for (uint64_t b = 0; b < nb; ++b)
       if (w[b] > W / (8.0 * G)) h = b + 1;
     h = std::min<uint64_t>(h, kMaxHeavyRows / 16);
+    double Wh = 0.0;
+    for (uint64_t b = 0; b < h; ++b) Wh += w[b];
+    // Second pass: the blocks each rank held in the first pass weigh its
+    // measured time per unit of estimated cost (mean 1).
+    std::vector<double> raw = w;
+    const auto& sp = E.shard_speed[n];
+    const auto& pb = E.prev_blocks[n];
+    if ((int)sp.size() == G && (int)pb.size() == G + 1) {
+      for (int r = 0; r < G; ++r)
+        for (uint64_t b = std::max<uint64_t>(pb[r], h); b < std::min<uint64_t>(pb[r + 1], nb); ++b)
+          w[b] *= sp[r];
+    }
     double Wn = 0.0;
     for (uint64_t b = h; b < nb; ++b) Wn += w[b];
     // Slab cuts over the remaining blocks at equal cost, each at the block
@@ -202,11 +252,55 @@ void shard_plan(Engine& E, const uint32_t* sel, uint64_t nsel) {
       while (b < nb && acc + 0.5 * w[b] <= target) acc += w[b++];
       cb[r] = b;
     }
+    // Estimated (uncorrected) cost of each rank's share: its slab and an
+    // equal part of the heavy prefix.
+    E.slab_cost[n].assign(G, Wh / G);
+    for (int r = 0; r < G; ++r)
+      for (uint64_t q = cb[r]; q < cb[r + 1]; ++q) E.slab_cost[n][r] += raw[q];
     E.heavy_rows[n] = std::min<uint64_t>(h * 16, E.dims[n]);
     E.slab[n][0] = 0;
     for (int r = 1; r < G; ++r) E.slab[n][r] = std::min<uint64_t>(cb[r] * 16, E.dims[n]);
     E.slab[n][G] = E.dims[n];
     E.slab_blocks[n] = cb;
+  }
+}
+
+void shard_calibrate(Engine& E) {
+  const int G = E.nranks, N = E.N;
+  std::vector<double> t(N, 0.0), all((size_t)G * N, 0.0);
+  cudaEvent_t e0 = E.ev[0], e1 = E.ev[1];
+  constexpr int kReps = 3;
+  for (int n = 0; n < N; ++n) {
+    E.mttkrp(n);  // warm-up
+    CPTC_CUDA(cudaEventRecord(e0, E.stream));
+    for (int r = 0; r < kReps; ++r) E.mttkrp(n);
+    CPTC_CUDA(cudaEventRecord(e1, E.stream));
+    CPTC_CUDA(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    CPTC_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    t[n] = ms / kReps;
+  }
+  comm_allgather_host(E, t.data(), N, all.data());
+  for (int n = 0; n < N; ++n) {
+    const auto& est = E.slab_cost[n];
+    std::vector<double> k(G, 1.0);
+    double mean = 0.0;
+    bool ok = (int)est.size() == G;
+    for (int r = 0; ok && r < G; ++r) {
+      const double tr = all[(size_t)r * N + n];
+      ok = est[r] > 0.0 && tr > 0.0;
+      if (ok) k[r] = tr / est[r];
+      mean += k[r];
+    }
+    if (!ok) {
+      E.shard_speed[n].clear();
+      E.prev_blocks[n].clear();
+      continue;
+    }
+    mean /= G;
+    for (auto& x : k) x /= mean;
+    E.shard_speed[n] = k;
+    E.prev_blocks[n] = E.slab_blocks[n];
   }
 }
 

@@ -435,6 +435,7 @@ void pack_tile_words(Engine& E) {
   CPTC_CUDA(cudaStreamSynchronize(s));
   const uint64_t total = last[0] + last[1];
   CPTC_REQUIRE(total < (1ull << 32), CPTC_E_UNSUP, "dense tile pool above 2^32 words");
+  for (int t = 0; t < 3; ++t) P.wcnt[t] = total;
   P.words.alloc(total + 4);
   CPTC_CUDA(cudaMemsetAsync(P.words.p, 0, (total + 4) * sizeof(uint32_t), s));
   P.pstart.alloc(n);
@@ -468,6 +469,7 @@ void compact_slot_pool(Engine& E, int slot) {
   const uint64_t n = P.cnt[slot];
   if (n == 0) {
     P.swords[slot].alloc(4);
+    P.wcnt[slot] = 0;
     return;
   }
   DArray<uint64_t> pc(n), nst(n);
@@ -482,6 +484,7 @@ void compact_slot_pool(Engine& E, int slot) {
   CPTC_CUDA(cudaMemcpyAsync(&last[1], pc.p + n - 1, 8, cudaMemcpyDeviceToHost, s));
   CPTC_CUDA(cudaStreamSynchronize(s));
   const uint64_t total = last[0] + last[1];
+  P.wcnt[slot] = total;
   P.swords[slot].alloc(total + 4);
   CPTC_CUDA(cudaMemsetAsync(P.swords[slot].p, 0, (total + 4) * sizeof(uint32_t), s));
   DArray<uint32_t> vs_new(n);

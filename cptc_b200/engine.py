@@ -165,6 +165,8 @@ class Engine:
         out = {k: getattr(s, k) for k, _ in N.Stats._fields_}
         out["dims"] = tuple(int(s.dims[m]) for m in range(s.order))
         out["fiber_mode"] = tuple(int(s.fiber_mode[m]) for m in range(s.order))
+        for k in ("local_sparse_nnz", "local_rows", "local_tiles", "local_tile_words"):
+            out[k] = tuple(int(getattr(s, k)[m]) for m in range(s.order))
         return out
 
     # -- factors ---------------------------------------------------------

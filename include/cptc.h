@@ -111,6 +111,14 @@ typedef struct cptc_stats {
   int nranks, rank_id;
   double reorder_ms;        /* relabelling share of build_ms (HITS, degree
                                order: on the device; order-3 CADR: host)     */
+  /* Per target mode, this rank's share of the MTTKRP (the whole mode on one
+   * rank): residual nonzeros, non-empty target rows of the residual view,
+   * dense tiles and the words of those tiles (nonzeros, each tile padded to
+   * a multiple of 4; order-3 tiles only). */
+  uint64_t local_sparse_nnz[CPTC_MAX_ORDER];
+  uint64_t local_rows[CPTC_MAX_ORDER];
+  uint64_t local_tiles[CPTC_MAX_ORDER];
+  uint64_t local_tile_words[CPTC_MAX_ORDER];
 } cptc_stats;
 
 int cptc_opts_default(cptc_opts* o);
