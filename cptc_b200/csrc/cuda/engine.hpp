@@ -19,13 +19,20 @@ constexpr uint32_t kFibFlag = 0x40000000u;
 constexpr uint32_t kIdxMask = 0x3FFFFFFFu;
 constexpr uint64_t kMaxGatherDim = (1ull << 30);
 
-// Nonzeros of one lane-group task in the sparse MTTKRP: 1024, smaller for
-// small views so that every SM gets work (a power of two >= 64).
+// Nonzeros of one lane-group task in the sparse MTTKRP: at most 1024, and
+// sized so that the tasks fill whole waves of the resident lane groups
+// (`slots`): a view of nnz nonzeros runs in ceil(nnz / (1024 slots)) waves of
+// equal tasks, so no wave is left almost empty (on 8 GPUs a rank with 5.1M
+// residual nonzeros in 256-nonzero tasks ran 2.1 waves and took 35% longer
+// than one with 4.6M); at least 64 nonzeros per task.
 constexpr int kTask = 1024;
-inline uint32_t task_size_for(uint64_t nnz) {
-  uint32_t t = kTask;
-  while (t > 64 && nnz / t < 148ull * 64) t >>= 1;
-  return t;
+inline uint32_t task_size_for(uint64_t nnz, uint64_t slots) {
+  if (slots == 0) slots = 148ull * 64;
+  const uint64_t waves = (nnz + kTask * slots - 1) / (kTask * slots);
+  uint64_t t = (nnz + waves * slots - 1) / (waves ? waves * slots : 1);
+  if (t < 64) t = 64;
+  if (t > (uint64_t)kTask) t = kTask;
+  return (uint32_t)t;
 }
 
 // Sorted view of the nonzeros for one target mode, in the order

@@ -29,6 +29,10 @@ struct MttkrpArgs {
 };
 
 void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s);
+// Lane groups the kernel launch_mttkrp_view picks for a view (records of
+// recw uint4 or SoA arrays, nout outer modes, rank R) keeps resident on the
+// whole of `device` at once.
+uint64_t mttkrp_view_slots(bool rec, int recw, int nout, int R, int device);
 // ms per launch of a gather-only replay of view v's order-3 residual MTTKRP
 // accesses (probe.cu): the same records and factor rows, no arithmetic.
 double time_gather_replay(const View& v, int R, const double* Fg, const double* Fo, int reps,

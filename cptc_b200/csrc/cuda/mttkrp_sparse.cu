@@ -669,7 +669,66 @@ void launch(const MttkrpArgs& a, cudaStream_t s) {
   CPTC_LAUNCH_CHECK();
 }
 
+// Lane groups of kernel `kern` (256 threads, GW-lane groups) resident on
+// the whole GPU at once.
+template <class K>
+uint64_t slots_of(K kern, int GW, bool carve, int device) {
+  if (carve)
+    CPTC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+  int sms = 148, per_sm = 0;
+  CPTC_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  CPTC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0));
+  if (per_sm < 1) per_sm = 1;
+  return (uint64_t)sms * per_sm * 8 * (32 / GW);
+}
+
 }  // namespace
+
+uint64_t mttkrp_view_slots(bool rec, int recw, int nout, int R, int device) {
+  if (rec && recw == 2) {
+    switch (nout * 1000 + R) {
+      case 2008: return slots_of(k_mttkrp_recns<8, 1, 2, 2>, 8, false, device);
+      case 2016: return slots_of(k_mttkrp_recns<8, 2, 2, 2>, 8, false, device);
+      case 2032: return slots_of(k_mttkrp_recns<16, 2, 2, 2>, 16, false, device);
+      case 2064: return slots_of(k_mttkrp_recns<16, 4, 2, 2>, 16, false, device);
+      case 2128: return slots_of(k_mttkrp_recns<32, 4, 1, 2>, 32, false, device);
+      case 3008: return slots_of(k_mttkrp_recns<8, 1, 2, 3>, 8, false, device);
+      case 3016: return slots_of(k_mttkrp_recns<8, 2, 2, 3>, 8, false, device);
+      case 3032: return slots_of(k_mttkrp_recns<16, 2, 2, 3>, 16, false, device);
+      case 3064: return slots_of(k_mttkrp_recns<16, 4, 2, 3>, 16, false, device);
+      case 3128: return slots_of(k_mttkrp_recns<32, 4, 1, 3>, 32, false, device);
+      case 4008: return slots_of(k_mttkrp_recns<8, 1, 2, 4>, 8, false, device);
+      case 4016: return slots_of(k_mttkrp_recns<8, 2, 2, 4>, 8, false, device);
+      case 4032: return slots_of(k_mttkrp_recns<16, 2, 2, 4>, 16, false, device);
+      case 4064: return slots_of(k_mttkrp_recns<16, 4, 2, 4>, 16, false, device);
+      default: return slots_of(k_mttkrp_recns<32, 4, 1, 4>, 32, false, device);
+    }
+  }
+  if (rec) {
+    switch (R) {
+      case 8: return slots_of(k_mttkrp_rec3s<8, 1, 4, 1, false>, 8, true, device);
+      case 16: return slots_of(k_mttkrp_rec3s<8, 2, 2, 4, false>, 8, true, device);
+      case 32: return slots_of(k_mttkrp_rec3s<16, 2, 2, 4, false>, 16, true, device);
+      case 64: return slots_of(k_mttkrp_rec3s<16, 4, 2, 1, true>, 16, false, device);
+      case 128: return slots_of(k_mttkrp_rec3s<32, 4, 1, 1, true>, 32, false, device);
+      default: break;
+    }
+    if (R <= 32) return slots_of(k_mttkrp_rec3<32, 1, false, 4>, 32, false, device);
+    if (R <= 64) return slots_of(k_mttkrp_rec3<32, 2, false, 2>, 32, false, device);
+    return slots_of(k_mttkrp_rec3<32, 4, false, 2>, 32, false, device);
+  }
+  switch (R) {
+    case 8: return slots_of(k_mttkrp_view<8, 1, true, 4>, 8, false, device);
+    case 16: return slots_of(k_mttkrp_view<16, 1, true, 8>, 16, false, device);
+    case 32: return slots_of(k_mttkrp_view<32, 1, true, 8>, 32, false, device);
+    case 64: return slots_of(k_mttkrp_view<32, 2, true, 4>, 32, false, device);
+    case 128: return slots_of(k_mttkrp_view<32, 4, true, 2>, 32, false, device);
+    default: break;
+  }
+  if (R <= 32) return slots_of(k_mttkrp_view<32, 1, false, 8>, 32, false, device);
+  if (R <= 64) return slots_of(k_mttkrp_view<32, 2, false, 4>, 32, false, device);
+  return slots_of(k_mttkrp_view<32, 4, false, 2>, 32, false, device);
+}
 
 void launch_mttkrp_view(const MttkrpArgs& a, cudaStream_t s) {
   if (a.nnz == 0 || a.ntasks <= a.task0) return;

@@ -13,6 +13,7 @@
 #include <numeric>
 
 #include "engine.hpp"
+#include "kernels.hpp"
 
 namespace cptc {
 
@@ -225,10 +226,12 @@ void build_view_order(Engine& E, View& v, int n, const int* order, int nother,
   k_rows_from_pos<<<grid_for(v.nrows, 256, 148 * 16), 256, 0, s>>>(pos.p, v.nrows, E.idx[n].p,
                                                                     perm_a.p, v.rows.p);
   CPTC_LAUNCH_CHECK();
-  // Sized for the whole view: on 8 GPUs, sizing for a rank's share (256
-  // instead of 1024 on config 4) measured slower (more row-boundary atomics
-  // and task set-up than the occupancy it gains).
-  v.task = task_size_for(nsel);
+  // Tasks in whole waves of the kernel's resident lane groups.
+  const bool recs = (v.nout == 1) ||
+                    (v.nout >= 2 && v.nout <= 4 &&
+                     (E.R == 8 || E.R == 16 || E.R == 32 || E.R == 64 || E.R == 128));
+  v.task = task_size_for(nsel, mttkrp_view_slots(recs, v.nout == 1 ? 1 : 2, v.nout, E.R,
+                                                 E.device));
   v.ntasks = (nsel + v.task - 1) / v.task;
   v.task_row.alloc(v.ntasks);
   k_task_rows<<<grid_for(v.ntasks, 256, 148 * 16), 256, 0, s>>>(pos.p, v.nrows, v.ntasks,
