@@ -10,7 +10,8 @@ for the order-3 ALS (cptc_b200/csrc/cuda/shard.cu, comm.cu):
     nonzeros (in the tensor's order), every G-th one starting at its rank;
   * per mode: local MTTKRP -> solve of the own slab rows -> one exchange:
     all-reduce of [Gram partial | fit dots], all-reduce of the heavy rows'
-    partial MTTKRP, every rank's solved slab broadcast to all -> every rank
+    partial MTTKRP, every rank's solved slab shared with all (the unowned
+    rows cleared, then one all-reduce of the rows past the prefix) -> every rank
     solves the heavy rows itself and adds their Gram and dots -> every rank
     normalises the whole factor.
 Run with gloo it checks the partition and the payload of the collectives on
@@ -100,14 +101,14 @@ def shard_als3(t, R, iters, rank, world, dist):
         dist.all_reduce(v)
         return v.numpy()
 
-    def broadcast_slabs(Fn, n):
+    def share_slabs(Fn, n):
+        # the rows past the heavy prefix that this rank does not own are
+        # cleared and rows [H, I) are summed over the ranks (comm.cu)
         H, slab, _ = plan[n]
-        for q in range(world):
-            lo, hi = max(slab[q], H), max(slab[q + 1], H)
-            if hi > lo:
-                v = torch.from_numpy(np.ascontiguousarray(Fn[lo:hi]))
-                dist.broadcast(v, src=q)
-                Fn[lo:hi] = v.numpy()
+        lo, hi = max(slab[rank], H), max(slab[rank + 1], H)
+        Fn[H:lo] = 0.0
+        Fn[hi:] = 0.0
+        Fn[H:] = allreduce(Fn[H:])
 
     for _ in range(iters):
         for n in range(3):
@@ -125,7 +126,7 @@ def shard_als3(t, R, iters, rank, world, dist):
             red = allreduce(np.concatenate(payload))
             if H > 0:
                 M[:H] = allreduce(M[:H])
-            broadcast_slabs(Fn, n)
+            share_slabs(Fn, n)
             if H > 0:  # the heavy rows, solved by every rank, added once
                 Fn[:H] = M[:H] @ A.T / lam
                 red[:R * R] += (Fn[:H].T @ Fn[:H]).ravel()

@@ -77,4 +77,11 @@ def test_noalloc_matches_allocating_residual_on_two_calls():
         got = _noalloc(t, R, factors, lam)
         assert np.isfinite(got)
         assert abs(got - want) <= FP64_TOL * abs(want), (got, want)
+        # anchored on the host as well: sum over the stored nonzeros of
+        # (v - xhat)^2 in numpy, the bound test_exact_residual uses
+        xhat = np.ones((t.nnz, R)) * lam
+        for m in range(len(t.idx)):
+            xhat = xhat * factors[m][t.idx[m]]
+        host = float(np.sum((t.vals - xhat.sum(axis=1)) ** 2))
+        assert abs(got - host) <= 1e-10 * host, (got, host)
         del e
