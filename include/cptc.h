@@ -63,7 +63,9 @@ enum { CPTC_SOLVER_DEFAULT = 0, CPTC_SOLVER_CHOL = 1, CPTC_SOLVER_PINV = 2 };
  * counterpart in the reference, which runs on one GPU).
  *   NCCL: one grouped NCCL call per mode update: all-reduce of the Gram
  *         partials (and fit dots), all-reduce of the heavy prefix's partial
- *         MTTKRP rows, broadcast of every rank's solved slab (the default).
+ *         MTTKRP rows, and an all-reduce of the factor rows past that prefix,
+ *         each rank contributing its solved slab and zeros elsewhere (the
+ *         default).
  *   PEER: reserved (a peer-memory exchange); cptc_build returns
  *         CPTC_E_UNSUP for it on several ranks. */
 enum { CPTC_EXCHANGE_NCCL = 0, CPTC_EXCHANGE_PEER = 1 };
@@ -227,7 +229,7 @@ int cptc_gather_peak(int device, uint64_t rows, int R, uint64_t n, int reps, dou
  *      column dots on the last mode)
  *   3  the exchange: partial sums, and on several GPUs one NCCL group
  *      (all-reduce of Gram and dots, all-reduce of the heavy prefix's
- *      MTTKRP, broadcast of every rank's solved rows), then the solve of
+ *      MTTKRP, all-reduce sharing every rank's solved rows), then the solve of
  *      the heavy prefix
  *   4  normalisation (and the fit on the last mode)
  * Writes at most `cap` values and returns how many (0 when phase timing is
