@@ -55,9 +55,10 @@ def parse_args():
     p.add_argument("--exchange", default="nccl", choices=["nccl"],
                    help="how the ranks combine a mode update (several GPUs): one grouped "
                         "NCCL call per mode update")
-    p.add_argument("--e2e-sharded", action="store_true",
-                   help="e2e on several GPUs: each rank uploads 1/G of every factor and the "
-                        "pieces are all-gathered on the GPUs (cptc_set_factors_sharded)")
+    p.add_argument("--e2e-replicated", action="store_true",
+                   help="e2e on several GPUs: every rank uploads and reads back whole factors "
+                        "(default: each rank moves its 1/G of every factor and the pieces are "
+                        "all-gathered on the GPUs, cptc_set_factors_sharded)")
     p.add_argument("--no-r128", action="store_true",
                    help="skip the R=128 sub-record of an R=32 run")
     p.add_argument("--phases", type=int, default=0,
@@ -313,7 +314,7 @@ def run_engine(a):
     h2d = sum(f.nbytes for f in host_F)
     barrier()
     te0 = time.perf_counter()
-    sharded = a.e2e_sharded and world > 1
+    sharded = (not a.e2e_replicated) and world > 1
     for _ in range(a.steps):
         for m in range(t.order):
             eng.set_factor(m, host_F[m], sharded=sharded)

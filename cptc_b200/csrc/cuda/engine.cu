@@ -668,7 +668,7 @@ void Engine::update_mode(int n, bool last) {
   phase_end(1);
   // The Gram partial (and fit dots) summed over blocks and ranks; with
   // several ranks grouped with the all-reduce of the heavy prefix's partial
-  // MTTKRP and the broadcast of every rank's solved slab.
+  // MTTKRP and the all-reduce that shares every rank's solved slab.
   double* gsum = comm_exchange_mode(*this, n, nb, last ? nd : -1);
   const uint64_t H = heavy_rows[n];
   if (H > 0) {

@@ -53,7 +53,7 @@ def test_cli_flags():
     out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--help"],
                          capture_output=True, text=True, check=True).stdout
     for flag in ("--gpus", "--steps", "--warmup", "--impl", "--rank", "--exchange",
-                 "--e2e-sharded", "--phases"):
+                 "--e2e-replicated", "--phases"):
         assert flag in out
 
 
