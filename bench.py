@@ -53,8 +53,8 @@ def parse_args():
     p.add_argument("--keep-tns", default="", help="reference arm: keep the .tns it writes here")
     p.add_argument("--ref-log", default="", help="reference arm: save cpTC's stdout here")
     p.add_argument("--exchange", default="nccl", choices=["nccl"],
-                   help="how the ranks combine a mode update (several GPUs): one grouped "
-                        "NCCL call per mode update")
+                   help="how the ranks combine a mode update (several GPUs): one NCCL "
+                        "all-reduce per mode update")
     p.add_argument("--e2e-replicated", action="store_true",
                    help="e2e on several GPUs: every rank uploads and reads back whole factors "
                         "(default: each rank moves its 1/G of every factor and the pieces are "

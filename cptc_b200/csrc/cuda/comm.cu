@@ -72,14 +72,10 @@ void comm_prepare(Engine& E) {
 
 namespace {
 
-// Every rank's solved rows [row_lo(q), row_hi(q)) of `base` into every
-// replica with one all-reduce: clear_unowned clears the rows past the heavy
-// prefix that this rank does not own (before the NCCL group), then
-// sum_rows sums rows [H, I) over the ranks (inside it).  A row has one
-// nonzero contribution, so its sum is the owner's values exactly (x + 0 = x)
-// and every replica holds the same bits.  One collective of (I - H) x R
-// doubles replaces G broadcasts of unequal slabs, which ran one after
-// another (8 B200s, config 4, mode 2: 0.15-0.18 ms per mode update).
+// The rows past the heavy prefix that this rank does not own, cleared: a
+// row of `base` summed over the ranks then has one nonzero term, so its sum
+// is the owner's values exactly (x + 0 = x) and every replica holds the same
+// bits.
 void clear_unowned(Engine& E, int n, double* base) {
   const uint64_t H = E.heavy_rows[n], I = E.dims[n], R = (uint64_t)E.R;
   const uint64_t lo = E.row_lo(n), hi = E.row_hi(n);
@@ -87,45 +83,44 @@ void clear_unowned(Engine& E, int n, double* base) {
   if (lo > H) CPTC_CUDA(cudaMemsetAsync(base + H * R, 0, (lo - H) * R * sizeof(double), E.stream));
   if (I > hi) CPTC_CUDA(cudaMemsetAsync(base + hi * R, 0, (I - hi) * R * sizeof(double), E.stream));
 }
-void sum_rows(Engine& E, int n, double* base) {
-  const uint64_t H = E.heavy_rows[n], I = E.dims[n], R = (uint64_t)E.R;
-  if (I <= H) return;
-  CPTC_NCCL(ncclAllReduce(base + H * R, base + H * R, (I - H) * R, ncclDouble, ncclSum,
-                          comm_of(E), E.stream));
-}
 
 }  // namespace
 
+// With several ranks the mode update's whole exchange is ONE all-reduce over
+// FtV, whose rows are free once the own slab is solved:
+//   rows [0, H)    the heavy prefix's partial MTTKRP (summed: the full rows),
+//   rows [H, I)    this rank's solved slab rows, zeros elsewhere (summed:
+//                  every rank's rows, exactly),
+//   past row I     the Gram partial sum and fit dots (summed: the totals);
+// then rows [H, I) are copied into F[n].  Grouping the three all-reduces and
+// G slab broadcasts of unequal length instead cost 0.05-0.1 ms per mode
+// update on 4 B200s (per-collective latency), one collective a fraction.
 double* comm_exchange_mode(Engine& E, int n, int nblk, int ndots) {
   const int RR = E.R * E.R;
-  double* out = E.comm_buf.p;
+  const uint64_t R = (uint64_t)E.R, I = E.dims[n], H = E.heavy_rows[n];
+  double* out = E.nranks > 1 ? E.FtV.p + I * R : E.comm_buf.p;
   launch_partial_sum(E.gpart.p, nblk, RR, out, E.stream);
   if (ndots >= 0) launch_partial_sum(E.dots.p, ndots, E.R, out + RR, E.stream);
   if (E.nranks > 1) {
-    const uint64_t H = E.heavy_rows[n];
-    clear_unowned(E, n, E.F[n].p);
-    CPTC_NCCL(ncclGroupStart());
-    CPTC_NCCL(ncclAllReduce(out, out, RR + (ndots >= 0 ? E.R : 0), ncclDouble, ncclSum, comm_of(E),
-                            E.stream));
-    if (H > 0)
-      CPTC_NCCL(ncclAllReduce(E.FtV.p, E.FtV.p, H * (uint64_t)E.R, ncclDouble, ncclSum, comm_of(E),
-                              E.stream));
-    sum_rows(E, n, E.F[n].p);
-    CPTC_NCCL(ncclGroupEnd());
+    const uint64_t lo = E.row_lo(n), hi = E.row_hi(n);
+    if (hi > lo)
+      CPTC_CUDA(cudaMemcpyAsync(E.FtV.p + lo * R, E.F[n].p + lo * R, (hi - lo) * R * sizeof(double),
+                                cudaMemcpyDeviceToDevice, E.stream));
+    clear_unowned(E, n, E.FtV.p);
+    CPTC_NCCL(ncclAllReduce(E.FtV.p, E.FtV.p, I * R + RR + (ndots >= 0 ? R : 0), ncclDouble,
+                            ncclSum, comm_of(E), E.stream));
+    if (I > H)
+      CPTC_CUDA(cudaMemcpyAsync(E.F[n].p + H * R, E.FtV.p + H * R, (I - H) * R * sizeof(double),
+                                cudaMemcpyDeviceToDevice, E.stream));
   }
   return out;
 }
 
 void comm_reduce_ftv(Engine& E, int n) {
   if (E.nranks == 1) return;
-  const uint64_t H = E.heavy_rows[n];
   clear_unowned(E, n, E.FtV.p);
-  CPTC_NCCL(ncclGroupStart());
-  if (H > 0)
-    CPTC_NCCL(ncclAllReduce(E.FtV.p, E.FtV.p, H * (uint64_t)E.R, ncclDouble, ncclSum, comm_of(E),
-                            E.stream));
-  sum_rows(E, n, E.FtV.p);
-  CPTC_NCCL(ncclGroupEnd());
+  CPTC_NCCL(ncclAllReduce(E.FtV.p, E.FtV.p, E.dims[n] * (uint64_t)E.R, ncclDouble, ncclSum,
+                          comm_of(E), E.stream));
 }
 
 void comm_allgather_rows(Engine& E, int n, double* base) {

@@ -3,10 +3,9 @@
 // Rows of every mode are owned in slabs and each rank holds only the
 // nonzeros of its rows, plus an equal share of a heavy prefix of rows whose
 // partial MTTKRPs are all-reduced (shard.cu).  A mode update then needs one
-// grouped NCCL call: the all-reduce of [Gram partial | fit dots], the
-// all-reduce of the heavy prefix and the all-reduce that puts every rank's
-// solved slab into every replica of the factor (each rank contributes its
-// own rows and zeros elsewhere).
+// NCCL all-reduce, over [the heavy prefix's partial MTTKRP | every rank's
+// solved slab, each rank contributing its own rows and zeros elsewhere |
+// Gram partial and fit dots].
 #pragma once
 #include "engine.hpp"
 
@@ -24,13 +23,13 @@ uint64_t slab_rows(const Engine& E, int m);
 
 // Sums, in a fixed order over blocks, the nblk per-block Gram partials
 // (R x R) and, when ndots >= 0, the ndots per-block column dot products (R,
-// stored after the Gram) into E.comm_buf; with several ranks, in one NCCL
-// group, all-reduces that buffer and the heavy prefix of FtV and shares
-// every rank's solved rows of F[n] with the others (its unowned rows past the
-// prefix cleared, then one all-reduce of rows [H, I)).  Returns E.comm_buf.
+// stored after the Gram).  One rank: into E.comm_buf.  Several ranks: into
+// FtV's rows past I_n, then one all-reduce of FtV = [heavy prefix's partial
+// MTTKRP | this rank's solved rows of F[n], zeros elsewhere | those sums],
+// and rows [H, I_n) copied back into F[n].  Returns where the sums are.
 double* comm_exchange_mode(Engine& E, int n, int nblk, int ndots);
-// The full MTTKRP of mode n in every rank's FtV (heavy prefix all-reduced,
-// slabs shared as in comm_exchange_mode).
+// The full MTTKRP of mode n in every rank's FtV (one all-reduce: heavy
+// prefix partials, own slab rows, zeros elsewhere).
 void comm_reduce_ftv(Engine& E, int n);
 // In place: every rank's transfer slab r of `base` (I_n rows padded to G
 // slabs) gathered into every rank's copy.

@@ -203,7 +203,9 @@ uint64_t Engine::padded_rows(int m) const {
 void Engine::alloc_workspace() {
   uint64_t maxd = 0;
   for (int m = 0; m < N; ++m) maxd = std::max<uint64_t>(maxd, padded_rows(m));
-  FtV.alloc(maxd * (uint64_t)R);
+  // FtV holds the MTTKRP of a mode; on several ranks its rows past the
+  // mode's length also carry the exchange's Gram and dot sums (R + 1 rows).
+  FtV.alloc((maxd + R + 1) * (uint64_t)R);
   FtF.alloc((uint64_t)R * R);
   Ainv.alloc(2 * (uint64_t)R * R + 1);
   gpart_blocks = 148;

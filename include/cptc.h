@@ -61,11 +61,10 @@ enum { CPTC_REORDER_NONE = 0, CPTC_REORDER_CADR = 1, CPTC_REORDER_HITS = 2,
 enum { CPTC_SOLVER_DEFAULT = 0, CPTC_SOLVER_CHOL = 1, CPTC_SOLVER_PINV = 2 };
 /* How the ranks of a multi-GPU context combine a mode update (no
  * counterpart in the reference, which runs on one GPU).
- *   NCCL: one grouped NCCL call per mode update: all-reduce of the Gram
- *         partials (and fit dots), all-reduce of the heavy prefix's partial
- *         MTTKRP rows, and an all-reduce of the factor rows past that prefix,
- *         each rank contributing its solved slab and zeros elsewhere (the
- *         default).
+ *   NCCL: one NCCL all-reduce per mode update, of one buffer holding the
+ *         heavy prefix's partial MTTKRP rows, the factor rows past that
+ *         prefix (each rank contributing its solved slab and zeros
+ *         elsewhere) and the Gram partials (and fit dots) (the default).
  *   PEER: reserved (a peer-memory exchange); cptc_build returns
  *         CPTC_E_UNSUP for it on several ranks. */
 enum { CPTC_EXCHANGE_NCCL = 0, CPTC_EXCHANGE_PEER = 1 };
@@ -139,7 +138,7 @@ const char* cptc_last_error(const cptc_ctx* ctx);
  * of equal estimated MTTKRP cost and each rank keeps only the nonzeros (FP64
  * residual and dense tiles) of its rows; a heavy prefix of rows (a Zipf
  * head) has its nonzeros dealt to all ranks and its partial rows
- * all-reduced.  Each mode update is one grouped NCCL call (see
+ * all-reduced.  Each mode update is one NCCL all-reduce (see
  * CPTC_EXCHANGE_NCCL) and every rank ends with the whole factor.  The
  * reference runs on one GPU.  A rank that stops calling leaves the others'
  * next collective waiting on the GPU: callers detect a lost rank on the host
@@ -228,8 +227,8 @@ int cptc_gather_peak(int device, uint64_t rows, int R, uint64_t n, int reps, dou
  *   2  apply the inverse to this rank's rows, Gram partials (and the fit's
  *      column dots on the last mode)
  *   3  the exchange: partial sums, and on several GPUs one NCCL group
- *      (all-reduce of Gram and dots, all-reduce of the heavy prefix's
- *      MTTKRP, all-reduce sharing every rank's solved rows), then the solve of
+ *      (one all-reduce of the heavy prefix's MTTKRP, every rank's solved
+ *      rows, Gram and dots), then the solve of
  *      the heavy prefix
  *   4  normalisation (and the fit on the last mode)
  * Writes at most `cap` values and returns how many (0 when phase timing is

@@ -8,12 +8,11 @@ for the order-3 ALS (cptc_b200/csrc/cuda/shard.cu, comm.cu):
     slabs of equal weight (each cut at the nearest block boundary);
   * each rank keeps the nonzeros of its slab and, of the heavy prefix's
     nonzeros (in the tensor's order), every G-th one starting at its rank;
-  * per mode: local MTTKRP -> solve of the own slab rows -> one exchange:
-    all-reduce of [Gram partial | fit dots], all-reduce of the heavy rows'
-    partial MTTKRP, every rank's solved slab shared with all (the unowned
-    rows cleared, then one all-reduce of the rows past the prefix) -> every rank
-    solves the heavy rows itself and adds their Gram and dots -> every rank
-    normalises the whole factor.
+  * per mode: local MTTKRP -> solve of the own slab rows -> one all-reduce
+    of [the heavy rows' partial MTTKRP | every rank's solved slab rows,
+    zeros elsewhere | Gram partial and fit dots] -> every rank solves the
+    heavy rows itself and adds their Gram and dots -> every rank normalises
+    the whole factor.
 Run with gloo it checks the partition and the payload of the collectives on
 the host.
 """
@@ -101,14 +100,20 @@ def shard_als3(t, R, iters, rank, world, dist):
         dist.all_reduce(v)
         return v.numpy()
 
-    def share_slabs(Fn, n):
-        # the rows past the heavy prefix that this rank does not own are
-        # cleared and rows [H, I) are summed over the ranks (comm.cu)
+    def exchange(M, Fn, hdr, n):
+        # one all-reduce over [MTTKRP rows of the heavy prefix | this rank's
+        # solved rows past it, zeros elsewhere | Gram and dot partials]
+        # (comm.cu: comm_exchange_mode)
         H, slab, _ = plan[n]
         lo, hi = max(slab[rank], H), max(slab[rank + 1], H)
-        Fn[H:lo] = 0.0
-        Fn[hi:] = 0.0
-        Fn[H:] = allreduce(Fn[H:])
+        buf = np.zeros((t.dims[n], R))
+        buf[:H] = M[:H]
+        buf[lo:hi] = Fn[lo:hi]
+        red = allreduce(np.concatenate([buf.ravel(), hdr]))
+        rows = red[:t.dims[n] * R].reshape(t.dims[n], R)
+        M[:H] = rows[:H]
+        Fn[H:] = rows[H:]
+        return red[t.dims[n] * R:]
 
     for _ in range(iters):
         for n in range(3):
@@ -123,10 +128,7 @@ def shard_als3(t, R, iters, rank, world, dist):
             payload = [(Fn[lo:hi].T @ Fn[lo:hi]).ravel()]
             if n == 2:
                 payload.append(np.einsum("kr,kr->r", Fn[lo:hi], M[lo:hi]))
-            red = allreduce(np.concatenate(payload))
-            if H > 0:
-                M[:H] = allreduce(M[:H])
-            share_slabs(Fn, n)
+            red = exchange(M, Fn, np.concatenate(payload), n)
             if H > 0:  # the heavy rows, solved by every rank, added once
                 Fn[:H] = M[:H] @ A.T / lam
                 red[:R * R] += (Fn[:H].T @ Fn[:H]).ravel()

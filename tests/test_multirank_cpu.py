@@ -3,7 +3,7 @@
 tests/multirank.py restates the engine's distributed ALS (rows in slabs of
 equal nonzero weight with each rank keeping its rows' nonzeros, a heavy prefix
 of rows shared out by nonzero and all-reduced, one exchange per mode: Gram
-all-reduce, heavy-row all-reduce, one all-reduce of the slabs) over world-size 2 and 3
+all-reduce, heavy-row all-reduce and the slabs in one all-reduce) over world-size 2 and 3
 gloo groups; it must reproduce the single-process ALS, and every rank must end
 with the same factors.  One tensor has a head row larger than a rank's share,
 so that row is split between ranks.
