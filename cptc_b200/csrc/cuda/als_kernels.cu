@@ -337,9 +337,12 @@ __global__ void __launch_bounds__(NWARP * 32) k_sweep_inverse(GPtrs g, int ng, i
 // ---------------------------------------------------------------------------
 // F[i, r] = sum_s FtV[i, s] * Ainv[s, r]  (Ainv symmetric), optionally divided
 // by lambda[r] (src/als.cu:496-500), with the Gram of the written rows
-// accumulated per block.  Rows are staged kGramRows at a time; Ainv lives in
-// shared memory.  Thread layout: 16 x 16 threads, each a TM x TM tile of the
-// 32-row x Rp output slab's Gram and of the product.
+// accumulated per block and, when dots is set, the fit's column dot products
+// sum_i F[i, r] * FtV[i, r] of the written rows (src/als.cu:659-715) per block
+// as well.  Rows are staged kGramRows at a time; Ainv lives in shared memory.
+// Thread layout: 16 x 16 threads, each a TM x TM tile of the 32-row x Rp
+// output slab's Gram and of the product; every output a thread writes is in
+// column tid % Rp (Rp divides 256), so its dot partial is one column's.
 // ---------------------------------------------------------------------------
 template <int TM>
 __global__ void __launch_bounds__(256) k_apply_solve(const double* __restrict__ FtV,
@@ -347,8 +350,10 @@ __global__ void __launch_bounds__(256) k_apply_solve(const double* __restrict__ 
                                                      const double* __restrict__ lambda,
                                                      int divide_lambda, uint64_t rows, int R,
                                                      double* __restrict__ F,
-                                                     double* __restrict__ part) {
+                                                     double* __restrict__ part,
+                                                     double* __restrict__ dots) {
   constexpr int Rp = 16 * TM;
+  static_assert(256 % Rp == 0, "a thread's outputs share one column");
   extern __shared__ double sm[];
   double* sA = sm;                      // Rp * Rp
   double* sX = sA + Rp * Rp;            // kGramRows * Rp  (FtV slab)
@@ -364,6 +369,7 @@ __global__ void __launch_bounds__(256) k_apply_solve(const double* __restrict__ 
   for (int x = 0; x < TM; ++x)
 #pragma unroll
     for (int y = 0; y < TM; ++y) acc[x][y] = 0.0;
+  double dacc = 0.0;
   for (uint64_t r0 = (uint64_t)blockIdx.x * kGramRows; r0 < rows;
        r0 += (uint64_t)gridDim.x * kGramRows) {
     const int nr = (int)((rows - r0 < (uint64_t)kGramRows) ? rows - r0 : kGramRows);
@@ -381,6 +387,7 @@ __global__ void __launch_bounds__(256) k_apply_solve(const double* __restrict__ 
         for (int k = 0; k < R; ++k) s = fma(sX[i * Rp + k], sA[k * Rp + r], s);
         if (divide_lambda) s /= lambda[r];
         F[(r0 + i) * (uint64_t)R + r] = s;
+        dacc = fma(s, sX[i * Rp + r], dacc);
       }
       sY[o] = s;
     }
@@ -388,6 +395,16 @@ __global__ void __launch_bounds__(256) k_apply_solve(const double* __restrict__ 
     gram_tile<TM>(sY, nr, Rp, a0, b0, acc);
   }
   store_partial<TM>(part + (uint64_t)blockIdx.x * R * R, R, a0, b0, acc);
+  if (dots != nullptr) {
+    __syncthreads();  // sX is free
+    sX[tid] = dacc;
+    __syncthreads();
+    if (tid < R) {
+      double t = 0.0;
+      for (int k = 0; k < 256 / Rp; ++k) t += sX[k * Rp + tid];
+      dots[(uint64_t)blockIdx.x * R + tid] = t;
+    }
+  }
 }
 
 __global__ void k_norm_finalize(const double* __restrict__ part, int nblk, int R,
@@ -429,29 +446,6 @@ __global__ void k_scale_cols(double* __restrict__ F, uint64_t n, int R,
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
        i += (uint64_t)gridDim.x * blockDim.x)
     F[i] *= scale[i % R];
-}
-
-__global__ void __launch_bounds__(256) k_col_dots(const double* __restrict__ F,
-                                                  const double* __restrict__ X, uint64_t rows,
-                                                  int R, double* __restrict__ part) {
-  __shared__ double sh[256];
-  // Thread t accumulates column (t % R) over rows t/R, t/R + 256/R, ...
-  const int tid = threadIdx.x;
-  const int per = 256 / R > 0 ? 256 / R : 1;
-  double s = 0.0;
-  if (R <= 256) {
-    const int c = tid % R, r0 = tid / R;
-    if (r0 < per)
-      for (uint64_t i = (uint64_t)blockIdx.x * per + r0; i < rows; i += (uint64_t)gridDim.x * per)
-        s = fma(F[i * R + c], X[i * R + c], s);
-  }
-  sh[tid] = s;
-  __syncthreads();
-  if (tid < R) {
-    double t = 0.0;
-    for (int k = 0; k < per; ++k) t += sh[k * R + tid];
-    part[(uint64_t)blockIdx.x * R + tid] = t;
-  }
 }
 
 __global__ void k_fit_final(const double* __restrict__ dot_part, int nblk,
@@ -603,7 +597,7 @@ void launch_sym_inverse(const double* const* Gs, int ng, int R, int mode, double
 
 int launch_apply_solve(const double* FtV, const double* Ainv, const double* lambda,
                        int divide_lambda, uint64_t rows, int R, double* F, double* part,
-                       int max_blocks, cudaStream_t s) {
+                       int max_blocks, cudaStream_t s, double* dots) {
   int nblk = (int)((rows + kGramRows - 1) / kGramRows);
   if (nblk > max_blocks) nblk = max_blocks;
   if (nblk < 1) nblk = 1;
@@ -614,7 +608,7 @@ int launch_apply_solve(const double* FtV, const double* Ainv, const double* lamb
     CPTC_CUDA(cudaFuncSetAttribute(k_apply_solve<TM>,                                        \
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
     k_apply_solve<TM><<<nblk, 256, smem, s>>>(FtV, Ainv, lambda, divide_lambda, rows, R, F,  \
-                                              part);                                         \
+                                              part, dots);                                   \
   } while (0)
   switch (Rp) {
     case 16: CPTC_APPLY(1); break;
@@ -659,17 +653,6 @@ void launch_scale_cols(double* F, uint64_t rows, int R, const double* scale, cud
   const uint64_t n = rows * (uint64_t)R;
   k_scale_cols<<<grid_for(n, 256, 148 * 32), 256, 0, s>>>(F, n, R, scale);
   CPTC_LAUNCH_CHECK();
-}
-
-int launch_col_dots(const double* F, const double* FtV, uint64_t rows, int R, double* part,
-                    int max_blocks, cudaStream_t s) {
-  const int per = 256 / R > 0 ? 256 / R : 1;
-  int nblk = (int)((rows + per - 1) / per);
-  if (nblk > max_blocks) nblk = max_blocks;
-  if (nblk < 1) nblk = 1;
-  k_col_dots<<<nblk, 256, 0, s>>>(F, FtV, rows, R, part);
-  CPTC_LAUNCH_CHECK();
-  return nblk;
 }
 
 void launch_fit_final(const double* dot_part, int nblk, const double* scale, const double* lambda,

@@ -660,13 +660,13 @@ void Engine::update_mode(int n, bool last) {
   phase_end(0);
   const int div = generic ? 0 : 1;
   const uint64_t lo = row_lo(n), rows = row_hi(n) - lo;
-  const int nb = launch_apply_solve(FtV.p + lo * R, Ainv.p, lambda.p, div, rows, R,
-                                    F[n].p + lo * R, gpart.p, gpart_blocks, stream);
   // The last mode also yields the fit's column dot products, taken on the
-  // solved (not yet normalised) rows and scaled with the column scales.
-  const int nd = last ? launch_col_dots(F[n].p + lo * R, FtV.p + lo * R, rows, R, dots.p,
-                                        gpart_blocks, stream)
-                      : 0;
+  // solved (not yet normalised) rows in the same pass and scaled with the
+  // column scales.
+  const int nb = launch_apply_solve(FtV.p + lo * R, Ainv.p, lambda.p, div, rows, R,
+                                    F[n].p + lo * R, gpart.p, gpart_blocks, stream,
+                                    last ? dots.p : nullptr);
+  const int nd = last ? nb : 0;
   phase_end(1);
   // The Gram partial (and fit dots) summed over blocks and ranks; with
   // several ranks grouped with the all-reduce of the heavy prefix's partial
@@ -677,12 +677,9 @@ void Engine::update_mode(int n, bool last) {
     // The heavy prefix, now summed over the ranks, is solved by every rank
     // (the same bits everywhere) and its Gram and dots added once.
     const int nbh = launch_apply_solve(FtV.p, Ainv.p, lambda.p, div, H, R, F[n].p, gpart.p,
-                                       gpart_blocks, stream);
+                                       gpart_blocks, stream, last ? dots.p : nullptr);
     launch_partial_sum_add(gpart.p, nbh, R * R, gsum, stream);
-    if (last) {
-      const int ndh = launch_col_dots(F[n].p, FtV.p, H, R, dots.p, gpart_blocks, stream);
-      launch_partial_sum_add(dots.p, ndh, R, gsum + (size_t)R * R, stream);
-    }
+    if (last) launch_partial_sum_add(dots.p, nbh, R, gsum + (size_t)R * R, stream);
   }
   phase_end(2);
   launch_norm_finalize(gsum, 1, R, generic ? 1 : 0, lambda.p, G[n].p, colscale(), stream);

@@ -149,10 +149,12 @@ enum { kInvPinv = 0, kInvCholRidge = 1, kInvAuto = 2 };
 void launch_sym_inverse(const double* const* Gs, int ng, int R, int mode, double* FtF,
                         double* Ainv, int* status, cudaStream_t s);
 // F[i,:] = (FtV[i,:] * Ainv) ./ (divide_lambda ? lambda : 1) for rows
-// [0, rows); partial Grams of the written rows into part; returns nblk.
+// [0, rows); partial Grams of the written rows into part and, when dots is
+// given, partials of the fit's column dots sum_i F[i,r] * FtV[i,r] into
+// dots (nblk x R); returns nblk.
 int launch_apply_solve(const double* FtV, const double* Ainv, const double* lambda,
                        int divide_lambda, uint64_t rows, int R, double* F, double* part,
-                       int max_blocks, cudaStream_t s);
+                       int max_blocks, cudaStream_t s, double* dots = nullptr);
 // From the Gram partials of the solved factor: column norms, new lambda and
 // the Gram of the normalised factor; scale[r] = multiplier for column r.
 //   generic_norm = 0: order-3 rule (norm < 1e-14 -> column 0, lambda 0,
@@ -164,9 +166,6 @@ void launch_norm_finalize(const double* part, int nblk, int R, int generic_norm,
 void launch_scale_cols(double* F, uint64_t rows, int R, const double* scale, cudaStream_t s);
 // y += x over n doubles.
 void launch_add_into(double* y, const double* x, uint64_t n, cudaStream_t s);
-// dots[r] partials of sum_i F[i,r] * FtV[i,r]; returns nblk.
-int launch_col_dots(const double* F, const double* FtV, uint64_t rows, int R, double* part,
-                    int max_blocks, cudaStream_t s);
 // out[0] = iprod = sum_r lambda_r dot_r (dot_r * scale[r] when scale is
 // given), out[1] = model^2.
 void launch_fit_final(const double* dot_part, int nblk, const double* scale, const double* lambda,
