@@ -359,7 +359,9 @@ def run_engine(a):
         eng.init_factors()
         eng.als(a.warmup)
         barrier()
-        reps128 = eng.als(min(a.steps, 10))
+        # as many iterations as the reference arm runs, so that the final
+        # fits of the two arms are taken after the same iteration
+        reps128 = eng.als(a.steps)
         prof128 = [eng.profile_mttkrp(n, reps=2) for n in range(t.order)]
         st128 = eng.stats()
         r128 = {"ms_per_iter": float(np.mean([r.ms for r in reps128])),
@@ -368,6 +370,7 @@ def run_engine(a):
                 "sparse_kernel_ms_per_mode": [p["sparse_ms"] for p in prof128],
                 "tile_kernel_ms_per_mode": [p["tiles_ms"] for p in prof128],
                 "final_fit": reps128[-1].fit,
+                "fit_iters": a.warmup + len(reps128),
                 "tf32_path": bool(st128["tf32_path"])}
         r128["gather_ceiling"] = gather_ceiling(eng, local, t, st128["sparse_nnz"], 128,
                                                 r128["sparse_kernel_ms_per_mode"])
@@ -640,7 +643,8 @@ def run_reference(a):
                 t128, f128, _ = run_ref_binary(a, binary, tns, 128, order)
                 r128 = {"ms_per_iter": float(np.mean(t128)) if t128 else None,
                         "median_ms_per_iter": float(np.median(t128)) if t128 else None,
-                        "iters": len(t128), "final_fit": f128[-1] if f128 else None}
+                        "iters": len(t128), "final_fit": f128[-1] if f128 else None,
+                        "fit_iters": len(f128)}
         except RuntimeError as e:
             print(json.dumps({"impl": "reference", "unavailable": str(e)}))
             return
