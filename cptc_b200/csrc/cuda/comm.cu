@@ -92,9 +92,10 @@ void clear_unowned(Engine& E, int n, double* base) {
 //   rows [H, I)    this rank's solved slab rows, zeros elsewhere (summed:
 //                  every rank's rows, exactly),
 //   past row I     the Gram partial sum and fit dots (summed: the totals);
-// then rows [H, I) are copied into F[n].  Grouping the three all-reduces and
-// G slab broadcasts of unequal length instead cost 0.05-0.1 ms per mode
-// update on 4 B200s (per-collective latency), one collective a fraction.
+// then rows [H, I) are copied into F[n].  Against G in-place broadcasts of
+// unequal slabs, which ran one after another, this cut mode 2's exchange
+// on config 4 from 0.145 to 0.10 ms on 4 B200s (0.17 ms on 8 with the
+// broadcasts); against three grouped all-reduces it measured the same.
 double* comm_exchange_mode(Engine& E, int n, int nblk, int ndots) {
   const int RR = E.R * E.R;
   const uint64_t R = (uint64_t)E.R, I = E.dims[n], H = E.heavy_rows[n];
