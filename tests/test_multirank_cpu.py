@@ -84,3 +84,21 @@ def test_sharded_als_with_a_split_head_row():
         sizes = [out[r][3][m] for r in range(3)]
         assert sum(sizes) == spec["nnz"]
         assert max(sizes) < 0.45 * spec["nnz"]  # the head row no longer sits on one rank
+
+
+def test_sharded_als_with_every_row_in_the_heavy_prefix():
+    # few 16-row blocks, each above an eighth of a rank's share on 4 ranks:
+    # every row of every mode is in the heavy prefix, so no rank owns a slab
+    # and each mode update is the prefix's all-reduce alone
+    spec = dict(dims=(80, 64, 12), nnz=6_000, seed=9, values="lognormal", R=8, iters=3)
+    out = _run(4, spec)
+    assert list(out[0][4]) == list(spec["dims"])
+    t = make_cpu_case(spec)
+    ref = np_als3(t, spec["R"], spec["iters"])
+    assert np.max(np.abs(out[0][0] - ref)) < 1e-10
+    for r in range(1, 4):
+        assert np.array_equal(out[r][0], out[0][0])
+        for a, b in zip(out[r][1], out[0][1]):
+            assert np.array_equal(a, b)
+    for m in range(3):
+        assert sum(out[r][3][m] for r in range(4)) == spec["nnz"]
