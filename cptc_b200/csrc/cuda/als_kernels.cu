@@ -628,27 +628,6 @@ void launch_norm_finalize(const double* part, int nblk, int R, int generic_norm,
   CPTC_LAUNCH_CHECK();
 }
 
-// y += x over n doubles (both 16-byte aligned device buffers).
-__global__ void k_add_into(double* __restrict__ y, const double* __restrict__ x, uint64_t n) {
-  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  const uint64_t n2 = n / 2;
-  double2* y2 = reinterpret_cast<double2*>(y);
-  const double2* x2 = reinterpret_cast<const double2*>(x);
-  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n2; i += stride) {
-    double2 a = y2[i];
-    const double2 b = x2[i];
-    a.x += b.x;
-    a.y += b.y;
-    y2[i] = a;
-  }
-  if (blockIdx.x == 0 && threadIdx.x == 0 && (n & 1)) y[n - 1] += x[n - 1];
-}
-
-void launch_add_into(double* y, const double* x, uint64_t n, cudaStream_t s) {
-  k_add_into<<<grid_for(n / 2 + 1, 256, 148 * 8), 256, 0, s>>>(y, x, n);
-  CPTC_LAUNCH_CHECK();
-}
-
 void launch_scale_cols(double* F, uint64_t rows, int R, const double* scale, cudaStream_t s) {
   const uint64_t n = rows * (uint64_t)R;
   k_scale_cols<<<grid_for(n, 256, 148 * 32), 256, 0, s>>>(F, n, R, scale);

@@ -164,8 +164,6 @@ int launch_apply_solve(const double* FtV, const double* Ainv, const double* lamb
 void launch_norm_finalize(const double* part, int nblk, int R, int generic_norm,
                           double* lambda, double* G, double* scale, cudaStream_t s);
 void launch_scale_cols(double* F, uint64_t rows, int R, const double* scale, cudaStream_t s);
-// y += x over n doubles.
-void launch_add_into(double* y, const double* x, uint64_t n, cudaStream_t s);
 // out[0] = iprod = sum_r lambda_r dot_r (dot_r * scale[r] when scale is
 // given), out[1] = model^2.
 void launch_fit_final(const double* dot_part, int nblk, const double* scale, const double* lambda,
